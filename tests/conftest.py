@@ -1,0 +1,30 @@
+"""Shared pytest setup: the `gpu` marker and the package path.
+
+Tests marked `gpu` need an sm_100 GPU and the built libwamb.so; everything
+else runs on CPU. The importable package (`wam_ops`) lives under
+`wam-egale_b200/`, which is put on sys.path here.
+"""
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+for p in (ROOT, ROOT / "wam-egale_b200"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU and libwamb.so")
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.fail("gpu test selected but no CUDA device is visible")
+    major, minor = torch.cuda.get_device_capability()
+    if (major, minor) != (10, 0):
+        pytest.fail(f"gpu tests need sm_100 (B200); got sm_{major}{minor}")
+    return torch.device("cuda", 0)

@@ -1,0 +1,73 @@
+"""tcgen05 GEMM (wamb_linear) against a torch fp32 reference on the GPU.
+
+Tolerance: the kernel accumulates in fp32 and rounds once to bf16, so the
+error against an fp32 reference of the same bf16 operands is bounded by the
+bf16 output rounding (|x| * 2^-8) plus fp32 accumulation-order noise.
+"""
+import pytest
+import torch
+
+from wam_ops import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, ws, bs):
+    w = torch.cat(ws, 0).float()
+    y = a.float() @ w.t()
+    if bs[0] is not None:
+        y = y + torch.cat(bs, 0).float()
+    return y
+
+
+def _close(out, ref):
+    err = (out.float() - ref).abs()
+    bound = ref.abs() * 2.0 ** -8 + 1e-2
+    assert torch.isfinite(out.float()).all()
+    assert (err <= bound).all(), f"max err {err.max().item()} / worst ratio {(err / bound).max().item()}"
+
+
+@pytest.mark.parametrize("m,k,n,groups", [
+    (128, 64, 64, 1), (200, 256, 256, 1), (880, 512, 384, 3), (1592, 1536, 1536, 1),
+    (64, 3072, 1024, 1), (7, 128, 128, 2),
+])
+def test_linear_bias(cuda_device, m, k, n, groups):
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + k)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.05).bfloat16() for _ in range(groups)]
+    bs = [torch.randn(n, device="cuda", generator=g).bfloat16() for _ in range(groups)]
+    out = ops.linear(a, ws, bs)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    _close(out, _ref(a, ws, bs))
+
+
+def test_linear_gelu(cuda_device):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    a = torch.randn(300, 256, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(512, 256, device="cuda", generator=g) * 0.05).bfloat16()
+    b = torch.randn(512, device="cuda", generator=g).bfloat16()
+    out = ops.linear(a, w, b, epilogue=_lib.EPI_GELU)
+    ref = torch.nn.functional.gelu(_ref(a, [w], [b]), approximate="tanh")
+    _close(out, ref)
+
+
+@pytest.mark.parametrize("temb_len,temb_f32", [(1, True), (40, False)])
+def test_linear_residual_gate(cuda_device, temb_len, temb_f32):
+    g = torch.Generator(device="cuda").manual_seed(2)
+    B, Q, D, K = 3, 40, 256, 512
+    a = torch.randn(B * Q, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(D, K, device="cuda", generator=g) * 0.05).bfloat16()
+    b = torch.randn(D, device="cuda", generator=g).bfloat16()
+    res = torch.randn(B * Q, D, device="cuda", generator=g).bfloat16()
+    table = torch.randn(6, D, device="cuda", generator=g)
+    temb = torch.randn(B, temb_len, 6, D, device="cuda", generator=g)
+    if not temb_f32:
+        temb = temb.bfloat16()
+    out = ops.linear(a, w, b, epilogue=_lib.EPI_RES_GATE, res=res, table=table, temb=temb,
+                     rows_per_batch=Q, gate_index=2)
+    gate = (table[2][None, None] + temb[:, :, 2].float()).expand(B, Q, D).reshape(B * Q, D)
+    ref = res.float() + _ref(a, [w], [b]) * gate
+    _close(out, ref)
+    out2 = ops.linear(a, w, b, epilogue=_lib.EPI_RES, res=res)
+    _close(out2, res.float() + _ref(a, [w], [b]))

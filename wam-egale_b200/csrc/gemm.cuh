@@ -1,0 +1,298 @@
+// Persistent tcgen05 GEMM for the block's dense projections:
+//   out[M, N] = epilogue( A[M, K] * W[N, K]^T + bias[N] )
+// A and W are bf16 row-major (K contiguous), accumulation is fp32 in TMEM.
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer (A tile 128x64, W tile BNx64, 128B swizzle)
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: tcgen05.ld -> bias / GELU / residual / gate -> bf16 stores
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the MMAs of tile i+1.
+//
+// The output columns may be split into up to three groups that each read a
+// different weight tensor (the separate to_q / to_k / to_v Linear weights of
+// the reference, model.py:318-320), so no concatenated weight copy is needed.
+#pragma once
+#include "common.cuh"
+
+namespace wamb {
+
+enum GemmEpilogue : int {
+  EPI_BIAS = 0,      // bf16(acc + b)
+  EPI_GELU = 1,      // bf16(gelu_tanh(acc + b))                 FFN1, model.py:733-735
+  EPI_RES = 2,       // bf16(res + (acc + b))                    cross-attn residual, model.py:783
+  EPI_RES_GATE = 3,  // bf16(res + (acc + b) * (table + temb))   gated residuals, model.py:771,792
+};
+
+struct GemmParams {
+  int M, N, K;
+  int n_per_group;                   // columns per weight group (N = groups * n_per_group)
+  const __nv_bfloat16* bias[3];      // per group, may be null
+  __nv_bfloat16* out;
+  long long ldo;                     // output row stride (elements)
+  int epi;
+  const __nv_bfloat16* res;          // residual [M, ldr]
+  long long ldr;
+  // Gate = table[gate_idx, col] + temb[b, l, gate_idx, col]  (model.py:751-759)
+  const float* table;                // [6, D] fp32
+  const void* temb;                  // [B, L, 6, D] fp32 or bf16
+  int temb_f32, temb_L, rows_per_batch, gate_idx, D;
+};
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr uint32_t BAR_OFF = STAGES * (A_BYTES + B_BYTES);
+  static constexpr uint32_t NBARS = 2 * STAGES + 5;
+  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+};
+
+WAMB_DEV float gelu_tanh(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), the formula of the
+  // reference's gelu_kernel (baseline/csrc/block.cu:119-124).
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+// Bounded wait used only on the teardown path (ignores the abort flag).
+WAMB_DEV void mbar_wait_teardown(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > WAMB_WAIT_TIMEOUT_NS) {
+      record_error(1);
+      return;
+    }
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                   const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
+                   const GemmParams p) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * STAGES;
+  const uint32_t tfull0 = empty0 + 8 * STAGES;
+  const uint32_t tempty0 = tfull0 + 16;
+  const uint32_t drain = tempty0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.M + GEMM_BM - 1) / GEMM_BM;
+  const int num_n = p.N / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = p.K / GEMM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB0);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer
+      int it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        const int m_blk = t % num_m, n_blk = t / num_m;
+        const int n0 = n_blk * BN;
+        const int g = n0 / p.n_per_group;
+        const int n_local = n0 - g * p.n_per_group;
+        const CUtensorMap* mb = g == 0 ? &tmB0 : (g == 1 ? &tmB1 : &tmB2);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(full0 + 8 * s, L::A_BYTES + L::B_BYTES);
+          tma_load_2d(smem_u32(sA + s * L::A_BYTES), &tmA, full0 + 8 * s, kb * GEMM_BK, m_blk * GEMM_BM);
+          tma_load_2d(smem_u32(sB + s * L::B_BYTES), mb, full0 + 8 * s, kb * GEMM_BK, n_local);
+        }
+        if (!ok) break;
+      }
+      // Teardown: wait for the last load issued into each stage to land.
+      for (int s = 0; s < STAGES; ++s) {
+        if (it > s) {
+          const int last = s + ((it - 1 - s) / STAGES) * STAGES;
+          mbar_wait_teardown(full0 + 8 * s, (last / STAGES) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------------- MMA issuer
+      constexpr uint32_t IDESC = idesc_bf16(GEMM_BM, BN, 0);
+      int it = 0, tc = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
+        const int acc = tc & 1;
+        const uint32_t aph = (tc >> 1) & 1;
+        if (!mbar_wait(tempty0 + 8 * acc, aph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * L::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * L::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            const uint64_t ad = sw128_desc(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(b_base + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+          }
+          umma_commit(empty0 + 8 * s);
+        }
+        if (!ok) break;
+        umma_commit(tfull0 + 8 * acc);
+      }
+      // Teardown: all MMAs issued by this thread must finish before TMEM is freed.
+      umma_commit(drain);
+      mbar_wait_teardown(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter accessible to this warp
+    const int row_in_tile = q * 32 + lane;
+    int tc = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
+      const int acc = tc & 1;
+      const uint32_t aph = (tc >> 1) & 1;
+      if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) break;
+      tc_fence_after();
+      const int m_blk = t % num_m, n_blk = t / num_m;
+      const int row = m_blk * GEMM_BM + row_in_tile;
+      const bool valid = row < p.M;
+      const int n0 = n_blk * BN;
+      const int g = n0 / p.n_per_group;
+      const int n_local0 = n0 - g * p.n_per_group;
+      const __nv_bfloat16* bias = p.bias[g];
+      const float* gate_tab = nullptr;
+      const float* gate_f32 = nullptr;
+      const __nv_bfloat16* gate_bf = nullptr;
+      if (p.epi == EPI_RES_GATE && valid) {
+        const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
+        const long long l = p.temb_L == 1 ? 0 : tok;
+        const long long off = ((static_cast<long long>(b) * p.temb_L + l) * 6 + p.gate_idx) * p.D;
+        gate_tab = p.table + static_cast<long long>(p.gate_idx) * p.D;
+        if (p.temb_f32) gate_f32 = static_cast<const float*>(p.temb) + off;
+        else gate_bf = static_cast<const __nv_bfloat16*>(p.temb) + off;
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, v);
+        tmem_wait_ld();
+        if (!valid) continue;
+        const int col = n0 + c * 32;            // output column
+        const int lcol = n_local0 + c * 32;     // column within the weight group
+        if (bias != nullptr) {
+          const uint4* bp = reinterpret_cast<const uint4*>(bias + lcol);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 w = __ldg(bp + j);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const float2 f = unpack_bf16(ws[h]);
+              v[8 * j + 2 * h] += f.x;
+              v[8 * j + 2 * h + 1] += f.y;
+            }
+          }
+        }
+        if (p.epi == EPI_GELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+        } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
+          if (p.epi == EPI_RES_GATE) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 tb = __ldg(reinterpret_cast<const float4*>(gate_tab + col + j));
+              float4 te;
+              if (gate_f32 != nullptr) {
+                te = __ldg(reinterpret_cast<const float4*>(gate_f32 + col + j));
+              } else {
+                const uint2 w = __ldg(reinterpret_cast<const uint2*>(gate_bf + col + j));
+                const float2 a = unpack_bf16(w.x), b2 = unpack_bf16(w.y);
+                te = make_float4(a.x, a.y, b2.x, b2.y);
+              }
+              v[j] *= tb.x + te.x;
+              v[j + 1] *= tb.y + te.y;
+              v[j + 2] *= tb.z + te.z;
+              v[j + 3] *= tb.w + te.w;
+            }
+          }
+          const uint4* rp = reinterpret_cast<const uint4*>(p.res + row * p.ldr + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 w = __ldg(rp + j);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const float2 f = unpack_bf16(ws[h]);
+              v[8 * j + 2 * h] += f.x;
+              v[8 * j + 2 * h + 1] += f.y;
+            }
+          }
+        }
+        uint4* op = reinterpret_cast<uint4*>(p.out + row * p.ldo + col);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+          w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+          w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+          w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+          op[j] = w;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty0 + 8 * acc);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+}  // namespace wamb

@@ -1,0 +1,417 @@
+// Memory-bound glue kernels of the block (one CTA per token row, 128-bit
+// vector loads, warp-shuffle reductions, fp32 math):
+//   ln_kernel        LayerNorm (no affine) + adaLN modulation   model.py:761-763, 786-788
+//                    LayerNorm (fp32 affine)                      model.py:775-776 (norm2)
+//   rms_rope_kernel  RMSNorm across all heads (* gamma) + 3D RoPE, K/V written
+//                    into the caller's KV-pool slots              model.py:609-623, 577-589
+//   kv_layout_kernel slot allocation with id eviction, run-tile list of the
+//                    visible KV, mask restore for update_cache=0  model.py:547-593, 667-686
+#pragma once
+#include "common.cuh"
+
+namespace wamb {
+
+// ---------------------------------------------------------------- helpers
+template <int NWARPS>
+WAMB_DEV float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();  // protect `red` from the previous use
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < NWARPS; ++i) t += red[i];
+  return t;
+}
+
+WAMB_DEV void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 w = *reinterpret_cast<const uint4*>(p);
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const float2 t = unpack_bf16(ws[h]);
+    f[2 * h] = t.x;
+    f[2 * h + 1] = t.y;
+  }
+}
+WAMB_DEV void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 w;
+  w.x = pack_bf16(f[0], f[1]);
+  w.y = pack_bf16(f[2], f[3]);
+  w.z = pack_bf16(f[4], f[5]);
+  w.w = pack_bf16(f[6], f[7]);
+  *reinterpret_cast<uint4*>(p) = w;
+}
+WAMB_DEV void load8f(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+// Modulation row: table[idx, col..col+8] + temb[..., idx, col..col+8] (model.py:751-759).
+WAMB_DEV void load_mod8(const float* table, const void* temb, int temb_f32, long long temb_off,
+                        int idx, int D, int col, float (&f)[8]) {
+  float t[8];
+  load8f(table + static_cast<long long>(idx) * D + col, f);
+  const long long o = temb_off + static_cast<long long>(idx) * D + col;
+  if (temb_f32) load8f(static_cast<const float*>(temb) + o, t);
+  else load8(static_cast<const __nv_bfloat16*>(temb) + o, t);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] += t[i];
+}
+
+// ------------------------------------------------------------ LayerNorm
+struct LnParams {
+  const __nv_bfloat16* x;
+  long long ldx;
+  __nv_bfloat16* out;
+  long long ldo;
+  int M, D;
+  float eps;
+  int affine;             // 1: y = LN(x) * gamma + beta ; 0: y = LN(x) * (1 + scale) + shift
+  const float* gamma;
+  const float* beta;
+  const float* table;     // [6, D]
+  const void* temb;       // [B, L, 6, D]
+  int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
+};
+
+template <int VPT>
+__global__ void ln_kernel(const LnParams p) {
+  constexpr int MAXW = 32;
+  __shared__ float red[MAXW];
+  const int row = blockIdx.x;
+  const int nthr = blockDim.x;
+  const int nw = nthr >> 5;
+  float v[VPT][8];
+  const __nv_bfloat16* xr = p.x + static_cast<long long>(row) * p.ldx;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    load8(xr + (i * nthr + threadIdx.x) * 8, v[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += v[i][j];
+  }
+  // Generic block reduction (number of warps known only at run time).
+  auto reduce = [&](float a) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+  };
+  const float mean = reduce(s) / p.D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float d = v[i][j] - mean;
+      q += d * d;
+    }
+  const float rstd = rsqrtf(reduce(q) / p.D + p.eps);
+  long long temb_off = 0;
+  if (!p.affine) {
+    const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
+    const long long l = p.temb_L == 1 ? 0 : tok;
+    temb_off = (static_cast<long long>(b) * p.temb_L + l) * 6 * p.D;
+  }
+  __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ldo;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int col = (i * nthr + threadIdx.x) * 8;
+    float a[8], b[8], y[8];
+    if (p.affine) {
+      load8f(p.gamma + col, a);
+      load8f(p.beta + col, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = (v[i][j] - mean) * rstd * a[j] + b[j];
+    } else {
+      load_mod8(p.table, p.temb, p.temb_f32, temb_off, p.scale_idx, p.D, col, a);
+      load_mod8(p.table, p.temb, p.temb_f32, temb_off, p.shift_idx, p.D, col, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = (v[i][j] - mean) * rstd * (1.f + a[j]) + b[j];
+    }
+    store8(orow + col, y);
+  }
+}
+
+// ------------------------------------------------------- RMSNorm + RoPE
+struct RmsParams {
+  __nv_bfloat16* x;        // [M, ld]: section 0 at column 0, section 1 at column D, V at 2D
+  long long ld;
+  int M, D, rows_per_batch;
+  int sections;            // 1 or 2
+  const __nv_bfloat16* gamma[2];
+  float eps[2];
+  const float2* freq;      // complex64 [freq_batch, rows_per_batch, 64] or null (no RoPE)
+  int freq_batch;
+  // Optional KV-pool destination for section 1 (K) and the V columns.
+  __nv_bfloat16* pool_k;
+  __nv_bfloat16* pool_v;
+  long long pool;          // slots per pool batch row
+  const int* slots;        // [rows_per_batch] pool slot of each new token
+};
+
+template <int VPT>
+__global__ void rms_rope_kernel(const RmsParams p) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int nthr = blockDim.x;
+  const int nw = nthr >> 5;
+  const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
+  __nv_bfloat16* xr = p.x + static_cast<long long>(row) * p.ld;
+  auto reduce = [&](float a) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+  };
+  const bool to_pool = p.pool_k != nullptr;
+  long long dst_row = 0;
+  if (to_pool) dst_row = static_cast<long long>(b) * p.pool + p.slots[tok];
+  for (int s = 0; s < p.sections; ++s) {
+    float v[VPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      load8(xr + s * p.D + (i * nthr + threadIdx.x) * 8, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+    const float rstd = rsqrtf(reduce(ss) / p.D + p.eps[s]);
+    __nv_bfloat16* dst = (s == 1 && to_pool) ? p.pool_k + dst_row * p.D : xr + s * p.D;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int col = (i * nthr + threadIdx.x) * 8;
+      float g[8], y[8];
+      load8(p.gamma[s] + col, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = v[i][j] * rstd * g[j];
+      if (p.freq != nullptr) {
+        // Pairs (2j, 2j+1) of each 128-wide head rotate by freq[b?, tok, j]
+        // (model.py:614-621, complex multiply).
+        const int fb = p.freq_batch == 1 ? 0 : b;
+        const float4* f = reinterpret_cast<const float4*>(
+            p.freq + (static_cast<long long>(fb) * p.rows_per_batch + tok) * 64 + ((col & 127) >> 1));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float4 c = f[h];  // (re0, im0, re1, im1)
+          const float a0 = y[4 * h], b0 = y[4 * h + 1], a1 = y[4 * h + 2], b1 = y[4 * h + 3];
+          y[4 * h] = a0 * c.x - b0 * c.y;
+          y[4 * h + 1] = a0 * c.y + b0 * c.x;
+          y[4 * h + 2] = a1 * c.z - b1 * c.w;
+          y[4 * h + 3] = a1 * c.w + b1 * c.z;
+        }
+      }
+      store8(dst + col, y);
+    }
+  }
+  if (to_pool) {
+    const uint4* src = reinterpret_cast<const uint4*>(xr + 2 * static_cast<long long>(p.D));
+    uint4* dst = reinterpret_cast<uint4*>(p.pool_v + dst_row * p.D);
+    for (int i = threadIdx.x; i < p.D / 8; i += nthr) dst[i] = src[i];
+  }
+}
+
+// ------------------------------------------------------------ KV layout
+// One CTA of 1024 threads. The pool mask is staged in shared memory; each
+// thread owns a contiguous segment of slots so that block scans follow the
+// physical slot order (the order of mask.nonzero() in the reference).
+constexpr int KV_THREADS = 1024;
+constexpr int KV_MAX_POOL = 16384;
+constexpr int KV_TILE = 128;
+
+struct KvParams {
+  uint8_t* mask;            // [pool] bool
+  long long* ids;           // [pool] int64
+  uint8_t* pred;            // [pool] bool
+  int pool;
+  int q;                    // new tokens per batch row
+  int update;               // 0 / 1 / 2
+  int candidate;            // read-only candidate verification
+  const long long* rows;    // [batch] candidate history rows
+  int batch, pool_batch;
+  int* new_slots;           // [q]   out: pool slot of each new token
+  int2* tiles;              // [pool] out: (first slot, length) of each visible run piece
+  int* counts;              // [2]   out: number of tiles, number of visible slots
+};
+
+WAMB_DEV int warp_incl_scan(int v) {
+  const int l = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (l >= o) v += t;
+  }
+  return v;
+}
+
+// Exclusive scan over the block in thread order; returns the prefix and the total.
+WAMB_DEV int block_excl_scan(int v, int* sh, int* total) {
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int inc = warp_incl_scan(v);
+  __syncthreads();
+  if (l == 31) sh[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    const int s = sh[l];
+    const int si = warp_incl_scan(s);
+    sh[l] = si - s;
+    if (l == 31) sh[32] = si;
+  }
+  __syncthreads();
+  const int res = sh[w] + inc - v;
+  *total = sh[32];
+  return res;
+}
+
+WAMB_DEV long long block_min_ll(long long v, long long* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const long long t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = t < v ? t : v;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  long long r = sh[0];
+  for (int i = 1; i < KV_THREADS / 32; ++i) r = sh[i] < r ? sh[i] : r;
+  return r;
+}
+WAMB_DEV long long block_max_ll(long long v, long long* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const long long t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = t > v ? t : v;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  long long r = sh[0];
+  for (int i = 1; i < KV_THREADS / 32; ++i) r = sh[i] > r ? sh[i] : r;
+  return r;
+}
+
+__global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams p) {
+  __shared__ uint8_t m[KV_MAX_POOL];
+  __shared__ int sh[33];
+  __shared__ long long shl[32];
+  __shared__ int s_err;
+  const int seg = (p.pool + KV_THREADS - 1) / KV_THREADS;
+  const int lo = threadIdx.x * seg;
+  const int hi = min(p.pool, lo + seg);
+  if (threadIdx.x == 0) s_err = 0;
+  for (int i = threadIdx.x; i < p.pool; i += KV_THREADS) m[i] = p.mask[i] ? 1 : 0;
+  __syncthreads();
+  int total = 0;
+
+  if (p.candidate) {
+    for (int i = threadIdx.x; i < p.batch; i += KV_THREADS)
+      if (p.rows[i] < 0 || p.rows[i] >= p.pool_batch) s_err = 3;
+  } else {
+    // free slots before allocation
+    int nfree = 0;
+    for (int i = lo; i < hi; ++i) nfree += !m[i];
+    block_excl_scan(nfree, sh, &total);
+    int need = p.q - total;
+    // Evict the smallest ids, lowest slot first among equal ids (model.py:553-563).
+    for (int iter = 0; need > 0 && iter <= p.pool; ++iter) {
+      long long mn = LLONG_MAX;
+      for (int i = lo; i < hi; ++i)
+        if (m[i] && p.ids[i] < mn) mn = p.ids[i];
+      mn = block_min_ll(mn, shl);
+      if (mn == LLONG_MAX) {
+        if (threadIdx.x == 0) s_err = 4;
+        break;
+      }
+      int c = 0;
+      for (int i = lo; i < hi; ++i) c += (m[i] && p.ids[i] == mn);
+      const int before = block_excl_scan(c, sh, &total);
+      int r = before;
+      for (int i = lo; i < hi; ++i) {
+        if (m[i] && p.ids[i] == mn) {
+          if (r < need) {
+            m[i] = 0;
+            p.ids[i] = -1;
+          }
+          ++r;
+        }
+      }
+      need -= total < need ? total : need;
+      __syncthreads();
+    }
+    __syncthreads();
+    if (s_err == 0) {
+      // next id = max(valid ids) + 1, or 0 (model.py:565-571)
+      long long mx = -1;
+      for (int i = lo; i < hi; ++i)
+        if (m[i] && p.ids[i] > mx) mx = p.ids[i];
+      mx = block_max_ll(mx, shl);
+      const long long next = mx < 0 ? 0 : mx + 1;
+      // first q free slots in physical order (model.py:551, 564)
+      nfree = 0;
+      for (int i = lo; i < hi; ++i) nfree += !m[i];
+      int r = block_excl_scan(nfree, sh, &total);
+      __syncthreads();
+      for (int i = lo; i < hi; ++i) {
+        if (!m[i]) {
+          if (r < p.q) {
+            p.new_slots[r] = i;
+            m[i] = 1;
+            p.ids[i] = next;
+            p.pred[i] = p.update == 1 ? 1 : 0;
+          }
+          ++r;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // Run-tile list: maximal runs of visible slots inside each 128-slot window.
+  {
+    int nt = 0, nv = 0;
+    for (int i = lo; i < hi; ++i) {
+      nv += m[i];
+      nt += m[i] && (i % KV_TILE == 0 || !m[i - 1]);
+    }
+    int vis = 0;
+    const int t0 = block_excl_scan(nt, sh, &total);
+    const int ntiles = total;
+    block_excl_scan(nv, sh, &vis);
+    int t = t0;
+    for (int i = lo; i < hi; ++i) {
+      if (m[i] && (i % KV_TILE == 0 || !m[i - 1])) {
+        int e = i + 1;
+        const int wend = min(p.pool, (i / KV_TILE + 1) * KV_TILE);
+        while (e < wend && m[e]) ++e;
+        p.tiles[t++] = make_int2(i, e - i);
+      }
+    }
+    if (threadIdx.x == 0) {
+      p.counts[0] = s_err ? 0 : ntiles;
+      p.counts[1] = s_err ? 0 : vis;
+      if (s_err) record_error(s_err);
+    }
+  }
+  __syncthreads();
+  // update_cache == 0 restores the mask of the new slots (model.py:592-593, 684-686).
+  if (!p.candidate && p.update == 0 && s_err == 0) {
+    for (int i = threadIdx.x; i < p.q; i += KV_THREADS) m[p.new_slots[i]] = 0;
+  }
+  __syncthreads();
+  if (!p.candidate)
+    for (int i = threadIdx.x; i < p.pool; i += KV_THREADS) p.mask[i] = m[i];
+}
+
+}  // namespace wamb

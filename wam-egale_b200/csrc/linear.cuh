@@ -1,0 +1,113 @@
+// Host launcher of the tcgen05 GEMM (gemm.cuh): tile-width choice, tensor
+// maps, argument checks.
+#pragma once
+#include "gemm.cuh"
+#include "host.cuh"
+
+namespace wamb {
+
+template <int BN, int STAGES>
+inline int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p,
+                          int sms, cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  static bool configured[64] = {};
+  int dev = 0;
+  WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+  if (!configured[dev]) {
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    configured[dev] = true;
+  }
+  const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * (p.N / BN);
+  const int grid = tiles < sms ? tiles : sms;
+  gemm_tc_kernel<BN, STAGES><<<grid, GEMM_THREADS, L::TOTAL, stream>>>(ta, tb[0], tb[1], tb[2], p);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+// Picks the widest tile (256/128/64 columns) that still gives every SM a
+// tile; falls back to the narrowest legal width for small problems.
+inline int choose_bn(int M, int N, int n_per_group, int sms) {
+  const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
+  const int cands[3] = {256, 128, 64};
+  int best = 0;
+  for (int c : cands) {
+    if (n_per_group % c) continue;
+    if (best == 0) best = c;
+    if (static_cast<long long>(num_m) * (N / c) >= sms) return c;
+    best = c;
+  }
+  return best;
+}
+
+inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
+  WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
+  WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
+  WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
+  WAMB_REQUIRE(a->k % GEMM_BK == 0, WAMB_ERR_SHAPE, "K=%d must be a multiple of 64", a->k);
+  WAMB_REQUIRE(a->n_per_group % 64 == 0, WAMB_ERR_SHAPE, "N per group=%d must be a multiple of 64",
+               a->n_per_group);
+  WAMB_REQUIRE(a->lda >= a->k && a->lda % 8 == 0, WAMB_ERR_ALIGN, "lda");
+  const long long N = static_cast<long long>(a->groups) * a->n_per_group;
+  WAMB_REQUIRE(a->ldo >= N && a->ldo % 8 == 0, WAMB_ERR_ALIGN, "ldo");
+  WAMB_REQUIRE(a->a && a->out, WAMB_ERR_ARG, "null A/out");
+  WAMB_REQUIRE(aligned16(a->a) && aligned16(a->out), WAMB_ERR_ALIGN, "A/out alignment");
+  for (int g = 0; g < a->groups; ++g) {
+    WAMB_REQUIRE(a->weight[g] && aligned16(a->weight[g]), WAMB_ERR_ARG, "weight[%d]", g);
+    WAMB_REQUIRE(!a->bias[g] || aligned16(a->bias[g]), WAMB_ERR_ALIGN, "bias[%d]", g);
+  }
+  WAMB_REQUIRE(a->epilogue >= 0 && a->epilogue <= 3, WAMB_ERR_ARG, "epilogue");
+  if (a->epilogue == WAMB_EPI_RES || a->epilogue == WAMB_EPI_RES_GATE) {
+    WAMB_REQUIRE(a->res && aligned16(a->res) && a->ldr >= N && a->ldr % 8 == 0, WAMB_ERR_ARG,
+                 "residual");
+  }
+  if (a->epilogue == WAMB_EPI_RES_GATE) {
+    WAMB_REQUIRE(a->table && a->temb && aligned16(a->table) && aligned16(a->temb), WAMB_ERR_ARG,
+                 "gate tables");
+    WAMB_REQUIRE(a->dim == N && a->dim % 8 == 0, WAMB_ERR_SHAPE, "gate dim must equal N");
+    WAMB_REQUIRE(a->rows_per_batch > 0 && a->temb_len >= 1 &&
+                     (a->temb_len == 1 || a->temb_len == a->rows_per_batch),
+                 WAMB_ERR_SHAPE, "temb_len must be 1 or rows_per_batch");
+    WAMB_REQUIRE(a->gate_index >= 0 && a->gate_index < 6, WAMB_ERR_ARG, "gate_index");
+  }
+  if (a->m == 0) return WAMB_OK;
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+
+  const int bn = choose_bn(a->m, static_cast<int>(N), a->n_per_group, di.sms);
+  CUtensorMap ta, tb[3];
+  rc = make_tmap_bf16(&ta, a->a, a->m, a->k, a->lda, GEMM_BM);
+  if (rc) return rc;
+  for (int g = 0; g < 3; ++g) {
+    const int src = g < a->groups ? g : 0;
+    rc = make_tmap_bf16(&tb[g], a->weight[src], a->n_per_group, a->k, a->k, bn);
+    if (rc) return rc;
+  }
+  GemmParams p{};
+  p.M = a->m;
+  p.N = static_cast<int>(N);
+  p.K = a->k;
+  p.n_per_group = a->n_per_group;
+  for (int g = 0; g < 3; ++g)
+    p.bias[g] = g < a->groups ? static_cast<const __nv_bfloat16*>(a->bias[g]) : nullptr;
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.ldo = a->ldo;
+  p.epi = a->epilogue;
+  p.res = static_cast<const __nv_bfloat16*>(a->res);
+  p.ldr = a->ldr;
+  p.table = a->table;
+  p.temb = a->temb;
+  p.temb_f32 = a->temb_is_f32;
+  p.temb_L = a->temb_len;
+  p.rows_per_batch = a->rows_per_batch > 0 ? a->rows_per_batch : 1;
+  p.gate_idx = a->gate_index;
+  p.D = a->dim;
+  switch (bn) {
+    case 256: return launch_gemm_bn<256, 4>(ta, tb, p, di.sms, stream);
+    case 128: return launch_gemm_bn<128, 6>(ta, tb, p, di.sms, stream);
+    default: return launch_gemm_bn<64, 8>(ta, tb, p, di.sms, stream);
+  }
+}
+
+}  // namespace wamb
