@@ -106,6 +106,129 @@ typedef struct wamb_linear_args {
 
 WAMB_API int wamb_linear(const wamb_linear_args* args, void* stream);
 
+/*
+ * Flash attention (non-causal, head_dim 128) on the tcgen05 tensor cores.
+ * Replaces the reference's FA2 `sdpa(q, k, v, scale)`
+ * (算子研究/wam_ops/optimized/csrc/attention.cu:121-181) and the pack + SDPA
+ * pair of its KV path (baseline/csrc/block.cu:213-224, 228-260): keys are read
+ * in place from up to two sources.
+ *   Query row r of batch row b is q[(b*q_rows + r)*ldq + q_col + h*128 + d].
+ *   Source 0: batch row b reads rows src0_batch_stride * s(b) + [tile rows],
+ *     s(b) = src0_map[b] if src0_map, 0 if src0_broadcast, else b; the
+ *     tiles are `tiles` (int32 pairs (first row, length <= 128), count in
+ *     device memory at *n_tiles) or, when tiles is NULL, [0, src0_len) in
+ *     128-row pieces. K at column k0_col + h*128 of k0, V likewise of v0.
+ *   Source 1 (optional, k1 != NULL): the q_rows own rows b*q_rows + [0, q_rows)
+ *     of k1 / v1 (candidate verification: history + private suffix).
+ * Output: out[(b*q_rows + r)*ldo + h*128 + d], bf16.
+ */
+typedef struct wamb_attention_args {
+  int32_t batch, heads, q_rows;
+  const void* q; int64_t ldq; int64_t q_total_rows; int32_t q_col;
+  const void* k0; const void* v0; int64_t ld0; int64_t src0_total_rows;
+  int32_t k0_col, v0_col;
+  int32_t src0_batch_stride;
+  const int64_t* src0_map;
+  int32_t src0_broadcast;
+  const int32_t* tiles; const int32_t* n_tiles;
+  int32_t src0_len;
+  const void* k1; const void* v1; int64_t ld1; int32_t k1_col, v1_col;
+  void* out; int64_t ldo;
+} wamb_attention_args;
+
+WAMB_API int wamb_attention(const wamb_attention_args* args, void* stream);
+
+/*
+ * One Wan-DiT transformer block forward (WanTransformerBlock.forward,
+ * 投机采样/wam-p0-worktree/wan_va/modules/model.py:741-794, with
+ * WanAttention.forward :595-691 and the "original" KV cache :547-593).
+ * Replaces the reference's native entry
+ *   forward(weights[27], x, context, temb, freq, cache[5], candidate_rows,
+ *           update, eps[7], debug, ...)
+ * of 算子研究/wam_ops/baseline/csrc/block.cu:262-311 and
+ * 算子研究/wam_ops/optimized/csrc/whole_layer.cu:1080-1229.
+ *
+ * weights[27] follow the reference order (baseline/native.py:31-46):
+ *  0 scale_shift_table [1,6,D] fp32 | 1,2 norm2 gamma,beta [D] fp32 (NULL: norm2 is Identity)
+ *  3..10 self to_q W,b / to_k W,b / to_v W,b / to_out W,b (W [D,D] bf16, b [D] bf16)
+ *  11,12 self norm_q / norm_k gamma [D] bf16
+ *  13..20 cross to_q / to_k / to_v / to_out (W,b) | 21,22 cross norm_q / norm_k gamma
+ *  23,24 ffn proj W [F,D], b [F] | 25,26 ffn out W [D,F], b [D]     (all bf16)
+ * eps[7]: norm1, norm2, norm3, self q, self k, cross q, cross k.
+ *
+ * Self KV cache (optional; cache_k NULL = no cache): the reference schema
+ * k, v [pool_batch, pool, H, 128] bf16, id [pool] int64, mask/is_pred [pool]
+ * bool (1 byte). update 0/1/2 as update_cache; the cache is mutated in place
+ * exactly as the reference does (new rows written, ids/is_pred set, mask set
+ * and, for update 0, restored). candidate_rows [batch] int64 selects the
+ * read-only candidate-verification path (update must be 0).
+ *
+ * Cross K/V: either cross_k/cross_v precomputed ([context_batch, C, D] bf16,
+ * from wamb_cross_kv), or computed per call from `context`. context_rows
+ * ([batch] int64, optional) maps each batch row to its context row;
+ * otherwise context_batch must be batch or 1.
+ *
+ * Scratch: `workspace` of wamb_block_workspace_bytes() bytes (caller-owned,
+ * 256-byte aligned); intermediates stay there after the call (debug taps).
+ */
+typedef struct wamb_block_args {
+  int32_t batch, tokens, dim, heads, ffn_dim;
+  int32_t context_tokens, context_batch;
+  const void* weights[27];
+  double eps[7];
+  const void* x;                 /* [batch, tokens, dim] bf16 */
+  const void* context;           /* [context_batch, context_tokens, dim] bf16 or NULL */
+  const void* cross_k;           /* [context_batch, context_tokens, dim] bf16 or NULL */
+  const void* cross_v;
+  const int64_t* context_rows;   /* [batch] or NULL */
+  const void* temb;              /* [batch, temb_len, 6, dim] */
+  int32_t temb_len, temb_is_f32;
+  const float* freq;             /* complex64 as float pairs [freq_batch, tokens, 64, 2] or NULL */
+  int32_t freq_batch;
+  void* cache_k; void* cache_v;
+  int64_t* cache_id; uint8_t* cache_mask; uint8_t* cache_pred;
+  int32_t pool, pool_batch;
+  const int64_t* candidate_rows; /* [batch] or NULL */
+  int32_t update;
+  void* out;                     /* [batch, tokens, dim] bf16 */
+  void* workspace; size_t workspace_bytes;
+} wamb_block_args;
+
+/* Named intermediates kept in the workspace (byte offsets; -1 = absent). */
+enum wamb_tap {
+  WAMB_TAP_MODULATED1 = 0,  /* [M, D]   LN1 + modulation */
+  WAMB_TAP_QKV = 1,         /* [M, 3D]  q | k | v (q,k after RMS + RoPE unless in the pool) */
+  WAMB_TAP_SELF_ATTN = 2,   /* [M, D] */
+  WAMB_TAP_RESIDUAL1 = 3,   /* [M, D] */
+  WAMB_TAP_NORM2 = 4,       /* [M, D] */
+  WAMB_TAP_CROSS_Q = 5,     /* [M, D]   after RMS */
+  WAMB_TAP_CROSS_K = 6,     /* [Bc*C, D] after RMS (computed per call only) */
+  WAMB_TAP_CROSS_V = 7,
+  WAMB_TAP_CROSS_ATTN = 8,  /* [M, D] */
+  WAMB_TAP_RESIDUAL2 = 9,   /* [M, D] */
+  WAMB_TAP_MODULATED3 = 10, /* [M, D] */
+  WAMB_TAP_GELU = 11,       /* [M, F] */
+  WAMB_TAP_KV_SLOTS = 12,   /* [tokens] int32 pool slot of each new token */
+  WAMB_TAP_KV_TILES = 13,   /* [pool] int32 pairs */
+  WAMB_TAP_KV_COUNTS = 14,  /* [2] int32: tiles, visible slots */
+  WAMB_TAP_COUNT = 15
+};
+
+WAMB_API size_t wamb_block_workspace_bytes(const wamb_block_args* args);
+/* Fills offsets[WAMB_TAP_COUNT]; returns the workspace size. */
+WAMB_API size_t wamb_block_workspace_layout(const wamb_block_args* args, int64_t* offsets);
+WAMB_API int wamb_block_forward(const wamb_block_args* args, void* stream);
+
+/*
+ * Cross-attention K/V of one block for a fixed context (the reference's
+ * WholeLayerBlock.prepare_context(context, precompute=True),
+ * 算子研究/wam_ops/optimized/whole_layer.py:41-67):
+ *   k = RMSNorm(context W_k^T + b_k) * gamma_k,  v = context W_v^T + b_v.
+ * weights/eps as in wamb_block_args (entries 15..18, 22 and eps[6] are read);
+ * k_out, v_out: [context_batch * context_tokens, dim] bf16.
+ */
+WAMB_API int wamb_cross_kv(const wamb_block_args* args, void* k_out, void* v_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,23 @@
+"""CPU oracle for the Wan-DiT block hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg
+(`--impl reference` and the `cpu_baseline` object) may import this package,
+and only as the checker or as the timed CPU reference. The product path
+(wam-egale_b200/) never imports it and has no CPU fallback.
+
+Contents:
+  wan_block.py   plain PyTorch (fp32, CPU) restatement of the reference's
+                 WanTransformerBlock / WanAttention / "original" KV cache /
+                 WanRotaryPosEmbed / get_mesh_id, each citing the reference
+                 file:line it follows.
+  synth.py       seeded synthetic inputs and weights for the BASELINE configs.
+
+Parity pin: tests/golden/make_golden.py runs the reference's own model.py
+source (AST-extracted, in the build container where the reference is
+mounted) on seeded inputs and commits the outputs as fixtures;
+tests/test_oracle_golden.py checks this restatement against them.
+The diffusers pieces the reference imports (FP32LayerNorm, FeedForward,
+Timesteps/TimestepEmbedding) are not in the reference tree; the first two are
+restated from the reference's own native restatements (pinned indirectly),
+the timestep embedder is outside the block and unpinned.
+"""

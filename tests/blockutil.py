@@ -1,0 +1,76 @@
+"""Helpers shared by the block parity tests: seeded oracle blocks, their
+bf16/fp32 GPU copies, the parity statistics and the stated tolerance.
+
+Parity gate: bf16 path vs the fp32 oracle on the same
+(bf16-representable) weights and inputs: cosine >= 0.9999 and
+max |err| <= 2e-2.
+"""
+import copy
+
+import torch
+import torch.nn.functional as F
+
+from oracle import wan_block as ob
+
+COS_MIN = 0.9999
+MAX_ABS = 2e-2
+
+
+def make_oracle_block(dim, ffn, heads, seed, cross_attn_norm=True, randomize=True):
+    """fp32 CPU oracle block with bf16-representable weights (so that the
+    comparison measures the kernels, not weight rounding)."""
+    torch.manual_seed(seed)
+    blk = ob.WanTransformerBlock(dim, ffn, heads, cross_attn_norm=cross_attn_norm, eps=1e-6)
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            if name.endswith("scale_shift_table"):
+                p.copy_(torch.randn_like(p) / dim ** 0.5)
+            elif "norm" in name and name.endswith("weight"):
+                p.copy_(1.0 + 0.1 * torch.randn_like(p) if randomize else torch.ones_like(p))
+            elif "norm" in name and name.endswith("bias"):
+                p.copy_(0.1 * torch.randn_like(p) if randomize else torch.zeros_like(p))
+            elif name.endswith("weight"):
+                p.copy_(torch.randn_like(p) * 0.02)
+            else:
+                p.copy_(0.02 * torch.randn_like(p) if randomize else torch.zeros_like(p))
+            p.copy_(p.bfloat16().float())
+    return blk.eval()
+
+
+def to_device_block(blk, device="cuda"):
+    """GPU copy with the reference dtype policy: fp32 modulation table and
+    norms (keep_in_fp32, model.py:812-825), bf16 everything else."""
+    g = copy.deepcopy(blk)
+    keep32 = ("scale_shift_table", "norm1", "norm2", "norm3")
+    for name, p in g.named_parameters():
+        fp32 = any(name.startswith(k) for k in keep32)
+        p.data = p.data.to(device=device, dtype=torch.float32 if fp32 else torch.bfloat16).contiguous()
+    g.attn1.attn_caches = {}
+    return g
+
+
+def stats(out, ref):
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    err = (out - ref).abs()
+    cos = F.cosine_similarity(out.flatten(), ref.flatten(), dim=0).item()
+    return {"max_abs": err.max().item(), "cos": cos, "finite": bool(torch.isfinite(out).all())}
+
+
+def assert_parity(out, ref, cos_min=COS_MIN, max_abs=MAX_ABS):
+    s = stats(out, ref)
+    assert s["finite"], s
+    assert s["cos"] >= cos_min and s["max_abs"] <= max_abs, s
+    return s
+
+
+def make_inputs(B, Q, D, C, heads, seed, temb_len=1, temb_dtype=torch.float32, ctx_batch=None):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, Q, D, generator=g).bfloat16().float()
+    ctx = torch.randn(ctx_batch or B, C, D, generator=g).bfloat16().float()
+    temb = (torch.randn(B, temb_len, 6, D, generator=g) * 0.5).to(temb_dtype).float()
+    grid = ob.get_mesh_id(max(1, Q // 8), 4, 2, 0)[:, :Q]
+    if grid.shape[1] < Q:
+        grid = torch.cat([grid, ob.get_mesh_id(1, Q - grid.shape[1], 1, 0, action=True)], 1)
+    rope = ob.WanRotaryPosEmbed(128)(grid[None])[:, :, None]
+    return x, ctx, temb, rope

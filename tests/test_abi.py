@@ -1,0 +1,90 @@
+"""CPU checks of the C ABI: the library loads, exports every entry point
+include/wamb.h declares, reports its version, computes workspace layouts and
+rejects bad arguments on the host without touching a GPU."""
+import ctypes
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from wam_ops import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "wamb.h"
+
+
+def test_header_symbols_exported():
+    lib = _lib.load()
+    declared = set(re.findall(r"WAMB_API\s+[\w\s\*]+?\b(wamb_\w+)\s*\(", HEADER.read_text()))
+    assert declared == set(_lib.EXPORTED)
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.wamb_abi_version() == 100
+
+
+@pytest.mark.parametrize("cname,pyname", [("wamb_linear_args", "LinearArgs"),
+                                            ("wamb_attention_args", "AttentionArgs"),
+                                            ("wamb_block_args", "BlockArgs")])
+def test_struct_layout_matches_header(tmp_path, cname, pyname):
+    """Every field offset of the ctypes mirror equals the C compiler's."""
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    st = getattr(_lib, pyname)
+    lines = [f'printf("%zu\\n", sizeof({cname}));']
+    lines += [f'printf("%zu\\n", offsetof({cname}, {f[0]}));' for f in st._fields_]
+    src = tmp_path / "probe.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"wamb.h\"\nint main(void){"
+                   + "".join(lines) + "return 0;}\n")
+    exe = tmp_path / "probe"
+    subprocess.run([cc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    want = [ctypes.sizeof(st)] + [getattr(st, f[0]).offset for f in st._fields_]
+    assert got == want
+
+
+def _args(**kw):
+    a = _lib.BlockArgs()
+    a.batch, a.tokens, a.dim, a.heads, a.ffn_dim = 1, 48, 256, 2, 512
+    a.context_tokens, a.context_batch = 32, 1
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_workspace_layout():
+    lib = _lib.load()
+    a = _args()
+    offs = (ctypes.c_int64 * len(_lib.TAPS))()
+    total = lib.wamb_block_workspace_layout(a, offs)
+    assert total == lib.wamb_block_workspace_bytes(a)
+    M, D, F = 48, 256, 512
+    assert offs[_lib.TAPS.index("modulated1")] == 0
+    assert offs[_lib.TAPS.index("kv_slots")] == -1          # no cache
+    assert offs[_lib.TAPS.index("norm2")] == -1             # weights[1] null -> Identity
+    assert total >= (10 * M * D + M * F) * 2
+    assert all(o % 256 == 0 for o in offs if o >= 0)
+
+
+@pytest.mark.parametrize("kw,code", [
+    ({"dim": 250}, 2),               # dim must be heads * 128
+    ({"tokens": 0}, 2),
+    ({"update": 3}, 1),
+])
+def test_block_forward_rejects_bad_args(kw, code):
+    lib = _lib.load()
+    a = _args(**kw)
+    rc = lib.wamb_block_forward(a, None)
+    assert rc != 0
+    assert lib.wamb_last_error()
+
+
+def test_linear_rejects_bad_shapes():
+    lib = _lib.load()
+    a = _lib.LinearArgs()
+    a.m, a.k, a.groups, a.n_per_group = 10, 100, 1, 64     # K not a multiple of 64
+    assert lib.wamb_linear(a, None) == 2
+    a.k, a.groups = 128, 4
+    assert lib.wamb_linear(a, None) == 1

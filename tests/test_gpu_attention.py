@@ -1,0 +1,116 @@
+"""tcgen05 flash attention (wamb_attention) against torch SDPA in fp32.
+
+Tolerance: P is rounded to bf16 before the PV product and the output once to
+bf16, so |out - ref| <= 1e-2 + 2e-2 * |ref| on N(0,1) inputs.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from wam_ops import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _sdpa_ref(q, k, v):
+    """q [B,Sq,H,d], k/v [B,Sk,H,d] -> fp32 [B,Sq,H,d]."""
+    o = F.scaled_dot_product_attention(q.float().transpose(1, 2), k.float().transpose(1, 2),
+                                       v.float().transpose(1, 2))
+    return o.transpose(1, 2)
+
+
+def _check(out, ref):
+    out = out.float()
+    assert torch.isfinite(out).all()
+    err = (out - ref).abs()
+    bound = 1e-2 + 2e-2 * ref.abs()
+    assert (err <= bound).all(), f"max err {err.max().item()}"
+    cos = F.cosine_similarity(out.flatten(), ref.flatten(), dim=0).item()
+    assert cos >= 0.9999, cos
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk", [(1, 1, 128, 128), (2, 3, 40, 24), (1, 2, 300, 700),
+                                       (2, 2, 7, 1), (1, 4, 129, 257), (3, 1, 1, 513)])
+def test_sdpa_contiguous(cuda_device, B, H, Sq, Sk):
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + Sq * 7 + Sk)
+    q = torch.randn(B, Sq, H, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, Sk, H, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, Sk, H, 128, device="cuda", generator=g).bfloat16()
+    _check(ops.sdpa(q, k, v), _sdpa_ref(q, k, v))
+
+
+def _tiles(mask):
+    """Host restatement of the kernel's tile list: maximal runs of visible
+    slots inside each 128-slot window."""
+    m = mask.cpu().tolist()
+    out = []
+    for i, on in enumerate(m):
+        if on and (i % 128 == 0 or not m[i - 1]):
+            e = i + 1
+            while e < len(m) and e % 128 != 0 and m[e]:
+                e += 1
+            out.append((i, e - i))
+    return out
+
+
+@pytest.mark.parametrize("pool,density", [(700, 1.0), (700, 0.6), (300, 0.1), (1000, 0.97)])
+def test_pool_tiles_ignore_stale_slots(cuda_device, pool, density):
+    """Keys read in place from a pool through a tile list; unused slots hold
+    NaN and must not leak into the output."""
+    g = torch.Generator(device="cuda").manual_seed(pool)
+    B, H, Q = 2, 2, 50
+    kp = torch.randn(B, pool, H, 128, device="cuda", generator=g).bfloat16()
+    vp = torch.randn(B, pool, H, 128, device="cuda", generator=g).bfloat16()
+    mask = torch.rand(pool, device="cuda", generator=g) < density
+    mask[3] = True
+    kp[:, ~mask] = float("nan")
+    vp[:, ~mask] = float("nan")
+    q = torch.randn(B, Q, H, 128, device="cuda", generator=g).bfloat16()
+    tl = _tiles(mask)
+    tiles = torch.tensor(tl, dtype=torch.int32, device="cuda").view(-1, 2)
+    n = torch.tensor([len(tl)], dtype=torch.int32, device="cuda")
+    out = ops.attention(q.view(B * Q, -1), kp.view(B * pool, -1), vp.view(B * pool, -1), heads=H,
+                        q_rows=Q, src0_batch_stride=pool, tiles=tiles, n_tiles=n)
+    idx = mask.nonzero().squeeze(-1)
+    ref = _sdpa_ref(q, kp[:, idx], vp[:, idx])
+    _check(out.view(B, Q, H, 128), ref)
+
+
+def test_candidate_two_sources(cuda_device):
+    """History rows selected by a row map plus each candidate's own K/V
+    (model.py:654-660)."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    Bp, pool, B, H, Q = 2, 400, 4, 2, 32
+    kp = torch.randn(Bp, pool, H, 128, device="cuda", generator=g).bfloat16()
+    vp = torch.randn(Bp, pool, H, 128, device="cuda", generator=g).bfloat16()
+    mask = torch.zeros(pool, dtype=torch.bool, device="cuda")
+    mask[:250] = True
+    mask[300:350] = True
+    rows = torch.tensor([0, 1, 0, 0], dtype=torch.int64, device="cuda")
+    qkv = torch.randn(B * Q, 3 * H * 128, device="cuda", generator=g).bfloat16()
+    tl = _tiles(mask)
+    tiles = torch.tensor(tl, dtype=torch.int32, device="cuda").view(-1, 2)
+    n = torch.tensor([len(tl)], dtype=torch.int32, device="cuda")
+    D = H * 128
+    out = ops.attention(qkv, kp.view(Bp * pool, -1), vp.view(Bp * pool, -1), heads=H, q_rows=Q,
+                        src0_batch_stride=pool, tiles=tiles, n_tiles=n, src0_map=rows,
+                        k1=qkv, v1=qkv, k1_col=D, v1_col=2 * D)
+    idx = mask.nonzero().squeeze(-1)
+    q = qkv[:, :D].view(B, Q, H, 128)
+    k_own = qkv[:, D:2 * D].view(B, Q, H, 128)
+    v_own = qkv[:, 2 * D:].view(B, Q, H, 128)
+    k = torch.cat([kp[:, idx].index_select(0, rows), k_own], 1)
+    v = torch.cat([vp[:, idx].index_select(0, rows), v_own], 1)
+    _check(out.view(B, Q, H, 128), _sdpa_ref(q, k, v))
+
+
+def test_broadcast_source(cuda_device):
+    g = torch.Generator(device="cuda").manual_seed(6)
+    B, H, Q, C = 3, 2, 70, 200
+    q = torch.randn(B * Q, H * 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(C, H * 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(C, H * 128, device="cuda", generator=g).bfloat16()
+    out = ops.attention(q, k, v, heads=H, q_rows=Q, src0_batch_stride=C, src0_len=C, src0_broadcast=True)
+    ref = _sdpa_ref(q.view(B, Q, H, 128), k.view(1, C, H, 128).expand(B, -1, -1, -1),
+                    v.view(1, C, H, 128).expand(B, -1, -1, -1))
+    _check(out.view(B, Q, H, 128), ref)

@@ -1,0 +1,161 @@
+"""Block parity: the B200 native block (through install_block / NativeBlock,
+i.e. through the C ABI) against the fp32 CPU oracle restatement of
+WanTransformerBlock.forward (model.py:741-794), including the KV-cache
+lifecycle (update_cache 0/1/2, id eviction), candidate verification and the
+prepared cross-K/V variant.
+
+Tolerance (stated): cosine >= 0.9999 and
+max |err| <= 2e-2 against the fp32 oracle on identical bf16-representable
+weights and inputs. Cache metadata (id, mask, is_pred) must match exactly.
+"""
+import pytest
+import torch
+
+from blockutil import assert_parity, make_inputs, make_oracle_block, stats, to_device_block
+from wam_ops import _lib
+from wam_ops.install import install_block, install_model
+from wam_ops.whole_layer import WholeLayerBlock
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_native(g, x, ctx, temb, rope, temb_dtype=torch.float32, **kw):
+    with torch.no_grad(), install_block(g):
+        out = g(x.cuda().bfloat16(), ctx.cuda().bfloat16(), temb.cuda().to(temb_dtype),
+                None if rope is None else rope.cuda(), **kw)
+    assert _lib.device_status() == 0
+    return out
+
+
+@pytest.mark.parametrize("B,Q,C,temb_len,temb_dtype,rope,norm2", [
+    (1, 40, 24, 1, torch.float32, True, True),
+    (2, 130, 77, 130, torch.bfloat16, True, True),
+    (3, 16, 512, 1, torch.float32, False, False),
+])
+def test_block_no_cache(cuda_device, B, Q, C, temb_len, temb_dtype, rope, norm2):
+    D, H, F = 256, 2, 512
+    blk = make_oracle_block(D, F, H, seed=B * 10 + Q, cross_attn_norm=norm2)
+    x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=Q, temb_len=temb_len, temb_dtype=temb_dtype)
+    r = r if rope else None
+    with torch.no_grad():
+        ref = blk(x, ctx, temb, r)
+    out = _run_native(to_device_block(blk), x, ctx, temb, r, temb_dtype)
+    assert_parity(out, ref)
+
+
+def test_block_context_broadcast(cuda_device):
+    D, H, F, B, Q, C = 256, 2, 512, 3, 24, 40
+    blk = make_oracle_block(D, F, H, seed=3)
+    x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=4, ctx_batch=1)
+    with torch.no_grad():
+        ref = blk(x, ctx.expand(B, -1, -1), temb, r)
+    assert_parity(_run_native(to_device_block(blk), x, ctx, temb, r), ref)
+
+
+def _cache_equal(oc, gc):
+    assert torch.equal(oc["id"], gc["id"].cpu())
+    assert torch.equal(oc["mask"], gc["mask"].cpu())
+    assert torch.equal(oc["is_pred"], gc["is_pred"].cpu())
+    valid = oc["mask"] | (oc["id"] >= 0)
+    idx = valid.nonzero().squeeze(-1)
+    s = stats(gc["k"][:, idx.cuda()], oc["k"][:, idx])
+    assert s["cos"] >= 0.9999 and s["max_abs"] <= 2e-2, s
+    s = stats(gc["v"][:, idx.cuda()], oc["v"][:, idx])
+    assert s["cos"] >= 0.9999 and s["max_abs"] <= 2e-2, s
+
+
+def test_block_kv_lifecycle_and_eviction(cuda_device):
+    """prefill (update 2) x2, denoise (update 0), commit prediction (update 1)
+    with eviction of the oldest chunk, then denoise again."""
+    D, H, F, B, Q, C, pool = 256, 2, 512, 2, 40, 24, 100
+    blk = make_oracle_block(D, F, H, seed=11)
+    g = to_device_block(blk)
+    blk.attn1.init_kv_cache("pos", pool, H, 128, "cpu", torch.float32, B)
+    g.attn1.init_kv_cache("pos", pool, H, 128, "cuda", torch.bfloat16, B)
+    for step, update in enumerate((2, 2, 0, 1, 0)):
+        x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=100 + step)
+        with torch.no_grad():
+            ref = blk(x, ctx, temb, r, update_cache=update)
+        out = _run_native(g, x, ctx, temb, r, update_cache=update)
+        assert_parity(out, ref)
+        _cache_equal(blk.attn1.attn_caches["pos"], g.attn1.attn_caches["pos"])
+
+
+def test_block_candidate_verification(cuda_device):
+    D, H, F, Bp, C, pool = 256, 2, 512, 2, 24, 200
+    blk = make_oracle_block(D, F, H, seed=21)
+    g = to_device_block(blk)
+    blk.attn1.init_kv_cache("pos", pool, H, 128, "cpu", torch.float32, Bp)
+    g.attn1.init_kv_cache("pos", pool, H, 128, "cuda", torch.bfloat16, Bp)
+    for step in range(2):
+        x, ctx, temb, r = make_inputs(Bp, 70, D, C, H, seed=200 + step)
+        with torch.no_grad():
+            blk(x, ctx, temb, r, update_cache=2)
+        _run_native(g, x, ctx, temb, r, update_cache=2)
+    rows = torch.tensor([0, 1, 1, 0], dtype=torch.int64)
+    B, Q = 4, 16
+    x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=300, temb_len=Q)
+    before = {k: v.clone() for k, v in g.attn1.attn_caches["pos"].items()}
+    with torch.no_grad():
+        ref = blk(x, ctx, temb, r, candidate_cache_rows=rows)
+    out = _run_native(g, x, ctx, temb, r, candidate_cache_rows=rows.cuda())
+    assert_parity(out, ref)
+    for k, v in g.attn1.attn_caches["pos"].items():
+        assert torch.equal(v, before[k]), f"candidate path wrote the cache ({k})"
+
+
+def test_block_rejects_bad_candidate_rows(cuda_device):
+    D, H, F = 256, 2, 512
+    blk = make_oracle_block(D, F, H, seed=31)
+    g = to_device_block(blk)
+    x, ctx, temb, r = make_inputs(2, 16, D, 8, H, seed=31)
+    with pytest.raises(ValueError):
+        _run_native(g, x, ctx, temb, r, candidate_cache_rows=torch.zeros(2, dtype=torch.int64, device="cuda"))
+
+
+def test_whole_layer_prepared_context(cuda_device):
+    D, H, F, B, Q, C = 256, 2, 512, 4, 32, 48
+    blk = make_oracle_block(D, F, H, seed=41)
+    x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=41)
+    ctx[2] = ctx[0]
+    ctx[3] = ctx[1]
+    with torch.no_grad():
+        ref = blk(x, ctx, temb, r)
+    g = to_device_block(blk)
+    with torch.no_grad():
+        w = WholeLayerBlock(g)
+        w.prepare_context(ctx.cuda().bfloat16(), precompute=True)
+        assert w.context_roots is not None and w.context_roots.numel() == 2
+        out = w(x.cuda().bfloat16(), ctx.cuda().bfloat16(), temb.cuda(), r.cuda())
+        dbg = w(x.cuda().bfloat16(), ctx.cuda().bfloat16(), temb.cuda(), r.cuda(), debug=True)
+    assert_parity(out, ref)
+    assert torch.equal(dbg["output"], out)
+    assert "modulated1" in dbg and "gelu" in dbg
+
+
+def test_cfg0_single_block(cuda_device):
+    """configs[0] shape (D 1536, 12 heads, FFN 8960, 1560 video + 32 action
+    tokens, 512 context tokens) against the fp32 oracle."""
+    D, H, F, B, Q, C = 1536, 12, 8960, 1, 1592, 512
+    blk = make_oracle_block(D, F, H, seed=0, randomize=False)
+    x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=0)
+    with torch.no_grad():
+        ref = blk(x, ctx, temb, r)
+    assert_parity(_run_native(to_device_block(blk), x, ctx, temb, r), ref)
+
+
+def test_install_model_restores_classes(cuda_device):
+    D, H, F = 256, 2, 512
+
+    class Model(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.blocks = torch.nn.ModuleList([to_device_block(make_oracle_block(D, F, H, seed=s))
+                                               for s in range(2)])
+
+    m = Model()
+    kinds = [type(b) for b in m.blocks]
+    with install_model(m, "optimized", execution_mode="persistent"):
+        assert all(type(b).__name__ == "TransformerBlock" for b in m.blocks)
+    assert [type(b) for b in m.blocks] == kinds
+    assert all("_native_block" not in b.__dict__ for b in m.blocks)

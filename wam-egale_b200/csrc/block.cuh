@@ -1,0 +1,410 @@
+// Host orchestration of one Wan-DiT block forward and the launchers of the
+// attention and glue kernels. Launch sequence of wamb_block_forward (all on
+// the caller's stream, no host synchronisation, no allocation):
+//   kv_layout (cache only) -> LN1+mod -> QKV GEMM (3 weight groups) ->
+//   RMS+RoPE (+K/V into pool slots) -> self attention -> O GEMM + gated
+//   residual -> LN2 -> cross-Q GEMM -> RMS -> [cross K/V GEMMs + RMS] ->
+//   cross attention -> cross-O GEMM + residual -> LN3+mod -> FFN1 GEMM+GELU ->
+//   FFN2 GEMM + gated residual.
+#pragma once
+#include <cmath>
+#include <type_traits>
+
+#include "attention.cuh"
+#include "glue.cuh"
+#include "host.cuh"
+#include "linear.cuh"
+
+namespace wamb {
+
+// ---------------------------------------------------------------- attention
+inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream) {
+  WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
+  WAMB_REQUIRE(a->batch >= 0 && a->heads > 0 && a->q_rows >= 0, WAMB_ERR_SHAPE, "bad dims");
+  if (a->batch == 0 || a->q_rows == 0) return WAMB_OK;
+  WAMB_REQUIRE(a->q && a->k0 && a->v0 && a->out, WAMB_ERR_ARG, "null q/k0/v0/out");
+  WAMB_REQUIRE(a->tiles != nullptr || a->src0_len >= 0, WAMB_ERR_ARG, "source 0 length");
+  WAMB_REQUIRE(a->tiles == nullptr || a->n_tiles != nullptr, WAMB_ERR_ARG, "tiles without count");
+  WAMB_REQUIRE(a->ldo % 8 == 0 && aligned16(a->out), WAMB_ERR_ALIGN, "out alignment");
+  WAMB_REQUIRE(a->q_col % 64 == 0 && a->k0_col % 64 == 0 && a->v0_col % 64 == 0, WAMB_ERR_ALIGN,
+               "column offsets must be multiples of 64");
+  WAMB_REQUIRE(a->ldq >= a->q_col + 128LL * a->heads && a->ld0 >= a->k0_col + 128LL * a->heads &&
+                   a->ld0 >= a->v0_col + 128LL * a->heads && a->ldo >= 128LL * a->heads,
+               WAMB_ERR_SHAPE, "row strides too small for the heads");
+  WAMB_REQUIRE(a->q_total_rows >= static_cast<int64_t>(a->batch) * a->q_rows, WAMB_ERR_SHAPE,
+               "q_total_rows");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  CUtensorMap tq, tk0, tv0, tk1, tv1;
+  if ((rc = make_tmap_bf16(&tq, a->q, a->q_total_rows, a->ldq, a->ldq, 128))) return rc;
+  if ((rc = make_tmap_bf16(&tk0, a->k0, a->src0_total_rows, a->ld0, a->ld0, 128))) return rc;
+  if ((rc = make_tmap_bf16(&tv0, a->v0, a->src0_total_rows, a->ld0, a->ld0, 128))) return rc;
+  AttnParams p{};
+  p.heads = a->heads;
+  p.q_rows = a->q_rows;
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.ldo = a->ldo;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
+  p.q_col = a->q_col;
+  p.src0_batch_stride = a->src0_batch_stride;
+  p.src0_map = reinterpret_cast<const long long*>(a->src0_map);
+  p.src0_broadcast = a->src0_broadcast;
+  p.tiles = reinterpret_cast<const int2*>(a->tiles);
+  p.n_tiles = a->n_tiles;
+  p.src0_len = a->src0_len;
+  p.k0_col = a->k0_col;
+  p.v0_col = a->v0_col;
+  if (a->k1 != nullptr) {
+    WAMB_REQUIRE(a->v1 && a->k1_col % 64 == 0 && a->v1_col % 64 == 0 &&
+                     a->ld1 >= a->k1_col + 128LL * a->heads && a->ld1 >= a->v1_col + 128LL * a->heads,
+                 WAMB_ERR_ARG, "source 1");
+    const int64_t rows1 = static_cast<int64_t>(a->batch) * a->q_rows;
+    if ((rc = make_tmap_bf16(&tk1, a->k1, rows1, a->ld1, a->ld1, 128))) return rc;
+    if ((rc = make_tmap_bf16(&tv1, a->v1, rows1, a->ld1, a->ld1, 128))) return rc;
+    p.has_src1 = 1;
+    p.k1_col = a->k1_col;
+    p.v1_col = a->v1_col;
+  } else {
+    tk1 = tk0;
+    tv1 = tv0;
+  }
+  static bool configured[64] = {};
+  int dev = 0;
+  WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+  if (!configured[dev]) {
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnSmem::TOTAL));
+    configured[dev] = true;
+  }
+  dim3 grid((a->q_rows + 127) / 128, a->heads, a->batch);
+  attn_tc_kernel<<<grid, ATT_THREADS, AttnSmem::TOTAL, stream>>>(tq, tk0, tv0, tk1, tv1, p);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+// -------------------------------------------------------------- row kernels
+// Vectors of 8 bf16 per thread per step; the block has D / (8 * VPT) threads.
+inline int row_vpt(int D) {
+  const int v8 = D / 8;
+  const int cands[6] = {1, 2, 3, 4, 6, 8};
+  for (int c : cands) {
+    if (v8 % c) continue;
+    const int t = v8 / c;
+    if (t % 32 == 0 && t <= 256) return c;
+  }
+  return 0;
+}
+
+template <typename F>
+inline int dispatch_vpt(int vpt, F&& f) {
+  switch (vpt) {
+    case 1: return f(std::integral_constant<int, 1>{});
+    case 2: return f(std::integral_constant<int, 2>{});
+    case 3: return f(std::integral_constant<int, 3>{});
+    case 4: return f(std::integral_constant<int, 4>{});
+    case 6: return f(std::integral_constant<int, 6>{});
+    case 8: return f(std::integral_constant<int, 8>{});
+  }
+  return fail(WAMB_ERR_SHAPE, "row width not supported");
+}
+
+inline int launch_ln(const LnParams& p, cudaStream_t s) {
+  if (p.M == 0) return WAMB_OK;
+  const int vpt = row_vpt(p.D);
+  WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
+  const int threads = p.D / (8 * vpt);
+  return dispatch_vpt(vpt, [&](auto v) {
+    ln_kernel<decltype(v)::value><<<p.M, threads, 0, s>>>(p);
+    WAMB_CHECK_CUDA(cudaGetLastError());
+    return static_cast<int>(WAMB_OK);
+  });
+}
+
+inline int launch_rms(const RmsParams& p, cudaStream_t s) {
+  if (p.M == 0) return WAMB_OK;
+  const int vpt = row_vpt(p.D);
+  WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
+  const int threads = p.D / (8 * vpt);
+  return dispatch_vpt(vpt, [&](auto v) {
+    rms_rope_kernel<decltype(v)::value><<<p.M, threads, 0, s>>>(p);
+    WAMB_CHECK_CUDA(cudaGetLastError());
+    return static_cast<int>(WAMB_OK);
+  });
+}
+
+// ------------------------------------------------------------ block forward
+struct BlockLayout {
+  int64_t off[WAMB_TAP_COUNT];
+  size_t total;
+};
+
+inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+inline BlockLayout block_layout(const wamb_block_args* a) {
+  BlockLayout L;
+  for (int i = 0; i < WAMB_TAP_COUNT; ++i) L.off[i] = -1;
+  const size_t M = static_cast<size_t>(a->batch) * a->tokens;
+  const size_t D = a->dim, F = a->ffn_dim;
+  const size_t MD = M * D * 2;
+  size_t o = 0;
+  auto put = [&](int tap, size_t bytes) {
+    L.off[tap] = static_cast<int64_t>(o);
+    o = align256(o + bytes);
+  };
+  put(WAMB_TAP_MODULATED1, MD);
+  put(WAMB_TAP_QKV, 3 * MD);
+  put(WAMB_TAP_SELF_ATTN, MD);
+  put(WAMB_TAP_RESIDUAL1, MD);
+  if (a->weights[1] != nullptr) put(WAMB_TAP_NORM2, MD);
+  put(WAMB_TAP_CROSS_Q, MD);
+  if (a->cross_k == nullptr) {
+    const size_t CD = static_cast<size_t>(a->context_batch) * a->context_tokens * D * 2;
+    put(WAMB_TAP_CROSS_K, CD);
+    put(WAMB_TAP_CROSS_V, CD);
+  }
+  put(WAMB_TAP_CROSS_ATTN, MD);
+  put(WAMB_TAP_RESIDUAL2, MD);
+  put(WAMB_TAP_MODULATED3, MD);
+  put(WAMB_TAP_GELU, M * F * 2);
+  if (a->cache_k != nullptr) {
+    put(WAMB_TAP_KV_SLOTS, static_cast<size_t>(a->tokens) * 4);
+    put(WAMB_TAP_KV_TILES, static_cast<size_t>(a->pool) * 8);
+    put(WAMB_TAP_KV_COUNTS, 16);
+  }
+  L.total = o;
+  return L;
+}
+
+inline int check_block_args(const wamb_block_args* a) {
+  WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
+  WAMB_REQUIRE(a->batch >= 1 && a->tokens >= 1, WAMB_ERR_SHAPE, "batch/tokens must be >= 1");
+  WAMB_REQUIRE(a->heads >= 1 && a->dim == a->heads * 128, WAMB_ERR_SHAPE,
+               "dim must be heads * 128 (head_dim 128)");
+  WAMB_REQUIRE(a->ffn_dim >= 64 && a->ffn_dim % 64 == 0, WAMB_ERR_SHAPE, "ffn_dim %% 64");
+  WAMB_REQUIRE(row_vpt(a->dim) > 0, WAMB_ERR_SHAPE, "dim %d unsupported", a->dim);
+  WAMB_REQUIRE(a->x && a->out && a->temb, WAMB_ERR_ARG, "null x/out/temb");
+  for (int i = 0; i < 27; ++i) {
+    if (i == 1 || i == 2) continue;
+    WAMB_REQUIRE(a->weights[i] != nullptr, WAMB_ERR_ARG, "weights[%d] is null", i);
+    WAMB_REQUIRE(aligned16(a->weights[i]), WAMB_ERR_ALIGN, "weights[%d] alignment", i);
+  }
+  WAMB_REQUIRE((a->weights[1] == nullptr) == (a->weights[2] == nullptr), WAMB_ERR_ARG,
+               "norm2 gamma and beta must both be given or both be null");
+  WAMB_REQUIRE(a->temb_len == 1 || a->temb_len == a->tokens, WAMB_ERR_SHAPE,
+               "temb_len must be 1 or tokens");
+  WAMB_REQUIRE(a->context_tokens >= 1 && a->context_batch >= 1, WAMB_ERR_SHAPE, "context dims");
+  WAMB_REQUIRE(a->context_rows != nullptr || a->context_batch == a->batch || a->context_batch == 1,
+               WAMB_ERR_SHAPE, "context_batch must be batch or 1 without context_rows");
+  WAMB_REQUIRE(a->cross_k != nullptr || a->context != nullptr, WAMB_ERR_ARG,
+               "need context or precomputed cross K/V");
+  WAMB_REQUIRE((a->cross_k == nullptr) == (a->cross_v == nullptr), WAMB_ERR_ARG, "cross_k/cross_v");
+  WAMB_REQUIRE(a->freq == nullptr || a->freq_batch == 1 || a->freq_batch == a->batch,
+               WAMB_ERR_SHAPE, "freq_batch must be 1 or batch");
+  WAMB_REQUIRE(a->update >= 0 && a->update <= 2, WAMB_ERR_ARG, "update must be 0, 1 or 2");
+  if (a->cache_k != nullptr) {
+    WAMB_REQUIRE(a->cache_v && a->cache_id && a->cache_mask && a->cache_pred, WAMB_ERR_KV,
+                 "cache schema: k, v, id, mask, is_pred");
+    WAMB_REQUIRE(a->pool >= 1 && a->pool <= KV_MAX_POOL, WAMB_ERR_KV, "pool size %d outside [1, %d]",
+                 a->pool, KV_MAX_POOL);
+    WAMB_REQUIRE(a->pool_batch >= 1, WAMB_ERR_KV, "pool_batch");
+    if (a->candidate_rows != nullptr) {
+      WAMB_REQUIRE(a->update == 0, WAMB_ERR_KV,
+                   "candidate verification requires existing read-only KV (update 0)");
+    } else {
+      WAMB_REQUIRE(a->pool_batch == a->batch, WAMB_ERR_KV, "KV branch contract: pool_batch == batch");
+      WAMB_REQUIRE(a->tokens <= a->pool, WAMB_ERR_KV, "chunk larger than the pool");
+    }
+  } else {
+    WAMB_REQUIRE(a->candidate_rows == nullptr, WAMB_ERR_KV,
+                 "candidate verification requires existing read-only KV");
+  }
+  const BlockLayout L = block_layout(a);
+  WAMB_REQUIRE(a->workspace != nullptr && a->workspace_bytes >= L.total, WAMB_ERR_WORKSPACE,
+               "workspace of %zu bytes needed (%zu given)", L.total, a->workspace_bytes);
+  WAMB_REQUIRE(reinterpret_cast<uintptr_t>(a->workspace) % 256 == 0, WAMB_ERR_ALIGN,
+               "workspace must be 256-byte aligned");
+  return WAMB_OK;
+}
+
+using bf = __nv_bfloat16;
+
+// Cross K/V of `context` into k_out / v_out (rows Bc*C).
+inline int cross_kv_impl(const wamb_block_args* a, void* k_out, void* v_out, cudaStream_t s) {
+  const int D = a->dim;
+  const int rows = a->context_batch * a->context_tokens;
+  WAMB_REQUIRE(a->context && k_out && v_out, WAMB_ERR_ARG, "cross K/V needs context and outputs");
+  int rc;
+  wamb_linear_args g{};
+  g.a = a->context; g.lda = D; g.m = rows; g.k = D; g.groups = 1; g.n_per_group = D;
+  g.ldo = D; g.epilogue = WAMB_EPI_BIAS;
+  g.weight[0] = a->weights[15]; g.bias[0] = a->weights[16]; g.out = k_out;
+  if ((rc = linear_impl(&g, s))) return rc;
+  g.weight[0] = a->weights[17]; g.bias[0] = a->weights[18]; g.out = v_out;
+  if ((rc = linear_impl(&g, s))) return rc;
+  RmsParams r{};
+  r.x = static_cast<bf*>(k_out); r.ld = D; r.M = rows; r.D = D; r.rows_per_batch = rows;
+  r.sections = 1; r.gamma[0] = static_cast<const bf*>(a->weights[22]);
+  r.eps[0] = static_cast<float>(a->eps[6]);
+  return launch_rms(r, s);
+}
+
+inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
+  int rc = check_block_args(a);
+  if (rc) return rc;
+  DeviceInfo di;
+  if ((rc = device_info(&di))) return rc;
+  const BlockLayout L = block_layout(a);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  auto buf = [&](int tap) -> bf* { return L.off[tap] < 0 ? nullptr : reinterpret_cast<bf*>(ws + L.off[tap]); };
+  const int B = a->batch, Q = a->tokens, D = a->dim, F = a->ffn_dim, H = a->heads;
+  const int M = B * Q;
+  const bool cache = a->cache_k != nullptr;
+  const bool cand = a->candidate_rows != nullptr;
+  const float* table = static_cast<const float*>(a->weights[0]);
+  bf* h1 = buf(WAMB_TAP_MODULATED1);
+  bf* qkv = buf(WAMB_TAP_QKV);
+  bf* attn = buf(WAMB_TAP_SELF_ATTN);
+  bf* h2 = buf(WAMB_TAP_RESIDUAL1);
+  bf* n2 = a->weights[1] ? buf(WAMB_TAP_NORM2) : h2;
+  bf* cq = buf(WAMB_TAP_CROSS_Q);
+  bf* ca = buf(WAMB_TAP_CROSS_ATTN);
+  bf* h3 = buf(WAMB_TAP_RESIDUAL2);
+  bf* f0 = buf(WAMB_TAP_MODULATED3);
+  bf* act = buf(WAMB_TAP_GELU);
+  int* slots = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_SLOTS]) : nullptr;
+  int* tiles = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_TILES]) : nullptr;
+  int* counts = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_COUNTS]) : nullptr;
+
+  // 1. KV bookkeeping on the device (no host sync, unlike block.cu:241-244).
+  if (cache) {
+    KvParams k{};
+    k.mask = a->cache_mask; k.ids = reinterpret_cast<long long*>(a->cache_id); k.pred = a->cache_pred;
+    k.pool = a->pool; k.q = Q; k.update = a->update; k.candidate = cand;
+    k.rows = reinterpret_cast<const long long*>(a->candidate_rows);
+    k.batch = B; k.pool_batch = a->pool_batch;
+    k.new_slots = slots; k.tiles = reinterpret_cast<int2*>(tiles); k.counts = counts;
+    kv_layout_kernel<<<1, KV_THREADS, 0, s>>>(k);
+    WAMB_CHECK_CUDA(cudaGetLastError());
+  }
+  // 2. LN1 + modulation (shift 0, scale 1)
+  LnParams ln{};
+  ln.x = static_cast<const bf*>(a->x); ln.ldx = D; ln.out = h1; ln.ldo = D; ln.M = M; ln.D = D;
+  ln.eps = static_cast<float>(a->eps[0]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
+  ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
+  ln.shift_idx = 0; ln.scale_idx = 1;
+  if ((rc = launch_ln(ln, s))) return rc;
+  // 3. QKV projection: three weight groups write q | k | v
+  wamb_linear_args g{};
+  g.a = h1; g.lda = D; g.m = M; g.k = D; g.groups = 3; g.n_per_group = D;
+  g.weight[0] = a->weights[3]; g.bias[0] = a->weights[4];
+  g.weight[1] = a->weights[5]; g.bias[1] = a->weights[6];
+  g.weight[2] = a->weights[7]; g.bias[2] = a->weights[8];
+  g.out = qkv; g.ldo = 3LL * D; g.epilogue = WAMB_EPI_BIAS;
+  if ((rc = linear_impl(&g, s))) return rc;
+  // 4. q/k RMSNorm across heads + RoPE; K/V into the pool slots
+  RmsParams r{};
+  r.x = qkv; r.ld = 3LL * D; r.M = M; r.D = D; r.rows_per_batch = Q; r.sections = 2;
+  r.gamma[0] = static_cast<const bf*>(a->weights[11]); r.gamma[1] = static_cast<const bf*>(a->weights[12]);
+  r.eps[0] = static_cast<float>(a->eps[3]); r.eps[1] = static_cast<float>(a->eps[4]);
+  r.freq = reinterpret_cast<const float2*>(a->freq); r.freq_batch = a->freq_batch;
+  if (cache && !cand) {
+    r.pool_k = static_cast<bf*>(a->cache_k); r.pool_v = static_cast<bf*>(a->cache_v);
+    r.pool = a->pool; r.slots = slots;
+  }
+  if ((rc = launch_rms(r, s))) return rc;
+  // 5. self attention
+  wamb_attention_args at{};
+  at.batch = B; at.heads = H; at.q_rows = Q;
+  at.q = qkv; at.ldq = 3LL * D; at.q_total_rows = M; at.q_col = 0;
+  at.out = attn; at.ldo = D;
+  if (cache) {
+    at.k0 = a->cache_k; at.v0 = a->cache_v; at.ld0 = D;
+    at.src0_total_rows = static_cast<int64_t>(a->pool_batch) * a->pool;
+    at.src0_batch_stride = a->pool;
+    at.src0_map = a->candidate_rows;
+    at.tiles = tiles; at.n_tiles = counts;
+    if (cand) { at.k1 = qkv; at.v1 = qkv; at.ld1 = 3LL * D; at.k1_col = D; at.v1_col = 2 * D; }
+  } else {
+    at.k0 = qkv; at.v0 = qkv; at.ld0 = 3LL * D; at.k0_col = D; at.v0_col = 2 * D;
+    at.src0_total_rows = M; at.src0_batch_stride = Q; at.src0_len = Q;
+  }
+  if ((rc = attention_impl(&at, s))) return rc;
+  // 6. O projection + gated residual (gate 2): h2 = x + o * gate_msa
+  g = wamb_linear_args{};
+  g.a = attn; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
+  g.weight[0] = a->weights[9]; g.bias[0] = a->weights[10]; g.out = h2; g.ldo = D;
+  g.epilogue = WAMB_EPI_RES_GATE; g.res = a->x; g.ldr = D; g.table = table; g.temb = a->temb;
+  g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 2;
+  g.dim = D;
+  if ((rc = linear_impl(&g, s))) return rc;
+  // 7. LN2 (fp32 affine) or Identity
+  if (a->weights[1] != nullptr) {
+    ln = LnParams{};
+    ln.x = h2; ln.ldx = D; ln.out = n2; ln.ldo = D; ln.M = M; ln.D = D;
+    ln.eps = static_cast<float>(a->eps[1]); ln.affine = 1;
+    ln.gamma = static_cast<const float*>(a->weights[1]); ln.beta = static_cast<const float*>(a->weights[2]);
+    ln.rows_per_batch = Q;
+    if ((rc = launch_ln(ln, s))) return rc;
+  }
+  // 8-9. cross Q projection + RMSNorm
+  g = wamb_linear_args{};
+  g.a = n2; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
+  g.weight[0] = a->weights[13]; g.bias[0] = a->weights[14]; g.out = cq; g.ldo = D;
+  g.epilogue = WAMB_EPI_BIAS;
+  if ((rc = linear_impl(&g, s))) return rc;
+  r = RmsParams{};
+  r.x = cq; r.ld = D; r.M = M; r.D = D; r.rows_per_batch = Q; r.sections = 1;
+  r.gamma[0] = static_cast<const bf*>(a->weights[21]); r.eps[0] = static_cast<float>(a->eps[5]);
+  if ((rc = launch_rms(r, s))) return rc;
+  // 10. cross K/V (per call unless precomputed)
+  const void* ck = a->cross_k;
+  const void* cv = a->cross_v;
+  if (ck == nullptr) {
+    bf* kb = buf(WAMB_TAP_CROSS_K);
+    bf* vb = buf(WAMB_TAP_CROSS_V);
+    if ((rc = cross_kv_impl(a, kb, vb, s))) return rc;
+    ck = kb;
+    cv = vb;
+  }
+  // 11. cross attention
+  at = wamb_attention_args{};
+  at.batch = B; at.heads = H; at.q_rows = Q;
+  at.q = cq; at.ldq = D; at.q_total_rows = M; at.q_col = 0;
+  at.k0 = ck; at.v0 = cv; at.ld0 = D;
+  at.src0_total_rows = static_cast<int64_t>(a->context_batch) * a->context_tokens;
+  at.src0_batch_stride = a->context_tokens; at.src0_len = a->context_tokens;
+  at.src0_map = a->context_rows;
+  at.src0_broadcast = a->context_rows == nullptr && a->context_batch == 1 && B > 1;
+  at.out = ca; at.ldo = D;
+  if ((rc = attention_impl(&at, s))) return rc;
+  // 12. cross O projection + residual: h3 = h2 + o
+  g = wamb_linear_args{};
+  g.a = ca; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
+  g.weight[0] = a->weights[19]; g.bias[0] = a->weights[20]; g.out = h3; g.ldo = D;
+  g.epilogue = WAMB_EPI_RES; g.res = h2; g.ldr = D;
+  if ((rc = linear_impl(&g, s))) return rc;
+  // 13. LN3 + modulation (shift 3, scale 4)
+  ln = LnParams{};
+  ln.x = h3; ln.ldx = D; ln.out = f0; ln.ldo = D; ln.M = M; ln.D = D;
+  ln.eps = static_cast<float>(a->eps[2]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
+  ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
+  ln.shift_idx = 3; ln.scale_idx = 4;
+  if ((rc = launch_ln(ln, s))) return rc;
+  // 14. FFN1 + GELU-tanh
+  g = wamb_linear_args{};
+  g.a = f0; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = F;
+  g.weight[0] = a->weights[23]; g.bias[0] = a->weights[24]; g.out = act; g.ldo = F;
+  g.epilogue = WAMB_EPI_GELU;
+  if ((rc = linear_impl(&g, s))) return rc;
+  // 15. FFN2 + gated residual (gate 5): out = h3 + f * c_gate_msa
+  g = wamb_linear_args{};
+  g.a = act; g.lda = F; g.m = M; g.k = F; g.groups = 1; g.n_per_group = D;
+  g.weight[0] = a->weights[25]; g.bias[0] = a->weights[26]; g.out = a->out; g.ldo = D;
+  g.epilogue = WAMB_EPI_RES_GATE; g.res = h3; g.ldr = D; g.table = table; g.temb = a->temb;
+  g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 5;
+  g.dim = D;
+  return linear_impl(&g, s);
+}
+
+}  // namespace wamb

@@ -82,6 +82,17 @@ WAMB_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag)
   }
 }
 
+// Bounded wait used only on the teardown path (ignores the abort flag).
+WAMB_DEV void mbar_wait_teardown(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > WAMB_WAIT_TIMEOUT_NS) {
+      record_error(1);
+      return;
+    }
+  }
+}
+
 // -------------------------------------------------------------------- TMA
 WAMB_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(

@@ -60,17 +60,6 @@ WAMB_DEV float gelu_tanh(float x) {
   return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
 }
 
-// Bounded wait used only on the teardown path (ignores the abort flag).
-WAMB_DEV void mbar_wait_teardown(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > WAMB_WAIT_TIMEOUT_NS) {
-      record_error(1);
-      return;
-    }
-  }
-}
-
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
@@ -202,7 +191,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int n0 = n_blk * BN;
       const int g = n0 / p.n_per_group;
       const int n_local0 = n0 - g * p.n_per_group;
-      const __nv_bfloat16* bias = p.bias[g];
+      const __nv_bfloat16* bias = g == 0 ? p.bias[0] : (g == 1 ? p.bias[1] : p.bias[2]);
       const float* gate_tab = nullptr;
       const float* gate_f32 = nullptr;
       const __nv_bfloat16* gate_bf = nullptr;

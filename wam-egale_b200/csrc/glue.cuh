@@ -176,9 +176,14 @@ __global__ void rms_rope_kernel(const RmsParams p) {
     for (int i = 0; i < nw; ++i) t += red[i];
     return t;
   };
-  const bool to_pool = p.pool_k != nullptr;
+  bool to_pool = p.pool_k != nullptr;
   long long dst_row = 0;
-  if (to_pool) dst_row = static_cast<long long>(b) * p.pool + p.slots[tok];
+  if (to_pool) {
+    const int slot = p.slots[tok];
+    // kv_layout_kernel writes -1 when it rejected the call: skip the pool write.
+    if (slot < 0 || slot >= p.pool) return;
+    dst_row = static_cast<long long>(b) * p.pool + slot;
+  }
   for (int s = 0; s < p.sections; ++s) {
     float v[VPT][8];
     float ss = 0.f;
@@ -188,13 +193,13 @@ __global__ void rms_rope_kernel(const RmsParams p) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
     }
-    const float rstd = rsqrtf(reduce(ss) / p.D + p.eps[s]);
+    const float rstd = rsqrtf(reduce(ss) / p.D + (s == 0 ? p.eps[0] : p.eps[1]));
     __nv_bfloat16* dst = (s == 1 && to_pool) ? p.pool_k + dst_row * p.D : xr + s * p.D;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int col = (i * nthr + threadIdx.x) * 8;
       float g[8], y[8];
-      load8(p.gamma[s] + col, g);
+      load8((s == 0 ? p.gamma[0] : p.gamma[1]) + col, g);
 #pragma unroll
       for (int j = 0; j < 8; ++j) y[j] = v[i][j] * rstd * g[j];
       if (p.freq != nullptr) {
@@ -398,6 +403,8 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams
         p.tiles[t++] = make_int2(i, e - i);
       }
     }
+    if (s_err && !p.candidate)
+      for (int i = threadIdx.x; i < p.q; i += KV_THREADS) p.new_slots[i] = -1;
     if (threadIdx.x == 0) {
       p.counts[0] = s_err ? 0 : ntiles;
       p.counts[1] = s_err ? 0 : vis;

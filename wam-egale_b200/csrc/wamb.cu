@@ -4,6 +4,7 @@
 #include "common.cuh"
 #include "host.cuh"
 #include "linear.cuh"
+#include "block.cuh"
 
 extern "C" {
 
@@ -24,6 +25,32 @@ int wamb_device_status(void* stream, int* device_code) {
 
 int wamb_linear(const wamb_linear_args* args, void* stream) {
   return wamb::linear_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+int wamb_attention(const wamb_attention_args* args, void* stream) {
+  return wamb::attention_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+size_t wamb_block_workspace_bytes(const wamb_block_args* args) {
+  if (args == nullptr) return 0;
+  return wamb::block_layout(args).total;
+}
+
+size_t wamb_block_workspace_layout(const wamb_block_args* args, int64_t* offsets) {
+  if (args == nullptr) return 0;
+  const wamb::BlockLayout L = wamb::block_layout(args);
+  if (offsets != nullptr)
+    for (int i = 0; i < WAMB_TAP_COUNT; ++i) offsets[i] = L.off[i];
+  return L.total;
+}
+
+int wamb_block_forward(const wamb_block_args* args, void* stream) {
+  return wamb::block_forward_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+int wamb_cross_kv(const wamb_block_args* args, void* k_out, void* v_out, void* stream) {
+  if (args == nullptr) return wamb::fail(WAMB_ERR_ARG, "null args");
+  return wamb::cross_kv_impl(args, k_out, v_out, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

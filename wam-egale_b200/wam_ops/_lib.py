@@ -32,9 +32,56 @@ class LinearArgs(ctypes.Structure):
 
 EPI_BIAS, EPI_GELU, EPI_RES, EPI_RES_GATE = 0, 1, 2, 3
 
+
+class AttentionArgs(ctypes.Structure):
+    """Mirror of `wamb_attention_args` (include/wamb.h)."""
+    _fields_ = [
+        ("batch", c_int32), ("heads", c_int32), ("q_rows", c_int32),
+        ("q", c_void_p), ("ldq", c_int64), ("q_total_rows", c_int64), ("q_col", c_int32),
+        ("k0", c_void_p), ("v0", c_void_p), ("ld0", c_int64), ("src0_total_rows", c_int64),
+        ("k0_col", c_int32), ("v0_col", c_int32),
+        ("src0_batch_stride", c_int32),
+        ("src0_map", c_void_p),
+        ("src0_broadcast", c_int32),
+        ("tiles", c_void_p), ("n_tiles", c_void_p),
+        ("src0_len", c_int32),
+        ("k1", c_void_p), ("v1", c_void_p), ("ld1", c_int64), ("k1_col", c_int32), ("v1_col", c_int32),
+        ("out", c_void_p), ("ldo", c_int64),
+    ]
+
+
+class BlockArgs(ctypes.Structure):
+    """Mirror of `wamb_block_args` (include/wamb.h)."""
+    _fields_ = [
+        ("batch", c_int32), ("tokens", c_int32), ("dim", c_int32), ("heads", c_int32),
+        ("ffn_dim", c_int32),
+        ("context_tokens", c_int32), ("context_batch", c_int32),
+        ("weights", c_void_p * 27),
+        ("eps", ctypes.c_double * 7),
+        ("x", c_void_p), ("context", c_void_p), ("cross_k", c_void_p), ("cross_v", c_void_p),
+        ("context_rows", c_void_p),
+        ("temb", c_void_p), ("temb_len", c_int32), ("temb_is_f32", c_int32),
+        ("freq", c_void_p), ("freq_batch", c_int32),
+        ("cache_k", c_void_p), ("cache_v", c_void_p), ("cache_id", c_void_p),
+        ("cache_mask", c_void_p), ("cache_pred", c_void_p),
+        ("pool", c_int32), ("pool_batch", c_int32),
+        ("candidate_rows", c_void_p),
+        ("update", c_int32),
+        ("out", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+# Workspace taps (enum wamb_tap).
+TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", "cross_k",
+        "cross_v", "cross_attention", "residual2", "modulated3", "gelu", "kv_slots",
+        "kv_tiles", "kv_counts")
+
 # Every symbol include/wamb.h declares; tests check the library exports them.
 EXPORTED = (
     "wamb_last_error", "wamb_abi_version", "wamb_device_status", "wamb_linear",
+    "wamb_attention", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
+    "wamb_block_forward", "wamb_cross_kv",
 )
 
 _lib = None
@@ -56,6 +103,13 @@ def load():
     lib.wamb_abi_version.restype = c_int32
     lib.wamb_device_status.argtypes = [c_void_p, ctypes.POINTER(c_int32)]
     lib.wamb_linear.argtypes = [ctypes.POINTER(LinearArgs), c_void_p]
+    lib.wamb_attention.argtypes = [ctypes.POINTER(AttentionArgs), c_void_p]
+    lib.wamb_block_workspace_bytes.argtypes = [ctypes.POINTER(BlockArgs)]
+    lib.wamb_block_workspace_bytes.restype = ctypes.c_size_t
+    lib.wamb_block_workspace_layout.argtypes = [ctypes.POINTER(BlockArgs), ctypes.POINTER(c_int64)]
+    lib.wamb_block_workspace_layout.restype = ctypes.c_size_t
+    lib.wamb_block_forward.argtypes = [ctypes.POINTER(BlockArgs), c_void_p]
+    lib.wamb_cross_kv.argtypes = [ctypes.POINTER(BlockArgs), c_void_p, c_void_p, c_void_p]
     _lib = lib
     return lib
 

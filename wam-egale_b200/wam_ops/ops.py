@@ -65,3 +65,51 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
         args.dim = n
     _lib.check(_lib.load().wamb_linear(args, _lib.stream_ptr()))
     return out
+
+
+def attention(q, k0, v0, *, heads, q_rows, q_col=0, k0_col=0, v0_col=0, src0_batch_stride,
+              src0_len=None, tiles=None, n_tiles=None, src0_map=None, src0_broadcast=False,
+              k1=None, v1=None, k1_col=0, v1_col=0, out=None):
+    """Flash attention over 2-D row-major views (see wamb_attention_args).
+
+    q: [batch*q_rows, ldq] bf16; k0/v0: [rows0, ld0] bf16; optional k1/v1:
+    [batch*q_rows, ld1]. tiles: int32 [n, 2] (first row, length) with the
+    count in the int32 device tensor n_tiles; otherwise src0_len rows.
+    Returns out [batch*q_rows, heads*128] bf16.
+    """
+    for name, t in (("q", q), ("k0", k0), ("v0", v0)):
+        _bf16_2d(t, name)
+    batch = q.shape[0] // q_rows
+    if out is None:
+        out = torch.empty(batch * q_rows, heads * 128, device=q.device, dtype=torch.bfloat16)
+    a = _lib.AttentionArgs()
+    a.batch, a.heads, a.q_rows = batch, heads, q_rows
+    a.q, a.ldq, a.q_total_rows, a.q_col = q.data_ptr(), q.stride(0), q.shape[0], q_col
+    a.k0, a.v0, a.ld0, a.src0_total_rows = k0.data_ptr(), v0.data_ptr(), k0.stride(0), k0.shape[0]
+    a.k0_col, a.v0_col = k0_col, v0_col
+    a.src0_batch_stride = src0_batch_stride
+    a.src0_map = None if src0_map is None else src0_map.data_ptr()
+    a.src0_broadcast = int(src0_broadcast)
+    if tiles is not None:
+        a.tiles, a.n_tiles = tiles.data_ptr(), n_tiles.data_ptr()
+    else:
+        a.src0_len = src0_len
+    if k1 is not None:
+        a.k1, a.v1, a.ld1, a.k1_col, a.v1_col = k1.data_ptr(), v1.data_ptr(), k1.stride(0), k1_col, v1_col
+    a.out, a.ldo = out.data_ptr(), out.stride(0)
+    _lib.check(_lib.load().wamb_attention(a, _lib.stream_ptr()))
+    return out
+
+
+def sdpa(q, k, v):
+    """The reference's `sdpa(q, k, v)` contract: contiguous bf16 [B, S, H, 128]
+    (算子研究/wam_ops/optimized/csrc/attention.cu:121-181); returns [B, Sq, H, 128]."""
+    B, Sq, H, d = q.shape
+    Sk = k.shape[1]
+    if d != 128 or k.shape != v.shape or k.shape[0] != B or k.shape[2] != H:
+        raise ValueError("expected q [B,Sq,H,128], k = v [B,Sk,H,128]")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("Q/K/V must be contiguous; no hidden copies")
+    out = attention(q.view(B * Sq, H * d), k.view(B * Sk, H * d), v.view(B * Sk, H * d), heads=H,
+                    q_rows=Sq, src0_batch_stride=Sk, src0_len=Sk)
+    return out.view(B, Sq, H, d)
