@@ -88,11 +88,12 @@ typedef struct wamb_linear_args {
   int32_t n_per_group;
   const void* weight[3];  /* [n_per_group, K] bf16 each */
   const void* bias[3];    /* [n_per_group] bf16 each, or NULL */
-  void* out;              /* [M, ldo] bf16 */
+  void* out;              /* [M, ldo] bf16, or fp32 when out_is_f32 */
   int64_t ldo;
   int32_t epilogue;       /* enum wamb_epilogue */
-  const void* res;        /* [M, ldr] bf16 (RES / RES_GATE) */
+  const void* res;        /* [M, ldr] bf16 (RES / RES_GATE), or fp32 when res_is_f32 */
   int64_t ldr;
+  int32_t res_is_f32, out_is_f32;
   /* RES_GATE: gate = table[gate_index*D + col] + temb[((b*temb_len + l)*6 + gate_index)*D + col]
    * with b = row / rows_per_batch and l = 0 if temb_len == 1 else row % rows_per_batch. */
   const float* table;     /* [6, D] fp32 */
@@ -168,6 +169,11 @@ WAMB_API int wamb_attention(const wamb_attention_args* args, void* stream);
  * ([batch] int64, optional) maps each batch row to its context row;
  * otherwise context_batch must be batch or 1.
  *
+ * Numerics: fp32 math everywhere except the tensor-core operands; the
+ * residual stream (after self- and cross-attention) stays fp32 inside the
+ * block, so only the GEMM / attention operands and the output are rounded to
+ * bf16 (the reference also rounds the two intermediate residuals).
+ *
  * Scratch: `workspace` of wamb_block_workspace_bytes() bytes (caller-owned,
  * 256-byte aligned); intermediates stay there after the call (debug taps).
  */
@@ -176,7 +182,8 @@ typedef struct wamb_block_args {
   int32_t context_tokens, context_batch;
   const void* weights[27];
   double eps[7];
-  const void* x;                 /* [batch, tokens, dim] bf16 */
+  const void* x;                 /* [batch, tokens, dim] bf16, or fp32 when x_is_f32 */
+  int32_t x_is_f32, out_is_f32;  /* fp32 residual stream in/out (30-layer stacks) */
   const void* context;           /* [context_batch, context_tokens, dim] bf16 or NULL */
   const void* cross_k;           /* [context_batch, context_tokens, dim] bf16 or NULL */
   const void* cross_v;
@@ -190,7 +197,7 @@ typedef struct wamb_block_args {
   int32_t pool, pool_batch;
   const int64_t* candidate_rows; /* [batch] or NULL */
   int32_t update;
-  void* out;                     /* [batch, tokens, dim] bf16 */
+  void* out;                     /* [batch, tokens, dim] bf16, or fp32 when out_is_f32 */
   void* workspace; size_t workspace_bytes;
 } wamb_block_args;
 
@@ -199,13 +206,13 @@ enum wamb_tap {
   WAMB_TAP_MODULATED1 = 0,  /* [M, D]   LN1 + modulation */
   WAMB_TAP_QKV = 1,         /* [M, 3D]  q | k | v (q,k after RMS + RoPE unless in the pool) */
   WAMB_TAP_SELF_ATTN = 2,   /* [M, D] */
-  WAMB_TAP_RESIDUAL1 = 3,   /* [M, D] */
+  WAMB_TAP_RESIDUAL1 = 3,   /* [M, D] fp32 (the residual stream stays fp32 inside the block) */
   WAMB_TAP_NORM2 = 4,       /* [M, D] */
   WAMB_TAP_CROSS_Q = 5,     /* [M, D]   after RMS */
   WAMB_TAP_CROSS_K = 6,     /* [Bc*C, D] after RMS (computed per call only) */
   WAMB_TAP_CROSS_V = 7,
   WAMB_TAP_CROSS_ATTN = 8,  /* [M, D] */
-  WAMB_TAP_RESIDUAL2 = 9,   /* [M, D] */
+  WAMB_TAP_RESIDUAL2 = 9,   /* [M, D] fp32 */
   WAMB_TAP_MODULATED3 = 10, /* [M, D] */
   WAMB_TAP_GELU = 11,       /* [M, F] */
   WAMB_TAP_KV_SLOTS = 12,   /* [tokens] int32 pool slot of each new token */

@@ -155,8 +155,8 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
   put(WAMB_TAP_MODULATED1, MD);
   put(WAMB_TAP_QKV, 3 * MD);
   put(WAMB_TAP_SELF_ATTN, MD);
-  put(WAMB_TAP_RESIDUAL1, MD);
-  if (a->weights[1] != nullptr) put(WAMB_TAP_NORM2, MD);
+  put(WAMB_TAP_RESIDUAL1, 2 * MD);  // fp32
+  put(WAMB_TAP_NORM2, MD);
   put(WAMB_TAP_CROSS_Q, MD);
   if (a->cross_k == nullptr) {
     const size_t CD = static_cast<size_t>(a->context_batch) * a->context_tokens * D * 2;
@@ -164,7 +164,7 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
     put(WAMB_TAP_CROSS_V, CD);
   }
   put(WAMB_TAP_CROSS_ATTN, MD);
-  put(WAMB_TAP_RESIDUAL2, MD);
+  put(WAMB_TAP_RESIDUAL2, 2 * MD);  // fp32
   put(WAMB_TAP_MODULATED3, MD);
   put(WAMB_TAP_GELU, M * F * 2);
   if (a->cache_k != nullptr) {
@@ -184,6 +184,8 @@ inline int check_block_args(const wamb_block_args* a) {
   WAMB_REQUIRE(a->ffn_dim >= 64 && a->ffn_dim % 64 == 0, WAMB_ERR_SHAPE, "ffn_dim %% 64");
   WAMB_REQUIRE(row_vpt(a->dim) > 0, WAMB_ERR_SHAPE, "dim %d unsupported", a->dim);
   WAMB_REQUIRE(a->x && a->out && a->temb, WAMB_ERR_ARG, "null x/out/temb");
+  WAMB_REQUIRE((a->x_is_f32 == 0 || a->x_is_f32 == 1) && (a->out_is_f32 == 0 || a->out_is_f32 == 1),
+               WAMB_ERR_ARG, "x_is_f32 / out_is_f32 must be 0 or 1");
   for (int i = 0; i < 27; ++i) {
     if (i == 1 || i == 2) continue;
     WAMB_REQUIRE(a->weights[i] != nullptr, WAMB_ERR_ARG, "weights[%d] is null", i);
@@ -265,11 +267,11 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   bf* h1 = buf(WAMB_TAP_MODULATED1);
   bf* qkv = buf(WAMB_TAP_QKV);
   bf* attn = buf(WAMB_TAP_SELF_ATTN);
-  bf* h2 = buf(WAMB_TAP_RESIDUAL1);
-  bf* n2 = a->weights[1] ? buf(WAMB_TAP_NORM2) : h2;
+  float* h2 = reinterpret_cast<float*>(buf(WAMB_TAP_RESIDUAL1));
+  bf* n2 = buf(WAMB_TAP_NORM2);
   bf* cq = buf(WAMB_TAP_CROSS_Q);
   bf* ca = buf(WAMB_TAP_CROSS_ATTN);
-  bf* h3 = buf(WAMB_TAP_RESIDUAL2);
+  float* h3 = reinterpret_cast<float*>(buf(WAMB_TAP_RESIDUAL2));
   bf* f0 = buf(WAMB_TAP_MODULATED3);
   bf* act = buf(WAMB_TAP_GELU);
   int* slots = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_SLOTS]) : nullptr;
@@ -289,7 +291,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   }
   // 2. LN1 + modulation (shift 0, scale 1)
   LnParams ln{};
-  ln.x = static_cast<const bf*>(a->x); ln.ldx = D; ln.out = h1; ln.ldo = D; ln.M = M; ln.D = D;
+  ln.x = a->x; ln.x_f32 = a->x_is_f32; ln.ldx = D; ln.out = h1; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[0]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
@@ -334,19 +336,18 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   g = wamb_linear_args{};
   g.a = attn; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
   g.weight[0] = a->weights[9]; g.bias[0] = a->weights[10]; g.out = h2; g.ldo = D;
-  g.epilogue = WAMB_EPI_RES_GATE; g.res = a->x; g.ldr = D; g.table = table; g.temb = a->temb;
+  g.epilogue = WAMB_EPI_RES_GATE; g.res = a->x; g.res_is_f32 = a->x_is_f32; g.ldr = D;
+  g.out_is_f32 = 1; g.table = table; g.temb = a->temb;
   g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 2;
   g.dim = D;
   if ((rc = linear_impl(&g, s))) return rc;
-  // 7. LN2 (fp32 affine) or Identity
-  if (a->weights[1] != nullptr) {
-    ln = LnParams{};
-    ln.x = h2; ln.ldx = D; ln.out = n2; ln.ldo = D; ln.M = M; ln.D = D;
-    ln.eps = static_cast<float>(a->eps[1]); ln.affine = 1;
-    ln.gamma = static_cast<const float*>(a->weights[1]); ln.beta = static_cast<const float*>(a->weights[2]);
-    ln.rows_per_batch = Q;
-    if ((rc = launch_ln(ln, s))) return rc;
-  }
+  // 7. LN2 (fp32 affine), or the bf16 cast when norm2 is Identity
+  ln = LnParams{};
+  ln.x = h2; ln.x_f32 = 1; ln.ldx = D; ln.out = n2; ln.ldo = D; ln.M = M; ln.D = D;
+  ln.eps = static_cast<float>(a->eps[1]); ln.affine = a->weights[1] != nullptr ? 1 : 2;
+  ln.gamma = static_cast<const float*>(a->weights[1]); ln.beta = static_cast<const float*>(a->weights[2]);
+  ln.rows_per_batch = Q;
+  if ((rc = launch_ln(ln, s))) return rc;
   // 8-9. cross Q projection + RMSNorm
   g = wamb_linear_args{};
   g.a = n2; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
@@ -382,11 +383,11 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   g = wamb_linear_args{};
   g.a = ca; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
   g.weight[0] = a->weights[19]; g.bias[0] = a->weights[20]; g.out = h3; g.ldo = D;
-  g.epilogue = WAMB_EPI_RES; g.res = h2; g.ldr = D;
+  g.epilogue = WAMB_EPI_RES; g.res = h2; g.res_is_f32 = 1; g.out_is_f32 = 1; g.ldr = D;
   if ((rc = linear_impl(&g, s))) return rc;
   // 13. LN3 + modulation (shift 3, scale 4)
   ln = LnParams{};
-  ln.x = h3; ln.ldx = D; ln.out = f0; ln.ldo = D; ln.M = M; ln.D = D;
+  ln.x = h3; ln.x_f32 = 1; ln.ldx = D; ln.out = f0; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[2]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 3; ln.scale_idx = 4;
@@ -401,7 +402,8 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   g = wamb_linear_args{};
   g.a = act; g.lda = F; g.m = M; g.k = F; g.groups = 1; g.n_per_group = D;
   g.weight[0] = a->weights[25]; g.bias[0] = a->weights[26]; g.out = a->out; g.ldo = D;
-  g.epilogue = WAMB_EPI_RES_GATE; g.res = h3; g.ldr = D; g.table = table; g.temb = a->temb;
+  g.epilogue = WAMB_EPI_RES_GATE; g.res = h3; g.res_is_f32 = 1; g.ldr = D;
+  g.out_is_f32 = a->out_is_f32; g.table = table; g.temb = a->temb;
   g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 5;
   g.dim = D;
   return linear_impl(&g, s);

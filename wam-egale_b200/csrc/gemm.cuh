@@ -5,7 +5,7 @@
 // Roles (192 threads, one CTA per SM):
 //   warp 0      TMA producer (A tile 128x64, W tile BNx64, 128B swizzle)
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld -> bias / GELU / residual / gate -> bf16 stores
+//   warps 2..5  epilogue: tcgen05.ld -> bias / GELU / residual / gate -> bf16 or fp32 stores
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i+1.
 //
@@ -28,11 +28,12 @@ struct GemmParams {
   int M, N, K;
   int n_per_group;                   // columns per weight group (N = groups * n_per_group)
   const __nv_bfloat16* bias[3];      // per group, may be null
-  __nv_bfloat16* out;
+  void* out;                         // [M, ldo] bf16, or fp32 when out_f32
   long long ldo;                     // output row stride (elements)
   int epi;
-  const __nv_bfloat16* res;          // residual [M, ldr]
+  const void* res;                   // residual [M, ldr] bf16, or fp32 when res_f32
   long long ldr;
+  int res_f32, out_f32;
   // Gate = table[gate_idx, col] + temb[b, l, gate_idx, col]  (model.py:751-759)
   const float* table;                // [6, D] fp32
   const void* temb;                  // [B, L, 6, D] fp32 or bf16
@@ -247,28 +248,48 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               v[j + 3] *= tb.w + te.w;
             }
           }
-          const uint4* rp = reinterpret_cast<const uint4*>(p.res + row * p.ldr + col);
+          if (p.res_f32) {
+            const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(p.res) +
+                                                               row * p.ldr + col);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 w = __ldg(rp + j);
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+            for (int j = 0; j < 8; ++j) {
+              const float4 f = __ldg(rp + j);
+              v[4 * j] += f.x;
+              v[4 * j + 1] += f.y;
+              v[4 * j + 2] += f.z;
+              v[4 * j + 3] += f.w;
+            }
+          } else {
+            const uint4* rp = reinterpret_cast<const uint4*>(
+                static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const float2 f = unpack_bf16(ws[h]);
-              v[8 * j + 2 * h] += f.x;
-              v[8 * j + 2 * h + 1] += f.y;
+            for (int j = 0; j < 4; ++j) {
+              const uint4 w = __ldg(rp + j);
+              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const float2 f = unpack_bf16(ws[h]);
+                v[8 * j + 2 * h] += f.x;
+                v[8 * j + 2 * h + 1] += f.y;
+              }
             }
           }
         }
-        uint4* op = reinterpret_cast<uint4*>(p.out + row * p.ldo + col);
+        if (p.out_f32) {
+          float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 w;
-          w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
-          w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
-          w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
-          w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
-          op[j] = w;
+          for (int j = 0; j < 8; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 w;
+            w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+            w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+            w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+            w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+            op[j] = w;
+          }
         }
       }
       tc_fence_before();

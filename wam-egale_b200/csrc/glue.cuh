@@ -64,13 +64,15 @@ WAMB_DEV void load_mod8(const float* table, const void* temb, int temb_f32, long
 
 // ------------------------------------------------------------ LayerNorm
 struct LnParams {
-  const __nv_bfloat16* x;
+  const void* x;          // [M, ldx] bf16, or fp32 when x_f32
   long long ldx;
+  int x_f32;
   __nv_bfloat16* out;
   long long ldo;
   int M, D;
   float eps;
   int affine;             // 1: y = LN(x) * gamma + beta ; 0: y = LN(x) * (1 + scale) + shift
+                          // 2: y = x (identity norm2, only the bf16 cast)
   const float* gamma;
   const float* beta;
   const float* table;     // [6, D]
@@ -86,13 +88,20 @@ __global__ void ln_kernel(const LnParams p) {
   const int nthr = blockDim.x;
   const int nw = nthr >> 5;
   float v[VPT][8];
-  const __nv_bfloat16* xr = p.x + static_cast<long long>(row) * p.ldx;
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    load8(xr + (i * nthr + threadIdx.x) * 8, v[i]);
+    const long long off = static_cast<long long>(row) * p.ldx + (i * nthr + threadIdx.x) * 8;
+    if (p.x_f32) load8f(static_cast<const float*>(p.x) + off, v[i]);
+    else load8(static_cast<const __nv_bfloat16*>(p.x) + off, v[i]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) s += v[i][j];
+  }
+  __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ldo;
+  if (p.affine == 2) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) store8(orow + (i * nthr + threadIdx.x) * 8, v[i]);
+    return;
   }
   // Generic block reduction (number of warps known only at run time).
   auto reduce = [&](float a) {
@@ -116,12 +125,11 @@ __global__ void ln_kernel(const LnParams p) {
     }
   const float rstd = rsqrtf(reduce(q) / p.D + p.eps);
   long long temb_off = 0;
-  if (!p.affine) {
+  if (p.affine == 0) {
     const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
     const long long l = p.temb_L == 1 ? 0 : tok;
     temb_off = (static_cast<long long>(b) * p.temb_L + l) * 6 * p.D;
   }
-  __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ldo;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int col = (i * nthr + threadIdx.x) * 8;

@@ -50,6 +50,8 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   WAMB_REQUIRE(a->lda >= a->k && a->lda % 8 == 0, WAMB_ERR_ALIGN, "lda");
   const long long N = static_cast<long long>(a->groups) * a->n_per_group;
   WAMB_REQUIRE(a->ldo >= N && a->ldo % 8 == 0, WAMB_ERR_ALIGN, "ldo");
+  WAMB_REQUIRE(a->out_is_f32 == 0 || a->out_is_f32 == 1, WAMB_ERR_ARG, "out_is_f32");
+  WAMB_REQUIRE(a->res_is_f32 == 0 || a->res_is_f32 == 1, WAMB_ERR_ARG, "res_is_f32");
   WAMB_REQUIRE(a->a && a->out, WAMB_ERR_ARG, "null A/out");
   WAMB_REQUIRE(aligned16(a->a) && aligned16(a->out), WAMB_ERR_ALIGN, "A/out alignment");
   for (int g = 0; g < a->groups; ++g) {
@@ -91,11 +93,13 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   p.n_per_group = a->n_per_group;
   for (int g = 0; g < 3; ++g)
     p.bias[g] = g < a->groups ? static_cast<const __nv_bfloat16*>(a->bias[g]) : nullptr;
-  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.out = a->out;
   p.ldo = a->ldo;
   p.epi = a->epilogue;
-  p.res = static_cast<const __nv_bfloat16*>(a->res);
+  p.res = a->res;
   p.ldr = a->ldr;
+  p.res_f32 = a->res_is_f32;
+  p.out_f32 = a->out_is_f32;
   p.table = a->table;
   p.temb = a->temb;
   p.temb_f32 = a->temb_is_f32;

@@ -23,7 +23,7 @@ class LinearArgs(ctypes.Structure):
         ("groups", c_int32), ("n_per_group", c_int32),
         ("weight", c_void_p * 3), ("bias", c_void_p * 3),
         ("out", c_void_p), ("ldo", c_int64), ("epilogue", c_int32),
-        ("res", c_void_p), ("ldr", c_int64),
+        ("res", c_void_p), ("ldr", c_int64), ("res_is_f32", c_int32), ("out_is_f32", c_int32),
         ("table", c_void_p), ("temb", c_void_p), ("temb_is_f32", c_int32),
         ("temb_len", c_int32), ("rows_per_batch", c_int32), ("gate_index", c_int32),
         ("dim", c_int32),
@@ -58,7 +58,8 @@ class BlockArgs(ctypes.Structure):
         ("context_tokens", c_int32), ("context_batch", c_int32),
         ("weights", c_void_p * 27),
         ("eps", ctypes.c_double * 7),
-        ("x", c_void_p), ("context", c_void_p), ("cross_k", c_void_p), ("cross_v", c_void_p),
+        ("x", c_void_p), ("x_is_f32", c_int32), ("out_is_f32", c_int32),
+        ("context", c_void_p), ("cross_k", c_void_p), ("cross_v", c_void_p),
         ("context_rows", c_void_p),
         ("temb", c_void_p), ("temb_len", c_int32), ("temb_is_f32", c_int32),
         ("freq", c_void_p), ("freq_batch", c_int32),

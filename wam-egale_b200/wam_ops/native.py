@@ -192,6 +192,7 @@ class NativeBlock:
         M = B * Q
         C = a.context_batch * a.context_tokens
         shapes = {"qkv": (M, 3 * D), "gelu": (M, F), "cross_k": (C, D), "cross_v": (C, D)}
+        fp32 = ("residual1", "residual2")
         result = {}
         for i, name in enumerate(_lib.TAPS):
             o = offs[i]
@@ -203,6 +204,9 @@ class NativeBlock:
                 continue
             shape = shapes.get(name, (M, D))
             n = shape[0] * shape[1]
-            result[name] = ws[o:o + 2 * n].view(torch.bfloat16).view(shape).clone()
+            if name in fp32:
+                result[name] = ws[o:o + 4 * n].view(torch.float32).view(shape).clone()
+            else:
+                result[name] = ws[o:o + 2 * n].view(torch.bfloat16).view(shape).clone()
         result["output"] = out
         return result

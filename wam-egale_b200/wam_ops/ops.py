@@ -24,6 +24,7 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
     shaped ones whose outputs are concatenated along the columns (the QKV
     projection reads the three reference Linear weights in place).
     """
+    out_f32 = out is not None and out.dtype == torch.float32
     if isinstance(weights, torch.Tensor):
         weights = [weights]
     if biases is None or isinstance(biases, torch.Tensor):
@@ -51,10 +52,12 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
         args.bias[i] = None if b is None else b.data_ptr()
     args.out = out.data_ptr()
     args.ldo = out.stride(0)
+    args.out_is_f32 = int(out_f32)
     args.epilogue = epilogue
     if res is not None:
         args.res = res.data_ptr()
         args.ldr = res.stride(0)
+        args.res_is_f32 = int(res.dtype == torch.float32)
     if table is not None:
         args.table = table.data_ptr()
         args.temb = temb.data_ptr()
