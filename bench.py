@@ -1,0 +1,365 @@
+"""Benchmark: 30-layer 5B-shape Wan-DiT denoise step on B200 (one process per GPU).
+
+Workload (BASELINE configs[4] per-GPU slice, configs[2] per rollout): every
+rank holds 8 independent rollouts, each one 880-token chunk (848 video + 32
+action tokens) attending to its own 3520-token self-KV history plus itself,
+with a prepared 512-token cross-K/V, through 30 layers of D 3072 / 24x128
+heads / FFN 14336, bf16 tensor-core math, update_cache=0 (the pool mask is
+restored, so every step sees the same cache). A "step" is one 30-layer
+denoise step of all 8 rollouts; weights (9.8 GB) and KV pools (13 GB) are far
+larger than L2, so no flush is needed between steps. Under torchrun each
+rank runs its own 8 rollouts (weak scaling) and the 32 action-token outputs
+of every rollout are all-gathered over NCCL after each step.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Rank 0 prints one JSON line (see the keys below). `value` is chunk-steps/s
+for the whole job (rollouts x ranks / step time), `ms_per_step` is the DiT
+denoise-step time. `--impl reference` times the reference algorithm's CPU
+implementation (the fp32 oracle port) on the host cores instead.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "wam-egale_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "chunk_denoise_steps_per_s"
+UNIT = "chunk-steps/s"
+CHUNK_STEPS = 10  # FastWAM denoise updates per action chunk (real_speculative.py:33,107)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def workload_config(n_gpus, batch):
+    return {"workload": "cfg4 slice: 8 rollouts/GPU of cfg2 (30-layer 5B-shape Wan-DiT denoise step, "
+                        "880-token chunk = 848 video + 32 action, 3520-token self-KV history, "
+                        "512-token prepared cross-K/V)",
+            "model": "Wan-DiT block stack D3072 H24x128 F14336 L30",
+            "global_batch": batch * n_gpus, "seq_len": 880, "kv_history": 3520, "context": 512,
+            "parallelism": f"rollouts sharded, {batch}/GPU" + (", NCCL all_gather of action outputs"
+                                                                if n_gpus > 1 else ""),
+            "l2": "inputs larger than L2 (9.8 GB weights + 13 GB KV per step)",
+            "chunk_steps_per_action_chunk": CHUNK_STEPS}
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(",") for r in Path(self.path).read_text().splitlines() if r.strip()]
+        os.unlink(self.path)
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                mhz.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not mhz:
+            return None
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# --------------------------------------------------------------- CPU side
+def cpu_reference_rate(layers=2, warmup=1, reps=1):
+    """The reference algorithm on the host cores: the fp32 oracle restatement
+    of the block (oracle/wan_block.py) for ONE cfg2 rollout, timed over
+    `layers` layers and scaled to a 30-layer step. Returns (value in
+    chunk-steps/s, threads, seconds per layer, sample text)."""
+    from oracle import wan_block as ob
+    from wam_ops import configs
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = configs.PRESETS["cfg2"]
+    D, H, F, Q = cfg.dim, cfg.heads, cfg.ffn, cfg.tokens
+    g = torch.Generator().manual_seed(0)
+    blk = ob.WanTransformerBlock(D, F, H, cross_attn_norm=True, eps=1e-6).eval()
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            if name.endswith("weight") and "norm" not in name:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+    pool, hist = cfg.pool_chunks * Q, cfg.history_chunks * Q
+    blk.attn1.init_kv_cache("pos", pool, H, 128, "cpu", torch.float32, 1)
+    c = blk.attn1.attn_caches["pos"]
+    c["k"].normal_(generator=g)
+    c["v"].normal_(generator=g)
+    c["mask"][:hist] = True
+    c["id"][:hist] = torch.arange(hist) // Q
+    x = torch.randn(1, Q, D, generator=g)
+    ctx = torch.randn(1, cfg.context, D, generator=g)
+    temb = configs.make_temb(cfg, 1, "cpu", g)
+    rope = configs.chunk_rope(cfg)
+    with torch.no_grad():
+        for _ in range(warmup):
+            blk(x, ctx, temb, rope, update_cache=0)
+        t0 = time.perf_counter()
+        for _ in range(reps * layers):
+            blk(x, ctx, temb, rope, update_cache=0)
+        dt = (time.perf_counter() - t0) / (reps * layers)
+    step = dt * cfg.layers
+    sample = (f"{reps * layers} layer forward(s) of one cfg2 rollout (880 tokens, 4400 visible keys, "
+              f"512 context, fp32), scaled x{cfg.layers} layers per step")
+    return 1.0 / step, torch.get_num_threads(), dt, sample
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path on the host (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    n = args.gpus
+    for _ in range(args.warmup):
+        cpu_reference_rate(layers=1, warmup=0)
+    rates, threads, sample = [], 1, ""
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r, threads, _, sample = cpu_reference_rate(layers=1, warmup=0)
+        rates.append(r)
+    wall = time.perf_counter() - t0
+    value = sum(rates) / len(rates)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, cfg2 shapes)",
+            "config": workload_config(n, 1) | {"sample_per_step": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": wall}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- GPU side
+def run_native(args):
+    from wam_ops import _lib, configs, ops
+    from wam_ops.stack import NativeStack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    cfg = configs.PRESETS["cfg4"]
+    B, Q, D = cfg.batch, cfg.tokens, cfg.dim
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    torch.set_grad_enabled(False)
+
+    blocks = configs.build_blocks(cfg, dev, seed=1234)
+    configs.fill_history(blocks, cfg, dev, gen, pool_batch=B)
+    stack = NativeStack(blocks)
+    ctx = torch.randn(B, cfg.context, D, generator=gen, device=dev).bfloat16()
+    stack.prepare_context(ctx)
+    x = torch.randn(B, Q, D, generator=gen, device=dev).bfloat16()
+    temb = configs.make_temb(cfg, B, dev, gen)
+    rope = configs.chunk_rope(cfg).to(dev)
+    torch.cuda.synchronize()
+    if _lib.device_status() != 0:
+        raise RuntimeError("device error during setup")
+
+    static = stack.capture(x, ctx, temb, rope, warmup=1)
+    A = 32  # action tokens per rollout
+    gathered = torch.empty(world * B, A, D, dtype=torch.bfloat16, device=dev) if world > 1 else None
+
+    def step():
+        out = stack.replay()
+        if pg is not None:
+            pg.all_gather_into_tensor(gathered, out[:, -A:].contiguous())
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if _lib.device_status() != 0:
+        raise RuntimeError("device error during warm-up")
+
+    clocks = Clocks(local)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if pg is not None:
+        pg.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms = t.item()
+    value = B * world / (ms / 1000.0)
+    dev_code = _lib.device_status()
+
+    # ---- e2e through the public API: pinned host input -> step -> host output
+    hx = x.cpu().pin_memory()
+    ht = temb.cpu().pin_memory()
+    hout = torch.empty(B, Q, D, dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        stack.replay(hx.to(dev, non_blocking=True), ht.to(dev, non_blocking=True))
+        hout.copy_(static["out"], non_blocking=True)
+    torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        static["x"].copy_(hx, non_blocking=True)
+        static["temb"].copy_(ht, non_blocking=True)
+        step()
+        hout.copy_(static["out"], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms_e2e], device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms_e2e = t.item()
+    e2e = {"value": B * world / (ms_e2e / 1000.0), "unit": UNIT,
+           "h2d_bytes_per_step": hx.numel() * 2 + ht.numel() * 4,
+           "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": ms_e2e}
+
+    # ---- roofline of the dominant kernel (FFN1 GEMM + GELU, M = 8 x 880)
+    M, F = B * Q, cfg.ffn
+    blk0 = blocks[0]
+    a = torch.randn(M, D, generator=gen, device=dev).bfloat16()
+    w1, b1 = blk0.ffn.net[0].proj.weight, blk0.ffn.net[0].proj.bias
+    act = torch.empty(M, F, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        ops.linear(a, w1, b1, epilogue=_lib.EPI_GELU, out=act)
+    reps = 20
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        ops.linear(a, w1, b1, epilogue=_lib.EPI_GELU, out=act)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    pk, pk_kind = peaks()
+    flops = 2.0 * M * F * D
+    achieved = flops / (k_ms / 1000.0) / 1e12
+    roof = {"kernel": "gemm_tc_kernel<256,4> FFN1+GELU (M 7040, N 14336, K 3072)",
+            "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": achieved / pk["bf16_tflops"], "traffic": None,
+            "peak_source": f"{pk_kind} bf16 burst", "ms_per_launch": k_ms,
+            "algorithmic_flops_per_launch": flops}
+    step_flops = stack_flops(cfg) * B
+    step_roof = {"achieved": step_flops / (ms / 1000.0) / 1e12, "unit": "TFLOP/s",
+                 "peak": pk["bf16_tflops_sustained"],
+                 "frac": step_flops / (ms / 1000.0) / 1e12 / pk["bf16_tflops_sustained"],
+                 "peak_source": f"{pk_kind} bf16 sustained", "algorithmic_flops_per_step": step_flops}
+
+    line = None
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded weights N(0,0.02), "
+                "zero biases, N(0,1) hidden/context, random unit-scale KV history)",
+                "config": workload_config(world, B) | {"action_chunks_per_s": value / CHUNK_STEPS},
+                "roofline": roof, "step_roofline": step_roof, "e2e": e2e,
+                "gpu_launches": stack.launches_per_step(with_cache=True) * args.steps,
+                "clocks": clk, "device_error": dev_code}
+    if pg is not None:
+        del static, stack
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            v, th, dt, sample = cpu_reference_rate()
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": th, "kind": "port",
+                                    "sample": sample}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def stack_flops(cfg):
+    """Algorithmic FLOPs of one 30-layer step for ONE rollout: the six
+    projections, the two FFN GEMMs and the QK^T / PV products of both
+    attentions (cross K/V prepared, not counted)."""
+    D, F, Q, C = cfg.dim, cfg.ffn, cfg.tokens, cfg.context
+    keys = cfg.history_chunks * Q + Q
+    proj = 2 * Q * D * (3 * D) + 2 * Q * D * D + 2 * Q * D * D + 2 * Q * D * D
+    ffn = 2 * 2 * Q * D * F
+    attn = 2 * 2 * Q * keys * D + 2 * 2 * Q * C * D
+    return cfg.layers * (proj + ffn + attn)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_native(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

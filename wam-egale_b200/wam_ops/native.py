@@ -99,8 +99,9 @@ class NativeBlock:
                   keep=None):
         keep = [] if keep is None else keep
         x = hidden_states
-        if not (x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() == 3):
-            raise RuntimeError("hidden_states must be a contiguous CUDA bf16 [B, Q, D] tensor")
+        if not (x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and x.is_contiguous()
+                and x.dim() == 3):
+            raise RuntimeError("hidden_states must be a contiguous CUDA bf16 (or fp32) [B, Q, D] tensor")
         B, Q, D = x.shape
         if D != self.dim:
             raise RuntimeError(f"hidden dim {D} != block dim {self.dim}")
@@ -111,6 +112,7 @@ class NativeBlock:
         for i, e in enumerate(self.eps):
             a.eps[i] = float(e)
         a.x = x.data_ptr()
+        a.x_is_f32 = int(x.dtype == torch.float32)
         if cross_kv is not None:
             k, v = cross_kv
             a.cross_k, a.cross_v = k.data_ptr(), v.data_ptr()
@@ -159,12 +161,18 @@ class NativeBlock:
                 raise ValueError("invalid candidate_cache_rows for this KV cache")
             a.candidate_rows = r.data_ptr()
         a.update = int(update_cache)
+        if out.shape != x.shape or out.dtype not in (torch.bfloat16, torch.float32) or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous bf16/fp32 tensor shaped like hidden_states")
         a.out = out.data_ptr()
+        a.out_is_f32 = int(out.dtype == torch.float32)
         return a
 
     def __call__(self, hidden_states, encoder_hidden_states, temb, rotary_emb,
                  update_cache=0, cache_name="pos", candidate_cache_rows=None, debug=False,
-                 cross_kv=None, context_rows=None):
+                 cross_kv=None, context_rows=None, out_dtype=None, out=None):
+        """Runs the block; returns hidden_states' dtype by default. out_dtype /
+        out select an fp32 output (the residual stream without the final bf16
+        rounding), which multi-layer stacks use between blocks."""
         if torch.is_grad_enabled():
             raise RuntimeError("NativeBlock is inference-only; use no_grad/inference_mode")
         block = self.block()
@@ -172,7 +180,8 @@ class NativeBlock:
         cache = caches.get(cache_name)
         if candidate_cache_rows is not None and (update_cache != 0 or cache is None):
             raise ValueError("candidate verification requires existing read-only KV")
-        out = torch.empty_like(hidden_states)
+        if out is None:
+            out = torch.empty_like(hidden_states, dtype=out_dtype or hidden_states.dtype)
         keep = []
         a = self.make_args(hidden_states, encoder_hidden_states, temb, rotary_emb, cache,
                            candidate_cache_rows, update_cache, out, cross_kv, context_rows, keep)

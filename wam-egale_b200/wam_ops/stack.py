@@ -1,0 +1,102 @@
+"""NativeStack: the 30-block denoise step of WanTransformer3DModel
+(model.py:1091-1098) on the B200 block, optionally as one CUDA graph.
+
+Each layer is a WholeLayerBlock with its cross-attention K/V prepared once
+per context (whole_layer.py). Between layers the residual stream stays fp32
+(the block's x_is_f32 / out_is_f32 mode): the first layer reads the caller's
+bf16 hidden states and the last layer writes bf16, so the stack rounds the
+residual stream once instead of once per layer. All layers share one
+workspace, so a step allocates nothing after the first call, and
+`capture()` records the whole step (420 kernel launches at 30 layers) in a
+CUDA graph that `replay()` launches with one call.
+"""
+import torch
+
+from . import _lib
+from .whole_layer import WholeLayerBlock
+
+
+class NativeStack:
+    def __init__(self, blocks):
+        self.layers = [WholeLayerBlock(b) for b in blocks]
+        self.graph = None
+        self._static = None
+
+    def prepare_context(self, context):
+        """Cross K/V of every layer for this context (outside timed regions)."""
+        with torch.no_grad():
+            for layer in self.layers:
+                layer.prepare_context(context, precompute=True)
+
+    def forward(self, hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache=0,
+                cache_name="pos", candidate_cache_rows=None, out=None):
+        """One denoise step through every layer; returns bf16 [B, Q, D]."""
+        if torch.is_grad_enabled():
+            raise RuntimeError("NativeStack is inference-only; use no_grad/inference_mode")
+        B, Q, D = hidden_states.shape
+        dev = hidden_states.device
+        bufs = [torch.empty(B, Q, D, dtype=torch.float32, device=dev) for _ in range(2)]
+        h = hidden_states
+        n = len(self.layers)
+        for i, layer in enumerate(self.layers):
+            last = i == n - 1
+            dst = (out if out is not None else torch.empty(B, Q, D, dtype=torch.bfloat16, device=dev)) \
+                if last else bufs[i % 2]
+            layer(h, encoder_hidden_states, temb, rotary_emb, update_cache, cache_name,
+                  candidate_cache_rows, out=dst)
+            h = dst
+        return h
+
+    __call__ = forward
+
+    def capture(self, hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache=0,
+                cache_name="pos", candidate_cache_rows=None, warmup=1):
+        """Record one step as a CUDA graph over static copies of the inputs.
+        update_cache must leave the cache ready for the next replay
+        (update 0 restores the mask, so repeated denoise steps are stable)."""
+        if update_cache != 0:
+            raise ValueError("graph capture is for repeated denoise steps (update_cache=0)")
+        static = {
+            "x": hidden_states.clone(), "temb": temb.clone(),
+            "rope": None if rotary_emb is None else rotary_emb.clone(),
+            "rows": None if candidate_cache_rows is None else candidate_cache_rows.clone(),
+        }
+        static["out"] = torch.empty_like(static["x"], dtype=torch.bfloat16)
+        args = (static["x"], encoder_hidden_states, static["temb"], static["rope"], 0, cache_name,
+                static["rows"])
+        with torch.no_grad():
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(warmup):
+                    self.forward(*args, out=static["out"])
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.forward(*args, out=static["out"])
+        self.graph, self._static = g, static
+        return static
+
+    def replay(self, hidden_states=None, temb=None):
+        """Copy new inputs into the captured buffers (if given) and replay."""
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        if hidden_states is not None:
+            self._static["x"].copy_(hidden_states, non_blocking=True)
+        if temb is not None:
+            self._static["temb"].copy_(temb, non_blocking=True)
+        self.graph.replay()
+        return self._static["out"]
+
+    def launches_per_step(self, with_cache, cross_prepared=True):
+        """Kernel launches of one step (the count bench.py reports): per layer
+        LN1, QKV, RMS+RoPE, attention, O, LN2, cross-Q, RMS, cross attention,
+        cross-O, LN3, FFN1, FFN2 = 13, + KV layout with a cache, + 3 when the
+        cross K/V is computed per call."""
+        per = 13 + (1 if with_cache else 0) + (0 if cross_prepared else 3)
+        return per * len(self.layers)
+
+
+def device_error():
+    """Synchronise and return the device error word (0 = ok)."""
+    return _lib.device_status()

@@ -56,8 +56,9 @@ class WholeLayerBlock:
             self.context_kv = [k, v]
 
     def __call__(self, hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache=0,
-                 cache_name="pos", candidate_cache_rows=None, debug=False):
+                 cache_name="pos", candidate_cache_rows=None, debug=False, out_dtype=None, out=None):
         cross = tuple(self.context_kv) if self.context_kv else None
         return self.native(hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache,
                            cache_name, candidate_cache_rows, debug, cross_kv=cross,
-                           context_rows=self.context_rows if cross is not None else None)
+                           context_rows=self.context_rows if cross is not None else None,
+                           out_dtype=out_dtype, out=out)
