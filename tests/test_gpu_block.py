@@ -69,16 +69,16 @@ def test_block_context_broadcast(cuda_device):
     assert_parity(_run_native(to_device_block(blk), x, ctx, temb, r), ref, rb)
 
 
-def _cache_equal(oc, gc):
+def _cache_equal(oc, gc, tc):
+    """Metadata exactly; pool rows (bf16 by the cache schema) under the parity
+    gate, bounded by the reference's own bf16 cache (tc) error."""
     assert torch.equal(oc["id"], gc["id"].cpu())
     assert torch.equal(oc["mask"], gc["mask"].cpu())
     assert torch.equal(oc["is_pred"], gc["is_pred"].cpu())
     valid = oc["mask"] | (oc["id"] >= 0)
     idx = valid.nonzero().squeeze(-1)
-    s = stats(gc["k"][:, idx.cuda()], oc["k"][:, idx])
-    assert s["cos"] >= 0.9999 and s["max_abs"] <= 2e-2, s
-    s = stats(gc["v"][:, idx.cuda()], oc["v"][:, idx])
-    assert s["cos"] >= 0.9999 and s["max_abs"] <= 2e-2, s
+    for name in ("k", "v"):
+        assert_parity(gc[name][:, idx.cuda()], oc[name][:, idx], tc[name][:, idx.cuda()])
 
 
 def test_block_kv_lifecycle_and_eviction(cuda_device):
@@ -98,7 +98,7 @@ def test_block_kv_lifecycle_and_eviction(cuda_device):
         rb = reference_bf16(tb, x, ctx, temb, r, update_cache=update)
         out = _run_native(g, x, ctx, temb, r, update_cache=update)
         assert_parity(out, ref, rb)
-        _cache_equal(blk.attn1.attn_caches["pos"], g.attn1.attn_caches["pos"])
+        _cache_equal(blk.attn1.attn_caches["pos"], g.attn1.attn_caches["pos"], tb.attn1.attn_caches["pos"])
 
 
 def test_block_candidate_verification(cuda_device):

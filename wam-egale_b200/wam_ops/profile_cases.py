@@ -1,0 +1,68 @@
+"""Small single-kernel cases for ncu captures (inputs larger than L2, a few
+hundred MB on the device, 3 warm-up launches then `--launches` more).
+
+  python wam-egale_b200/wam_ops/profile_cases.py ffn1 [--m 2048] [--launches 1]
+  python wam-egale_b200/wam_ops/profile_cases.py attention [--q 880] [--pool 4400]
+  python wam-egale_b200/wam_ops/profile_cases.py rms | ln
+
+ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (cfg2 weights)
+attention  self attention of one cfg2 rollout over a 4400-slot pool (24 heads)
+rms        RMSNorm + RoPE of the q/k/v projection output, K/V into the pool
+ln         LayerNorm + adaLN modulation
+"""
+import argparse
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+import torch  # noqa: E402
+
+from wam_ops import _lib, configs, ops  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["ffn1", "attention", "rms", "ln"])
+    ap.add_argument("--m", type=int, default=2048)
+    ap.add_argument("--q", type=int, default=880)
+    ap.add_argument("--pool", type=int, default=4400)
+    ap.add_argument("--launches", type=int, default=1)
+    a = ap.parse_args()
+    torch.set_grad_enabled(False)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    D, H, F = 3072, 24, 14336
+    if a.case == "ffn1":
+        x = torch.randn(a.m, D, generator=g, device=dev).bfloat16()
+        w = (torch.randn(F, D, generator=g, device=dev) * 0.02).bfloat16()
+        b = torch.zeros(F, device=dev, dtype=torch.bfloat16)
+        out = torch.empty(a.m, F, device=dev, dtype=torch.bfloat16)
+        run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_GELU, out=out)  # noqa: E731
+    elif a.case == "attention":
+        q = torch.randn(a.q, D, generator=g, device=dev).bfloat16()
+        kp = torch.randn(a.pool, D, generator=g, device=dev).bfloat16()
+        vp = torch.randn(a.pool, D, generator=g, device=dev).bfloat16()
+        out = torch.empty(a.q, D, device=dev, dtype=torch.bfloat16)
+        run = lambda: ops.attention(q, kp, vp, heads=H, q_rows=a.q, src0_batch_stride=a.pool,  # noqa: E731
+                                    src0_len=a.pool, out=out)
+    else:
+        cfg = configs.PRESETS["cfg2"]
+        blk = configs.build_blocks(configs.Config("p", D, H, F, 1, 1, (1, 16, 53), (8, 4, 1), 8), dev)[0]
+        from wam_ops.native import NativeBlock
+        nb = NativeBlock(blk)
+        x = torch.randn(1, a.q, D, generator=g, device=dev).bfloat16()
+        ctx = torch.randn(1, 8, D, generator=g, device=dev).bfloat16()
+        temb = configs.make_temb(cfg, 1, dev, g)
+        rope = configs.rope_freqs(torch.zeros(3, a.q)).to(dev)
+        run = lambda: nb(x, ctx, temb, rope)  # noqa: E731
+    for _ in range(3 + a.launches):
+        run()
+    torch.cuda.synchronize()
+    code = _lib.device_status()
+    print(f"{a.case}: ok, device status {code}")
+    return 0 if code == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
