@@ -227,6 +227,30 @@ WAMB_API size_t wamb_block_workspace_layout(const wamb_block_args* args, int64_t
 WAMB_API int wamb_block_forward(const wamb_block_args* args, void* stream);
 
 /*
+ * wamb_block_forward without a caller-provided workspace. This entry point
+ * has no counterpart in the reference. It is for callers that cannot
+ * allocate device memory at the point where they run the block: work being
+ * recorded into a CUDA graph (a cudaMalloc during stream capture is an error
+ * that invalidates the capture), serving loops that must not hit the device
+ * allocator (cudaMalloc can synchronise the device), and hosts that reach
+ * the library through a thin FFI and have no device allocator of their own.
+ *
+ * The scratch is a fixed array of WAMB_NOALLOC_SCRATCH_BYTES in device
+ * memory, defined once in the library; every GPU that loads libwamb.so holds
+ * it until the process exits. A call whose workspace need
+ * (wamb_block_workspace_bytes) exceeds it returns WAMB_ERR_WORKSPACE and
+ * launches nothing. args->workspace and args->workspace_bytes are ignored;
+ * everything else is as for wamb_block_forward. The first call on a device
+ * looks up the array's device address (make it before any stream capture on
+ * that device). All calls share the one array and it keeps the last call's
+ * contents (nothing in it needs to start at zero): calls that can overlap on
+ * the GPU, e.g. on two streams without ordering, race on it.
+ * Allocates nothing: no cudaMalloc, no cudaFree.
+ */
+#define WAMB_NOALLOC_SCRATCH_BYTES (32u << 20)
+WAMB_API int wamb_block_forward_noalloc(const wamb_block_args* args, void* stream);
+
+/*
  * Cross-attention K/V of one block for a fixed context (the reference's
  * WholeLayerBlock.prepare_context(context, precompute=True),
  * 算子研究/wam_ops/optimized/whole_layer.py:41-67):

@@ -6,6 +6,34 @@
 #include "linear.cuh"
 #include "block.cuh"
 
+namespace wamb {
+
+// Scratch of wamb_block_forward_noalloc: a fixed device array, so that the
+// entry point never calls the allocator. Host code must not pass the symbol
+// itself to a kernel (on the host it only names the array); its device
+// address is looked up once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[WAMB_NOALLOC_SCRATCH_BYTES];
+
+inline int noalloc_scratch_address(void** out) {
+  static void* addr[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+  WAMB_REQUIRE(dev >= 0 && dev < 64, WAMB_ERR_CUDA, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    WAMB_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    WAMB_REQUIRE(p != nullptr && reinterpret_cast<uintptr_t>(p) % 256 == 0, WAMB_ERR_CUDA,
+                 "scratch array address %p", p);
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return WAMB_OK;
+}
+
+}  // namespace wamb
+
 extern "C" {
 
 const char* wamb_last_error(void) { return wamb::g_last_error.c_str(); }
@@ -46,6 +74,23 @@ size_t wamb_block_workspace_layout(const wamb_block_args* args, int64_t* offsets
 
 int wamb_block_forward(const wamb_block_args* args, void* stream) {
   return wamb::block_forward_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+int wamb_block_forward_noalloc(const wamb_block_args* args, void* stream) {
+  if (args == nullptr) return wamb::fail(WAMB_ERR_ARG, "null args");
+  const size_t need = wamb::block_layout(args).total;
+  if (need > WAMB_NOALLOC_SCRATCH_BYTES)
+    return wamb::fail(WAMB_ERR_WORKSPACE,
+                      "this block call needs %zu bytes of scratch; the no-allocation entry point "
+                      "has %u (use wamb_block_forward with a workspace)",
+                      need, WAMB_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  int rc = wamb::noalloc_scratch_address(&scratch);
+  if (rc) return rc;
+  wamb_block_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = WAMB_NOALLOC_SCRATCH_BYTES;
+  return wamb::block_forward_impl(&a, static_cast<cudaStream_t>(stream));
 }
 
 int wamb_cross_kv(const wamb_block_args* args, void* k_out, void* v_out, void* stream) {

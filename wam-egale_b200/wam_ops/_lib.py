@@ -82,8 +82,11 @@ TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", 
 EXPORTED = (
     "wamb_last_error", "wamb_abi_version", "wamb_device_status", "wamb_linear",
     "wamb_attention", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
-    "wamb_block_forward", "wamb_cross_kv",
+    "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc",
 )
+
+# Size of the fixed scratch array behind wamb_block_forward_noalloc.
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _lib = None
 
@@ -111,6 +114,7 @@ def load():
     lib.wamb_block_workspace_layout.restype = ctypes.c_size_t
     lib.wamb_block_forward.argtypes = [ctypes.POINTER(BlockArgs), c_void_p]
     lib.wamb_cross_kv.argtypes = [ctypes.POINTER(BlockArgs), c_void_p, c_void_p, c_void_p]
+    lib.wamb_block_forward_noalloc.argtypes = [ctypes.POINTER(BlockArgs), c_void_p]
     _lib = lib
     return lib
 
