@@ -184,6 +184,7 @@ def run_reference(args):
 # --------------------------------------------------------------- GPU side
 def run_native(args):
     from wam_ops import _lib, configs, ops
+    from wam_ops.rollouts import gather_actions
     from wam_ops.stack import NativeStack
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -216,12 +217,11 @@ def run_native(args):
 
     static = stack.capture(x, ctx, temb, rope, warmup=1)
     A = 32  # action tokens per rollout
-    gathered = torch.empty(world * B, A, D, dtype=torch.bfloat16, device=dev) if world > 1 else None
 
     def step():
         out = stack.replay()
         if pg is not None:
-            pg.all_gather_into_tensor(gathered, out[:, -A:].contiguous())
+            gather_actions(out, A)  # NCCL all_gather of every rollout's action rows
         return out
 
     for _ in range(args.warmup):
