@@ -112,69 +112,80 @@ class Clocks:
 
 
 # --------------------------------------------------------------- CPU side
-def cpu_reference_rate(layers=2, warmup=1, reps=1):
+class CpuReference:
     """The reference algorithm on the host cores: the fp32 oracle restatement
-    of the block (oracle/wan_block.py) for ONE cfg2 rollout, timed over
-    `layers` layers and scaled to a 30-layer step. Returns (value in
-    chunk-steps/s, threads, seconds per layer, sample text)."""
-    from oracle import wan_block as ob
-    from wam_ops import configs
+    of the block (oracle/wan_block.py) for ONE cfg2 rollout (880 tokens
+    attending to a 3520-token history + itself, 512 context tokens). One
+    sample = `layers` layer forwards, scaled to a 30-layer step."""
 
-    torch.set_num_threads(os.cpu_count() or 1)
-    cfg = configs.PRESETS["cfg2"]
-    D, H, F, Q = cfg.dim, cfg.heads, cfg.ffn, cfg.tokens
-    g = torch.Generator().manual_seed(0)
-    blk = ob.WanTransformerBlock(D, F, H, cross_attn_norm=True, eps=1e-6).eval()
-    with torch.no_grad():
-        for name, p in blk.named_parameters():
-            if name.endswith("weight") and "norm" not in name:
-                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
-    pool, hist = cfg.pool_chunks * Q, cfg.history_chunks * Q
-    blk.attn1.init_kv_cache("pos", pool, H, 128, "cpu", torch.float32, 1)
-    c = blk.attn1.attn_caches["pos"]
-    c["k"].normal_(generator=g)
-    c["v"].normal_(generator=g)
-    c["mask"][:hist] = True
-    c["id"][:hist] = torch.arange(hist) // Q
-    x = torch.randn(1, Q, D, generator=g)
-    ctx = torch.randn(1, cfg.context, D, generator=g)
-    temb = configs.make_temb(cfg, 1, "cpu", g)
-    rope = configs.chunk_rope(cfg)
-    with torch.no_grad():
-        for _ in range(warmup):
-            blk(x, ctx, temb, rope, update_cache=0)
-        t0 = time.perf_counter()
-        for _ in range(reps * layers):
-            blk(x, ctx, temb, rope, update_cache=0)
-        dt = (time.perf_counter() - t0) / (reps * layers)
-    step = dt * cfg.layers
-    sample = (f"{reps * layers} layer forward(s) of one cfg2 rollout (880 tokens, 4400 visible keys, "
-              f"512 context, fp32), scaled x{cfg.layers} layers per step")
-    return 1.0 / step, torch.get_num_threads(), dt, sample
+    def __init__(self):
+        from oracle import wan_block as ob
+        from wam_ops import configs
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        cfg = self.cfg = configs.PRESETS["cfg2"]
+        D, H, F, Q = cfg.dim, cfg.heads, cfg.ffn, cfg.tokens
+        g = torch.Generator().manual_seed(0)
+        blk = ob.WanTransformerBlock(D, F, H, cross_attn_norm=True, eps=1e-6).eval()
+        with torch.no_grad():
+            for name, p in blk.named_parameters():
+                if name.endswith("weight") and "norm" not in name:
+                    p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+        pool, hist = cfg.pool_chunks * Q, cfg.history_chunks * Q
+        blk.attn1.init_kv_cache("pos", pool, H, 128, "cpu", torch.float32, 1)
+        c = blk.attn1.attn_caches["pos"]
+        c["k"].normal_(generator=g)
+        c["v"].normal_(generator=g)
+        c["mask"][:hist] = True
+        c["id"][:hist] = torch.arange(hist) // Q
+        self.blk = blk
+        self.args = (torch.randn(1, Q, D, generator=g), torch.randn(1, cfg.context, D, generator=g),
+                     configs.make_temb(cfg, 1, "cpu", g), configs.chunk_rope(cfg))
+
+    def sample(self, layers=1):
+        """Seconds per layer over `layers` forwards (update_cache=0)."""
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            for _ in range(layers):
+                self.blk(*self.args, update_cache=0)
+            return (time.perf_counter() - t0) / layers
+
+    def describe(self, layers):
+        return (f"{layers} layer forward(s) of one cfg2 rollout (880 tokens, 4400 visible keys, "
+                f"512 context, fp32) per sample, scaled x{self.cfg.layers} layers per step")
+
+
+def cpu_reference_rate(layers=2):
+    """(chunk-steps/s, threads, seconds per layer, sample text) of the CPU reference."""
+    ref = CpuReference()
+    ref.sample(1)                       # warm-up
+    dt = ref.sample(layers)
+    return 1.0 / (dt * ref.cfg.layers), torch.get_num_threads(), dt, ref.describe(layers)
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU path on the host (rank 0 only)."""
+    """--impl reference: the reference's CPU path on the host (rank 0 only);
+    each step is one layer forward of one rollout, scaled to 30 layers."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     n = args.gpus
+    ref = CpuReference()
     for _ in range(args.warmup):
-        cpu_reference_rate(layers=1, warmup=0)
-    rates, threads, sample = [], 1, ""
+        ref.sample(1)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        r, threads, _, sample = cpu_reference_rate(layers=1, warmup=0)
-        rates.append(r)
+    per_layer = [ref.sample(1) for _ in range(args.steps)]
     wall = time.perf_counter() - t0
-    value = sum(rates) / len(rates)
+    step_s = sum(per_layer) / len(per_layer) * ref.cfg.layers
+    value = 1.0 / step_s
+    sample = ref.describe(1)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * step_s,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, cfg2 shapes)",
             "config": workload_config(n, 1) | {"sample_per_step": sample},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": wall}
     print(json.dumps(line), flush=True)
