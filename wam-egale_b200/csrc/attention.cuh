@@ -2,14 +2,21 @@
 //   out[b, q, h, :] = softmax(Q[b, q, h] K[b, :, h]^T / sqrt(128)) V[b, :, h]
 // the reference's custom_sdpa (model.py:37-40) for self and cross attention.
 //
-// One CTA per (128-row query tile, head, batch row); 192 threads:
-//   warps 0..3  softmax: one thread per query row; S read from TMEM, P written
-//               as bf16 into a 128B-swizzled SMEM tile, O rescaled in TMEM,
-//               final O / l written to global memory
-//   warp 4      TMA producer: Q once, K and V tiles double-buffered
-//   warp 5      TMEM owner + MMA issuer: S_j = Q K_j^T into one of two TMEM
-//               S buffers, O += P_j V_j (V is an MN-major operand)
-// TMEM columns: S0 [0,128), S1 [128,256), O [256,384).
+// One CTA per (256 query rows = two 128-row tiles A and B, head, batch row);
+// both tiles share every K/V tile that is loaded. 320 threads:
+//   warps 0..3  softmax of tile A, warps 4..7 softmax of tile B: one thread
+//               per query row; S read from TMEM, P written back to TMEM as
+//               packed bf16 over the S columns, O rescaled in TMEM only when
+//               the row max grows by more than 2^8 (the final O / l uses the
+//               same stale max, so the result is exact)
+//   warp 8      TMA producer: Q once, K and V tiles double-buffered
+//   warp 9      TMEM owner + MMA issuer, in the order
+//               PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one tile's
+//               softmax runs the tensor core works on the other tile.
+//               S = Q K^T reads both operands from SMEM; O += P V reads P
+//               from TMEM and V from SMEM as an MN-major operand.
+// TMEM columns: S/P of A [0,128), S/P of B [128,256), O_A [256,384), O_B [384,512).
+// SMEM: Q_A, Q_B, K x2, V x2 tiles of 128 rows x 128 bf16 (192 KB).
 //
 // Keys come from up to two sources:
 //   source 0  the KV pool (or a contiguous K/V tensor), read as a list of
@@ -26,9 +33,10 @@
 
 namespace wamb {
 
-constexpr int ATT_THREADS = 192;
+constexpr int ATT_THREADS = 320;
 constexpr uint32_t ATT_TILE_BYTES = 128 * 128 * 2;  // 128 rows x 128 bf16
 constexpr uint32_t ATT_ATOM = 128 * 128;            // one 64-column half: 128 rows x 128 B
+constexpr float ATT_RESCALE_LOG2 = 8.f;             // rescale O only when the max grows > 2^8
 
 struct AttnParams {
   int heads;
@@ -51,13 +59,11 @@ struct AttnParams {
 };
 
 struct AttnSmem {
-  static constexpr uint32_t Q_OFF = 0;
-  static constexpr uint32_t K_OFF = Q_OFF + ATT_TILE_BYTES;
-  static constexpr uint32_t V_OFF = K_OFF + 2 * ATT_TILE_BYTES;
-  static constexpr uint32_t P_OFF = V_OFF + 2 * ATT_TILE_BYTES;
-  static constexpr uint32_t BAR_OFF = P_OFF + ATT_TILE_BYTES;
-  // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_empty[2],
-  // p_full, pv_done, drain
+  static constexpr uint32_t Q_OFF = 0;                               // Q_A, Q_B
+  static constexpr uint32_t K_OFF = Q_OFF + 2 * ATT_TILE_BYTES;      // K x2
+  static constexpr uint32_t V_OFF = K_OFF + 2 * ATT_TILE_BYTES;      // V x2
+  static constexpr uint32_t BAR_OFF = V_OFF + 2 * ATT_TILE_BYTES;
+  // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], p_full[2], o_done, drain
   static constexpr uint32_t NBARS = 16;
   static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
 };
@@ -104,25 +110,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t sQ = smem_u32(smem + L::Q_OFF);
   const uint32_t sK = smem_u32(smem + L::K_OFF);
   const uint32_t sV = smem_u32(smem + L::V_OFF);
-  uint8_t* sP_ptr = smem + L::P_OFF;
-  const uint32_t sP = smem_u32(sP_ptr);
   const uint32_t bar0 = smem_u32(smem + L::BAR_OFF);
   const uint32_t q_full = bar0;
-  const uint32_t k_full = bar0 + 8;       // [2]
+  const uint32_t k_full = bar0 + 8;       // [2] by stage
   const uint32_t v_full = bar0 + 24;      // [2]
   const uint32_t k_empty = bar0 + 40;     // [2]
   const uint32_t v_empty = bar0 + 56;     // [2]
-  const uint32_t s_full = bar0 + 72;      // [2]
-  const uint32_t s_empty = bar0 + 88;     // [2]
-  const uint32_t p_full = bar0 + 104;
-  const uint32_t pv_done = bar0 + 112;
-  const uint32_t drain = bar0 + 120;
+  const uint32_t s_full = bar0 + 72;      // [2] by query tile
+  const uint32_t p_full = bar0 + 88;      // [2] by query tile
+  const uint32_t o_done = bar0 + 104;
+  const uint32_t drain = bar0 + 112;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y;
-  const int q0 = blockIdx.x * 128;
+  const int q0 = blockIdx.x * 256;
+  const bool has_b = q0 + 128 < p.q_rows;   // the second query tile holds rows
   const int n0 = p.tiles != nullptr ? *p.n_tiles : (p.src0_len + 127) / 128;
   const int n1 = p.has_src1 ? (p.q_rows + 127) / 128 : 0;
   const int n = n0 + n1;
@@ -135,15 +139,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(k_empty + 8 * i, 1);
       mbar_init(v_empty + 8 * i, 1);
       mbar_init(s_full + 8 * i, 1);
-      mbar_init(s_empty + 8 * i, 128);
+      mbar_init(p_full + 8 * i, 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
+    mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -152,14 +155,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
       const int qrow = b * p.q_rows + q0;
       const int qcol = p.q_col + h * 128;
-      mbar_arrive_expect_tx(q_full, ATT_TILE_BYTES);
+      mbar_arrive_expect_tx(q_full, (has_b ? 2 : 1) * ATT_TILE_BYTES);
       tma_load_2d(sQ, &tmQ, q_full, qcol, qrow);
       tma_load_2d(sQ + ATT_ATOM, &tmQ, q_full, qcol + 64, qrow);
+      if (has_b) {
+        tma_load_2d(sQ + ATT_TILE_BYTES, &tmQ, q_full, qcol, qrow + 128);
+        tma_load_2d(sQ + ATT_TILE_BYTES + ATT_ATOM, &tmQ, q_full, qcol + 64, qrow + 128);
+      }
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int st = j & 1;
@@ -187,43 +194,53 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         mbar_wait_teardown(bar, (j >> 1) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // --------------------------------------------------------- MMA issuer
     constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0);
     constexpr uint32_t IDESC_O = idesc_bf16(128, 128, 1);
-    bool ok = mbar_wait(q_full, 0, abort_flag);
-    auto issue_s = [&](int j) -> bool {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait(k_full + 8 * st, ph, abort_flag)) return false;
-      if (!mbar_wait(s_empty + 8 * st, ph ^ 1, abort_flag)) return false;
-      tc_fence_after();
+    const int ntq = has_b ? 2 : 1;
+    // S_t = Q_t K^T (stage st) into TMEM columns [t*128, t*128+128).
+    auto issue_s = [&](int t, int st) {
       if (lane == 0) {
+        const uint32_t qb = sQ + t * ATT_TILE_BYTES;
         const uint32_t kb = sK + st * ATT_TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * ATT_ATOM + (kk & 3) * 32;
-          umma_bf16(tmem + st * 128, sw128_desc(sQ + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
+          umma_bf16(tmem + t * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
                     IDESC_S, kk > 0);
         }
-        umma_commit(s_full + 8 * st);
-        umma_commit(k_empty + 8 * st);
+        umma_commit(s_full + 8 * t);
+      }
+    };
+    // O_t += P_t V (stage st); P_t is packed bf16 in TMEM columns [t*128, t*128+64).
+    auto issue_pv = [&](int t, int st, int ksteps, bool acc) {
+      if (lane == 0) {
+        const uint32_t vb = sV + st * ATT_TILE_BYTES;
+        for (int kk = 0; kk < ksteps; ++kk)
+          umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                       sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, acc || kk > 0);
+      }
+    };
+    bool ok = mbar_wait(q_full, 0, abort_flag);
+    if (ok && n > 0) {
+      ok = mbar_wait(k_full, 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < ntq; ++t) issue_s(t, 0);
+        if (lane == 0) umma_commit(k_empty);
       }
       __syncwarp();
-      return true;
-    };
-    if (ok && n > 0) ok = issue_s(0);
+    }
     for (int j = 0; ok && j < n; ++j) {
-      if (j + 1 < n && !issue_s(j + 1)) break;
       const int st = j & 1;
-      if (!mbar_wait(p_full, j & 1, abort_flag)) break;
+      const KvTile tl = att_tile(p, j, n0, b);
+      const int ksteps = (tl.len + 15) >> 4;
       if (!mbar_wait(v_full + 8 * st, (j >> 1) & 1, abort_flag)) break;
-      const KvTile t = att_tile(p, j, n0, b);
-      const int ksteps = (t.len + 15) >> 4;
-      if (t.len & 15) {
+      if (tl.len & 15) {
         // Zero V rows [len, 16*ksteps) in both 64-column halves.
         uint8_t* vt = smem + L::V_OFF + st * ATT_TILE_BYTES;
-        const int r0 = t.len, r1 = ksteps * 16;
+        const int r0 = tl.len, r1 = ksteps * 16;
         for (int i = lane; i < (r1 - r0) * 16; i += 32) {
           const int r = r0 + (i >> 4), c = i & 15;
           uint8_t* dst = vt + (c >> 3) * ATT_ATOM + r * 128 + (c & 7) * 16;
@@ -232,116 +249,123 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         fence_proxy_async();
         __syncwarp();
       }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t vb = sV + st * ATT_TILE_BYTES;
-        for (int kk = 0; kk < ksteps; ++kk) {
-          const uint32_t poff = (kk >> 2) * ATT_ATOM + (kk & 3) * 32;
-          umma_bf16(tmem + 256, sw128_desc(sP + poff, 16, 1024),
-                    sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, (j > 0 || kk > 0));
+      const bool next = j + 1 < n;
+      const int nst = (j + 1) & 1;
+      bool knext = false;
+      for (int t = 0; t < ntq; ++t) {
+        if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(t, st, ksteps, j > 0);
+        if (t == ntq - 1 && lane == 0) umma_commit(v_empty + 8 * st);
+        if (next) {
+          if (!knext) {
+            if (!mbar_wait(k_full + 8 * nst, ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            knext = true;
+          }
+          issue_s(t, nst);
         }
-        umma_commit(pv_done);
-        umma_commit(v_empty + 8 * st);
+        __syncwarp();
       }
+      if (ok && next && lane == 0) umma_commit(k_empty + 8 * nst);
       __syncwarp();
     }
     if (lane == 0) {
+      umma_commit(o_done);
       umma_commit(drain);
       mbar_wait_teardown(drain, 0);
     }
     __syncwarp();
   } else {
     // -------------------------------------------------- softmax / epilogue
-    const int r = warp * 32 + lane;  // query row within the tile == TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(s_full + 8 * sb, (j >> 1) & 1, abort_flag)) { ok = false; break; }
+    const int t = warp >> 2;          // query tile of this warp
+    const int wq = warp & 3;          // TMEM lane quarter
+    const int r = wq * 32 + lane;     // query row within the tile == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t s_col = t * 128, o_col = 256 + t * 128;
+    float m_used = -INFINITY, l = 0.f;  // running max (scaled log2 units) and row sum
+    bool ok = t == 0 || has_b;
+    for (int j = 0; ok && j < n; ++j) {
+      if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       float s[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float t32[32];
-        tmem_ld32(tmem + lane_base + sb * 128 + c * 32, t32);
+        tmem_ld32(tmem + lane_base + s_col + c * 32, t32);
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = t32[i];
       }
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(s_empty + 8 * sb);
       const int len = att_tile(p, j, n0, b).len;
+      if (len < 128) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= len) s[i] = -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        if (i >= len) s[i] = -INFINITY;
-        mx = fmaxf(mx, s[i]);
-      }
-      const float m_new = fmaxf(m, mx);
+      for (int i = 0; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      mx *= p.scale_log2;
+      // Keep the stale max unless the new one exceeds it by more than 2^8.
+      const bool grow = mx > m_used + ATT_RESCALE_LOG2;
+      const float m_new = grow ? mx : m_used;
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f((m - m_use) * p.scale_log2);
-      const float bias = -m_use * p.scale_log2;
+      const float alpha = grow ? exp2f(m_used - m_use) : 1.f;
       float rs = 0.f;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        s[i] = exp2f(fmaf(s[i], p.scale_log2, bias));
-        rs += s[i];
-      }
-      if (j > 0) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-      }
-      // P row -> swizzled K-major SMEM tile (two 64-key halves).
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 w;
-        w.x = pack_bf16(s[8 * c + 0], s[8 * c + 1]);
-        w.y = pack_bf16(s[8 * c + 2], s[8 * c + 3]);
-        w.z = pack_bf16(s[8 * c + 4], s[8 * c + 5]);
-        w.w = pack_bf16(s[8 * c + 6], s[8 * c + 7]);
-        uint8_t* dst = sP_ptr + (c >> 3) * ATT_ATOM + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = w;
+        for (int i = 0; i < 32; ++i) {
+          const float a = exp2f(fmaf(s[c * 64 + 2 * i], p.scale_log2, -m_use));
+          const float bb = exp2f(fmaf(s[c * 64 + 2 * i + 1], p.scale_log2, -m_use));
+          rs += a + bb;
+          pk[i] = pack_bf16(a, bb);
+        }
+        tmem_st32u(tmem + lane_base + s_col + c * 32, pk);
       }
-      fence_proxy_async();
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O_t is stable: S_t(j) was issued after PV_t(j-1) and has completed.
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float o[32];
-          tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+          tmem_ld32(tmem + lane_base + o_col + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tmem + lane_base + 256 + c * 32, o);
+          tmem_st32(tmem + lane_base + o_col + c * 32, o);
         }
-        tmem_wait_st();
       }
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(p_full + 8 * t);
       l = l * alpha + rs;
-      m = m_new;
+      m_used = m_new;
     }
-    if (ok && n > 0) ok = mbar_wait(pv_done, (n - 1) & 1, abort_flag);
-    tc_fence_after();
-    const int qr = q0 + r;
-    const bool store = qr < p.q_rows;
-    __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
-    const float inv = (ok && n > 0 && l > 0.f) ? 1.f / l : 0.f;
+    if (t == 0 || has_b) {
+      if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
+      tc_fence_after();
+      const int qr = q0 + t * 128 + r;
+      const bool store = qr < p.q_rows;
+      __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
+      const float inv = (ok && n > 0 && l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float o[32];
-      tmem_ld32(tmem + lane_base + 256 + c * 32, o);
-      tmem_wait_ld();
-      if (store) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tmem_ld32(tmem + lane_base + o_col + c * 32, o);
+        tmem_wait_ld();
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint4 w;
-          w.x = pack_bf16(o[8 * k + 0] * inv, o[8 * k + 1] * inv);
-          w.y = pack_bf16(o[8 * k + 2] * inv, o[8 * k + 3] * inv);
-          w.z = pack_bf16(o[8 * k + 4] * inv, o[8 * k + 5] * inv);
-          w.w = pack_bf16(o[8 * k + 6] * inv, o[8 * k + 7] * inv);
-          dst[k] = w;
+          for (int k = 0; k < 4; ++k) {
+            uint4 w;
+            w.x = pack_bf16(o[8 * k + 0] * inv, o[8 * k + 1] * inv);
+            w.y = pack_bf16(o[8 * k + 2] * inv, o[8 * k + 3] * inv);
+            w.z = pack_bf16(o[8 * k + 4] * inv, o[8 * k + 5] * inv);
+            w.w = pack_bf16(o[8 * k + 6] * inv, o[8 * k + 7] * inv);
+            dst[k] = w;
+          }
         }
       }
     }
@@ -349,7 +373,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -77,7 +77,7 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream) {
                                          AttnSmem::TOTAL));
     configured[dev] = true;
   }
-  dim3 grid((a->q_rows + 127) / 128, a->heads, a->batch);
+  dim3 grid((a->q_rows + 255) / 256, a->heads, a->batch);
   attn_tc_kernel<<<grid, ATT_THREADS, AttnSmem::TOTAL, stream>>>(tq, tk0, tv0, tk1, tv1, p);
   WAMB_CHECK_CUDA(cudaGetLastError());
   return WAMB_OK;

@@ -2,11 +2,11 @@
 hundred MB on the device, 3 warm-up launches then `--launches` more).
 
   python wam-egale_b200/wam_ops/profile_cases.py ffn1 [--m 2048] [--launches 1]
-  python wam-egale_b200/wam_ops/profile_cases.py attention [--q 880] [--pool 4400]
+  python wam-egale_b200/wam_ops/profile_cases.py attention [--q 880] [--pool 4400] [--batch 8]
   python wam-egale_b200/wam_ops/profile_cases.py rms | ln
 
 ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (cfg2 weights)
-attention  self attention of one cfg2 rollout over a 4400-slot pool (24 heads)
+attention  self attention of `batch` cfg2 rollouts over 4400-key pools (24 heads)
 rms        RMSNorm + RoPE of the q/k/v projection output, K/V into the pool
 ln         LayerNorm + adaLN modulation
 """
@@ -27,6 +27,7 @@ def main():
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--q", type=int, default=880)
     ap.add_argument("--pool", type=int, default=4400)
+    ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--launches", type=int, default=1)
     a = ap.parse_args()
     torch.set_grad_enabled(False)
@@ -40,10 +41,10 @@ def main():
         out = torch.empty(a.m, F, device=dev, dtype=torch.bfloat16)
         run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_GELU, out=out)  # noqa: E731
     elif a.case == "attention":
-        q = torch.randn(a.q, D, generator=g, device=dev).bfloat16()
-        kp = torch.randn(a.pool, D, generator=g, device=dev).bfloat16()
-        vp = torch.randn(a.pool, D, generator=g, device=dev).bfloat16()
-        out = torch.empty(a.q, D, device=dev, dtype=torch.bfloat16)
+        q = torch.randn(a.batch * a.q, D, generator=g, device=dev).bfloat16()
+        kp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
+        vp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
+        out = torch.empty(a.batch * a.q, D, device=dev, dtype=torch.bfloat16)
         run = lambda: ops.attention(q, kp, vp, heads=H, q_rows=a.q, src0_batch_stride=a.pool,  # noqa: E731
                                     src0_len=a.pool, out=out)
     else:
