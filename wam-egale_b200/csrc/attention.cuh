@@ -8,15 +8,18 @@
 //               per query row; S read from TMEM, P written back to TMEM as
 //               packed bf16 over the S columns, O rescaled in TMEM only when
 //               the row max grows by more than 2^8 (the final O / l uses the
-//               same stale max, so the result is exact)
-//   warp 8      TMA producer: Q once, K and V tiles double-buffered
+//               same stale max, so the result is exact). Half of the exp2s
+//               run on the MUFU (ex2.approx), half as a cubic on the FMA pipe
+//               with packed f32x2 arithmetic, so neither pipe limits.
+//   warp 8      TMA producer: Q once, K tiles triple- and V tiles
+//               double-buffered, plus L2 prefetch of the tiles 3 ahead
 //   warp 9      TMEM owner + MMA issuer, in the order
 //               PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one tile's
 //               softmax runs the tensor core works on the other tile.
 //               S = Q K^T reads both operands from SMEM; O += P V reads P
 //               from TMEM and V from SMEM as an MN-major operand.
 // TMEM columns: S/P of A [0,128), S/P of B [128,256), O_A [256,384), O_B [384,512).
-// SMEM: Q_A, Q_B, K x2, V x2 tiles of 128 rows x 128 bf16 (192 KB).
+// SMEM: Q_A, Q_B, K x3, V x2 tiles of 128 rows x 128 bf16 (224 KB).
 //
 // Keys come from up to two sources:
 //   source 0  the KV pool (or a contiguous K/V tensor), read as a list of
@@ -37,6 +40,74 @@ constexpr int ATT_THREADS = 320;
 constexpr uint32_t ATT_TILE_BYTES = 128 * 128 * 2;  // 128 rows x 128 bf16
 constexpr uint32_t ATT_ATOM = 128 * 128;            // one 64-column half: 128 rows x 128 B
 constexpr float ATT_RESCALE_LOG2 = 8.f;             // rescale O only when the max grows > 2^8
+constexpr int ATT_KSTAGES = 3;
+constexpr int ATT_VSTAGES = 2;
+constexpr int ATT_PREFETCH = 3;                     // L2 prefetch distance in K/V tiles
+// 2^f ~= C0 + f (C1 + f (C2 + f C3)) for f in [-0.5, 0.5]: minimax relative
+// error 7.5e-5 (fit by csrc/exp2_fit.py), far below bf16's 2^-9 for P.
+constexpr float ATT_EXP2_C0 = 0.9999281167984009f;
+constexpr float ATT_EXP2_C1 = 0.6932609677314758f;
+constexpr float ATT_EXP2_C2 = 0.2426108419895172f;
+constexpr float ATT_EXP2_C3 = 0.05517144873738289f;
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic).
+WAMB_DEV uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+WAMB_DEV float2 f2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+WAMB_DEV uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+WAMB_DEV uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+WAMB_DEV uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+WAMB_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+WAMB_DEV float ex2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x for a pair on the FMA pipe: x clamped to >= -125, rounded to n + f with
+// |f| <= 1/2 by the 1.5 * 2^23 shifter, 2^f from the cubic, n added to the
+// exponent field (the shifter's bit pattern vanishes from (bits << 23)).
+WAMB_DEV uint64_t ex2_poly2(uint64_t x2) {
+  const float2 xv = f2_split(x2);
+  const uint64_t x = f2(fmaxf(xv.x, -125.f), fmaxf(xv.y, -125.f));
+  const uint64_t shifter = f2(12582912.f, 12582912.f);
+  const uint64_t t = fadd2(x, shifter);
+  const uint64_t f = fsub2(x, fsub2(t, shifter));
+  uint64_t p = ffma2(f, f2(ATT_EXP2_C3, ATT_EXP2_C3), f2(ATT_EXP2_C2, ATT_EXP2_C2));
+  p = ffma2(p, f, f2(ATT_EXP2_C1, ATT_EXP2_C1));
+  p = ffma2(p, f, f2(ATT_EXP2_C0, ATT_EXP2_C0));
+  const float2 pv = f2_split(p), tv = f2_split(t);
+  return f2(__int_as_float(__float_as_int(pv.x) + (__float_as_int(tv.x) << 23)),
+            __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
+}
+WAMB_DEV void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
 
 struct AttnParams {
   int heads;
@@ -59,13 +130,14 @@ struct AttnParams {
 };
 
 struct AttnSmem {
-  static constexpr uint32_t Q_OFF = 0;                               // Q_A, Q_B
-  static constexpr uint32_t K_OFF = Q_OFF + 2 * ATT_TILE_BYTES;      // K x2
-  static constexpr uint32_t V_OFF = K_OFF + 2 * ATT_TILE_BYTES;      // V x2
-  static constexpr uint32_t BAR_OFF = V_OFF + 2 * ATT_TILE_BYTES;
-  // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], p_full[2], o_done, drain
-  static constexpr uint32_t NBARS = 16;
+  static constexpr uint32_t Q_OFF = 0;                                          // Q_A, Q_B
+  static constexpr uint32_t K_OFF = Q_OFF + 2 * ATT_TILE_BYTES;                 // K x3
+  static constexpr uint32_t V_OFF = K_OFF + ATT_KSTAGES * ATT_TILE_BYTES;       // V x2
+  static constexpr uint32_t BAR_OFF = V_OFF + ATT_VSTAGES * ATT_TILE_BYTES;
+  // q_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], p_full[2], o_done, drain
+  static constexpr uint32_t NBARS = 18;
   static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+  static_assert(TOTAL <= 232448, "attention shared memory exceeds 227 KB");
 };
 
 struct KvTile {
@@ -112,14 +184,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t sV = smem_u32(smem + L::V_OFF);
   const uint32_t bar0 = smem_u32(smem + L::BAR_OFF);
   const uint32_t q_full = bar0;
-  const uint32_t k_full = bar0 + 8;       // [2] by stage
-  const uint32_t v_full = bar0 + 24;      // [2]
-  const uint32_t k_empty = bar0 + 40;     // [2]
-  const uint32_t v_empty = bar0 + 56;     // [2]
-  const uint32_t s_full = bar0 + 72;      // [2] by query tile
-  const uint32_t p_full = bar0 + 88;      // [2] by query tile
-  const uint32_t o_done = bar0 + 104;
-  const uint32_t drain = bar0 + 112;
+  const uint32_t k_full = bar0 + 8;       // [3] by K stage
+  const uint32_t k_empty = bar0 + 32;     // [3]
+  const uint32_t v_full = bar0 + 56;      // [2] by V stage
+  const uint32_t v_empty = bar0 + 72;     // [2]
+  const uint32_t s_full = bar0 + 88;      // [2] by query tile
+  const uint32_t p_full = bar0 + 104;     // [2] by query tile
+  const uint32_t o_done = bar0 + 120;
+  const uint32_t drain = bar0 + 128;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -133,10 +205,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < ATT_KSTAGES; ++i) {
       mbar_init(k_full + 8 * i, 1);
-      mbar_init(v_full + 8 * i, 1);
       mbar_init(k_empty + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(v_full + 8 * i, 1);
       mbar_init(v_empty + 8 * i, 1);
       mbar_init(s_full + 8 * i, 1);
       mbar_init(p_full + 8 * i, 128);
@@ -167,43 +241,61 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tma_load_2d(sQ + ATT_TILE_BYTES, &tmQ, q_full, qcol, qrow + 128);
         tma_load_2d(sQ + ATT_TILE_BYTES + ATT_ATOM, &tmQ, q_full, qcol + 64, qrow + 128);
       }
-      int issued = 0;
+      // Order: K_j then V_j; K runs up to ATT_KSTAGES tiles ahead of the MMA,
+      // V up to ATT_VSTAGES, and tiles ATT_PREFETCH ahead are pulled into L2.
+      auto src_of = [&](const KvTile& t, const CUtensorMap*& mk, const CUtensorMap*& mv, int& kc,
+                        int& vc) {
+        mk = t.src ? &tmK1 : &tmK0;
+        mv = t.src ? &tmV1 : &tmV0;
+        kc = (t.src ? p.k1_col : p.k0_col) + h * 128;
+        vc = (t.src ? p.v1_col : p.v0_col) + h * 128;
+      };
+      int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
         const KvTile t = att_tile(p, j, n0, b);
-        const CUtensorMap* mk = t.src ? &tmK1 : &tmK0;
-        const CUtensorMap* mv = t.src ? &tmV1 : &tmV0;
-        const int kc = (t.src ? p.k1_col : p.k0_col) + h * 128;
-        const int vc = (t.src ? p.v1_col : p.v0_col) + h * 128;
-        if (!mbar_wait(k_empty + 8 * st, ph ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(k_full + 8 * st, ATT_TILE_BYTES);
-        tma_load_2d(sK + st * ATT_TILE_BYTES, mk, k_full + 8 * st, kc, t.row);
-        tma_load_2d(sK + st * ATT_TILE_BYTES + ATT_ATOM, mk, k_full + 8 * st, kc + 64, t.row);
-        if (!mbar_wait(v_empty + 8 * st, ph ^ 1, abort_flag)) { issued = 2 * j + 1; break; }
-        mbar_arrive_expect_tx(v_full + 8 * st, ATT_TILE_BYTES);
-        tma_load_2d(sV + st * ATT_TILE_BYTES, mv, v_full + 8 * st, vc, t.row);
-        tma_load_2d(sV + st * ATT_TILE_BYTES + ATT_ATOM, mv, v_full + 8 * st, vc + 64, t.row);
-        issued = 2 * j + 2;
+        const CUtensorMap *mk, *mv;
+        int kc, vc;
+        src_of(t, mk, mv, kc, vc);
+        if (j + ATT_PREFETCH < n) {
+          const KvTile tp = att_tile(p, j + ATT_PREFETCH, n0, b);
+          const CUtensorMap *pk, *pv;
+          int pkc, pvc;
+          src_of(tp, pk, pv, pkc, pvc);
+          tma_prefetch_2d(pk, pkc, tp.row);
+          tma_prefetch_2d(pk, pkc + 64, tp.row);
+          tma_prefetch_2d(pv, pvc, tp.row);
+          tma_prefetch_2d(pv, pvc + 64, tp.row);
+        }
+        const int ks = j % ATT_KSTAGES;
+        if (!mbar_wait(k_empty + 8 * ks, ((j / ATT_KSTAGES) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full + 8 * ks, ATT_TILE_BYTES);
+        tma_load_2d(sK + ks * ATT_TILE_BYTES, mk, k_full + 8 * ks, kc, t.row);
+        tma_load_2d(sK + ks * ATT_TILE_BYTES + ATT_ATOM, mk, k_full + 8 * ks, kc + 64, t.row);
+        k_issued = j + 1;
+        const int vs = j & 1;
+        if (!mbar_wait(v_empty + 8 * vs, ((j >> 1) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full + 8 * vs, ATT_TILE_BYTES);
+        tma_load_2d(sV + vs * ATT_TILE_BYTES, mv, v_full + 8 * vs, vc, t.row);
+        tma_load_2d(sV + vs * ATT_TILE_BYTES + ATT_ATOM, mv, v_full + 8 * vs, vc + 64, t.row);
+        v_issued = j + 1;
       }
       // Teardown: loads still in flight must land before the CTA exits.
       mbar_wait_teardown(q_full, 0);
-      for (int i = issued - 1; i >= 0 && i >= issued - 4; --i) {
-        const int j = i >> 1;
-        const uint32_t bar = (i & 1) ? v_full + 8 * (j & 1) : k_full + 8 * (j & 1);
-        mbar_wait_teardown(bar, (j >> 1) & 1);
-      }
+      for (int j = max(0, k_issued - ATT_KSTAGES); j < k_issued; ++j)
+        mbar_wait_teardown(k_full + 8 * (j % ATT_KSTAGES), (j / ATT_KSTAGES) & 1);
+      for (int j = max(0, v_issued - ATT_VSTAGES); j < v_issued; ++j)
+        mbar_wait_teardown(v_full + 8 * (j & 1), (j >> 1) & 1);
     }
   } else if (warp == 9) {
     // --------------------------------------------------------- MMA issuer
     constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0);
     constexpr uint32_t IDESC_O = idesc_bf16(128, 128, 1);
     const int ntq = has_b ? 2 : 1;
-    // S_t = Q_t K^T (stage st) into TMEM columns [t*128, t*128+128).
-    auto issue_s = [&](int t, int st) {
+    // S_t = Q_t K^T (K stage ks) into TMEM columns [t*128, t*128+128).
+    auto issue_s = [&](int t, int ks) {
       if (lane == 0) {
         const uint32_t qb = sQ + t * ATT_TILE_BYTES;
-        const uint32_t kb = sK + st * ATT_TILE_BYTES;
+        const uint32_t kb = sK + ks * ATT_TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * ATT_ATOM + (kk & 3) * 32;
@@ -250,7 +342,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         __syncwarp();
       }
       const bool next = j + 1 < n;
-      const int nst = (j + 1) & 1;
+      const int nks = (j + 1) % ATT_KSTAGES;
       bool knext = false;
       for (int t = 0; t < ntq; ++t) {
         if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
@@ -259,15 +351,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (t == ntq - 1 && lane == 0) umma_commit(v_empty + 8 * st);
         if (next) {
           if (!knext) {
-            if (!mbar_wait(k_full + 8 * nst, ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(k_full + 8 * nks, ((j + 1) / ATT_KSTAGES) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
             knext = true;
           }
-          issue_s(t, nst);
+          issue_s(t, nks);
         }
         __syncwarp();
       }
-      if (ok && next && lane == 0) umma_commit(k_empty + 8 * nst);
+      if (ok && next && lane == 0) umma_commit(k_empty + 8 * nks);
       __syncwarp();
     }
     if (lane == 0) {
@@ -305,26 +397,42 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      for (int i = 0; i < 128; i += 2) mx = fmax3(mx, s[i], s[i + 1]);
       mx *= p.scale_log2;
       // Keep the stale max unless the new one exceeds it by more than 2^8.
       const bool grow = mx > m_used + ATT_RESCALE_LOG2;
       const float m_new = grow ? mx : m_used;
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = grow ? exp2f(m_used - m_use) : 1.f;
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
+      const uint64_t neg_m2 = f2(-m_use, -m_use);
+      uint64_t sum2 = f2(0.f, 0.f);
+      {
+        // keys 0..63: exp2 on the MUFU
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float a = exp2f(fmaf(s[c * 64 + 2 * i], p.scale_log2, -m_use));
-          const float bb = exp2f(fmaf(s[c * 64 + 2 * i + 1], p.scale_log2, -m_use));
-          rs += a + bb;
+          const float2 x = f2_split(ffma2(f2(s[2 * i], s[2 * i + 1]), scale2, neg_m2));
+          const float a = ex2_mufu(x.x), bb = ex2_mufu(x.y);
+          sum2 = fadd2(sum2, f2(a, bb));
           pk[i] = pack_bf16(a, bb);
         }
-        tmem_st32u(tmem + lane_base + s_col + c * 32, pk);
+        tmem_st32u(tmem + lane_base + s_col, pk);
       }
+      {
+        // keys 64..127: exp2 as a cubic on the FMA pipe
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint64_t e = ex2_poly2(ffma2(f2(s[64 + 2 * i], s[64 + 2 * i + 1]), scale2, neg_m2));
+          sum2 = fadd2(sum2, e);
+          const float2 ev = f2_split(e);
+          pk[i] = pack_bf16(ev.x, ev.y);
+        }
+        tmem_st32u(tmem + lane_base + s_col + 32, pk);
+      }
+      const float2 sv = f2_split(sum2);
+      const float rs = sv.x + sv.y;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // O_t is stable: S_t(j) was issued after PV_t(j-1) and has completed.
 #pragma unroll 1
