@@ -4,22 +4,25 @@
 //
 // One CTA per (256 query rows = two 128-row tiles A and B, head, batch row);
 // both tiles share every K/V tile that is loaded. 320 threads:
-//   warps 0..3  softmax of tile A, warps 4..7 softmax of tile B: one thread
-//               per query row; S read from TMEM, P written back to TMEM as
-//               packed bf16 over the S columns, O rescaled in TMEM only when
-//               the row max grows by more than 2^8 (the final O / l uses the
-//               same stale max, so the result is exact). Half of the exp2s
-//               run on the MUFU (ex2.approx), half as a cubic on the FMA pipe
-//               with packed f32x2 arithmetic, so neither pipe limits.
-//   warp 8      TMA producer: Q once, K tiles triple- and V tiles
-//               double-buffered, plus L2 prefetch of the tiles 3 ahead
+//   warps 0..7  softmax, on tile A(j) then tile B(j), A(j+1), ...: two
+//               threads per query row (warps w and w+4 share the TMEM lanes
+//               of quarter w), each handling 64 of the 128 keys and 64 of the
+//               128 O columns; the partial row maxima are exchanged through
+//               SMEM. S is read from TMEM, P written back to TMEM as packed
+//               bf16 over the S columns, O rescaled in TMEM only when the row
+//               max grows by more than 2^8 (the final O / l uses the same
+//               stale max, so the result is exact). Three quarters of the
+//               exp2s run on the MUFU (ex2.approx), one quarter as a cubic on
+//               the FMA pipe with packed f32x2 arithmetic.
+//   warp 8      TMA producer: Q once, then K_0, V_0, K_1, V_1, ... through
+//               one 5-slot ring (the order both are consumed and released in)
 //   warp 9      TMEM owner + MMA issuer, in the order
 //               PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one tile's
 //               softmax runs the tensor core works on the other tile.
 //               S = Q K^T reads both operands from SMEM; O += P V reads P
 //               from TMEM and V from SMEM as an MN-major operand.
 // TMEM columns: S/P of A [0,128), S/P of B [128,256), O_A [256,384), O_B [384,512).
-// SMEM: Q_A, Q_B, K x3, V x2 tiles of 128 rows x 128 bf16 (224 KB).
+// SMEM: Q_A, Q_B and a 5-slot K/V ring of 128 rows x 128 bf16 tiles (224 KB).
 //
 // Keys come from up to two sources:
 //   source 0  the KV pool (or a contiguous K/V tensor), read as a list of
@@ -40,9 +43,7 @@ constexpr int ATT_THREADS = 320;
 constexpr uint32_t ATT_TILE_BYTES = 128 * 128 * 2;  // 128 rows x 128 bf16
 constexpr uint32_t ATT_ATOM = 128 * 128;            // one 64-column half: 128 rows x 128 B
 constexpr float ATT_RESCALE_LOG2 = 8.f;             // rescale O only when the max grows > 2^8
-constexpr int ATT_KSTAGES = 3;
-constexpr int ATT_VSTAGES = 2;
-constexpr int ATT_PREFETCH = 3;                     // L2 prefetch distance in K/V tiles
+constexpr int ATT_SLOTS = 5;                        // K/V ring: load L = 2j (K_j) or 2j+1 (V_j)
 // 2^f ~= C0 + f (C1 + f (C2 + f C3)) for f in [-0.5, 0.5]: minimax relative
 // error 7.5e-5 (fit by csrc/exp2_fit.py), far below bf16's 2^-9 for P.
 constexpr float ATT_EXP2_C0 = 0.9999281167984009f;
@@ -102,13 +103,6 @@ WAMB_DEV uint64_t ex2_poly2(uint64_t x2) {
   return f2(__int_as_float(__float_as_int(pv.x) + (__float_as_int(tv.x) << 23)),
             __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
 }
-WAMB_DEV void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 struct AttnParams {
   int heads;
   int q_rows;               // query rows per batch row
@@ -130,13 +124,13 @@ struct AttnParams {
 };
 
 struct AttnSmem {
-  static constexpr uint32_t Q_OFF = 0;                                          // Q_A, Q_B
-  static constexpr uint32_t K_OFF = Q_OFF + 2 * ATT_TILE_BYTES;                 // K x3
-  static constexpr uint32_t V_OFF = K_OFF + ATT_KSTAGES * ATT_TILE_BYTES;       // V x2
-  static constexpr uint32_t BAR_OFF = V_OFF + ATT_VSTAGES * ATT_TILE_BYTES;
-  // q_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], p_full[2], o_done, drain
-  static constexpr uint32_t NBARS = 18;
-  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+  static constexpr uint32_t Q_OFF = 0;                                    // Q_A, Q_B
+  static constexpr uint32_t RING_OFF = Q_OFF + 2 * ATT_TILE_BYTES;        // K/V ring
+  static constexpr uint32_t BAR_OFF = RING_OFF + ATT_SLOTS * ATT_TILE_BYTES;
+  // q_full, full[5], empty[5], s_full[2], p_full[2], o_done, drain, pair[4]
+  static constexpr uint32_t NBARS = 21;
+  static constexpr uint32_t RED_OFF = BAR_OFF + NBARS * 8 + 16;   // float [2 halves][128 rows]
+  static constexpr uint32_t TOTAL = 1024 + RED_OFF + 2 * 128 * 4;
   static_assert(TOTAL <= 232448, "attention shared memory exceeds 227 KB");
 };
 
@@ -180,18 +174,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sQ = smem_u32(smem + L::Q_OFF);
-  const uint32_t sK = smem_u32(smem + L::K_OFF);
-  const uint32_t sV = smem_u32(smem + L::V_OFF);
+  const uint32_t sRing = smem_u32(smem + L::RING_OFF);
   const uint32_t bar0 = smem_u32(smem + L::BAR_OFF);
   const uint32_t q_full = bar0;
-  const uint32_t k_full = bar0 + 8;       // [3] by K stage
-  const uint32_t k_empty = bar0 + 32;     // [3]
-  const uint32_t v_full = bar0 + 56;      // [2] by V stage
-  const uint32_t v_empty = bar0 + 72;     // [2]
+  const uint32_t full = bar0 + 8;         // [5] by ring slot
+  const uint32_t empty = bar0 + 48;       // [5]
   const uint32_t s_full = bar0 + 88;      // [2] by query tile
   const uint32_t p_full = bar0 + 104;     // [2] by query tile
   const uint32_t o_done = bar0 + 120;
   const uint32_t drain = bar0 + 128;
+  const uint32_t pair_bar = bar0 + 136;   // [4] by TMEM lane quarter, 64 arrivals
+  // Load L (K_j: L = 2j, V_j: L = 2j+1) lives in slot L % 5; its phase is (L / 5) & 1.
+  auto slot_addr = [&](int L) { return sRing + (L % ATT_SLOTS) * ATT_TILE_BYTES; };
+  auto slot_full = [&](int L) { return full + 8 * (L % ATT_SLOTS); };
+  auto slot_empty = [&](int L) { return empty + 8 * (L % ATT_SLOTS); };
+  auto slot_phase = [&](int L) { return static_cast<uint32_t>((L / ATT_SLOTS) & 1); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -205,18 +202,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < ATT_KSTAGES; ++i) {
-      mbar_init(k_full + 8 * i, 1);
-      mbar_init(k_empty + 8 * i, 1);
+    for (int i = 0; i < ATT_SLOTS; ++i) {
+      mbar_init(full + 8 * i, 1);
+      mbar_init(empty + 8 * i, 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(v_full + 8 * i, 1);
-      mbar_init(v_empty + 8 * i, 1);
       mbar_init(s_full + 8 * i, 1);
-      mbar_init(p_full + 8 * i, 128);
+      mbar_init(p_full + 8 * i, 256);
     }
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(pair_bar + 8 * i, 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -241,8 +237,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tma_load_2d(sQ + ATT_TILE_BYTES, &tmQ, q_full, qcol, qrow + 128);
         tma_load_2d(sQ + ATT_TILE_BYTES + ATT_ATOM, &tmQ, q_full, qcol + 64, qrow + 128);
       }
-      // Order: K_j then V_j; K runs up to ATT_KSTAGES tiles ahead of the MMA,
-      // V up to ATT_VSTAGES, and tiles ATT_PREFETCH ahead are pulled into L2.
       auto src_of = [&](const KvTile& t, const CUtensorMap*& mk, const CUtensorMap*& mv, int& kc,
                         int& vc) {
         mk = t.src ? &tmK1 : &tmK0;
@@ -250,52 +244,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         kc = (t.src ? p.k1_col : p.k0_col) + h * 128;
         vc = (t.src ? p.v1_col : p.v0_col) + h * 128;
       };
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n; ++j) {
+      int issued = 0;   // ring loads issued
+      for (int L = 0; L < 2 * n; ++L) {
+        const int j = L >> 1;
         const KvTile t = att_tile(p, j, n0, b);
         const CUtensorMap *mk, *mv;
         int kc, vc;
         src_of(t, mk, mv, kc, vc);
-        if (j + ATT_PREFETCH < n) {
-          const KvTile tp = att_tile(p, j + ATT_PREFETCH, n0, b);
-          const CUtensorMap *pk, *pv;
-          int pkc, pvc;
-          src_of(tp, pk, pv, pkc, pvc);
-          tma_prefetch_2d(pk, pkc, tp.row);
-          tma_prefetch_2d(pk, pkc + 64, tp.row);
-          tma_prefetch_2d(pv, pvc, tp.row);
-          tma_prefetch_2d(pv, pvc + 64, tp.row);
-        }
-        const int ks = j % ATT_KSTAGES;
-        if (!mbar_wait(k_empty + 8 * ks, ((j / ATT_KSTAGES) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(k_full + 8 * ks, ATT_TILE_BYTES);
-        tma_load_2d(sK + ks * ATT_TILE_BYTES, mk, k_full + 8 * ks, kc, t.row);
-        tma_load_2d(sK + ks * ATT_TILE_BYTES + ATT_ATOM, mk, k_full + 8 * ks, kc + 64, t.row);
-        k_issued = j + 1;
-        const int vs = j & 1;
-        if (!mbar_wait(v_empty + 8 * vs, ((j >> 1) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(v_full + 8 * vs, ATT_TILE_BYTES);
-        tma_load_2d(sV + vs * ATT_TILE_BYTES, mv, v_full + 8 * vs, vc, t.row);
-        tma_load_2d(sV + vs * ATT_TILE_BYTES + ATT_ATOM, mv, v_full + 8 * vs, vc + 64, t.row);
-        v_issued = j + 1;
+        if (!mbar_wait(slot_empty(L), slot_phase(L) ^ 1, abort_flag)) break;
+        const CUtensorMap* m = (L & 1) ? mv : mk;
+        const int col = (L & 1) ? vc : kc;
+        mbar_arrive_expect_tx(slot_full(L), ATT_TILE_BYTES);
+        tma_load_2d(slot_addr(L), m, slot_full(L), col, t.row);
+        tma_load_2d(slot_addr(L) + ATT_ATOM, m, slot_full(L), col + 64, t.row);
+        issued = L + 1;
       }
       // Teardown: loads still in flight must land before the CTA exits.
       mbar_wait_teardown(q_full, 0);
-      for (int j = max(0, k_issued - ATT_KSTAGES); j < k_issued; ++j)
-        mbar_wait_teardown(k_full + 8 * (j % ATT_KSTAGES), (j / ATT_KSTAGES) & 1);
-      for (int j = max(0, v_issued - ATT_VSTAGES); j < v_issued; ++j)
-        mbar_wait_teardown(v_full + 8 * (j & 1), (j >> 1) & 1);
+      for (int L = max(0, issued - ATT_SLOTS); L < issued; ++L)
+        mbar_wait_teardown(slot_full(L), slot_phase(L));
     }
   } else if (warp == 9) {
     // --------------------------------------------------------- MMA issuer
     constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0);
     constexpr uint32_t IDESC_O = idesc_bf16(128, 128, 1);
     const int ntq = has_b ? 2 : 1;
-    // S_t = Q_t K^T (K stage ks) into TMEM columns [t*128, t*128+128).
-    auto issue_s = [&](int t, int ks) {
+    // S_t = Q_t K_j^T (ring load 2j) into TMEM columns [t*128, t*128+128).
+    auto issue_s = [&](int t, int j) {
       if (lane == 0) {
         const uint32_t qb = sQ + t * ATT_TILE_BYTES;
-        const uint32_t kb = sK + ks * ATT_TILE_BYTES;
+        const uint32_t kb = slot_addr(2 * j);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * ATT_ATOM + (kk & 3) * 32;
@@ -305,10 +283,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         umma_commit(s_full + 8 * t);
       }
     };
-    // O_t += P_t V (stage st); P_t is packed bf16 in TMEM columns [t*128, t*128+64).
-    auto issue_pv = [&](int t, int st, int ksteps, bool acc) {
+    // O_t += P_t V_j (ring load 2j+1); P_t is packed bf16 in TMEM columns [t*128, t*128+64).
+    auto issue_pv = [&](int t, int j, int ksteps, bool acc) {
       if (lane == 0) {
-        const uint32_t vb = sV + st * ATT_TILE_BYTES;
+        const uint32_t vb = slot_addr(2 * j + 1);
         for (int kk = 0; kk < ksteps; ++kk)
           umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
                        sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, acc || kk > 0);
@@ -316,22 +294,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     };
     bool ok = mbar_wait(q_full, 0, abort_flag);
     if (ok && n > 0) {
-      ok = mbar_wait(k_full, 0, abort_flag);
+      ok = mbar_wait(slot_full(0), slot_phase(0), abort_flag);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < ntq; ++t) issue_s(t, 0);
-        if (lane == 0) umma_commit(k_empty);
+        if (lane == 0) umma_commit(slot_empty(0));
       }
       __syncwarp();
     }
     for (int j = 0; ok && j < n; ++j) {
-      const int st = j & 1;
       const KvTile tl = att_tile(p, j, n0, b);
       const int ksteps = (tl.len + 15) >> 4;
-      if (!mbar_wait(v_full + 8 * st, (j >> 1) & 1, abort_flag)) break;
+      if (!mbar_wait(slot_full(2 * j + 1), slot_phase(2 * j + 1), abort_flag)) break;
       if (tl.len & 15) {
         // Zero V rows [len, 16*ksteps) in both 64-column halves.
-        uint8_t* vt = smem + L::V_OFF + st * ATT_TILE_BYTES;
+        uint8_t* vt = smem + L::RING_OFF + ((2 * j + 1) % ATT_SLOTS) * ATT_TILE_BYTES;
         const int r0 = tl.len, r1 = ksteps * 16;
         for (int i = lane; i < (r1 - r0) * 16; i += 32) {
           const int r = r0 + (i >> 4), c = i & 15;
@@ -342,24 +319,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         __syncwarp();
       }
       const bool next = j + 1 < n;
-      const int nks = (j + 1) % ATT_KSTAGES;
       bool knext = false;
       for (int t = 0; t < ntq; ++t) {
         if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(t, st, ksteps, j > 0);
-        if (t == ntq - 1 && lane == 0) umma_commit(v_empty + 8 * st);
+        issue_pv(t, j, ksteps, j > 0);
+        if (t == ntq - 1 && lane == 0) umma_commit(slot_empty(2 * j + 1));
         if (next) {
           if (!knext) {
-            if (!mbar_wait(k_full + 8 * nks, ((j + 1) / ATT_KSTAGES) & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(slot_full(2 * j + 2), slot_phase(2 * j + 2), abort_flag)) { ok = false; break; }
             tc_fence_after();
             knext = true;
           }
-          issue_s(t, nks);
+          issue_s(t, j + 1);
         }
         __syncwarp();
       }
-      if (ok && next && lane == 0) umma_commit(k_empty + 8 * nks);
+      if (ok && next && lane == 0) umma_commit(slot_empty(2 * j + 2));
       __syncwarp();
     }
     if (lane == 0) {
@@ -370,98 +346,113 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     __syncwarp();
   } else {
     // -------------------------------------------------- softmax / epilogue
-    const int t = warp >> 2;          // query tile of this warp
     const int wq = warp & 3;          // TMEM lane quarter
+    const int hf = warp >> 2;         // which 64 keys / 64 O columns of the row
     const int r = wq * 32 + lane;     // query row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t s_col = t * 128, o_col = 256 + t * 128;
-    float m_used = -INFINITY, l = 0.f;  // running max (scaled log2 units) and row sum
-    bool ok = t == 0 || has_b;
+    float* red = reinterpret_cast<float*>(smem + L::RED_OFF);   // [2][128]
+    // The two threads of a row (warps wq and wq + 4) meet at mbarrier pair[wq]
+    // (64 arrivals per phase; bounded wait like every other wait here).
+    uint32_t pair_phase = 0;
+    auto pair_sync = [&]() {
+      mbar_arrive(pair_bar + 8 * wq);
+      mbar_wait(pair_bar + 8 * wq, pair_phase, abort_flag);
+      pair_phase ^= 1;
+    };
+    auto pair_exchange = [&](float v) {
+      red[hf * 128 + r] = v;
+      pair_sync();
+      const float o = red[(hf ^ 1) * 128 + r];
+      pair_sync();
+      return o;
+    };
+    const int ntq = has_b ? 2 : 1;
+    float m_used[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    bool ok = true;
     for (int j = 0; ok && j < n; ++j) {
-      if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float t32[32];
-        tmem_ld32(tmem + lane_base + s_col + c * 32, t32);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t32[i];
-      }
-      tmem_wait_ld();
       const int len = att_tile(p, j, n0, b).len;
-      if (len < 128) {
+      for (int t = 0; t < ntq; ++t) {
+        if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t s_col = t * 128 + hf * 64;
+        float s[64];
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= len) s[i] = -INFINITY;
-      }
-      float mx = -INFINITY;
+        for (int c = 0; c < 2; ++c) {
+          float t32[32];
+          tmem_ld32(tmem + lane_base + s_col + c * 32, t32);
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) mx = fmax3(mx, s[i], s[i + 1]);
-      mx *= p.scale_log2;
-      // Keep the stale max unless the new one exceeds it by more than 2^8.
-      const bool grow = mx > m_used + ATT_RESCALE_LOG2;
-      const float m_new = grow ? mx : m_used;
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = grow ? exp2f(m_used - m_use) : 1.f;
-      const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
-      const uint64_t neg_m2 = f2(-m_use, -m_use);
-      uint64_t sum2 = f2(0.f, 0.f);
-      {
-        // keys 0..63: exp2 on the MUFU
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = t32[i];
+        }
+        tmem_wait_ld();
+        if (len < 128) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (hf * 64 + i >= len) s[i] = -INFINITY;
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) mx = fmax3(mx, s[i], s[i + 1]);
+        mx = fmaxf(mx, pair_exchange(mx)) * p.scale_log2;
+        // Keep the stale max unless the new one exceeds it by more than 2^8.
+        const bool grow = mx > m_used[t] + ATT_RESCALE_LOG2;
+        const float m_new = grow ? mx : m_used[t];
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = grow ? exp2f(m_used[t] - m_use) : 1.f;
+        const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
+        const uint64_t neg_m2 = f2(-m_use, -m_use);
+        uint64_t sum2 = f2(0.f, 0.f);
         uint32_t pk[32];
+        // keys 0..47 of this half: exp2 on the MUFU; keys 48..63: the cubic
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 24; ++i) {
           const float2 x = f2_split(ffma2(f2(s[2 * i], s[2 * i + 1]), scale2, neg_m2));
           const float a = ex2_mufu(x.x), bb = ex2_mufu(x.y);
           sum2 = fadd2(sum2, f2(a, bb));
           pk[i] = pack_bf16(a, bb);
         }
-        tmem_st32u(tmem + lane_base + s_col, pk);
-      }
-      {
-        // keys 64..127: exp2 as a cubic on the FMA pipe
-        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const uint64_t e = ex2_poly2(ffma2(f2(s[64 + 2 * i], s[64 + 2 * i + 1]), scale2, neg_m2));
+        for (int i = 24; i < 32; ++i) {
+          const uint64_t e = ex2_poly2(ffma2(f2(s[2 * i], s[2 * i + 1]), scale2, neg_m2));
           sum2 = fadd2(sum2, e);
           const float2 ev = f2_split(e);
           pk[i] = pack_bf16(ev.x, ev.y);
         }
-        tmem_st32u(tmem + lane_base + s_col + 32, pk);
-      }
-      const float2 sv = f2_split(sum2);
-      const float rs = sv.x + sv.y;
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O_t is stable: S_t(j) was issued after PV_t(j-1) and has completed.
+        // P of keys [64 hf, 64 hf + 64) -> packed TMEM columns [t*128 + 32 hf, +32)
+        tmem_st32u(tmem + lane_base + t * 128 + hf * 32, pk);
+        const float2 sv = f2_split(sum2);
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // O_t is stable: S_t(j) was issued after PV_t(j-1) and has completed.
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float o[32];
-          tmem_ld32(tmem + lane_base + o_col + c * 32, o);
-          tmem_wait_ld();
+          for (int c = 0; c < 2; ++c) {
+            float o[32];
+            const uint32_t oc = 256 + t * 128 + hf * 64 + c * 32;
+            tmem_ld32(tmem + lane_base + oc, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tmem + lane_base + o_col + c * 32, o);
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tmem + lane_base + oc, o);
+          }
         }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full + 8 * t);
+        l[t] = l[t] * alpha + (sv.x + sv.y);
+        m_used[t] = m_new;
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(p_full + 8 * t);
-      l = l * alpha + rs;
-      m_used = m_new;
     }
-    if (t == 0 || has_b) {
-      if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
-      tc_fence_after();
+    if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
+    tc_fence_after();
+    for (int t = 0; t < ntq; ++t) {
+      const float lt = l[t] + pair_exchange(l[t]);
       const int qr = q0 + t * 128 + r;
       const bool store = qr < p.q_rows;
-      __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
-      const float inv = (ok && n > 0 && l > 0.f) ? 1.f / l : 0.f;
+      __nv_bfloat16* orow =
+          p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128 + hf * 64;
+      const float inv = (ok && n > 0 && lt > 0.f) ? 1.f / lt : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float o[32];
-        tmem_ld32(tmem + lane_base + o_col + c * 32, o);
+        tmem_ld32(tmem + lane_base + 256 + t * 128 + hf * 64 + c * 32, o);
         tmem_wait_ld();
         if (store) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);

@@ -52,14 +52,16 @@ WAMB_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes (or ~0.2 ms pass) instead of re-polling the barrier.
 WAMB_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(200000u)
       : "memory");
   return ok != 0;
 }
@@ -71,7 +73,7 @@ WAMB_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag)
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 31u) == 0) {
+    if ((it & 3u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer() - t0 > WAMB_WAIT_TIMEOUT_NS || it > (1u << 30)) {
         *abort_flag = 1;
