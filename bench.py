@@ -311,7 +311,7 @@ def run_native(args):
     pk, pk_kind = peaks()
     flops = 2.0 * M * F * D
     achieved = flops / (k_ms / 1000.0) / 1e12
-    roof = {"kernel": "gemm_tc_kernel<256,4> FFN1+GELU (M 7040, N 14336, K 3072)",
+    roof = {"kernel": "gemm_tc2_kernel (2-CTA 256x256 tiles) FFN1+GELU (M 7040, N 14336, K 3072)",
             "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
             "frac": achieved / pk["bf16_tflops"], "traffic": None,
             "peak_source": f"{pk_kind} bf16 burst", "ms_per_launch": k_ms,

@@ -1,5 +1,9 @@
 """tcgen05 GEMM (wamb_linear) against a torch fp32 reference on the GPU.
 
+Shapes with M >= 512, N per group a multiple of 256 and at least 74
+256 x 256 tiles take the two-CTA (cta_group::2) kernel; the others the
+one-CTA kernel with 64/128/256-column tiles.
+
 Tolerance: the kernel accumulates in fp32 and rounds once to bf16, so the
 error against an fp32 reference of the same bf16 operands is bounded by the
 bf16 output rounding (|x| * 2^-8) plus fp32 accumulation-order noise.
@@ -30,6 +34,8 @@ def _close(out, ref):
 @pytest.mark.parametrize("m,k,n,groups", [
     (128, 64, 64, 1), (200, 256, 256, 1), (880, 512, 384, 3), (1592, 1536, 1536, 1),
     (64, 3072, 1024, 1), (7, 128, 128, 2),
+    # two-CTA path: M tail whose second 128-row half is wholly out of range
+    (1040, 512, 3072, 3), (4096, 3072, 3072, 1),
 ])
 def test_linear_bias(cuda_device, m, k, n, groups):
     g = torch.Generator(device="cuda").manual_seed(m * 7 + k)
@@ -71,3 +77,28 @@ def test_linear_residual_gate(cuda_device, temb_len, temb_f32):
     _close(out, ref)
     out2 = ops.linear(a, w, b, epilogue=_lib.EPI_RES, res=res)
     _close(out2, res.float() + _ref(a, [w], [b]))
+
+
+@pytest.mark.parametrize("res_f32", [False, True])
+def test_linear_pair_epilogues(cuda_device, res_f32):
+    """Two-CTA kernel (M 1300, N 4608): GELU, and the gated residual with a
+    bf16 or fp32 residual stream and fp32 output."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    B, Q, D, K = 2, 650, 4608, 768
+    a = torch.randn(B * Q, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(D, K, device="cuda", generator=g) * 0.05).bfloat16()
+    b = torch.randn(D, device="cuda", generator=g).bfloat16()
+    out = ops.linear(a, w, b, epilogue=_lib.EPI_GELU)
+    _close(out, torch.nn.functional.gelu(_ref(a, [w], [b]), approximate="tanh"))
+    res = torch.randn(B * Q, D, device="cuda", generator=g)
+    if not res_f32:
+        res = res.bfloat16()
+    table = torch.randn(6, D, device="cuda", generator=g)
+    temb = torch.randn(B, 1, 6, D, device="cuda", generator=g)
+    out = torch.empty(B * Q, D, device="cuda", dtype=torch.float32)
+    ops.linear(a, w, b, epilogue=_lib.EPI_RES_GATE, res=res, table=table, temb=temb,
+               rows_per_batch=Q, gate_index=5, out=out)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    gate = (table[5][None, None] + temb[:, :, 5]).expand(B, Q, D).reshape(B * Q, D)
+    _close(out, res.float() + _ref(a, [w], [b]) * gate)

@@ -61,6 +61,117 @@ WAMB_DEV float gelu_tanh(float x) {
   return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
 }
 
+// Epilogue of one output tile for the calling thread's row: BN columns of
+// the fp32 accumulator at TMEM address `taddr` (this warp's lane quarter)
+// -> bias / GELU / residual / gate -> bf16 or fp32 stores. Every lane must
+// call it (tcgen05.ld is warp-collective); rows >= M only skip the stores.
+template <int BN>
+WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, int n0) {
+  const bool valid = row < p.M;
+  const int g = n0 / p.n_per_group;
+  const int n_local0 = n0 - g * p.n_per_group;
+  const __nv_bfloat16* bias = g == 0 ? p.bias[0] : (g == 1 ? p.bias[1] : p.bias[2]);
+  const float* gate_tab = nullptr;
+  const float* gate_f32 = nullptr;
+  const __nv_bfloat16* gate_bf = nullptr;
+  if (p.epi == EPI_RES_GATE && valid) {
+    const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
+    const long long l = p.temb_L == 1 ? 0 : tok;
+    const long long off = ((static_cast<long long>(b) * p.temb_L + l) * 6 + p.gate_idx) * p.D;
+    gate_tab = p.table + static_cast<long long>(p.gate_idx) * p.D;
+    if (p.temb_f32) gate_f32 = static_cast<const float*>(p.temb) + off;
+    else gate_bf = static_cast<const __nv_bfloat16*>(p.temb) + off;
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    float v[32];
+    tmem_ld32(taddr + c * 32, v);
+    tmem_wait_ld();
+    if (!valid) continue;
+    const int col = n0 + c * 32;            // output column
+    const int lcol = n_local0 + c * 32;     // column within the weight group
+    if (bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(bias + lcol);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = __ldg(bp + j);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = unpack_bf16(ws[h]);
+          v[8 * j + 2 * h] += f.x;
+          v[8 * j + 2 * h + 1] += f.y;
+        }
+      }
+    }
+    if (p.epi == EPI_GELU) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
+      if (p.epi == EPI_RES_GATE) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 tb = __ldg(reinterpret_cast<const float4*>(gate_tab + col + j));
+          float4 te;
+          if (gate_f32 != nullptr) {
+            te = __ldg(reinterpret_cast<const float4*>(gate_f32 + col + j));
+          } else {
+            const uint2 w = __ldg(reinterpret_cast<const uint2*>(gate_bf + col + j));
+            const float2 a = unpack_bf16(w.x), b2 = unpack_bf16(w.y);
+            te = make_float4(a.x, a.y, b2.x, b2.y);
+          }
+          v[j] *= tb.x + te.x;
+          v[j + 1] *= tb.y + te.y;
+          v[j + 2] *= tb.z + te.z;
+          v[j + 3] *= tb.w + te.w;
+        }
+      }
+      if (p.res_f32) {
+        const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(p.res) +
+                                                           row * p.ldr + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 f = __ldg(rp + j);
+          v[4 * j] += f.x;
+          v[4 * j + 1] += f.y;
+          v[4 * j + 2] += f.z;
+          v[4 * j + 3] += f.w;
+        }
+      } else {
+        const uint4* rp = reinterpret_cast<const uint4*>(
+            static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 w = __ldg(rp + j);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float2 f = unpack_bf16(ws[h]);
+            v[8 * j + 2 * h] += f.x;
+            v[8 * j + 2 * h + 1] += f.y;
+          }
+        }
+      }
+    }
+    if (p.out_f32) {
+      float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 w;
+        w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+        w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+        w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+        w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+        op[j] = w;
+      }
+    }
+  }
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
@@ -187,111 +298,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) break;
       tc_fence_after();
       const int m_blk = t % num_m, n_blk = t / num_m;
-      const int row = m_blk * GEMM_BM + row_in_tile;
-      const bool valid = row < p.M;
-      const int n0 = n_blk * BN;
-      const int g = n0 / p.n_per_group;
-      const int n_local0 = n0 - g * p.n_per_group;
-      const __nv_bfloat16* bias = g == 0 ? p.bias[0] : (g == 1 ? p.bias[1] : p.bias[2]);
-      const float* gate_tab = nullptr;
-      const float* gate_f32 = nullptr;
-      const __nv_bfloat16* gate_bf = nullptr;
-      if (p.epi == EPI_RES_GATE && valid) {
-        const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
-        const long long l = p.temb_L == 1 ? 0 : tok;
-        const long long off = ((static_cast<long long>(b) * p.temb_L + l) * 6 + p.gate_idx) * p.D;
-        gate_tab = p.table + static_cast<long long>(p.gate_idx) * p.D;
-        if (p.temb_f32) gate_f32 = static_cast<const float*>(p.temb) + off;
-        else gate_bf = static_cast<const __nv_bfloat16*>(p.temb) + off;
-      }
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, v);
-        tmem_wait_ld();
-        if (!valid) continue;
-        const int col = n0 + c * 32;            // output column
-        const int lcol = n_local0 + c * 32;     // column within the weight group
-        if (bias != nullptr) {
-          const uint4* bp = reinterpret_cast<const uint4*>(bias + lcol);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 w = __ldg(bp + j);
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const float2 f = unpack_bf16(ws[h]);
-              v[8 * j + 2 * h] += f.x;
-              v[8 * j + 2 * h + 1] += f.y;
-            }
-          }
-        }
-        if (p.epi == EPI_GELU) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-        } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
-          if (p.epi == EPI_RES_GATE) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 tb = __ldg(reinterpret_cast<const float4*>(gate_tab + col + j));
-              float4 te;
-              if (gate_f32 != nullptr) {
-                te = __ldg(reinterpret_cast<const float4*>(gate_f32 + col + j));
-              } else {
-                const uint2 w = __ldg(reinterpret_cast<const uint2*>(gate_bf + col + j));
-                const float2 a = unpack_bf16(w.x), b2 = unpack_bf16(w.y);
-                te = make_float4(a.x, a.y, b2.x, b2.y);
-              }
-              v[j] *= tb.x + te.x;
-              v[j + 1] *= tb.y + te.y;
-              v[j + 2] *= tb.z + te.z;
-              v[j + 3] *= tb.w + te.w;
-            }
-          }
-          if (p.res_f32) {
-            const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(p.res) +
-                                                               row * p.ldr + col);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 f = __ldg(rp + j);
-              v[4 * j] += f.x;
-              v[4 * j + 1] += f.y;
-              v[4 * j + 2] += f.z;
-              v[4 * j + 3] += f.w;
-            }
-          } else {
-            const uint4* rp = reinterpret_cast<const uint4*>(
-                static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 w = __ldg(rp + j);
-              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const float2 f = unpack_bf16(ws[h]);
-                v[8 * j + 2 * h] += f.x;
-                v[8 * j + 2 * h + 1] += f.y;
-              }
-            }
-          }
-        }
-        if (p.out_f32) {
-          float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        } else {
-          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 w;
-            w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
-            w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
-            w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
-            w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
-            op[j] = w;
-          }
-        }
-      }
+      gemm_epilogue_tile<BN>(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
+                             m_blk * GEMM_BM + row_in_tile, n_blk * BN);
       tc_fence_before();
       mbar_arrive(tempty0 + 8 * acc);
     }

@@ -1,0 +1,254 @@
+// Two-CTA (cta_group::2) variant of the tcgen05 GEMM for large M:
+// a cluster of 2 CTAs computes a 256 x 256 output tile with M=256
+// tcgen05.mma instructions issued by the leader CTA. Each CTA loads its own
+// 128 rows of A and its own 128 of the tile's 256 weight rows, so a CTA
+// moves 32 KB per 64-wide k-block instead of 48 KB for a 128 x 256 tile on
+// one SM: the shared weight tile crosses the L2 -> SM path once per pair.
+//
+// Barriers (per CTA):
+//   full[s]    leader only: one arrive_expect_tx (both CTAs' bytes); both
+//              CTAs' TMA loads complete_tx on the leader's barrier
+//   empty[s]   both CTAs: one arrival from the leader's commit (sent to both)
+//   tfull[a]   both CTAs: one arrival from the leader's commit (sent to both)
+//   tempty[a]  leader only: 8 arrivals, one per epilogue warp of either CTA
+//   bye        exit handshake: the other CTA arrives once (remote arrive)
+// TMEM: 2 accumulators x 256 columns per CTA (rows 0-127 of the tile in the
+// leader's TMEM, rows 128-255 in the peer's).
+#pragma once
+#include "gemm.cuh"
+
+namespace wamb {
+
+constexpr int GEMM2_STAGES = 6;
+
+struct Gemm2Smem {
+  static constexpr uint32_t A_BYTES = 128 * GEMM_BK * 2;  // this CTA's 128 rows of A
+  static constexpr uint32_t B_BYTES = 128 * GEMM_BK * 2;  // this CTA's 128 of 256 weight rows
+  static constexpr uint32_t BAR_OFF = GEMM2_STAGES * (A_BYTES + B_BYTES);
+  static constexpr uint32_t NBARS = 2 * GEMM2_STAGES + 6;
+  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+};
+
+WAMB_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+WAMB_DEV uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+WAMB_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+WAMB_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+// TMA load into this CTA's shared memory that completes on the mbarrier at
+// `bar_cluster` (the leader CTA's full barrier).
+WAMB_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                               int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+WAMB_DEV void umma2_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at this offset in both CTAs of the pair when
+// all previously issued tcgen05 ops of this thread complete.
+WAMB_DEV void umma2_commit_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+// Same, arriving only on this CTA's barrier (every tcgen05 op of a kernel
+// uses one cta_group, so the teardown drain needs the ::2 form too).
+WAMB_DEV void umma2_commit_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                    const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
+                    const GemmParams p) {
+  using L = Gemm2Smem;
+  constexpr int STAGES = GEMM2_STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * STAGES;
+  const uint32_t tfull0 = empty0 + 8 * STAGES;
+  const uint32_t tempty0 = tfull0 + 16;
+  const uint32_t drain = tempty0 + 16;
+  const uint32_t bye = drain + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_m = (p.M + 255) / 256;
+  const int num_n = p.N / 256;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = p.K / GEMM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 8);
+    }
+    mbar_init(drain, 1);
+    mbar_init(bye, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB0);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  // Both CTAs' barriers and TMEM exist before any cross-CTA signal.
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer
+      int it = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
+        const int m_blk = t % num_m, n_blk = t / num_m;
+        const int n0 = n_blk * 256;
+        const int g = n0 / p.n_per_group;
+        const int n_local = n0 - g * p.n_per_group;
+        const CUtensorMap* mb = g == 0 ? &tmB0 : (g == 1 ? &tmB1 : &tmB2);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) { ok = false; break; }
+          const uint32_t full_leader = map_to_rank(full0 + 8 * s, 0);
+          if (leader) mbar_arrive_expect_tx(full0 + 8 * s, 2 * (L::A_BYTES + L::B_BYTES));
+          tma_load_2d_pair(smem_u32(sA + s * L::A_BYTES), &tmA, full_leader, kb * GEMM_BK,
+                           m_blk * 256 + rank * 128);
+          tma_load_2d_pair(smem_u32(sB + s * L::B_BYTES), mb, full_leader, kb * GEMM_BK,
+                           n_local + rank * 128);
+        }
+        if (!ok) break;
+      }
+      // Teardown: this CTA's last loads must land before it may exit (their
+      // completion is counted on the leader's barrier, so wait on the
+      // consumer side instead: the final empty arrivals).
+      for (int s = 0; s < STAGES; ++s) {
+        if (it > s) {
+          const int last = s + ((it - 1 - s) / STAGES) * STAGES;
+          mbar_wait_teardown(empty0 + 8 * s, (last / STAGES) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // --------------------------------------------------- MMA issuer (leader)
+      constexpr uint32_t IDESC = idesc_bf16(256, 256, 0);
+      int it = 0, tc = 0;
+      for (int t = pair; t < num_tiles; t += npairs, ++tc) {
+        const int acc = tc & 1;
+        const uint32_t aph = (tc >> 1) & 1;
+        if (!mbar_wait(tempty0 + 8 * acc, aph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 256;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * L::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * L::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk)
+            umma2_bf16(d_tmem, sw128_desc(a_base + kk * 32, 16, 1024),
+                       sw128_desc(b_base + kk * 32, 16, 1024), IDESC, (kb | kk) != 0);
+          umma2_commit_both(empty0 + 8 * s);
+        }
+        if (!ok) break;
+        umma2_commit_both(tfull0 + 8 * acc);
+      }
+      // Teardown: all MMAs issued by this thread must finish before TMEM is freed.
+      umma2_commit_local(drain);
+      mbar_wait_teardown(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter accessible to this warp
+    const int row_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
+    const uint32_t tempty_leader0 = map_to_rank(tempty0, 0);
+    int tc = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++tc) {
+      const int acc = tc & 1;
+      const uint32_t aph = (tc >> 1) & 1;
+      if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) break;
+      tc_fence_after();
+      const int m_blk = t % num_m, n_blk = t / num_m;
+      const int row = m_blk * 256 + row_in_tile;
+      const int n0 = n_blk * 256;
+      gemm_epilogue_tile<256>(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256, row,
+                              n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_leader0 + 8 * acc);
+    }
+  }
+
+  // Exit handshake: neither CTA leaves (or frees TMEM) while the other may
+  // still signal its barriers or read its shared memory.
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_remote(map_to_rank(bye, rank ^ 1));
+    mbar_wait_teardown(bye, 0);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(512u)
+                 : "memory");
+  }
+}
+
+}  // namespace wamb

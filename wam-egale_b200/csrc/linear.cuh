@@ -2,6 +2,7 @@
 // maps, argument checks.
 #pragma once
 #include "gemm.cuh"
+#include "gemm2.cuh"
 #include "host.cuh"
 
 namespace wamb {
@@ -22,6 +23,38 @@ inline int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap* tb, const Ge
   const int grid = tiles < sms ? tiles : sms;
   gemm_tc_kernel<BN, STAGES><<<grid, GEMM_THREADS, L::TOTAL, stream>>>(ta, tb[0], tb[1], tb[2], p);
   WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+// Two-CTA launch: clusters of 2 along x, one cluster per pair of SMs.
+inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p, int sms,
+                        cudaStream_t stream) {
+  static int resident[64] = {};  // co-resident clusters per device, 0 = not queried
+  int dev = 0;
+  WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Gemm2Smem::TOTAL;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (resident[dev] == 0) {
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Gemm2Smem::TOTAL));
+    cfg.gridDim = dim3(sms, 1, 1);
+    int n = 0;
+    WAMB_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel, &cfg));
+    resident[dev] = n > 0 ? n : 1;
+  }
+  const int tiles = ((p.M + 255) / 256) * (p.N / 256);
+  const int pairs = tiles < resident[dev] ? tiles : resident[dev];
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel, ta, tb[0], tb[1], tb[2], p));
   return WAMB_OK;
 }
 
@@ -77,13 +110,18 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   int rc = device_info(&di);
   if (rc) return rc;
 
-  const int bn = choose_bn(a->m, static_cast<int>(N), a->n_per_group, di.sms);
+  // 2-CTA 256 x 256 tiles when the weight groups split into 256-wide tiles
+  // and there are enough of them to give every SM pair one; otherwise one
+  // CTA per 128 x BN tile.
+  const long long pair_tiles = ((a->m + 255) / 256) * (N / 256);
+  const bool pair = a->m >= 512 && a->n_per_group % 256 == 0 && pair_tiles >= di.sms / 2;
+  const int bn = pair ? 256 : choose_bn(a->m, static_cast<int>(N), a->n_per_group, di.sms);
   CUtensorMap ta, tb[3];
-  rc = make_tmap_bf16(&ta, a->a, a->m, a->k, a->lda, GEMM_BM);
+  rc = make_tmap_bf16(&ta, a->a, a->m, a->k, a->lda, 128);
   if (rc) return rc;
   for (int g = 0; g < 3; ++g) {
     const int src = g < a->groups ? g : 0;
-    rc = make_tmap_bf16(&tb[g], a->weight[src], a->n_per_group, a->k, a->k, bn);
+    rc = make_tmap_bf16(&tb[g], a->weight[src], a->n_per_group, a->k, a->k, pair ? 128 : bn);
     if (rc) return rc;
   }
   GemmParams p{};
@@ -107,6 +145,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   p.rows_per_batch = a->rows_per_batch > 0 ? a->rows_per_batch : 1;
   p.gate_idx = a->gate_index;
   p.D = a->dim;
+  if (pair) return launch_gemm2(ta, tb, p, di.sms, stream);
   switch (bn) {
     case 256: return launch_gemm_bn<256, 4>(ta, tb, p, di.sms, stream);
     case 128: return launch_gemm_bn<128, 6>(ta, tb, p, di.sms, stream);
