@@ -216,7 +216,7 @@ def run_native(args):
 
     blocks = configs.build_blocks(cfg, dev, seed=1234)
     configs.fill_history(blocks, cfg, dev, gen, pool_batch=B)
-    stack = NativeStack(blocks)
+    stack = NativeStack(blocks, fp8=args.fp8)
     ctx = torch.randn(B, cfg.context, D, generator=gen, device=dev).bfloat16()
     stack.prepare_context(ctx)
     x = torch.randn(B, Q, D, generator=gen, device=dev).bfloat16()
@@ -298,35 +298,55 @@ def run_native(args):
     a = torch.randn(M, D, generator=gen, device=dev).bfloat16()
     w1, b1 = blk0.ffn.net[0].proj.weight, blk0.ffn.net[0].proj.bias
     act = torch.empty(M, F, dtype=torch.bfloat16, device=dev)
+    if args.fp8:
+        a8, sa = ops.quantize_rows(a)
+        w8, sw = stack.layers[0].native.w8[23], stack.layers[0].native.w8_scale[23]
+        run = lambda: ops.linear(a8, w8, b1, epilogue=_lib.EPI_GELU, out=act,  # noqa: E731
+                                 a_scale=sa, w_scales=sw)
+    else:
+        run = lambda: ops.linear(a, w1, b1, epilogue=_lib.EPI_GELU, out=act)  # noqa: E731
     for _ in range(3):
-        ops.linear(a, w1, b1, epilogue=_lib.EPI_GELU, out=act)
+        run()
     reps = 20
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(reps):
-        ops.linear(a, w1, b1, epilogue=_lib.EPI_GELU, out=act)
+        run()
     e1.record(stream)
     torch.cuda.synchronize()
     k_ms = e0.elapsed_time(e1) / reps
     pk, pk_kind = peaks()
     flops = 2.0 * M * F * D
     achieved = flops / (k_ms / 1000.0) / 1e12
-    roof = {"kernel": "gemm_tc2_kernel (2-CTA 256x256 tiles) FFN1+GELU (M 7040, N 14336, K 3072)",
-            "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": achieved / pk["bf16_tflops"], "traffic": None,
-            "peak_source": f"{pk_kind} bf16 burst", "ms_per_launch": k_ms,
-            "algorithmic_flops_per_launch": flops}
-    step_flops = stack_flops(cfg) * B
+    # No fp8 GEMM peak is measured on this pool: the E4M3 tensor rate is
+    # twice the bf16 one on B200, so the fp8 denominator is 2x the bf16 burst.
+    tc_mult = 2.0 if args.fp8 else 1.0
+    kpeak = pk["bf16_tflops"] * tc_mult
+    roof = {"kernel": f"gemm_tc2_kernel<{'E4M3' if args.fp8 else 'bf16'}> (2-CTA 256x256 tiles) "
+                      "FFN1+GELU (M 7040, N 14336, K 3072)",
+            "bound": "tensor", "achieved": achieved, "peak": kpeak, "unit": "TFLOP/s",
+            "frac": achieved / kpeak, "traffic": None,
+            "peak_source": f"{pk_kind} bf16 burst" + (" x 2 for E4M3" if args.fp8 else ""),
+            "ms_per_launch": k_ms, "algorithmic_flops_per_launch": flops}
+    gemm_flops, attn_flops = stack_flops(cfg, split=True)
+    step_flops = (gemm_flops + attn_flops) * B
+    sus = pk["bf16_tflops_sustained"] * 1e12
+    floor_s = B * (gemm_flops / (sus * tc_mult) + attn_flops / sus)
     step_roof = {"achieved": step_flops / (ms / 1000.0) / 1e12, "unit": "TFLOP/s",
-                 "peak": pk["bf16_tflops_sustained"],
-                 "frac": step_flops / (ms / 1000.0) / 1e12 / pk["bf16_tflops_sustained"],
-                 "peak_source": f"{pk_kind} bf16 sustained", "algorithmic_flops_per_step": step_flops}
+                 "peak": pk["bf16_tflops_sustained"] * (tc_mult if args.fp8 else 1.0),
+                 "frac": floor_s / (ms / 1000.0),
+                 "peak_source": f"{pk_kind} bf16 sustained" + (
+                     "; frac = (GEMM FLOPs at 2x + attention FLOPs at 1x) / time" if args.fp8 else ""),
+                 "algorithmic_flops_per_step": step_flops}
 
     line = None
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded weights N(0,0.02), "
+                "vs_baseline": None,
+                "dtype": ("fp8-e4m3 GEMMs (per-channel weight / per-token activation scales), "
+                          "bf16 attention" if args.fp8 else "bf16"),
+                "data": "synthetic (seeded weights N(0,0.02), "
                 "zero biases, N(0,1) hidden/context, random unit-scale KV history)",
                 "config": workload_config(world, B) | {"action_chunks_per_s": value / CHUNK_STEPS},
                 "roofline": roof, "step_roofline": step_roof, "e2e": e2e,
@@ -345,15 +365,18 @@ def run_native(args):
     return 0
 
 
-def stack_flops(cfg):
+def stack_flops(cfg, split=False):
     """Algorithmic FLOPs of one 30-layer step for ONE rollout: the six
     projections, the two FFN GEMMs and the QK^T / PV products of both
-    attentions (cross K/V prepared, not counted)."""
+    attentions (cross K/V prepared, not counted). split=True returns
+    (GEMM FLOPs, attention FLOPs)."""
     D, F, Q, C = cfg.dim, cfg.ffn, cfg.tokens, cfg.context
     keys = cfg.history_chunks * Q + Q
     proj = 2 * Q * D * (3 * D) + 2 * Q * D * D + 2 * Q * D * D + 2 * Q * D * D
     ffn = 2 * 2 * Q * D * F
     attn = 2 * 2 * Q * keys * D + 2 * 2 * Q * C * D
+    if split:
+        return cfg.layers * (proj + ffn), cfg.layers * attn
     return cfg.layers * (proj + ffn + attn)
 
 
@@ -364,6 +387,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fp8", action="store_true",
+                    help="E4M3 GEMMs (the FP8 weight path); default is the bf16 drop-in")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

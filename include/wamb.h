@@ -103,9 +103,31 @@ typedef struct wamb_linear_args {
   int32_t rows_per_batch;
   int32_t gate_index;
   int32_t dim;            /* D (= N for the gated epilogue) */
+  /* FP8 operands (no counterpart in the reference, which is bf16-only,
+   * baseline/csrc/gemm.h:36-38). a_is_fp8 = 1: A is [M, lda] E4M3 bytes with
+   * the per-row scale a_scale[M] (fp32), weight[g] is [n_per_group, K] E4M3
+   * with the per-output-channel scale w_scale[g][n_per_group] (fp32); the
+   * fp32 accumulator is multiplied by a_scale[row] * w_scale[g][col] before
+   * the bias and the epilogue. Requires K % 128 == 0 and lda % 16 == 0. */
+  int32_t a_is_fp8;
+  const float* a_scale;
+  const float* w_scale[3];
 } wamb_linear_args;
 
 WAMB_API int wamb_linear(const wamb_linear_args* args, void* stream);
+
+/*
+ * Row-wise E4M3 quantization (no counterpart in the reference):
+ *   amax[r]  = max(max_c |x[r, c]|, 1e-20)
+ *   scale[r] = amax[r] / 448
+ *   out[r,c] = e4m3(x[r, c] * (448 / amax[r]))  (round to nearest even, saturating)
+ * x is [m, ldx] bf16, or fp32 when x_is_f32; out is [m, ldo] bytes.
+ * Gives the per-token activation scales of the FP8 path and, applied to a
+ * weight [N, K], its per-output-channel scales. Requires k % 8 == 0, ldx and
+ * ldo multiples of 16 bytes / 8 elements, 16-byte aligned pointers.
+ */
+WAMB_API int wamb_quantize_rows(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, int32_t k,
+                                void* out, int64_t ldo, float* scale, void* stream);
 
 /*
  * Flash attention (non-causal, head_dim 128) on the tcgen05 tensor cores.
@@ -199,6 +221,18 @@ typedef struct wamb_block_args {
   int32_t update;
   void* out;                     /* [batch, tokens, dim] bf16, or fp32 when out_is_f32 */
   void* workspace; size_t workspace_bytes;
+  /* FP8-E4M3 weight path (no counterpart in the reference). fp8 = 1 runs the
+   * eight GEMMs of the step (self q/k/v/out, cross q/out, FFN proj/out) on
+   * w8[i] ([N, K] E4M3, i in 3, 5, 7, 9, 13, 19, 23, 25) with the
+   * per-output-channel scales w8_scale[i] (fp32 [N], from
+   * wamb_quantize_rows), and E4M3 activations with per-token scales, written
+   * by the producing LayerNorm (LN1, LN2, LN3) or by a row-quantize pass
+   * (self/cross attention output, GELU output). weights[] must still hold the
+   * bf16 tensors (biases, norms, and the cross K/V projections 15/17 stay
+   * bf16). */
+  int32_t fp8;
+  const void* w8[27];
+  const float* w8_scale[27];
 } wamb_block_args;
 
 /* Named intermediates kept in the workspace (byte offsets; -1 = absent). */
@@ -218,7 +252,9 @@ enum wamb_tap {
   WAMB_TAP_KV_SLOTS = 12,   /* [tokens] int32 pool slot of each new token */
   WAMB_TAP_KV_TILES = 13,   /* [pool] int32 pairs */
   WAMB_TAP_KV_COUNTS = 14,  /* [2] int32: tiles, visible slots */
-  WAMB_TAP_COUNT = 15
+  WAMB_TAP_A8 = 15,         /* fp8 only: [M, F] E4M3, the last quantized GEMM input */
+  WAMB_TAP_A8_SCALE = 16,   /* fp8 only: [M] fp32 per-row scales of WAMB_TAP_A8 */
+  WAMB_TAP_COUNT = 17
 };
 
 WAMB_API size_t wamb_block_workspace_bytes(const wamb_block_args* args);

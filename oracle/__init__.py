@@ -10,7 +10,8 @@ Contents:
                  WanTransformerBlock / WanAttention / "original" KV cache /
                  WanRotaryPosEmbed / get_mesh_id, each citing the reference
                  file:line it follows.
-  synth.py       seeded synthetic inputs and weights for the BASELINE configs.
+  fp8.py         the FP8-E4M3 GEMM path (no reference counterpart): row
+                 quantization and a block copy with quantized GEMMs.
 
 Parity pin: tests/golden/make_golden.py runs the reference's own model.py
 source (AST-extracted, in the build container where the reference is

@@ -20,7 +20,7 @@ def test_header_symbols_exported():
     assert declared == set(_lib.EXPORTED)
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.wamb_abi_version() == 100
+    assert lib.wamb_abi_version() == _lib.ABI_VERSION
 
 
 @pytest.mark.parametrize("cname,pyname", [("wamb_linear_args", "LinearArgs"),
@@ -66,6 +66,34 @@ def test_workspace_layout():
     assert offs[_lib.TAPS.index("norm2")] >= 0
     assert total >= (12 * M * D + M * F) * 2                # residual stream taps are fp32
     assert all(o % 256 == 0 for o in offs if o >= 0)
+    assert offs[_lib.TAPS.index("a8")] == -1                # bf16 path
+
+
+def test_workspace_layout_fp8():
+    """FP8 path: no bf16 LayerNorm outputs, one E4M3 buffer of M x max(D, F)
+    bytes and M fp32 row scales instead."""
+    lib = _lib.load()
+    a = _args(fp8=1)
+    offs = (ctypes.c_int64 * len(_lib.TAPS))()
+    total = lib.wamb_block_workspace_layout(a, offs)
+    M, F = 48, 512
+    for t in ("modulated1", "norm2", "modulated3"):
+        assert offs[_lib.TAPS.index(t)] == -1
+    a8, sc = offs[_lib.TAPS.index("a8")], offs[_lib.TAPS.index("a8_scale")]
+    assert a8 >= 0 and sc >= a8 + M * F and total >= sc + 4 * M
+
+
+def test_fp8_block_requires_e4m3_weights():
+    lib = _lib.load()
+    a = _args(fp8=1)
+    assert lib.wamb_block_forward(a, None) != 0
+    assert lib.wamb_last_error()
+
+
+def test_quantize_rows_rejects_bad_args():
+    lib = _lib.load()
+    assert lib.wamb_quantize_rows(None, 8, 0, 4, 8, None, 16, None, None) != 0   # null pointers
+    assert lib.wamb_quantize_rows(None, 8, 0, 4, 12, None, 16, None, None) == 2  # k % 8
 
 
 @pytest.mark.parametrize("kw,code", [
@@ -88,3 +116,5 @@ def test_linear_rejects_bad_shapes():
     assert lib.wamb_linear(a, None) == 2
     a.k, a.groups = 128, 4
     assert lib.wamb_linear(a, None) == 1
+    a.k, a.groups, a.a_is_fp8 = 192, 1, 1                 # E4M3 K must be a multiple of 128
+    assert lib.wamb_linear(a, None) == 2

@@ -121,6 +121,13 @@ inline int launch_ln(const LnParams& p, cudaStream_t s) {
   });
 }
 
+inline int launch_quant(const QuantParams& p, cudaStream_t s) {
+  if (p.M == 0) return WAMB_OK;
+  quant_rows_kernel<<<p.M, 256, 0, s>>>(p);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
 inline int launch_rms(const RmsParams& p, cudaStream_t s) {
   if (p.M == 0) return WAMB_OK;
   const int vpt = row_vpt(p.D);
@@ -152,11 +159,12 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
     L.off[tap] = static_cast<int64_t>(o);
     o = align256(o + bytes);
   };
-  put(WAMB_TAP_MODULATED1, MD);
+  const bool f8 = a->fp8 == 1;  // LN outputs go to the E4M3 buffer instead
+  if (!f8) put(WAMB_TAP_MODULATED1, MD);
   put(WAMB_TAP_QKV, 3 * MD);
   put(WAMB_TAP_SELF_ATTN, MD);
   put(WAMB_TAP_RESIDUAL1, 2 * MD);  // fp32
-  put(WAMB_TAP_NORM2, MD);
+  if (!f8) put(WAMB_TAP_NORM2, MD);
   put(WAMB_TAP_CROSS_Q, MD);
   if (a->cross_k == nullptr) {
     const size_t CD = static_cast<size_t>(a->context_batch) * a->context_tokens * D * 2;
@@ -165,8 +173,12 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
   }
   put(WAMB_TAP_CROSS_ATTN, MD);
   put(WAMB_TAP_RESIDUAL2, 2 * MD);  // fp32
-  put(WAMB_TAP_MODULATED3, MD);
+  if (!f8) put(WAMB_TAP_MODULATED3, MD);
   put(WAMB_TAP_GELU, M * F * 2);
+  if (f8) {
+    put(WAMB_TAP_A8, M * (F > D ? F : D));
+    put(WAMB_TAP_A8_SCALE, M * 4);
+  }
   if (a->cache_k != nullptr) {
     put(WAMB_TAP_KV_SLOTS, static_cast<size_t>(a->tokens) * 4);
     put(WAMB_TAP_KV_TILES, static_cast<size_t>(a->pool) * 8);
@@ -175,6 +187,9 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
   L.total = o;
   return L;
 }
+
+// Weight slots that the FP8 path reads as E4M3 (the eight GEMMs of the step).
+constexpr int kFp8Weights[8] = {3, 5, 7, 9, 13, 19, 23, 25};
 
 inline int check_block_args(const wamb_block_args* a) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
@@ -204,6 +219,15 @@ inline int check_block_args(const wamb_block_args* a) {
   WAMB_REQUIRE(a->freq == nullptr || a->freq_batch == 1 || a->freq_batch == a->batch,
                WAMB_ERR_SHAPE, "freq_batch must be 1 or batch");
   WAMB_REQUIRE(a->update >= 0 && a->update <= 2, WAMB_ERR_ARG, "update must be 0, 1 or 2");
+  WAMB_REQUIRE(a->fp8 == 0 || a->fp8 == 1, WAMB_ERR_ARG, "fp8 must be 0 or 1");
+  if (a->fp8) {
+    WAMB_REQUIRE(a->ffn_dim % 128 == 0, WAMB_ERR_SHAPE, "fp8 needs ffn_dim %% 128 == 0");
+    for (int i : kFp8Weights) {
+      WAMB_REQUIRE(a->w8[i] && aligned16(a->w8[i]), WAMB_ERR_ARG, "w8[%d] null or misaligned", i);
+      WAMB_REQUIRE(a->w8_scale[i] && aligned16(a->w8_scale[i]), WAMB_ERR_ARG,
+                   "w8_scale[%d] null or misaligned", i);
+    }
+  }
   if (a->cache_k != nullptr) {
     WAMB_REQUIRE(a->cache_v && a->cache_id && a->cache_mask && a->cache_pred, WAMB_ERR_KV,
                  "cache schema: k, v, id, mask, is_pred");
@@ -277,6 +301,27 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   int* slots = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_SLOTS]) : nullptr;
   int* tiles = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_TILES]) : nullptr;
   int* counts = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_COUNTS]) : nullptr;
+  // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
+  const bool f8 = a->fp8 == 1;
+  uint8_t* a8 = f8 ? ws + L.off[WAMB_TAP_A8] : nullptr;
+  float* a8s = f8 ? reinterpret_cast<float*>(ws + L.off[WAMB_TAP_A8_SCALE]) : nullptr;
+  auto gemm_input = [&](wamb_linear_args& g, const void* a_bf16, int widx) {
+    if (f8) {
+      g.a = a8; g.a_is_fp8 = 1; g.a_scale = a8s;
+      for (int j = 0; j < g.groups; ++j) {
+        g.weight[j] = a->w8[widx + 2 * j];
+        g.w_scale[j] = a->w8_scale[widx + 2 * j];
+      }
+    } else {
+      g.a = a_bf16;
+      for (int j = 0; j < g.groups; ++j) g.weight[j] = a->weights[widx + 2 * j];
+    }
+  };
+  auto quantize = [&](const void* x, long long ldx, int k) {
+    QuantParams qp{};
+    qp.x = x; qp.ldx = ldx; qp.M = M; qp.K = k; qp.out = a8; qp.ldo = k; qp.scale = a8s;
+    return launch_quant(qp, s);
+  };
 
   // 1. KV bookkeeping on the device (no host sync, unlike block.cu:241-244).
   if (cache) {
@@ -295,13 +340,13 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln.eps = static_cast<float>(a->eps[0]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
+  if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
   if ((rc = launch_ln(ln, s))) return rc;
   // 3. QKV projection: three weight groups write q | k | v
   wamb_linear_args g{};
-  g.a = h1; g.lda = D; g.m = M; g.k = D; g.groups = 3; g.n_per_group = D;
-  g.weight[0] = a->weights[3]; g.bias[0] = a->weights[4];
-  g.weight[1] = a->weights[5]; g.bias[1] = a->weights[6];
-  g.weight[2] = a->weights[7]; g.bias[2] = a->weights[8];
+  g.lda = D; g.m = M; g.k = D; g.groups = 3; g.n_per_group = D;
+  gemm_input(g, h1, 3);
+  g.bias[0] = a->weights[4]; g.bias[1] = a->weights[6]; g.bias[2] = a->weights[8];
   g.out = qkv; g.ldo = 3LL * D; g.epilogue = WAMB_EPI_BIAS;
   if ((rc = linear_impl(&g, s))) return rc;
   // 4. q/k RMSNorm across heads + RoPE; K/V into the pool slots
@@ -332,10 +377,12 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     at.src0_total_rows = M; at.src0_batch_stride = Q; at.src0_len = Q;
   }
   if ((rc = attention_impl(&at, s))) return rc;
+  if (f8 && (rc = quantize(attn, D, D))) return rc;
   // 6. O projection + gated residual (gate 2): h2 = x + o * gate_msa
   g = wamb_linear_args{};
-  g.a = attn; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
-  g.weight[0] = a->weights[9]; g.bias[0] = a->weights[10]; g.out = h2; g.ldo = D;
+  g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
+  gemm_input(g, attn, 9);
+  g.bias[0] = a->weights[10]; g.out = h2; g.ldo = D;
   g.epilogue = WAMB_EPI_RES_GATE; g.res = a->x; g.res_is_f32 = a->x_is_f32; g.ldr = D;
   g.out_is_f32 = 1; g.table = table; g.temb = a->temb;
   g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 2;
@@ -347,11 +394,13 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln.eps = static_cast<float>(a->eps[1]); ln.affine = a->weights[1] != nullptr ? 1 : 2;
   ln.gamma = static_cast<const float*>(a->weights[1]); ln.beta = static_cast<const float*>(a->weights[2]);
   ln.rows_per_batch = Q;
+  if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
   if ((rc = launch_ln(ln, s))) return rc;
   // 8-9. cross Q projection + RMSNorm
   g = wamb_linear_args{};
-  g.a = n2; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
-  g.weight[0] = a->weights[13]; g.bias[0] = a->weights[14]; g.out = cq; g.ldo = D;
+  g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
+  gemm_input(g, n2, 13);
+  g.bias[0] = a->weights[14]; g.out = cq; g.ldo = D;
   g.epilogue = WAMB_EPI_BIAS;
   if ((rc = linear_impl(&g, s))) return rc;
   r = RmsParams{};
@@ -379,10 +428,12 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   at.src0_broadcast = a->context_rows == nullptr && a->context_batch == 1 && B > 1;
   at.out = ca; at.ldo = D;
   if ((rc = attention_impl(&at, s))) return rc;
+  if (f8 && (rc = quantize(ca, D, D))) return rc;
   // 12. cross O projection + residual: h3 = h2 + o
   g = wamb_linear_args{};
-  g.a = ca; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
-  g.weight[0] = a->weights[19]; g.bias[0] = a->weights[20]; g.out = h3; g.ldo = D;
+  g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = D;
+  gemm_input(g, ca, 19);
+  g.bias[0] = a->weights[20]; g.out = h3; g.ldo = D;
   g.epilogue = WAMB_EPI_RES; g.res = h2; g.res_is_f32 = 1; g.out_is_f32 = 1; g.ldr = D;
   if ((rc = linear_impl(&g, s))) return rc;
   // 13. LN3 + modulation (shift 3, scale 4)
@@ -391,17 +442,21 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln.eps = static_cast<float>(a->eps[2]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 3; ln.scale_idx = 4;
+  if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
   if ((rc = launch_ln(ln, s))) return rc;
   // 14. FFN1 + GELU-tanh
   g = wamb_linear_args{};
-  g.a = f0; g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = F;
-  g.weight[0] = a->weights[23]; g.bias[0] = a->weights[24]; g.out = act; g.ldo = F;
+  g.lda = D; g.m = M; g.k = D; g.groups = 1; g.n_per_group = F;
+  gemm_input(g, f0, 23);
+  g.bias[0] = a->weights[24]; g.out = act; g.ldo = F;
   g.epilogue = WAMB_EPI_GELU;
   if ((rc = linear_impl(&g, s))) return rc;
+  if (f8 && (rc = quantize(act, F, F))) return rc;
   // 15. FFN2 + gated residual (gate 5): out = h3 + f * c_gate_msa
   g = wamb_linear_args{};
-  g.a = act; g.lda = F; g.m = M; g.k = F; g.groups = 1; g.n_per_group = D;
-  g.weight[0] = a->weights[25]; g.bias[0] = a->weights[26]; g.out = a->out; g.ldo = D;
+  g.lda = F; g.m = M; g.k = F; g.groups = 1; g.n_per_group = D;
+  gemm_input(g, act, 25);
+  g.bias[0] = a->weights[26]; g.out = a->out; g.ldo = D;
   g.epilogue = WAMB_EPI_RES_GATE; g.res = h3; g.res_is_f32 = 1; g.ldr = D;
   g.out_is_f32 = a->out_is_f32; g.table = table; g.temb = a->temb;
   g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 5;

@@ -1,11 +1,14 @@
 // Persistent tcgen05 GEMM for the block's dense projections:
 //   out[M, N] = epilogue( A[M, K] * W[N, K]^T + bias[N] )
-// A and W are bf16 row-major (K contiguous), accumulation is fp32 in TMEM.
+// A and W are bf16 row-major (K contiguous), or E4M3 with a per-row scale
+// for A and a per-output-channel scale for W; accumulation is fp32 in TMEM.
 //
-// Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer (A tile 128x64, W tile BNx64, 128B swizzle)
+// Roles (320 threads, one CTA per SM):
+//   warp 0      TMA producer (A tile 128 rows x 128 bytes, W tile BN rows x
+//               128 bytes, 128B swizzle: 64 bf16 or 128 E4M3 of K)
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld -> bias / GELU / residual / gate -> bf16 or fp32 stores
+//   warps 2..9  epilogue: tcgen05.ld -> bias / GELU / residual / gate -> bf16 or fp32 stores;
+//               two warps per TMEM lane quarter, each on half of the tile's columns
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i+1.
 //
@@ -38,11 +41,16 @@ struct GemmParams {
   const float* table;                // [6, D] fp32
   const void* temb;                  // [B, L, 6, D] fp32 or bf16
   int temb_f32, temb_L, rows_per_batch, gate_idx, D;
+  // E4M3 operands: acc * a_scale[row] * w_scale[group][col] (null for bf16)
+  const float* a_scale;
+  const float* w_scale[3];
 };
 
 constexpr int GEMM_BM = 128;
-constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_BK = 64;          // bf16 elements per k-block (128 bytes)
+constexpr int GEMM_BK8 = 128;        // E4M3 elements per k-block (128 bytes)
+constexpr int GEMM_THREADS = 320;
+constexpr int GEMM_EPI_WARPS = 8;
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -55,22 +63,31 @@ struct GemmSmem {
 };
 
 WAMB_DEV float gelu_tanh(float x) {
-  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), the formula of the
-  // reference's gelu_kernel (baseline/csrc/block.cu:119-124).
+  // 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3): the formula of the
+  // reference's gelu_kernel (baseline/csrc/block.cu:119-124), evaluated as
+  // x / (1 + exp(-2u)) (since 1 + tanh(u) = 2 / (1 + exp(-2u))) with one
+  // ex2.approx and one approximate reciprocal: relative error ~1e-6, against
+  // 2^-9 for the bf16 rounding that follows. x -> -inf gives x / inf = -0.
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+  const float u = k0 * fmaf(k1 * x * x, x, x);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * -2.8853900817779268f));  // -2 log2(e) u
+  return __fdividef(x, 1.f + e);
 }
 
-// Epilogue of one output tile for the calling thread's row: BN columns of
-// the fp32 accumulator at TMEM address `taddr` (this warp's lane quarter)
-// -> bias / GELU / residual / gate -> bf16 or fp32 stores. Every lane must
-// call it (tcgen05.ld is warp-collective); rows >= M only skip the stores.
-template <int BN>
-WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, int n0) {
+// Epilogue of one output tile for the calling thread's row: 32-column
+// chunks [c0, c1) of the fp32 accumulator at TMEM address `taddr` (this
+// warp's lane quarter, column 0 of the tile) -> bias / GELU / residual /
+// gate -> bf16 or fp32 stores. Every lane must call it (tcgen05.ld is
+// warp-collective); rows >= M only skip the stores.
+WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, int n0, int c0,
+                                 int c1) {
   const bool valid = row < p.M;
   const int g = n0 / p.n_per_group;
   const int n_local0 = n0 - g * p.n_per_group;
   const __nv_bfloat16* bias = g == 0 ? p.bias[0] : (g == 1 ? p.bias[1] : p.bias[2]);
+  const float* wscale = g == 0 ? p.w_scale[0] : (g == 1 ? p.w_scale[1] : p.w_scale[2]);
+  const float ascale = p.a_scale != nullptr && valid ? __ldg(p.a_scale + row) : 1.f;
   const float* gate_tab = nullptr;
   const float* gate_f32 = nullptr;
   const __nv_bfloat16* gate_bf = nullptr;
@@ -83,13 +100,24 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
     else gate_bf = static_cast<const __nv_bfloat16*>(p.temb) + off;
   }
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
+  for (int c = c0; c < c1; ++c) {
     float v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
     if (!valid) continue;
     const int col = n0 + c * 32;            // output column
     const int lcol = n_local0 + c * 32;     // column within the weight group
+    if (p.a_scale != nullptr) {
+      const float4* sp = reinterpret_cast<const float4*>(wscale + lcol);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 w = __ldg(sp + j);
+        v[4 * j] *= ascale * w.x;
+        v[4 * j + 1] *= ascale * w.y;
+        v[4 * j + 2] *= ascale * w.z;
+        v[4 * j + 3] *= ascale * w.w;
+      }
+    }
     if (bias != nullptr) {
       const uint4* bp = reinterpret_cast<const uint4*>(bias + lcol);
 #pragma unroll
@@ -172,7 +200,7 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool F8>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
@@ -196,7 +224,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int num_m = (p.M + GEMM_BM - 1) / GEMM_BM;
   const int num_n = p.N / BN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = p.K / GEMM_BK;
+  constexpr int KB = F8 ? GEMM_BK8 : GEMM_BK;
+  const int num_kb = p.K / KB;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -205,7 +234,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, 128);
+      mbar_init(tempty0 + 8 * a, 32 * GEMM_EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -240,8 +269,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(full0 + 8 * s, L::A_BYTES + L::B_BYTES);
-          tma_load_2d(smem_u32(sA + s * L::A_BYTES), &tmA, full0 + 8 * s, kb * GEMM_BK, m_blk * GEMM_BM);
-          tma_load_2d(smem_u32(sB + s * L::B_BYTES), mb, full0 + 8 * s, kb * GEMM_BK, n_local);
+          tma_load_2d(smem_u32(sA + s * L::A_BYTES), &tmA, full0 + 8 * s, kb * KB, m_blk * GEMM_BM);
+          tma_load_2d(smem_u32(sB + s * L::B_BYTES), mb, full0 + 8 * s, kb * KB, n_local);
         }
         if (!ok) break;
       }
@@ -256,7 +285,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // --------------------------------------------------------- MMA issuer
-      constexpr uint32_t IDESC = idesc_bf16(GEMM_BM, BN, 0);
+      constexpr uint32_t IDESC = F8 ? idesc_e4m3(GEMM_BM, BN) : idesc_bf16(GEMM_BM, BN, 0);
       int it = 0, tc = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
         const int acc = tc & 1;
@@ -273,10 +302,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t a_base = smem_u32(sA + s * L::A_BYTES);
           const uint32_t b_base = smem_u32(sB + s * L::B_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per k-block
             const uint64_t ad = sw128_desc(a_base + kk * 32, 16, 1024);
             const uint64_t bd = sw128_desc(b_base + kk * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+            if constexpr (F8) umma_e4m3(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+            else umma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
           }
           umma_commit(empty0 + 8 * s);
         }
@@ -290,6 +320,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter accessible to this warp
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     int tc = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
@@ -298,8 +329,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) break;
       tc_fence_after();
       const int m_blk = t % num_m, n_blk = t / num_m;
-      gemm_epilogue_tile<BN>(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
-                             m_blk * GEMM_BM + row_in_tile, n_blk * BN);
+      gemm_epilogue_tile(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
+                         m_blk * GEMM_BM + row_in_tile, n_blk * BN, half * (BN / 64),
+                         (half + 1) * (BN / 64));
       tc_fence_before();
       mbar_arrive(tempty0 + 8 * acc);
     }

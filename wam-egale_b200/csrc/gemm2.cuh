@@ -10,7 +10,7 @@
 //              CTAs' TMA loads complete_tx on the leader's barrier
 //   empty[s]   both CTAs: one arrival from the leader's commit (sent to both)
 //   tfull[a]   both CTAs: one arrival from the leader's commit (sent to both)
-//   tempty[a]  leader only: 8 arrivals, one per epilogue warp of either CTA
+//   tempty[a]  leader only: 16 arrivals, one per epilogue warp of either CTA
 //   bye        exit handshake: the other CTA arrives once (remote arrive)
 // TMEM: 2 accumulators x 256 columns per CTA (rows 0-127 of the tile in the
 // leader's TMEM, rows 128-255 in the peer's).
@@ -22,8 +22,8 @@ namespace wamb {
 constexpr int GEMM2_STAGES = 6;
 
 struct Gemm2Smem {
-  static constexpr uint32_t A_BYTES = 128 * GEMM_BK * 2;  // this CTA's 128 rows of A
-  static constexpr uint32_t B_BYTES = 128 * GEMM_BK * 2;  // this CTA's 128 of 256 weight rows
+  static constexpr uint32_t A_BYTES = 128 * 128;  // this CTA's 128 rows of A x 128 bytes of K
+  static constexpr uint32_t B_BYTES = 128 * 128;  // this CTA's 128 of 256 weight rows
   static constexpr uint32_t BAR_OFF = GEMM2_STAGES * (A_BYTES + B_BYTES);
   static constexpr uint32_t NBARS = 2 * GEMM2_STAGES + 6;
   static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
@@ -58,6 +58,15 @@ WAMB_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t ba
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
       : "memory");
 }
+WAMB_DEV void umma2_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 WAMB_DEV void umma2_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                          uint32_t accumulate) {
   asm volatile(
@@ -84,6 +93,7 @@ WAMB_DEV void umma2_commit_local(uint32_t bar) {
                : "memory");
 }
 
+template <bool F8>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
@@ -112,7 +122,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int num_m = (p.M + 255) / 256;
   const int num_n = p.N / 256;
   const int num_tiles = num_m * num_n;
-  const int num_kb = p.K / GEMM_BK;
+  constexpr int KB = F8 ? GEMM_BK8 : GEMM_BK;
+  const int num_kb = p.K / KB;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -121,7 +132,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, 8);
+      mbar_init(tempty0 + 8 * a, 2 * GEMM_EPI_WARPS);
     }
     mbar_init(drain, 1);
     mbar_init(bye, 1);
@@ -163,9 +174,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) { ok = false; break; }
           const uint32_t full_leader = map_to_rank(full0 + 8 * s, 0);
           if (leader) mbar_arrive_expect_tx(full0 + 8 * s, 2 * (L::A_BYTES + L::B_BYTES));
-          tma_load_2d_pair(smem_u32(sA + s * L::A_BYTES), &tmA, full_leader, kb * GEMM_BK,
+          tma_load_2d_pair(smem_u32(sA + s * L::A_BYTES), &tmA, full_leader, kb * KB,
                            m_blk * 256 + rank * 128);
-          tma_load_2d_pair(smem_u32(sB + s * L::B_BYTES), mb, full_leader, kb * GEMM_BK,
+          tma_load_2d_pair(smem_u32(sB + s * L::B_BYTES), mb, full_leader, kb * KB,
                            n_local + rank * 128);
         }
         if (!ok) break;
@@ -183,7 +194,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // --------------------------------------------------- MMA issuer (leader)
-      constexpr uint32_t IDESC = idesc_bf16(256, 256, 0);
+      constexpr uint32_t IDESC = F8 ? idesc_e4m3(256, 256) : idesc_bf16(256, 256, 0);
       int it = 0, tc = 0;
       for (int t = pair; t < num_tiles; t += npairs, ++tc) {
         const int acc = tc & 1;
@@ -200,9 +211,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t a_base = smem_u32(sA + s * L::A_BYTES);
           const uint32_t b_base = smem_u32(sB + s * L::B_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk)
-            umma2_bf16(d_tmem, sw128_desc(a_base + kk * 32, 16, 1024),
-                       sw128_desc(b_base + kk * 32, 16, 1024), IDESC, (kb | kk) != 0);
+          for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per k-block
+            const uint64_t ad = sw128_desc(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(b_base + kk * 32, 16, 1024);
+            if constexpr (F8) umma2_e4m3(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+            else umma2_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+          }
           umma2_commit_both(empty0 + 8 * s);
         }
         if (!ok) break;
@@ -215,6 +229,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter accessible to this warp
+    const int half = (warp - 2) >> 2;  // columns [half * 128, half * 128 + 128)
     const int row_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
     const uint32_t tempty_leader0 = map_to_rank(tempty0, 0);
     int tc = 0;
@@ -226,8 +241,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int m_blk = t % num_m, n_blk = t / num_m;
       const int row = m_blk * 256 + row_in_tile;
       const int n0 = n_blk * 256;
-      gemm_epilogue_tile<256>(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256, row,
-                              n0);
+      gemm_epilogue_tile(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256, row, n0,
+                         half * 4, half * 4 + 4);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty_leader0 + 8 * acc);

@@ -2,6 +2,8 @@
 // vector loads, warp-shuffle reductions, fp32 math):
 //   ln_kernel        LayerNorm (no affine) + adaLN modulation   model.py:761-763, 786-788
 //                    LayerNorm (fp32 affine)                      model.py:775-776 (norm2)
+//                    optionally written as E4M3 + per-row scale (FP8 path)
+//   quant_rows_kernel per-row E4M3 quantization of a bf16 / fp32 matrix
 //   rms_rope_kernel  RMSNorm across all heads (* gamma) + 3D RoPE, K/V written
 //                    into the caller's KV-pool slots              model.py:609-623, 577-589
 //   kv_layout_kernel slot allocation with id eviction, run-tile list of the
@@ -75,6 +77,8 @@ struct LnParams {
                           // 2: y = x (identity norm2, only the bf16 cast)
   const float* gamma;
   const float* beta;
+  uint8_t* out8;          // non-null: write E4M3 [M, ldo] + out_scale[M] instead of bf16
+  float* out_scale;
   const float* table;     // [6, D]
   const void* temb;       // [B, L, 6, D]
   int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
@@ -97,13 +101,7 @@ __global__ void ln_kernel(const LnParams p) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) s += v[i][j];
   }
-  __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ldo;
-  if (p.affine == 2) {
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) store8(orow + (i * nthr + threadIdx.x) * 8, v[i]);
-    return;
-  }
-  // Generic block reduction (number of warps known only at run time).
+  // Generic block reductions (number of warps known only at run time).
   auto reduce = [&](float a) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
@@ -114,6 +112,45 @@ __global__ void ln_kernel(const LnParams p) {
     for (int i = 0; i < nw; ++i) t += red[i];
     return t;
   };
+  auto reduce_max = [&](float a) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
+    return t;
+  };
+  // Row output: bf16, or E4M3 with the row scale amax / 448 (quant_rows_kernel rule).
+  auto emit = [&](float (&y)[VPT][8]) {
+    if (p.out8 == nullptr) {
+      __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ldo;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) store8(orow + (i * nthr + threadIdx.x) * 8, y[i]);
+      return;
+    }
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(y[i][j]));
+    const float amax = fmaxf(reduce_max(am), 1e-20f);
+    const float inv = 448.f / amax;
+    if (threadIdx.x == 0) p.out_scale[row] = amax / 448.f;
+    uint8_t* orow = p.out8 + static_cast<long long>(row) * p.ldo;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float t[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = y[i][j] * inv;
+      *reinterpret_cast<uint2*>(orow + (i * nthr + threadIdx.x) * 8) = pack_e4m3x8(t);
+    }
+  };
+  if (p.affine == 2) {
+    emit(v);
+    return;
+  }
   const float mean = reduce(s) / p.D;
   float q = 0.f;
 #pragma unroll
@@ -145,7 +182,53 @@ __global__ void ln_kernel(const LnParams p) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) y[j] = (v[i][j] - mean) * rstd * (1.f + a[j]) + b[j];
     }
-    store8(orow + col, y);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[i][j] = y[j];
+  }
+  emit(v);
+}
+
+// --------------------------------------------------- row E4M3 quantization
+struct QuantParams {
+  const void* x;          // [M, ldx] bf16, or fp32 when x_f32
+  long long ldx;
+  int x_f32;
+  int M, K;
+  uint8_t* out;           // [M, ldo] E4M3
+  long long ldo;
+  float* scale;           // [M]: amax / 448
+};
+
+// One CTA per row: amax over the row (pass 1), then E4M3(x * 448 / amax)
+// (pass 2, re-reading the row from L1/L2).
+__global__ void __launch_bounds__(256) quant_rows_kernel(const QuantParams p) {
+  __shared__ float red[8];
+  const long long row = blockIdx.x;
+  float am = 0.f;
+  for (int c = threadIdx.x * 8; c < p.K; c += 256 * 8) {
+    float f[8];
+    if (p.x_f32) load8f(static_cast<const float*>(p.x) + row * p.ldx + c, f);
+    else load8(static_cast<const __nv_bfloat16*>(p.x) + row * p.ldx + c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(f[j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
+  __syncthreads();
+  am = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) am = fmaxf(am, red[i]);
+  const float amax = fmaxf(am, 1e-20f);
+  const float inv = 448.f / amax;
+  if (threadIdx.x == 0) p.scale[row] = amax / 448.f;
+  for (int c = threadIdx.x * 8; c < p.K; c += 256 * 8) {
+    float f[8];
+    if (p.x_f32) load8f(static_cast<const float*>(p.x) + row * p.ldx + c, f);
+    else load8(static_cast<const __nv_bfloat16*>(p.x) + row * p.ldx + c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] *= inv;
+    *reinterpret_cast<uint2*>(p.out + row * p.ldo + c) = pack_e4m3x8(f);
   }
 }
 

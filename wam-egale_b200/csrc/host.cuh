@@ -83,6 +83,12 @@ inline int make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t rows, uint64
   return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, ld, box_rows, 64);
 }
 
+// E4M3 operand: 128 bytes (= 128 elements) of K per box row.
+inline int make_tmap_e4m3(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols,
+                          uint64_t ld, uint32_t box_rows) {
+  return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols, ld, box_rows, 128);
+}
+
 struct DeviceInfo {
   int sms = 0;
 };

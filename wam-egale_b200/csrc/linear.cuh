@@ -7,7 +7,7 @@
 
 namespace wamb {
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool F8>
 inline int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p,
                           int sms, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
@@ -15,18 +15,19 @@ inline int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap* tb, const Ge
   int dev = 0;
   WAMB_CHECK_CUDA(cudaGetDevice(&dev));
   if (!configured[dev]) {
-    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES>,
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, F8>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     configured[dev] = true;
   }
   const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * (p.N / BN);
   const int grid = tiles < sms ? tiles : sms;
-  gemm_tc_kernel<BN, STAGES><<<grid, GEMM_THREADS, L::TOTAL, stream>>>(ta, tb[0], tb[1], tb[2], p);
+  gemm_tc_kernel<BN, STAGES, F8><<<grid, GEMM_THREADS, L::TOTAL, stream>>>(ta, tb[0], tb[1], tb[2], p);
   WAMB_CHECK_CUDA(cudaGetLastError());
   return WAMB_OK;
 }
 
 // Two-CTA launch: clusters of 2 along x, one cluster per pair of SMs.
+template <bool F8>
 inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p, int sms,
                         cudaStream_t stream) {
   static int resident[64] = {};  // co-resident clusters per device, 0 = not queried
@@ -44,17 +45,17 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (resident[dev] == 0) {
-    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<F8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Gemm2Smem::TOTAL));
     cfg.gridDim = dim3(sms, 1, 1);
     int n = 0;
-    WAMB_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel, &cfg));
+    WAMB_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<F8>, &cfg));
     resident[dev] = n > 0 ? n : 1;
   }
   const int tiles = ((p.M + 255) / 256) * (p.N / 256);
   const int pairs = tiles < resident[dev] ? tiles : resident[dev];
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel, ta, tb[0], tb[1], tb[2], p));
+  WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<F8>, ta, tb[0], tb[1], tb[2], p));
   return WAMB_OK;
 }
 
@@ -77,10 +78,13 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
-  WAMB_REQUIRE(a->k % GEMM_BK == 0, WAMB_ERR_SHAPE, "K=%d must be a multiple of 64", a->k);
+  WAMB_REQUIRE(a->a_is_fp8 == 0 || a->a_is_fp8 == 1, WAMB_ERR_ARG, "a_is_fp8 must be 0 or 1");
+  const bool f8 = a->a_is_fp8 == 1;
+  WAMB_REQUIRE(a->k % (f8 ? GEMM_BK8 : GEMM_BK) == 0, WAMB_ERR_SHAPE, "K=%d must be a multiple of %d",
+               a->k, f8 ? GEMM_BK8 : GEMM_BK);
   WAMB_REQUIRE(a->n_per_group % 64 == 0, WAMB_ERR_SHAPE, "N per group=%d must be a multiple of 64",
                a->n_per_group);
-  WAMB_REQUIRE(a->lda >= a->k && a->lda % 8 == 0, WAMB_ERR_ALIGN, "lda");
+  WAMB_REQUIRE(a->lda >= a->k && a->lda % (f8 ? 16 : 8) == 0, WAMB_ERR_ALIGN, "lda");
   const long long N = static_cast<long long>(a->groups) * a->n_per_group;
   WAMB_REQUIRE(a->ldo >= N && a->ldo % 8 == 0, WAMB_ERR_ALIGN, "ldo");
   WAMB_REQUIRE(a->out_is_f32 == 0 || a->out_is_f32 == 1, WAMB_ERR_ARG, "out_is_f32");
@@ -90,7 +94,10 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   for (int g = 0; g < a->groups; ++g) {
     WAMB_REQUIRE(a->weight[g] && aligned16(a->weight[g]), WAMB_ERR_ARG, "weight[%d]", g);
     WAMB_REQUIRE(!a->bias[g] || aligned16(a->bias[g]), WAMB_ERR_ALIGN, "bias[%d]", g);
+    if (f8)
+      WAMB_REQUIRE(a->w_scale[g] && aligned16(a->w_scale[g]), WAMB_ERR_ARG, "w_scale[%d]", g);
   }
+  if (f8) WAMB_REQUIRE(a->a_scale != nullptr, WAMB_ERR_ARG, "a_scale");
   WAMB_REQUIRE(a->epilogue >= 0 && a->epilogue <= 3, WAMB_ERR_ARG, "epilogue");
   if (a->epilogue == WAMB_EPI_RES || a->epilogue == WAMB_EPI_RES_GATE) {
     WAMB_REQUIRE(a->res && aligned16(a->res) && a->ldr >= N && a->ldr % 8 == 0, WAMB_ERR_ARG,
@@ -117,11 +124,12 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   const bool pair = a->m >= 512 && a->n_per_group % 256 == 0 && pair_tiles >= di.sms / 2;
   const int bn = pair ? 256 : choose_bn(a->m, static_cast<int>(N), a->n_per_group, di.sms);
   CUtensorMap ta, tb[3];
-  rc = make_tmap_bf16(&ta, a->a, a->m, a->k, a->lda, 128);
+  auto tmap = f8 ? make_tmap_e4m3 : make_tmap_bf16;
+  rc = tmap(&ta, a->a, a->m, a->k, a->lda, 128);
   if (rc) return rc;
   for (int g = 0; g < 3; ++g) {
     const int src = g < a->groups ? g : 0;
-    rc = make_tmap_bf16(&tb[g], a->weight[src], a->n_per_group, a->k, a->k, pair ? 128 : bn);
+    rc = tmap(&tb[g], a->weight[src], a->n_per_group, a->k, a->k, pair ? 128 : bn);
     if (rc) return rc;
   }
   GemmParams p{};
@@ -145,12 +153,20 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   p.rows_per_batch = a->rows_per_batch > 0 ? a->rows_per_batch : 1;
   p.gate_idx = a->gate_index;
   p.D = a->dim;
-  if (pair) return launch_gemm2(ta, tb, p, di.sms, stream);
-  switch (bn) {
-    case 256: return launch_gemm_bn<256, 4>(ta, tb, p, di.sms, stream);
-    case 128: return launch_gemm_bn<128, 6>(ta, tb, p, di.sms, stream);
-    default: return launch_gemm_bn<64, 8>(ta, tb, p, di.sms, stream);
+  if (f8) {
+    p.a_scale = a->a_scale;
+    for (int g = 0; g < 3; ++g) p.w_scale[g] = g < a->groups ? a->w_scale[g] : nullptr;
   }
+  auto launch = [&](auto f8c) {
+    constexpr bool F8 = decltype(f8c)::value;
+    if (pair) return launch_gemm2<F8>(ta, tb, p, di.sms, stream);
+    switch (bn) {
+      case 256: return launch_gemm_bn<256, 4, F8>(ta, tb, p, di.sms, stream);
+      case 128: return launch_gemm_bn<128, 6, F8>(ta, tb, p, di.sms, stream);
+      default: return launch_gemm_bn<64, 8, F8>(ta, tb, p, di.sms, stream);
+    }
+  };
+  return f8 ? launch(std::true_type{}) : launch(std::false_type{});
 }
 
 }  // namespace wamb

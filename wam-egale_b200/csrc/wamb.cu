@@ -38,7 +38,7 @@ extern "C" {
 
 const char* wamb_last_error(void) { return wamb::g_last_error.c_str(); }
 
-int wamb_abi_version(void) { return 100; }
+int wamb_abi_version(void) { return 101; }
 
 int wamb_device_status(void* stream, int* device_code) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -53,6 +53,20 @@ int wamb_device_status(void* stream, int* device_code) {
 
 int wamb_linear(const wamb_linear_args* args, void* stream) {
   return wamb::linear_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+int wamb_quantize_rows(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, int32_t k, void* out,
+                       int64_t ldo, float* scale, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(m >= 0 && k > 0 && k % 8 == 0, WAMB_ERR_SHAPE, "quantize: m >= 0, k %% 8 == 0");
+  WAMB_REQUIRE(x_is_f32 == 0 || x_is_f32 == 1, WAMB_ERR_ARG, "x_is_f32 must be 0 or 1");
+  WAMB_REQUIRE(ldx >= k && ldo >= k && ldx % 8 == 0 && ldo % 16 == 0, WAMB_ERR_ALIGN, "ldx / ldo");
+  WAMB_REQUIRE(x && out && scale && aligned16(x) && aligned16(out) && aligned16(scale), WAMB_ERR_ALIGN,
+               "null or misaligned pointer");
+  QuantParams p{};
+  p.x = x; p.ldx = ldx; p.x_f32 = x_is_f32; p.M = m; p.K = k;
+  p.out = static_cast<uint8_t*>(out); p.ldo = ldo; p.scale = scale;
+  return launch_quant(p, static_cast<cudaStream_t>(stream));
 }
 
 int wamb_attention(const wamb_attention_args* args, void* stream) {

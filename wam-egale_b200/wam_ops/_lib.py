@@ -27,6 +27,7 @@ class LinearArgs(ctypes.Structure):
         ("table", c_void_p), ("temb", c_void_p), ("temb_is_f32", c_int32),
         ("temb_len", c_int32), ("rows_per_batch", c_int32), ("gate_index", c_int32),
         ("dim", c_int32),
+        ("a_is_fp8", c_int32), ("a_scale", c_void_p), ("w_scale", c_void_p * 3),
     ]
 
 
@@ -70,19 +71,25 @@ class BlockArgs(ctypes.Structure):
         ("update", c_int32),
         ("out", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("fp8", c_int32), ("w8", c_void_p * 27), ("w8_scale", c_void_p * 27),
     ]
 
 
 # Workspace taps (enum wamb_tap).
 TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", "cross_k",
         "cross_v", "cross_attention", "residual2", "modulated3", "gelu", "kv_slots",
-        "kv_tiles", "kv_counts")
+        "kv_tiles", "kv_counts", "a8", "a8_scale")
+
+# Weight slots the FP8 path reads as E4M3 (self q/k/v/out, cross q/out, FFN).
+FP8_WEIGHTS = (3, 5, 7, 9, 13, 19, 23, 25)
+
+ABI_VERSION = 101
 
 # Every symbol include/wamb.h declares; tests check the library exports them.
 EXPORTED = (
     "wamb_last_error", "wamb_abi_version", "wamb_device_status", "wamb_linear",
     "wamb_attention", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
-    "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc",
+    "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc", "wamb_quantize_rows",
 )
 
 # Size of the fixed scratch array behind wamb_block_forward_noalloc.
@@ -115,6 +122,10 @@ def load():
     lib.wamb_block_forward.argtypes = [ctypes.POINTER(BlockArgs), c_void_p]
     lib.wamb_cross_kv.argtypes = [ctypes.POINTER(BlockArgs), c_void_p, c_void_p, c_void_p]
     lib.wamb_block_forward_noalloc.argtypes = [ctypes.POINTER(BlockArgs), c_void_p]
+    lib.wamb_quantize_rows.argtypes = [c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p, c_int64,
+                                       c_void_p, c_void_p]
+    if lib.wamb_abi_version() != ABI_VERSION:
+        raise WambError(f"{LIB_PATH} has ABI {lib.wamb_abi_version()}, expected {ABI_VERSION}: rebuild")
     _lib = lib
     return lib
 

@@ -76,10 +76,21 @@ def _check_weights(weights):
     return out
 
 
+def quantize_weights_fp8(weights):
+    """E4M3 copies of the eight step GEMM weights with per-output-channel
+    fp32 scales (wamb_quantize_rows on each [N, K] weight), indexed like the
+    27 reference parameters (None elsewhere)."""
+    from .ops import quantize_rows
+    w8, sc = [None] * 27, [None] * 27
+    for i in _lib.FP8_WEIGHTS:
+        w8[i], sc[i] = quantize_rows(weights[i])
+    return w8, sc
+
+
 class NativeBlock:
     """Bind the original parameter tensors; forward contains no Torch math ops."""
 
-    def __init__(self, block, fused_ffn1=False, mode="sequential"):
+    def __init__(self, block, fused_ffn1=False, mode="sequential", fp8=False):
         if mode not in ("sequential", "tiled", "persistent"):
             raise ValueError("mode must be sequential, tiled or persistent")
         self.mode = mode
@@ -92,6 +103,8 @@ class NativeBlock:
         self.ffn_dim = block.ffn.net[0].proj.weight.shape[0]
         if self.dim != self.heads * 128:
             raise ValueError("the B200 block supports head_dim 128 only")
+        self.fp8 = bool(fp8)
+        self.w8, self.w8_scale = quantize_weights_fp8(self.weights) if self.fp8 else (None, None)
 
     # --------------------------------------------------------------- args
     def make_args(self, hidden_states, encoder_hidden_states, temb, rotary_emb, cache,
@@ -161,6 +174,10 @@ class NativeBlock:
                 raise ValueError("invalid candidate_cache_rows for this KV cache")
             a.candidate_rows = r.data_ptr()
         a.update = int(update_cache)
+        if self.fp8:
+            a.fp8 = 1
+            for i in _lib.FP8_WEIGHTS:
+                a.w8[i], a.w8_scale[i] = self.w8[i].data_ptr(), self.w8_scale[i].data_ptr()
         if out.shape != x.shape or out.dtype not in (torch.bfloat16, torch.float32) or not out.is_contiguous():
             raise RuntimeError("out must be a contiguous bf16/fp32 tensor shaped like hidden_states")
         a.out = out.data_ptr()
@@ -201,11 +218,17 @@ class NativeBlock:
         M = B * Q
         C = a.context_batch * a.context_tokens
         shapes = {"qkv": (M, 3 * D), "gelu": (M, F), "cross_k": (C, D), "cross_v": (C, D)}
+        if a.fp8:
+            o8, os_ = offs[_lib.TAPS.index("a8")], offs[_lib.TAPS.index("a8_scale")]
+            result["a8"] = ws[o8:o8 + M * max(D, F)].clone()  # last quantized GEMM input, raw E4M3
+            result["a8_scale"] = ws[os_:os_ + 4 * M].view(torch.float32).clone()
         fp32 = ("residual1", "residual2")
         result = {}
         for i, name in enumerate(_lib.TAPS):
             o = offs[i]
             if o < 0:
+                continue
+            if name.startswith("a8"):
                 continue
             if name.startswith("kv_"):
                 n = {"kv_slots": Q, "kv_tiles": 2 * a.pool, "kv_counts": 2}[name]

@@ -17,23 +17,40 @@ def _bf16_2d(t, name):
 
 
 def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
-           table=None, temb=None, rows_per_batch=None, gate_index=0):
+           table=None, temb=None, rows_per_batch=None, gate_index=0, a_scale=None, w_scales=None):
     """out = epilogue(a @ cat(weights).T + cat(biases)) on the tcgen05 GEMM.
 
     `weights` is one [N, K] bf16 tensor or a list of up to three equally
     shaped ones whose outputs are concatenated along the columns (the QKV
     projection reads the three reference Linear weights in place).
+
+    FP8: with `a` and the weights float8_e4m3fn, `a_scale` ([M] fp32 row
+    scales) and `w_scales` (one [N] fp32 per weight) are required and the
+    product is a_scale[m] * w_scale[n] * (a8 @ w8.T) (see quantize_rows).
     """
     out_f32 = out is not None and out.dtype == torch.float32
     if isinstance(weights, torch.Tensor):
         weights = [weights]
     if biases is None or isinstance(biases, torch.Tensor):
         biases = [biases] * len(weights) if biases is None else [biases]
-    _bf16_2d(a, "a")
+    fp8 = a.dtype == torch.float8_e4m3fn
+    if isinstance(w_scales, torch.Tensor):
+        w_scales = [w_scales]
+    if fp8:
+        if a.dim() != 2 or a.stride(1) != 1 or not a.is_cuda:
+            raise ValueError("a must be a 2-D row-major CUDA tensor")
+        if a_scale is None or w_scales is None or len(w_scales) != len(weights):
+            raise ValueError("FP8 linear needs a_scale and one w_scale per weight")
+        for t in [a_scale, *w_scales]:
+            if t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError("FP8 scales must be contiguous fp32")
+    else:
+        _bf16_2d(a, "a")
+    wdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
     n_g, k = weights[0].shape
     for w in weights:
-        if w.shape != (n_g, k) or not w.is_contiguous() or w.dtype != torch.bfloat16:
-            raise ValueError("weights must be contiguous bf16 [N, K] of equal shape")
+        if w.shape != (n_g, k) or not w.is_contiguous() or w.dtype != wdt:
+            raise ValueError(f"weights must be contiguous {wdt} [N, K] of equal shape")
     if a.shape[1] != k:
         raise ValueError("a and weight K differ")
     m = a.shape[0]
@@ -54,6 +71,11 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
     args.ldo = out.stride(0)
     args.out_is_f32 = int(out_f32)
     args.epilogue = epilogue
+    if fp8:
+        args.a_is_fp8 = 1
+        args.a_scale = a_scale.data_ptr()
+        for i, ws in enumerate(w_scales):
+            args.w_scale[i] = ws.data_ptr()
     if res is not None:
         args.res = res.data_ptr()
         args.ldr = res.stride(0)
@@ -68,6 +90,24 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
         args.dim = n
     _lib.check(_lib.load().wamb_linear(args, _lib.stream_ptr()))
     return out
+
+
+def quantize_rows(x, out=None, scale=None):
+    """Row-wise E4M3 quantization on the GPU (wamb_quantize_rows): returns
+    (q [M, K] float8_e4m3fn, scale [M] fp32) with scale = amax / 448 and
+    q = e4m3(x * 448 / amax), amax = max(max |x[r]|, 1e-20). Used for
+    activations (per token) and for weights (per output channel)."""
+    if x.dim() != 2 or x.stride(1) != 1 or x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda:
+        raise ValueError("x must be a 2-D row-major bf16/fp32 CUDA tensor")
+    m, k = x.shape
+    if out is None:
+        out = torch.empty(m, k, device=x.device, dtype=torch.float8_e4m3fn)
+    if scale is None:
+        scale = torch.empty(m, device=x.device, dtype=torch.float32)
+    _lib.check(_lib.load().wamb_quantize_rows(
+        x.data_ptr(), x.stride(0), int(x.dtype == torch.float32), m, k, out.data_ptr(), out.stride(0),
+        scale.data_ptr(), _lib.stream_ptr()))
+    return out, scale
 
 
 def attention(q, k0, v0, *, heads, q_rows, q_col=0, k0_col=0, v0_col=0, src0_batch_stride,

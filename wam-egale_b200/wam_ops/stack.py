@@ -17,8 +17,11 @@ from .whole_layer import WholeLayerBlock
 
 
 class NativeStack:
-    def __init__(self, blocks):
-        self.layers = [WholeLayerBlock(b) for b in blocks]
+    def __init__(self, blocks, fp8=False):
+        """fp8=True runs the step's GEMMs on E4M3 weights (per-output-channel
+        scales) and per-token E4M3 activations (the block's fp8 mode)."""
+        self.fp8 = bool(fp8)
+        self.layers = [WholeLayerBlock(b, fp8=fp8) for b in blocks]
         self.graph = None
         self._static = None
 
@@ -92,8 +95,9 @@ class NativeStack:
         """Kernel launches of one step (the count bench.py reports): per layer
         LN1, QKV, RMS+RoPE, attention, O, LN2, cross-Q, RMS, cross attention,
         cross-O, LN3, FFN1, FFN2 = 13, + KV layout with a cache, + 3 when the
-        cross K/V is computed per call."""
-        per = 13 + (1 if with_cache else 0) + (0 if cross_prepared else 3)
+        cross K/V is computed per call, + 3 row-quantize passes (self and cross
+        attention output, GELU output) in fp8 mode."""
+        per = 13 + (1 if with_cache else 0) + (0 if cross_prepared else 3) + (3 if self.fp8 else 0)
         return per * len(self.layers)
 
 

@@ -16,9 +16,9 @@ from .native import NativeBlock
 class WholeLayerBlock:
     production_admitted = True
 
-    def __init__(self, block):
+    def __init__(self, block, fp8=False):
         self.block = block
-        self.native = NativeBlock(block)
+        self.native = NativeBlock(block, fp8=fp8)
         self.context_rows = self.context_roots = None
         self.context_kv = []
 
