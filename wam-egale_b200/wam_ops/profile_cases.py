@@ -1,11 +1,12 @@
 """Small single-kernel cases for ncu captures (inputs larger than L2, a few
 hundred MB on the device, 3 warm-up launches then `--launches` more).
 
-  python wam-egale_b200/wam_ops/profile_cases.py ffn1 [--m 2048] [--launches 1]
+  python wam-egale_b200/wam_ops/profile_cases.py ffn1 [--m 2048] [--launches 1] [--fp8]
   python wam-egale_b200/wam_ops/profile_cases.py attention [--q 880] [--pool 4400] [--batch 8]
   python wam-egale_b200/wam_ops/profile_cases.py rms | ln
 
-ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (cfg2 weights)
+ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (cfg2 weights); --fp8: E4M3
+           operands (quantized once before the timed launches)
 attention  self attention of `batch` cfg2 rollouts over 4400-key pools (24 heads)
 rms        RMSNorm + RoPE of the q/k/v projection output, K/V into the pool
 ln         LayerNorm + adaLN modulation
@@ -29,6 +30,7 @@ def main():
     ap.add_argument("--pool", type=int, default=4400)
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--launches", type=int, default=1)
+    ap.add_argument("--fp8", action="store_true")
     a = ap.parse_args()
     torch.set_grad_enabled(False)
     dev = torch.device("cuda", 0)
@@ -39,7 +41,13 @@ def main():
         w = (torch.randn(F, D, generator=g, device=dev) * 0.02).bfloat16()
         b = torch.zeros(F, device=dev, dtype=torch.bfloat16)
         out = torch.empty(a.m, F, device=dev, dtype=torch.bfloat16)
-        run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_GELU, out=out)  # noqa: E731
+        if a.fp8:
+            x8, sx = ops.quantize_rows(x)
+            w8, sw = ops.quantize_rows(w)
+            run = lambda: ops.linear(x8, w8, b, epilogue=_lib.EPI_GELU, out=out,  # noqa: E731
+                                     a_scale=sx, w_scales=sw)
+        else:
+            run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_GELU, out=out)  # noqa: E731
     elif a.case == "attention":
         q = torch.randn(a.batch * a.q, D, generator=g, device=dev).bfloat16()
         kp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
