@@ -4,19 +4,21 @@
 //
 // One CTA per (256 query rows = two 128-row tiles A and B, head, batch row);
 // both tiles share every K/V tile that is loaded. 320 threads:
-//   warps 0..7  softmax, on tile A(j) then tile B(j), A(j+1), ...: two
-//               threads per query row (warps w and w+4 share the TMEM lanes
-//               of quarter w), each handling 64 of the 128 keys and 64 of the
-//               128 O columns; the partial row maxima are exchanged through
-//               SMEM. S is read from TMEM, P written back to TMEM as packed
-//               bf16 over the S columns, O rescaled in TMEM only when the row
-//               max grows by more than 2^8 (the final O / l uses the same
-//               stale max, so the result is exact). Three quarters of the
-//               exp2s run on the MUFU (ex2.approx), one quarter as a cubic on
-//               the FMA pipe with packed f32x2 arithmetic.
+//   warps 0..7  softmax: warps 0-3 on tile A, warps 4-7 on tile B, both
+//               tiles at the same time, one thread per query row (its TMEM
+//               lane), all 128 keys of the tile, so no cross-thread
+//               reduction is needed. S is read from TMEM, P written back to
+//               TMEM as packed bf16 over the S columns, O rescaled in TMEM
+//               only when the row max grows by more than 2^8 (the final
+//               O / l uses the same stale max, so the result is exact).
+//               Three quarters of the exp2s run on the MUFU (ex2.approx),
+//               one quarter as a cubic on the FMA pipe with packed f32x2
+//               arithmetic. Each warp signals the MMA issuer with one
+//               arrival (a shared-memory barrier op per thread would queue
+//               behind the tensor core's operand reads).
 //   warp 8      TMA producer: Q once, then K_0, V_0, K_1, V_1, ... through
 //               one 5-slot ring (the order both are consumed and released in)
-//   warp 9      TMEM owner + MMA issuer, in the order
+//   warp 9      TMEM owner; its lane 0 issues the MMAs, in the order
 //               PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): while one tile's
 //               softmax runs the tensor core works on the other tile.
 //               S = Q K^T reads both operands from SMEM; O += P V reads P
@@ -40,6 +42,8 @@
 namespace wamb {
 
 constexpr int ATT_THREADS = 320;
+constexpr int ATT_PRODUCER_WARP = 8;
+constexpr int ATT_MMA_WARP = 9;
 constexpr uint32_t ATT_TILE_BYTES = 128 * 128 * 2;  // 128 rows x 128 bf16
 constexpr uint32_t ATT_ATOM = 128 * 128;            // one 64-column half: 128 rows x 128 B
 constexpr float ATT_RESCALE_LOG2 = 8.f;             // rescale O only when the max grows > 2^8
@@ -127,10 +131,9 @@ struct AttnSmem {
   static constexpr uint32_t Q_OFF = 0;                                    // Q_A, Q_B
   static constexpr uint32_t RING_OFF = Q_OFF + 2 * ATT_TILE_BYTES;        // K/V ring
   static constexpr uint32_t BAR_OFF = RING_OFF + ATT_SLOTS * ATT_TILE_BYTES;
-  // q_full, full[5], empty[5], s_full[2], p_full[2], o_done, drain, pair[4]
-  static constexpr uint32_t NBARS = 21;
-  static constexpr uint32_t RED_OFF = BAR_OFF + NBARS * 8 + 16;   // float [2 halves][128 rows]
-  static constexpr uint32_t TOTAL = 1024 + RED_OFF + 2 * 128 * 4;
+  // q_full, full[5], empty[5], s_full[2], p_full[2], o_done, drain
+  static constexpr uint32_t NBARS = 17;
+  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
   static_assert(TOTAL <= 232448, "attention shared memory exceeds 227 KB");
 };
 
@@ -183,7 +186,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t p_full = bar0 + 104;     // [2] by query tile
   const uint32_t o_done = bar0 + 120;
   const uint32_t drain = bar0 + 128;
-  const uint32_t pair_bar = bar0 + 136;   // [4] by TMEM lane quarter, 64 arrivals
   // Load L (K_j: L = 2j, V_j: L = 2j+1) lives in slot L % 5; its phase is (L / 5) & 1.
   auto slot_addr = [&](int L) { return sRing + (L % ATT_SLOTS) * ATT_TILE_BYTES; };
   auto slot_full = [&](int L) { return full + 8 * (L % ATT_SLOTS); };
@@ -208,15 +210,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + 8 * i, 1);
-      mbar_init(p_full + 8 * i, 256);
+      mbar_init(p_full + 8 * i, 4);   // one arrival per softmax warp of the tile
     }
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(pair_bar + 8 * i, 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == ATT_MMA_WARP) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == ATT_PRODUCER_WARP) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
       const int qrow = b * p.q_rows + q0;
@@ -264,14 +265,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       for (int L = max(0, issued - ATT_SLOTS); L < issued; ++L)
         mbar_wait_teardown(slot_full(L), slot_phase(L));
     }
-  } else if (warp == 9) {
-    // --------------------------------------------------------- MMA issuer
+  } else if (warp == ATT_MMA_WARP) {
+   if (lane == 0) {
+    // ------------------------------------------------ MMA issuer (lane 0)
     constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0);
     constexpr uint32_t IDESC_O = idesc_bf16(128, 128, 1);
     const int ntq = has_b ? 2 : 1;
     // S_t = Q_t K_j^T (ring load 2j) into TMEM columns [t*128, t*128+128).
     auto issue_s = [&](int t, int j) {
-      if (lane == 0) {
+      {
         const uint32_t qb = sQ + t * ATT_TILE_BYTES;
         const uint32_t kb = slot_addr(2 * j);
 #pragma unroll
@@ -285,7 +287,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     };
     // O_t += P_t V_j (ring load 2j+1); P_t is packed bf16 in TMEM columns [t*128, t*128+64).
     auto issue_pv = [&](int t, int j, int ksteps, bool acc) {
-      if (lane == 0) {
+      {
         const uint32_t vb = slot_addr(2 * j + 1);
         for (int kk = 0; kk < ksteps; ++kk)
           umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
@@ -298,9 +300,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < ntq; ++t) issue_s(t, 0);
-        if (lane == 0) umma_commit(slot_empty(0));
+        umma_commit(slot_empty(0));
       }
-      __syncwarp();
     }
     for (int j = 0; ok && j < n; ++j) {
       const KvTile tl = att_tile(p, j, n0, b);
@@ -310,13 +311,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         // Zero V rows [len, 16*ksteps) in both 64-column halves.
         uint8_t* vt = smem + L::RING_OFF + ((2 * j + 1) % ATT_SLOTS) * ATT_TILE_BYTES;
         const int r0 = tl.len, r1 = ksteps * 16;
-        for (int i = lane; i < (r1 - r0) * 16; i += 32) {
+        for (int i = 0; i < (r1 - r0) * 16; ++i) {
           const int r = r0 + (i >> 4), c = i & 15;
           uint8_t* dst = vt + (c >> 3) * ATT_ATOM + r * 128 + (c & 7) * 16;
           *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async();
-        __syncwarp();
       }
       const bool next = j + 1 < n;
       bool knext = false;
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         issue_pv(t, j, ksteps, j > 0);
-        if (t == ntq - 1 && lane == 0) umma_commit(slot_empty(2 * j + 1));
+        if (t == ntq - 1) umma_commit(slot_empty(2 * j + 1));
         if (next) {
           if (!knext) {
             if (!mbar_wait(slot_full(2 * j + 2), slot_phase(2 * j + 2), abort_flag)) { ok = false; break; }
@@ -333,126 +333,112 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           }
           issue_s(t, j + 1);
         }
-        __syncwarp();
       }
-      if (ok && next && lane == 0) umma_commit(slot_empty(2 * j + 2));
-      __syncwarp();
+      if (ok && next) umma_commit(slot_empty(2 * j + 2));
     }
-    if (lane == 0) {
-      umma_commit(o_done);
-      umma_commit(drain);
-      mbar_wait_teardown(drain, 0);
-    }
+    umma_commit(o_done);
+    umma_commit(drain);
+    mbar_wait_teardown(drain, 0);
+   }
     __syncwarp();
   } else {
     // -------------------------------------------------- softmax / epilogue
+    const int t = warp >> 2;          // query tile of this warp
     const int wq = warp & 3;          // TMEM lane quarter
-    const int hf = warp >> 2;         // which 64 keys / 64 O columns of the row
     const int r = wq * 32 + lane;     // query row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    float* red = reinterpret_cast<float*>(smem + L::RED_OFF);   // [2][128]
-    // The two threads of a row (warps wq and wq + 4) meet at mbarrier pair[wq]
-    // (64 arrivals per phase; bounded wait like every other wait here).
-    uint32_t pair_phase = 0;
-    auto pair_sync = [&]() {
-      mbar_arrive(pair_bar + 8 * wq);
-      mbar_wait(pair_bar + 8 * wq, pair_phase, abort_flag);
-      pair_phase ^= 1;
-    };
-    auto pair_exchange = [&](float v) {
-      red[hf * 128 + r] = v;
-      pair_sync();
-      const float o = red[(hf ^ 1) * 128 + r];
-      pair_sync();
-      return o;
-    };
-    const int ntq = has_b ? 2 : 1;
-    float m_used[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    const bool active = t == 0 || has_b;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; ok && j < n; ++j) {
+    for (int j = 0; active && ok && j < n; ++j) {
       const int len = att_tile(p, j, n0, b).len;
-      for (int t = 0; t < ntq; ++t) {
-        if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t s_col = t * 128 + hf * 64;
-        float s[64];
+      if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float s[128];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float t32[32];
-          tmem_ld32(tmem + lane_base + s_col + c * 32, t32);
+      for (int c = 0; c < 4; ++c) {
+        float t32[32];
+        tmem_ld32(tmem + lane_base + t * 128 + c * 32, t32);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = t32[i];
-        }
-        tmem_wait_ld();
-        if (len < 128) {
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t32[i];
+      }
+      tmem_wait_ld();
+      if (len < 128) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (hf * 64 + i >= len) s[i] = -INFINITY;
-        }
-        float mx = -INFINITY;
+        for (int i = 0; i < 128; ++i)
+          if (i >= len) s[i] = -INFINITY;
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 64; i += 2) mx = fmax3(mx, s[i], s[i + 1]);
-        mx = fmaxf(mx, pair_exchange(mx)) * p.scale_log2;
-        // Keep the stale max unless the new one exceeds it by more than 2^8.
-        const bool grow = mx > m_used[t] + ATT_RESCALE_LOG2;
-        const float m_new = grow ? mx : m_used[t];
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = grow ? exp2f(m_used[t] - m_use) : 1.f;
-        const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
-        const uint64_t neg_m2 = f2(-m_use, -m_use);
-        uint64_t sum2 = f2(0.f, 0.f);
-        uint32_t pk[32];
-        // keys 0..47 of this half: exp2 on the MUFU; keys 48..63: the cubic
+      for (int i = 0; i < 64; i += 2) {
+        mx0 = fmax3(mx0, s[i], s[i + 1]);
+        mx1 = fmax3(mx1, s[64 + i], s[64 + i + 1]);
+      }
+      const float mx = fmaxf(mx0, mx1) * p.scale_log2;
+      // Keep the stale max unless the new one exceeds it by more than 2^8.
+      const bool grow = mx > m_used + ATT_RESCALE_LOG2;
+      const float m_new = grow ? mx : m_used;
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = grow ? exp2f(m_used - m_use) : 1.f;
+      const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
+      const uint64_t neg_m2 = f2(-m_use, -m_use);
+      uint64_t sum2 = f2(0.f, 0.f);
+      // Four chunks of 32 keys; in each, keys 0..23 take the MUFU exp2 and
+      // keys 24..31 the cubic. P of keys [32 c, +32) -> packed TMEM columns
+      // [t*128 + 16 c, +16).
 #pragma unroll
-        for (int i = 0; i < 24; ++i) {
-          const float2 x = f2_split(ffma2(f2(s[2 * i], s[2 * i + 1]), scale2, neg_m2));
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 12; ++i) {
+          const int k = 32 * c + 2 * i;
+          const float2 x = f2_split(ffma2(f2(s[k], s[k + 1]), scale2, neg_m2));
           const float a = ex2_mufu(x.x), bb = ex2_mufu(x.y);
           sum2 = fadd2(sum2, f2(a, bb));
           pk[i] = pack_bf16(a, bb);
         }
 #pragma unroll
-        for (int i = 24; i < 32; ++i) {
-          const uint64_t e = ex2_poly2(ffma2(f2(s[2 * i], s[2 * i + 1]), scale2, neg_m2));
+        for (int i = 12; i < 16; ++i) {
+          const int k = 32 * c + 2 * i;
+          const uint64_t e = ex2_poly2(ffma2(f2(s[k], s[k + 1]), scale2, neg_m2));
           sum2 = fadd2(sum2, e);
           const float2 ev = f2_split(e);
           pk[i] = pack_bf16(ev.x, ev.y);
         }
-        // P of keys [64 hf, 64 hf + 64) -> packed TMEM columns [t*128 + 32 hf, +32)
-        tmem_st32u(tmem + lane_base + t * 128 + hf * 32, pk);
-        const float2 sv = f2_split(sum2);
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {
-          // O_t is stable: S_t(j) was issued after PV_t(j-1) and has completed.
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            float o[32];
-            const uint32_t oc = 256 + t * 128 + hf * 64 + c * 32;
-            tmem_ld32(tmem + lane_base + oc, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tmem + lane_base + oc, o);
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(p_full + 8 * t);
-        l[t] = l[t] * alpha + (sv.x + sv.y);
-        m_used[t] = m_new;
+        tmem_st16u(tmem + lane_base + t * 128 + c * 16, pk);
       }
+      const float2 sv = f2_split(sum2);
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O_t is stable: S_t(j) was issued after PV_t(j-1) and has completed.
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          const uint32_t oc = 256 + t * 128 + c * 32;
+          tmem_ld32(tmem + lane_base + oc, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tmem + lane_base + oc, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full + 8 * t);
+      l = l * alpha + (sv.x + sv.y);
+      m_used = m_new;
     }
-    if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
-    tc_fence_after();
-    for (int t = 0; t < ntq; ++t) {
-      const float lt = l[t] + pair_exchange(l[t]);
+    if (active) {
+      if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
+      tc_fence_after();
       const int qr = q0 + t * 128 + r;
       const bool store = qr < p.q_rows;
-      __nv_bfloat16* orow =
-          p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128 + hf * 64;
-      const float inv = (ok && n > 0 && lt > 0.f) ? 1.f / lt : 0.f;
+      __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
+      const float inv = (ok && n > 0 && l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float o[32];
-        tmem_ld32(tmem + lane_base + 256 + t * 128 + hf * 64 + c * 32, o);
+        tmem_ld32(tmem + lane_base + 256 + t * 128 + c * 32, o);
         tmem_wait_ld();
         if (store) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
@@ -472,7 +458,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == ATT_MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -115,7 +115,8 @@ inline int launch_ln(const LnParams& p, cudaStream_t s) {
   WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
   const int threads = p.D / (8 * vpt);
   return dispatch_vpt(vpt, [&](auto v) {
-    ln_kernel<decltype(v)::value><<<p.M, threads, 0, s>>>(p);
+    constexpr int R = ln_rows(decltype(v)::value);
+    ln_kernel<decltype(v)::value><<<(p.M + R - 1) / R, threads, 0, s>>>(p);
     WAMB_CHECK_CUDA(cudaGetLastError());
     return static_cast<int>(WAMB_OK);
   });

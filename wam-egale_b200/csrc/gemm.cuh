@@ -99,8 +99,29 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
     if (p.temb_f32) gate_f32 = static_cast<const float*>(p.temb) + off;
     else gate_bf = static_cast<const __nv_bfloat16*>(p.temb) + off;
   }
+  // Residual rows are fetched one chunk ahead (raw 128-bit words: 8 for
+  // fp32, 4 for bf16), so their DRAM latency overlaps the previous chunk.
+  const bool has_res = valid && (p.epi == EPI_RES || p.epi == EPI_RES_GATE);
+  uint4 rnext[8];
+  auto fetch_res = [&](int c) {
+    const int col = n0 + c * 32;
+    if (p.res_f32) {
+      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const float*>(p.res) + row * p.ldr + col);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) rnext[j] = __ldg(rp + j);
+    } else {
+      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) rnext[j] = __ldg(rp + j);
+    }
+  };
+  if (has_res) fetch_res(c0);
 #pragma unroll 1
   for (int c = c0; c < c1; ++c) {
+    uint4 rcur[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rcur[j] = rnext[j];
+    if (has_res && c + 1 < c1) fetch_res(c + 1);
     float v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
@@ -155,22 +176,17 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
         }
       }
       if (p.res_f32) {
-        const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(p.res) +
-                                                           row * p.ldr + col);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 f = __ldg(rp + j);
-          v[4 * j] += f.x;
-          v[4 * j + 1] += f.y;
-          v[4 * j + 2] += f.z;
-          v[4 * j + 3] += f.w;
+          v[4 * j] += __uint_as_float(rcur[j].x);
+          v[4 * j + 1] += __uint_as_float(rcur[j].y);
+          v[4 * j + 2] += __uint_as_float(rcur[j].z);
+          v[4 * j + 3] += __uint_as_float(rcur[j].w);
         }
       } else {
-        const uint4* rp = reinterpret_cast<const uint4*>(
-            static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint4 w = __ldg(rp + j);
+          const uint4 w = rcur[j];
           const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
@@ -234,7 +250,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, 32 * GEMM_EPI_WARPS);
+      mbar_init(tempty0 + 8 * a, GEMM_EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -333,7 +349,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                          m_blk * GEMM_BM + row_in_tile, n_blk * BN, half * (BN / 64),
                          (half + 1) * (BN / 64));
       tc_fence_before();
-      mbar_arrive(tempty0 + 8 * acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
     }
   }
 

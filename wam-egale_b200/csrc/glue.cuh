@@ -84,108 +84,152 @@ struct LnParams {
   int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
 };
 
+// Rows per CTA of ln_kernel: several rows share one load of the modulation
+// (or gamma / beta) vectors and one pair of barriers per reduction.
+__host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 2 ? 4 : (vpt <= 4 ? 2 : 1); }
+
 template <int VPT>
 __global__ void ln_kernel(const LnParams p) {
-  constexpr int MAXW = 32;
-  __shared__ float red[MAXW];
-  const int row = blockIdx.x;
+  constexpr int R = ln_rows(VPT);
+  __shared__ float red[32 * R];
+  const int row0 = blockIdx.x * R;
   const int nthr = blockDim.x;
   const int nw = nthr >> 5;
-  float v[VPT][8];
-  float s = 0.f;
+  // All R rows are loaded up front (R * VPT * 16 B in flight per thread).
+  float v[R][VPT][8];
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const long long off = static_cast<long long>(row) * p.ldx + (i * nthr + threadIdx.x) * 8;
-    if (p.x_f32) load8f(static_cast<const float*>(p.x) + off, v[i]);
-    else load8(static_cast<const __nv_bfloat16*>(p.x) + off, v[i]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s += v[i][j];
-  }
-  // Generic block reductions (number of warps known only at run time).
-  auto reduce = [&](float a) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
-    __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t += red[i];
-    return t;
-  };
-  auto reduce_max = [&](float a) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
-    __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
-    return t;
-  };
-  // Row output: bf16, or E4M3 with the row scale amax / 448 (quant_rows_kernel rule).
-  auto emit = [&](float (&y)[VPT][8]) {
-    if (p.out8 == nullptr) {
-      __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ldo;
-#pragma unroll
-      for (int i = 0; i < VPT; ++i) store8(orow + (i * nthr + threadIdx.x) * 8, y[i]);
-      return;
-    }
-    float am = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPT; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(y[i][j]));
-    const float amax = fmaxf(reduce_max(am), 1e-20f);
-    const float inv = 448.f / amax;
-    if (threadIdx.x == 0) p.out_scale[row] = amax / 448.f;
-    uint8_t* orow = p.out8 + static_cast<long long>(row) * p.ldo;
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r < p.M ? row0 + r : p.M - 1;  // tail rows: recompute the last row, no store
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      float t[8];
+      const long long off = static_cast<long long>(row) * p.ldx + (i * nthr + threadIdx.x) * 8;
+      if (p.x_f32) load8f(static_cast<const float*>(p.x) + off, v[r][i]);
+      else load8(static_cast<const __nv_bfloat16*>(p.x) + off, v[r][i]);
+    }
+  }
+  // Block reductions of R values at once (number of warps known only at run time).
+  auto reduce = [&](float (&a)[R], bool is_max) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) t[j] = y[i][j] * inv;
-      *reinterpret_cast<uint2*>(orow + (i * nthr + threadIdx.x) * 8) = pack_e4m3x8(t);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float t = __shfl_xor_sync(0xffffffffu, a[r], o);
+        a[r] = is_max ? fmaxf(a[r], t) : a[r] + t;
+      }
+    __syncthreads();  // protect `red` from the previous use
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int r = 0; r < R; ++r) red[(threadIdx.x >> 5) * R + r] = a[r];
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float t = is_max ? 0.f : 0.f;
+      for (int w = 0; w < nw; ++w) t = is_max ? fmaxf(t, red[w * R + r]) : t + red[w * R + r];
+      a[r] = t;
+    }
+  };
+  // Row output: bf16, or E4M3 with the row scale amax / 448 (quant_rows_kernel rule).
+  auto emit = [&]() {
+    if (p.out8 == nullptr) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (row0 + r >= p.M) continue;
+        __nv_bfloat16* orow = p.out + static_cast<long long>(row0 + r) * p.ldo;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) store8(orow + (i * nthr + threadIdx.x) * 8, v[r][i]);
+      }
+      return;
+    }
+    float am[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      am[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) am[r] = fmaxf(am[r], fabsf(v[r][i][j]));
+    }
+    reduce(am, true);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (row0 + r >= p.M) continue;
+      const float amax = fmaxf(am[r], 1e-20f);
+      const float inv = 448.f / amax;
+      if (threadIdx.x == 0) p.out_scale[row0 + r] = amax / 448.f;
+      uint8_t* orow = p.out8 + static_cast<long long>(row0 + r) * p.ldo;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = v[r][i][j] * inv;
+        *reinterpret_cast<uint2*>(orow + (i * nthr + threadIdx.x) * 8) = pack_e4m3x8(t);
+      }
     }
   };
   if (p.affine == 2) {
-    emit(v);
+    emit();
     return;
   }
-  const float mean = reduce(s) / p.D;
-  float q = 0.f;
+  float mean[R], var[R];
 #pragma unroll
-  for (int i = 0; i < VPT; ++i)
+  for (int r = 0; r < R; ++r) {
+    mean[r] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float d = v[i][j] - mean;
-      q += d * d;
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mean[r] += v[r][i][j];
+  }
+  reduce(mean, false);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    mean[r] /= p.D;
+    var[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[r][i][j] - mean[r];
+        var[r] += d * d;
+      }
+  }
+  reduce(var, false);
+  // Per-column multiplier / offset: gamma / beta (affine), or 1 + scale /
+  // shift of the row's (batch, token) modulation, reloaded only when it
+  // changes between consecutive rows.
+  long long key[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    key[r] = 0;
+    if (p.affine == 0) {
+      const int row = row0 + r < p.M ? row0 + r : p.M - 1;
+      const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
+      const long long l = p.temb_L == 1 ? 0 : tok;
+      key[r] = (static_cast<long long>(b) * p.temb_L + l) * 6 * p.D;  // temb offset of (b, l)
     }
-  const float rstd = rsqrtf(reduce(q) / p.D + p.eps);
-  long long temb_off = 0;
-  if (p.affine == 0) {
-    const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
-    const long long l = p.temb_L == 1 ? 0 : tok;
-    temb_off = (static_cast<long long>(b) * p.temb_L + l) * 6 * p.D;
   }
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int col = (i * nthr + threadIdx.x) * 8;
-    float a[8], b[8], y[8];
-    if (p.affine) {
-      load8f(p.gamma + col, a);
-      load8f(p.beta + col, b);
+    float mul[8], add[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = (v[i][j] - mean) * rstd * a[j] + b[j];
-    } else {
-      load_mod8(p.table, p.temb, p.temb_f32, temb_off, p.scale_idx, p.D, col, a);
-      load_mod8(p.table, p.temb, p.temb_f32, temb_off, p.shift_idx, p.D, col, b);
+    for (int r = 0; r < R; ++r) {
+      if (r == 0 || key[r] != key[r - 1]) {
+        if (p.affine) {
+          load8f(p.gamma + col, mul);
+          load8f(p.beta + col, add);
+        } else {
+          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.scale_idx, p.D, col, mul);
+          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.shift_idx, p.D, col, add);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = (v[i][j] - mean) * rstd * (1.f + a[j]) + b[j];
+          for (int j = 0; j < 8; ++j) mul[j] += 1.f;
+        }
+      }
+      const float rstd = rsqrtf(var[r] / p.D + p.eps);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[r][i][j] = (v[r][i][j] - mean[r]) * rstd * mul[j] + add[j];
     }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[i][j] = y[j];
   }
-  emit(v);
+  emit();
 }
 
 // --------------------------------------------------- row E4M3 quantization
