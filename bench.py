@@ -365,6 +365,90 @@ def run_native(args):
     return 0
 
 
+def run_verify(args):
+    """--workload cfg3: one 30-layer speculative-verify step on 1 GPU: 4
+    candidate chunks x 32 action tokens attending to a read-only 3520-token
+    history (candidate_cache_rows = [0, 0, 0, 0]) plus their own K/V, 512
+    prepared context tokens, per-token temb. HBM-bound (weight streaming):
+    the roofline line is bytes / time against the measured copy bandwidth."""
+    from wam_ops import _lib, configs
+    from wam_ops.stack import NativeStack
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cfg = configs.PRESETS["cfg3"]
+    B, Q, D, F = cfg.candidates, cfg.tokens, cfg.dim, cfg.ffn
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    torch.set_grad_enabled(False)
+    blocks = configs.build_blocks(cfg, dev, seed=4321)
+    configs.fill_history(blocks, cfg, dev, gen, pool_batch=1)
+    stack = NativeStack(blocks, fp8=args.fp8)
+    ctx = torch.randn(1, cfg.context, D, generator=gen, device=dev).bfloat16()
+    stack.prepare_context(ctx)
+    x = torch.randn(B, Q, D, generator=gen, device=dev).bfloat16()
+    temb = configs.make_temb(cfg, B, dev, gen, per_token=Q)
+    rope = configs.chunk_rope(cfg, f_shift=cfg.history_chunks).to(dev)
+    rows = torch.zeros(B, dtype=torch.int64, device=dev)
+    static = stack.capture(x, ctx, temb, rope, candidate_cache_rows=rows, warmup=1)
+    for _ in range(args.warmup):
+        stack.replay()
+    torch.cuda.synchronize()
+    if _lib.device_status() != 0:
+        raise RuntimeError("device error during warm-up")
+    clocks = Clocks(0)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    time.sleep(0.3)
+    e0.record(stream)
+    for _ in range(args.steps):
+        stack.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    hx, ht = x.cpu().pin_memory(), temb.cpu().pin_memory()
+    hout = torch.empty(B, Q, D, dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        static["x"].copy_(hx, non_blocking=True)
+        static["temb"].copy_(ht, non_blocking=True)
+        stack.replay()
+        hout.copy_(static["out"], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    # Algorithmic bytes of one step: every GEMM weight once (self q/k/v/out,
+    # cross q/out, FFN), the visible history K/V once, the prepared cross K/V.
+    wbytes = 1 if args.fp8 else 2
+    hist = cfg.history_chunks * configs.PRESETS["cfg2"].tokens
+    per_layer = (6 * D * D + 2 * D * F) * wbytes + hist * D * 2 * 2 + cfg.context * D * 2 * 2
+    step_bytes = per_layer * cfg.layers
+    pk, pk_kind = peaks()
+    achieved = step_bytes / (ms / 1000.0) / 1e9
+    line = {"metric": "verify_steps_per_s", "value": 1000.0 / ms, "unit": "verify-steps/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8-e4m3 GEMMs, bf16 attention" if args.fp8 else "bf16",
+            "data": "synthetic (seeded weights N(0,0.02), random unit-scale KV history)",
+            "config": {"workload": "cfg3: 30-layer verify of 4 candidates x 32 action tokens over a "
+                                   "read-only 3520-token history, 512 context tokens",
+                       "global_batch": B, "seq_len": Q, "kv_history": hist, "context": cfg.context,
+                       "l2": "inputs larger than L2 (weights streamed every step)"},
+            "roofline": {"kernel": "whole step (GEMM weight streaming dominates)", "bound": "hbm",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                         "peak_source": f"{pk_kind} HBM copy", "algorithmic_bytes_per_step": step_bytes},
+            "e2e": {"value": 1000.0 / ms_e2e, "unit": "verify-steps/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": hx.numel() * 2 + ht.numel() * 4,
+                    "d2h_bytes_per_step": hout.numel() * 2},
+            "gpu_launches": stack.launches_per_step(with_cache=True) * args.steps,
+            "clocks": clk, "device_error": _lib.device_status()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def stack_flops(cfg, split=False):
     """Algorithmic FLOPs of one 30-layer step for ONE rollout: the six
     projections, the two FFN GEMMs and the QK^T / PV products of both
@@ -389,11 +473,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 GEMMs (the FP8 weight path); default is the bf16 drop-in")
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg3"],
+                    help="cfg4 (default, the headline): 8 cfg2 rollouts per GPU; cfg3: the "
+                         "4 x 32-token candidate verify step on one GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "cfg3":
+        return run_verify(args)
     return run_native(args)
 
 
