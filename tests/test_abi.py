@@ -118,3 +118,18 @@ def test_linear_rejects_bad_shapes():
     assert lib.wamb_linear(a, None) == 1
     a.k, a.groups, a.a_is_fp8 = 192, 1, 1                 # E4M3 K must be a multiple of 128
     assert lib.wamb_linear(a, None) == 2
+
+
+def test_workspace_layout_split_region():
+    """Small token counts reserve split-K scratch at the end of the
+    workspace (optional: the layout's SPLITK offset is enough to run);
+    large ones reserve none."""
+    lib = _lib.load()
+    small = _args(batch=4, tokens=32, dim=3072, heads=24, ffn_dim=14336)
+    offs = (ctypes.c_int64 * len(_lib.TAPS))()
+    total = lib.wamb_block_workspace_layout(small, offs)
+    sk = offs[_lib.TAPS.index("splitk")]
+    assert sk > 0 and total > sk and sk == max(o for o in offs if o >= 0)
+    big = _args(batch=8, tokens=880, dim=3072, heads=24, ffn_dim=14336)
+    lib.wamb_block_workspace_layout(big, offs)
+    assert offs[_lib.TAPS.index("splitk")] == -1

@@ -102,3 +102,44 @@ def test_linear_pair_epilogues(cuda_device, res_f32):
     assert _lib.device_status() == 0
     gate = (table[5][None, None] + temb[:, :, 5]).expand(B, Q, D).reshape(B * Q, D)
     _close(out, res.float() + _ref(a, [w], [b]) * gate)
+
+
+@pytest.mark.parametrize("m,k,n,groups,epi", [
+    (128, 8192, 3072, 1, "bias"), (128, 14336, 3072, 1, "res_gate"), (224, 8192, 1536, 3, "bias"),
+    (100, 4096, 2560, 1, "gelu"), (128, 14336, 3072, 1, "res"),
+])
+def test_linear_split_k(cuda_device, m, k, n, groups, epi):
+    """Small M with a split-K workspace: K is split across CTAs and the last
+    split of each tile slice sums the partials; the result must meet the
+    same bound as the unsplit GEMM and equal it in split order twice."""
+    g = torch.Generator(device="cuda").manual_seed(m + k + n)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16() for _ in range(groups)]
+    bs = [torch.randn(n, device="cuda", generator=g).bfloat16() for _ in range(groups)]
+    split = torch.empty(16 << 20, dtype=torch.uint8, device="cuda")
+    split.fill_(0xAB)   # garbage counters: the call must zero what it needs
+    N = n * groups
+    kw, ref = {}, _ref(a, ws, bs)
+    if epi == "gelu":
+        kw["epilogue"] = _lib.EPI_GELU
+        ref = torch.nn.functional.gelu(ref, approximate="tanh")
+    elif epi in ("res", "res_gate"):
+        res = torch.randn(m, N, device="cuda", generator=g)
+        kw.update(epilogue=_lib.EPI_RES if epi == "res" else _lib.EPI_RES_GATE, res=res)
+        if epi == "res_gate":
+            table = torch.randn(6, N, device="cuda", generator=g)
+            temb = torch.randn(1, 1, 6, N, device="cuda", generator=g)
+            kw.update(table=table, temb=temb, rows_per_batch=m, gate_index=5)
+            ref = res + ref * (table[5] + temb[0, 0, 5])[None]
+        else:
+            ref = res + ref
+        kw["out"] = torch.empty(m, N, device="cuda", dtype=torch.float32)
+    out1 = ops.linear(a, ws, bs, split_ws=split, **kw)
+    out1 = out1.clone()
+    out2 = ops.linear(a, ws, bs, split_ws=split, **kw)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    _close(out1, ref)
+    assert torch.equal(out1, out2)            # deterministic: partials summed in split order
+    tiles = (m + 127) // 128 * (N // 128)
+    assert torch.count_nonzero(split[:tiles * 8 * 4]) == 0   # the tile counters are left at zero

@@ -144,7 +144,8 @@ inline int launch_rms(const RmsParams& p, cudaStream_t s) {
 // ------------------------------------------------------------ block forward
 struct BlockLayout {
   int64_t off[WAMB_TAP_COUNT];
-  size_t total;
+  size_t total;     // with the optional split-K scratch (WAMB_TAP_SPLITK) at the end
+  size_t minimum;   // without it: enough to run (small-M GEMMs then run unsplit)
 };
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -185,6 +186,11 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
     put(WAMB_TAP_KV_TILES, static_cast<size_t>(a->pool) * 8);
     put(WAMB_TAP_KV_COUNTS, 16);
   }
+  L.minimum = o;
+  const int m = static_cast<int>(M), d = a->dim, fd = a->ffn_dim;
+  if (gemm_would_split(m, 3 * d, d, d, f8) || gemm_would_split(m, d, d, d, f8) ||
+      gemm_would_split(m, fd, fd, d, f8) || gemm_would_split(m, d, d, fd, f8))
+    put(WAMB_TAP_SPLITK, kSplitReserveBytes);
   L.total = o;
   return L;
 }
@@ -247,8 +253,8 @@ inline int check_block_args(const wamb_block_args* a) {
                  "candidate verification requires existing read-only KV");
   }
   const BlockLayout L = block_layout(a);
-  WAMB_REQUIRE(a->workspace != nullptr && a->workspace_bytes >= L.total, WAMB_ERR_WORKSPACE,
-               "workspace of %zu bytes needed (%zu given)", L.total, a->workspace_bytes);
+  WAMB_REQUIRE(a->workspace != nullptr && a->workspace_bytes >= L.minimum, WAMB_ERR_WORKSPACE,
+               "workspace of %zu bytes needed (%zu given)", L.minimum, a->workspace_bytes);
   WAMB_REQUIRE(reinterpret_cast<uintptr_t>(a->workspace) % 256 == 0, WAMB_ERR_ALIGN,
                "workspace must be 256-byte aligned");
   return WAMB_OK;
@@ -302,6 +308,18 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   int* slots = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_SLOTS]) : nullptr;
   int* tiles = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_TILES]) : nullptr;
   int* counts = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_COUNTS]) : nullptr;
+  // Split-K scratch of the small-M GEMMs, when the workspace has room for it;
+  // its counters are zeroed once here and every split GEMM leaves them zero.
+  void* split_ws = nullptr;
+  if (L.off[WAMB_TAP_SPLITK] >= 0 && a->workspace_bytes >= L.total) {
+    split_ws = ws + L.off[WAMB_TAP_SPLITK];
+    WAMB_CHECK_CUDA(cudaMemsetAsync(split_ws, 0, kSplitCounterBytes, s));
+  }
+  auto run_gemm = [&](wamb_linear_args& g) {
+    g.split_ws = split_ws;
+    g.split_ws_bytes = split_ws ? static_cast<int64_t>(kSplitReserveBytes) : 0;
+    return linear_impl(&g, s, true);
+  };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
   const bool f8 = a->fp8 == 1;
   uint8_t* a8 = f8 ? ws + L.off[WAMB_TAP_A8] : nullptr;
@@ -349,7 +367,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   gemm_input(g, h1, 3);
   g.bias[0] = a->weights[4]; g.bias[1] = a->weights[6]; g.bias[2] = a->weights[8];
   g.out = qkv; g.ldo = 3LL * D; g.epilogue = WAMB_EPI_BIAS;
-  if ((rc = linear_impl(&g, s))) return rc;
+  if ((rc = run_gemm(g))) return rc;
   // 4. q/k RMSNorm across heads + RoPE; K/V into the pool slots
   RmsParams r{};
   r.x = qkv; r.ld = 3LL * D; r.M = M; r.D = D; r.rows_per_batch = Q; r.sections = 2;
@@ -388,7 +406,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   g.out_is_f32 = 1; g.table = table; g.temb = a->temb;
   g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 2;
   g.dim = D;
-  if ((rc = linear_impl(&g, s))) return rc;
+  if ((rc = run_gemm(g))) return rc;
   // 7. LN2 (fp32 affine), or the bf16 cast when norm2 is Identity
   ln = LnParams{};
   ln.x = h2; ln.x_f32 = 1; ln.ldx = D; ln.out = n2; ln.ldo = D; ln.M = M; ln.D = D;
@@ -403,7 +421,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   gemm_input(g, n2, 13);
   g.bias[0] = a->weights[14]; g.out = cq; g.ldo = D;
   g.epilogue = WAMB_EPI_BIAS;
-  if ((rc = linear_impl(&g, s))) return rc;
+  if ((rc = run_gemm(g))) return rc;
   r = RmsParams{};
   r.x = cq; r.ld = D; r.M = M; r.D = D; r.rows_per_batch = Q; r.sections = 1;
   r.gamma[0] = static_cast<const bf*>(a->weights[21]); r.eps[0] = static_cast<float>(a->eps[5]);
@@ -436,7 +454,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   gemm_input(g, ca, 19);
   g.bias[0] = a->weights[20]; g.out = h3; g.ldo = D;
   g.epilogue = WAMB_EPI_RES; g.res = h2; g.res_is_f32 = 1; g.out_is_f32 = 1; g.ldr = D;
-  if ((rc = linear_impl(&g, s))) return rc;
+  if ((rc = run_gemm(g))) return rc;
   // 13. LN3 + modulation (shift 3, scale 4)
   ln = LnParams{};
   ln.x = h3; ln.x_f32 = 1; ln.ldx = D; ln.out = f0; ln.ldo = D; ln.M = M; ln.D = D;
@@ -451,7 +469,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   gemm_input(g, f0, 23);
   g.bias[0] = a->weights[24]; g.out = act; g.ldo = F;
   g.epilogue = WAMB_EPI_GELU;
-  if ((rc = linear_impl(&g, s))) return rc;
+  if ((rc = run_gemm(g))) return rc;
   if (f8 && (rc = quantize(act, F, F))) return rc;
   // 15. FFN2 + gated residual (gate 5): out = h3 + f * c_gate_msa
   g = wamb_linear_args{};
@@ -462,7 +480,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   g.out_is_f32 = a->out_is_f32; g.table = table; g.temb = a->temb;
   g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 5;
   g.dim = D;
-  return linear_impl(&g, s);
+  return run_gemm(g);
 }
 
 }  // namespace wamb

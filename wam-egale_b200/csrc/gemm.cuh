@@ -44,6 +44,15 @@ struct GemmParams {
   // E4M3 operands: acc * a_scale[row] * w_scale[group][col] (null for bf16)
   const float* a_scale;
   const float* w_scale[3];
+  // Split-K (one-CTA kernel, small M): work unit u = tile * splits + s sums
+  // k-blocks [s * kb_per_split, (s + 1) * kb_per_split). Each split writes
+  // its fp32 partial tile to part[(tile * splits + s) * 128 * BN ...]; the
+  // last of the splits to finish a warp's slice (counter cnt[tile * 8 +
+  // slice], left at 0 again) sums the partials in split order and runs the
+  // epilogue, so the result does not depend on which split ends last.
+  int splits, kb_per_split;
+  float* part;
+  int* cnt;
 };
 
 constexpr int GEMM_BM = 128;
@@ -75,76 +84,121 @@ WAMB_DEV float gelu_tanh(float x) {
   return __fdividef(x, 1.f + e);
 }
 
-// Epilogue of one output tile for the calling thread's row: 32-column
-// chunks [c0, c1) of the fp32 accumulator at TMEM address `taddr` (this
-// warp's lane quarter, column 0 of the tile) -> bias / GELU / residual /
-// gate -> bf16 or fp32 stores. Every lane must call it (tcgen05.ld is
-// warp-collective); rows >= M only skip the stores.
-WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, int n0, int c0,
-                                 int c1) {
-  const bool valid = row < p.M;
-  const int g = n0 / p.n_per_group;
-  const int n_local0 = n0 - g * p.n_per_group;
-  const __nv_bfloat16* bias = g == 0 ? p.bias[0] : (g == 1 ? p.bias[1] : p.bias[2]);
-  const float* wscale = g == 0 ? p.w_scale[0] : (g == 1 ? p.w_scale[1] : p.w_scale[2]);
-  const float ascale = p.a_scale != nullptr && valid ? __ldg(p.a_scale + row) : 1.f;
-  const float* gate_tab = nullptr;
-  const float* gate_f32 = nullptr;
-  const __nv_bfloat16* gate_bf = nullptr;
-  if (p.epi == EPI_RES_GATE && valid) {
+// Per-row context of the epilogue (the calling thread's output row).
+struct EpiRow {
+  bool valid;
+  int g, n_local0;
+  const __nv_bfloat16* bias;
+  const float* wscale;
+  float ascale;
+  const float* gate_tab;
+  const float* gate_f32;
+  const __nv_bfloat16* gate_bf;
+};
+
+WAMB_DEV EpiRow epi_row(const GemmParams& p, int row, int n0) {
+  EpiRow e;
+  e.valid = row < p.M;
+  e.g = n0 / p.n_per_group;
+  e.n_local0 = n0 - e.g * p.n_per_group;
+  e.bias = e.g == 0 ? p.bias[0] : (e.g == 1 ? p.bias[1] : p.bias[2]);
+  e.wscale = e.g == 0 ? p.w_scale[0] : (e.g == 1 ? p.w_scale[1] : p.w_scale[2]);
+  e.ascale = p.a_scale != nullptr && e.valid ? __ldg(p.a_scale + row) : 1.f;
+  e.gate_tab = nullptr;
+  e.gate_f32 = nullptr;
+  e.gate_bf = nullptr;
+  if (p.epi == EPI_RES_GATE && e.valid) {
     const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
     const long long l = p.temb_L == 1 ? 0 : tok;
     const long long off = ((static_cast<long long>(b) * p.temb_L + l) * 6 + p.gate_idx) * p.D;
-    gate_tab = p.table + static_cast<long long>(p.gate_idx) * p.D;
-    if (p.temb_f32) gate_f32 = static_cast<const float*>(p.temb) + off;
-    else gate_bf = static_cast<const __nv_bfloat16*>(p.temb) + off;
+    e.gate_tab = p.table + static_cast<long long>(p.gate_idx) * p.D;
+    if (p.temb_f32) e.gate_f32 = static_cast<const float*>(p.temb) + off;
+    else e.gate_bf = static_cast<const __nv_bfloat16*>(p.temb) + off;
   }
-  // Residual rows are fetched one chunk ahead (raw 128-bit words: 8 for
-  // fp32, 4 for bf16), so their DRAM latency overlaps the previous chunk.
-  const bool has_res = valid && (p.epi == EPI_RES || p.epi == EPI_RES_GATE);
-  uint4 rnext[8];
-  auto fetch_res = [&](int c) {
-    const int col = n0 + c * 32;
-    if (p.res_f32) {
-      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const float*>(p.res) + row * p.ldr + col);
+  return e;
+}
+
+// Raw residual words of 32 columns starting at `col` (8 x 128 bits for
+// fp32, 4 for bf16).
+WAMB_DEV void epi_fetch_res(const GemmParams& p, int row, int col, uint4 (&r)[8]) {
+  if (p.res_f32) {
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const float*>(p.res) + row * p.ldr + col);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) rnext[j] = __ldg(rp + j);
-    } else {
-      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
+    for (int j = 0; j < 8; ++j) r[j] = __ldg(rp + j);
+  } else {
+    const uint4* rp =
+        reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) rnext[j] = __ldg(rp + j);
+    for (int j = 0; j < 4; ++j) r[j] = __ldg(rp + j);
+  }
+}
+
+// One 32-column chunk c of the row: accumulator values v -> E4M3 scales,
+// bias, GELU / residual / gate -> bf16 or fp32 stores. `res` holds the
+// chunk's residual words for the residual epilogues.
+WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], int row, int n0, int c,
+                        const uint4 (&res)[8]) {
+  const int col = n0 + c * 32;            // output column
+  const int lcol = e.n_local0 + c * 32;   // column within the weight group
+  if (p.a_scale != nullptr) {
+    const float4* sp = reinterpret_cast<const float4*>(e.wscale + lcol);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(sp + j);
+      v[4 * j] *= e.ascale * w.x;
+      v[4 * j + 1] *= e.ascale * w.y;
+      v[4 * j + 2] *= e.ascale * w.z;
+      v[4 * j + 3] *= e.ascale * w.w;
     }
-  };
-  if (has_res) fetch_res(c0);
-#pragma unroll 1
-  for (int c = c0; c < c1; ++c) {
-    uint4 rcur[8];
+  }
+  if (e.bias != nullptr) {
+    const uint4* bp = reinterpret_cast<const uint4*>(e.bias + lcol);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) rcur[j] = rnext[j];
-    if (has_res && c + 1 < c1) fetch_res(c + 1);
-    float v[32];
-    tmem_ld32(taddr + c * 32, v);
-    tmem_wait_ld();
-    if (!valid) continue;
-    const int col = n0 + c * 32;            // output column
-    const int lcol = n_local0 + c * 32;     // column within the weight group
-    if (p.a_scale != nullptr) {
-      const float4* sp = reinterpret_cast<const float4*>(wscale + lcol);
+    for (int j = 0; j < 4; ++j) {
+      const uint4 w = __ldg(bp + j);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 w = __ldg(sp + j);
-        v[4 * j] *= ascale * w.x;
-        v[4 * j + 1] *= ascale * w.y;
-        v[4 * j + 2] *= ascale * w.z;
-        v[4 * j + 3] *= ascale * w.w;
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16(ws[h]);
+        v[8 * j + 2 * h] += f.x;
+        v[8 * j + 2 * h + 1] += f.y;
       }
     }
-    if (bias != nullptr) {
-      const uint4* bp = reinterpret_cast<const uint4*>(bias + lcol);
+  }
+  if (p.epi == EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
+    if (p.epi == EPI_RES_GATE) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 tb = __ldg(reinterpret_cast<const float4*>(e.gate_tab + col + j));
+        float4 te;
+        if (e.gate_f32 != nullptr) {
+          te = __ldg(reinterpret_cast<const float4*>(e.gate_f32 + col + j));
+        } else {
+          const uint2 w = __ldg(reinterpret_cast<const uint2*>(e.gate_bf + col + j));
+          const float2 a = unpack_bf16(w.x), b2 = unpack_bf16(w.y);
+          te = make_float4(a.x, a.y, b2.x, b2.y);
+        }
+        v[j] *= tb.x + te.x;
+        v[j + 1] *= tb.y + te.y;
+        v[j + 2] *= tb.z + te.z;
+        v[j + 3] *= tb.w + te.w;
+      }
+    }
+    if (p.res_f32) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] += __uint_as_float(res[j].x);
+        v[4 * j + 1] += __uint_as_float(res[j].y);
+        v[4 * j + 2] += __uint_as_float(res[j].z);
+        v[4 * j + 3] += __uint_as_float(res[j].w);
+      }
+    } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint4 w = __ldg(bp + j);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const uint32_t ws[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           const float2 f = unpack_bf16(ws[h]);
@@ -153,66 +207,105 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
         }
       }
     }
-    if (p.epi == EPI_GELU) {
+  }
+  if (p.out_f32) {
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-    } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
-      if (p.epi == EPI_RES_GATE) {
+    for (int j = 0; j < 8; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 tb = __ldg(reinterpret_cast<const float4*>(gate_tab + col + j));
-          float4 te;
-          if (gate_f32 != nullptr) {
-            te = __ldg(reinterpret_cast<const float4*>(gate_f32 + col + j));
-          } else {
-            const uint2 w = __ldg(reinterpret_cast<const uint2*>(gate_bf + col + j));
-            const float2 a = unpack_bf16(w.x), b2 = unpack_bf16(w.y);
-            te = make_float4(a.x, a.y, b2.x, b2.y);
-          }
-          v[j] *= tb.x + te.x;
-          v[j + 1] *= tb.y + te.y;
-          v[j + 2] *= tb.z + te.z;
-          v[j + 3] *= tb.w + te.w;
-        }
-      }
-      if (p.res_f32) {
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+      op[j] = w;
+    }
+  }
+}
+
+// Epilogue of one output tile for the calling thread's row: 32-column
+// chunks [c0, c1) of the fp32 accumulator at TMEM address `taddr` (this
+// warp's lane quarter, column 0 of the tile). Every lane must call it
+// (tcgen05.ld is warp-collective); rows >= M only skip the stores.
+WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, int n0, int c0,
+                                 int c1) {
+  const EpiRow e = epi_row(p, row, n0);
+  // Residual rows are fetched one chunk ahead, so their DRAM latency
+  // overlaps the previous chunk.
+  const bool has_res = e.valid && (p.epi == EPI_RES || p.epi == EPI_RES_GATE);
+  uint4 rnext[8];
+  if (has_res) epi_fetch_res(p, row, n0 + c0 * 32, rnext);
+#pragma unroll 1
+  for (int c = c0; c < c1; ++c) {
+    uint4 rcur[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          v[4 * j] += __uint_as_float(rcur[j].x);
-          v[4 * j + 1] += __uint_as_float(rcur[j].y);
-          v[4 * j + 2] += __uint_as_float(rcur[j].z);
-          v[4 * j + 3] += __uint_as_float(rcur[j].w);
-        }
-      } else {
+    for (int j = 0; j < 8; ++j) rcur[j] = rnext[j];
+    if (has_res && c + 1 < c1) epi_fetch_res(p, row, n0 + (c + 1) * 32, rnext);
+    float v[32];
+    tmem_ld32(taddr + c * 32, v);
+    tmem_wait_ld();
+    if (!e.valid) continue;
+    epi_chunk(p, e, v, row, n0, c, rcur);
+  }
+}
+
+// Split-K, step 1, for one warp slice (rows q*32.., chunks [c0, c1)):
+// this split's fp32 partial from TMEM into its workspace slot.
+// `part_tile` points at split 0 of the tile ([splits][128][BN] fp32).
+template <int BN>
+WAMB_DEV void gemm_split_store(uint32_t taddr, float* part_tile, int split, int row_in_tile, int c0,
+                               int c1) {
+  float* mine = part_tile + (static_cast<long long>(split) * 128 + row_in_tile) * BN;
+#pragma unroll 1
+  for (int c = c0; c < c1; ++c) {
+    float v[32];
+    tmem_ld32(taddr + c * 32, v);
+    tmem_wait_ld();
+    float4* dst = reinterpret_cast<float4*>(mine + c * 32);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 w = rcur[j];
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    for (int j = 0; j < 8; ++j) __stcg(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+  }
+}
+
+// Split-K, step 2: count this split in; the last split to finish the slice
+// sums all partials in split order and runs the epilogue.
+template <int BN>
+WAMB_DEV void gemm_split_finish(const GemmParams& p, const float* part_tile, int row_in_tile, int row,
+                                int n0, int c0, int c1, int* counter) {
+  const int lane = threadIdx.x & 31;
+  __threadfence();   // this lane's partial is visible device-wide before the count
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) old = atomicAdd(counter, 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old != p.splits - 1) return;
+  __threadfence();   // every other split's partial is visible to this warp
+  if (lane == 0) *counter = 0;  // ready for the next launch
+  const EpiRow e = epi_row(p, row, n0);
+  if (!e.valid) return;
+#pragma unroll 1
+  for (int c = c0; c < c1; ++c) {
+    uint4 res[8];
+    if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) epi_fetch_res(p, row, n0 + c * 32, res);
+    float v[32];
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const float2 f = unpack_bf16(ws[h]);
-            v[8 * j + 2 * h] += f.x;
-            v[8 * j + 2 * h + 1] += f.y;
-          }
-        }
+    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    for (int s2 = 0; s2 < p.splits; ++s2) {
+      const float4* src = reinterpret_cast<const float4*>(
+          part_tile + (static_cast<long long>(s2) * 128 + row_in_tile) * BN + c * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 f = __ldcg(src + j);
+        v[4 * j] += f.x;
+        v[4 * j + 1] += f.y;
+        v[4 * j + 2] += f.z;
+        v[4 * j + 3] += f.w;
       }
     }
-    if (p.out_f32) {
-      float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
-      uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 w;
-        w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
-        w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
-        w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
-        w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
-        op[j] = w;
-      }
-    }
+    epi_chunk(p, e, v, row, n0, c, res);
   }
 }
 
@@ -242,6 +335,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int num_tiles = num_m * num_n;
   constexpr int KB = F8 ? GEMM_BK8 : GEMM_BK;
   const int num_kb = p.K / KB;
+  const int splits = p.splits > 1 ? p.splits : 1;
+  const int num_units = num_tiles * splits;   // unit u: tile u / splits, split u % splits
+  auto unit_kb = [&](int u, int& kb0, int& kb1) {
+    if (splits == 1) { kb0 = 0; kb1 = num_kb; return; }
+    kb0 = (u % splits) * p.kb_per_split;
+    kb1 = min(num_kb, kb0 + p.kb_per_split);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -273,14 +373,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
       int it = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const int t = u / splits;
         const int m_blk = t % num_m, n_blk = t / num_m;
         const int n0 = n_blk * BN;
         const int g = n0 / p.n_per_group;
         const int n_local = n0 - g * p.n_per_group;
         const CUtensorMap* mb = g == 0 ? &tmB0 : (g == 1 ? &tmB1 : &tmB2);
+        int kb0, kb1;
+        unit_kb(u, kb0, kb1);
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) { ok = false; break; }
@@ -303,14 +406,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // --------------------------------------------------------- MMA issuer
       constexpr uint32_t IDESC = F8 ? idesc_e4m3(GEMM_BM, BN) : idesc_bf16(GEMM_BM, BN, 0);
       int it = 0, tc = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
+      for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tc) {
         const int acc = tc & 1;
         const uint32_t aph = (tc >> 1) & 1;
         if (!mbar_wait(tempty0 + 8 * acc, aph ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        int kb0, kb1;
+        unit_kb(u, kb0, kb1);
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) { ok = false; break; }
@@ -321,8 +426,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per k-block
             const uint64_t ad = sw128_desc(a_base + kk * 32, 16, 1024);
             const uint64_t bd = sw128_desc(b_base + kk * 32, 16, 1024);
-            if constexpr (F8) umma_e4m3(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
-            else umma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+            const uint32_t accum = kb > kb0 || kk > 0;
+            if constexpr (F8) umma_e4m3(d_tmem, ad, bd, IDESC, accum);
+            else umma_bf16(d_tmem, ad, bd, IDESC, accum);
           }
           umma_commit(empty0 + 8 * s);
         }
@@ -339,18 +445,30 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     int tc = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tc) {
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
       if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) break;
       tc_fence_after();
+      const int t = u / splits;
       const int m_blk = t % num_m, n_blk = t / num_m;
-      gemm_epilogue_tile(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
-                         m_blk * GEMM_BM + row_in_tile, n_blk * BN, half * (BN / 64),
-                         (half + 1) * (BN / 64));
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const int row = m_blk * GEMM_BM + row_in_tile;
+      const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
+      if (splits == 1) {
+        gemm_epilogue_tile(p, taddr, row, n_blk * BN, c0, c1);
+      } else {
+        float* part_tile = p.part + static_cast<long long>(t) * splits * 128 * BN;
+        gemm_split_store<BN>(taddr, part_tile, u % splits, row_in_tile, c0, c1);
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
+      if (lane == 0) mbar_arrive(tempty0 + 8 * acc);   // accumulator free for the next unit
+      if (splits > 1) {
+        const float* part_tile = p.part + static_cast<long long>(t) * splits * 128 * BN;
+        gemm_split_finish<BN>(p, part_tile, row_in_tile, row, n_blk * BN, c0, c1,
+                              p.cnt + t * GEMM_EPI_WARPS + (warp - 2));
+      }
     }
   }
 

@@ -19,7 +19,7 @@ inline int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap* tb, const Ge
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     configured[dev] = true;
   }
-  const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * (p.N / BN);
+  const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * (p.N / BN) * (p.splits > 1 ? p.splits : 1);
   const int grid = tiles < sms ? tiles : sms;
   gemm_tc_kernel<BN, STAGES, F8><<<grid, GEMM_THREADS, L::TOTAL, stream>>>(ta, tb[0], tb[1], tb[2], p);
   WAMB_CHECK_CUDA(cudaGetLastError());
@@ -74,7 +74,60 @@ inline int choose_bn(int M, int N, int n_per_group, int sms) {
   return best;
 }
 
-inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
+// Split-K plan of the one-CTA kernel: when the output tiles at the chosen
+// width leave SMs idle (small M: the verify batch, a short chunk), use
+// 128-wide tiles and split K so that tiles x splits fills the SMs, each
+// split keeping at least 32 k-blocks (measured on B200 at M 128: a 6-way
+// split of K 14336 takes the FFN-out GEMM from 66 to 45 us, while 2-3 way
+// splits of K 3072 are slower than the unsplit kernel).
+// Returns splits (1 = none).
+struct SplitPlan {
+  int bn, splits, kb_per_split;
+};
+constexpr int kSplitCounterBytes = 256 * 1024;   // room for 8 counters per tile of up to 8192 tiles
+
+inline SplitPlan plan_split(int M, int N, int n_per_group, int num_kb, int sms, int bn0) {
+  SplitPlan sp{bn0, 1, num_kb};
+  const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
+  if (static_cast<long long>(num_m) * (N / bn0) >= sms) return sp;
+  const int bn = n_per_group % 128 == 0 ? 128 : bn0;
+  const int tiles = num_m * (N / bn);
+  int s = sms / tiles;
+  if (s > num_kb / 32) s = num_kb / 32;
+  if (s < 2) return sp;
+  sp.bn = bn;
+  sp.kb_per_split = (num_kb + s - 1) / s;
+  sp.splits = (num_kb + sp.kb_per_split - 1) / sp.kb_per_split;   // no empty split
+  return sp;
+}
+
+// Workspace bytes a split plan needs: counters, then [tiles][splits][128][bn] fp32.
+inline size_t split_bytes(int M, int N, const SplitPlan& sp) {
+  if (sp.splits <= 1) return 0;
+  const size_t tiles = static_cast<size_t>((M + GEMM_BM - 1) / GEMM_BM) * (N / sp.bn);
+  return kSplitCounterBytes + tiles * sp.splits * 128 * sp.bn * 4;
+}
+
+// Largest split-K scratch any plan can take on a GPU of up to kSplitMaxSms
+// SMs: units = tiles x splits <= SMs, each unit's partial 128 x 128 fp32.
+constexpr int kSplitMaxSms = 160;
+constexpr size_t kSplitReserveBytes =
+    static_cast<size_t>(kSplitCounterBytes) + static_cast<size_t>(kSplitMaxSms) * 128 * 128 * 4;
+
+// Whether a GEMM of this shape would split K on a B200 (148 SMs): the block
+// reserves split-K scratch only when one of its GEMMs would.
+inline bool gemm_would_split(int M, int N, int n_per_group, int K, bool f8) {
+  constexpr int sms = 148;
+  if (M <= 0) return false;
+  const long long pair_tiles = ((M + 255) / 256) * (N / 256);
+  if (M >= 512 && n_per_group % 256 == 0 && pair_tiles >= sms / 2) return false;
+  const int bn0 = choose_bn(M, N, n_per_group, sms);
+  return plan_split(M, N, n_per_group, K / (f8 ? GEMM_BK8 : GEMM_BK), sms, bn0).splits > 1;
+}
+
+// counters_zero: the caller guarantees the workspace's counter area is zero
+// (the block zeroes it once per call; split GEMMs leave it zero).
+inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool counters_zero = false) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
@@ -122,7 +175,21 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   // CTA per 128 x BN tile.
   const long long pair_tiles = ((a->m + 255) / 256) * (N / 256);
   const bool pair = a->m >= 512 && a->n_per_group % 256 == 0 && pair_tiles >= di.sms / 2;
-  const int bn = pair ? 256 : choose_bn(a->m, static_cast<int>(N), a->n_per_group, di.sms);
+  int bn = pair ? 256 : choose_bn(a->m, static_cast<int>(N), a->n_per_group, di.sms);
+  SplitPlan sp{bn, 1, 0};
+  if (!pair && a->split_ws != nullptr) {
+    sp = plan_split(a->m, static_cast<int>(N), a->n_per_group, a->k / (f8 ? GEMM_BK8 : GEMM_BK), di.sms, bn);
+    if (sp.splits > 1) {
+      WAMB_REQUIRE(reinterpret_cast<uintptr_t>(a->split_ws) % 256 == 0, WAMB_ERR_ALIGN,
+                   "split workspace must be 256-byte aligned");
+      const size_t tiles = static_cast<size_t>((a->m + GEMM_BM - 1) / GEMM_BM) * (N / sp.bn);
+      if (tiles * GEMM_EPI_WARPS * sizeof(int) > static_cast<size_t>(kSplitCounterBytes) ||
+          split_bytes(a->m, static_cast<int>(N), sp) > static_cast<size_t>(a->split_ws_bytes))
+        sp = SplitPlan{bn, 1, 0};   // too little room: no split
+      else
+        bn = sp.bn;
+    }
+  }
   CUtensorMap ta, tb[3];
   auto tmap = f8 ? make_tmap_e4m3 : make_tmap_bf16;
   rc = tmap(&ta, a->a, a->m, a->k, a->lda, 128);
@@ -156,6 +223,15 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   if (f8) {
     p.a_scale = a->a_scale;
     for (int g = 0; g < 3; ++g) p.w_scale[g] = g < a->groups ? a->w_scale[g] : nullptr;
+  }
+  p.splits = sp.splits;
+  if (sp.splits > 1) {
+    uint8_t* ws = static_cast<uint8_t*>(a->split_ws);
+    p.kb_per_split = sp.kb_per_split;
+    p.cnt = reinterpret_cast<int*>(ws);
+    p.part = reinterpret_cast<float*>(ws + kSplitCounterBytes);
+    const size_t tiles = static_cast<size_t>((a->m + GEMM_BM - 1) / GEMM_BM) * (N / sp.bn);
+    if (!counters_zero) WAMB_CHECK_CUDA(cudaMemsetAsync(ws, 0, tiles * GEMM_EPI_WARPS * sizeof(int), stream));
   }
   auto launch = [&](auto f8c) {
     constexpr bool F8 = decltype(f8c)::value;
