@@ -101,7 +101,13 @@ def test_block_kv_lifecycle_and_eviction(cuda_device):
         _cache_equal(blk.attn1.attn_caches["pos"], g.attn1.attn_caches["pos"], tb.attn1.attn_caches["pos"])
 
 
-def test_block_candidate_verification(cuda_device):
+@pytest.mark.parametrize("rows,Q", [
+    ([0, 1, 1, 0], 16),           # different history rows: one CTA set per candidate
+    ([1, 1, 1, 1], 16),           # one shared row: grouped candidates, split key tiles
+    ([0] * 10, 16),               # grouped, 160 query rows: two tiles, private keys in two tiles
+    ([0, 0, 0], 40),              # grouped, candidate boundaries inside a tile
+])
+def test_block_candidate_verification(cuda_device, rows, Q):
     D, H, F, Bp, C, pool = 256, 2, 512, 2, 24, 200
     blk = make_oracle_block(D, F, H, seed=21)
     g = to_device_block(blk)
@@ -115,9 +121,9 @@ def test_block_candidate_verification(cuda_device):
             blk(x, ctx, temb, r, update_cache=2)
         reference_bf16(tb, x, ctx, temb, r, update_cache=2)
         _run_native(g, x, ctx, temb, r, update_cache=2)
-    rows = torch.tensor([0, 1, 1, 0], dtype=torch.int64)
-    B, Q = 4, 16
-    x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=300, temb_len=Q)
+    rows = torch.tensor(rows, dtype=torch.int64)
+    B = len(rows)
+    x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=300 + Q + B, temb_len=Q)
     before = {k: v.clone() for k, v in g.attn1.attn_caches["pos"].items()}
     with torch.no_grad():
         ref = blk(x, ctx, temb, r, candidate_cache_rows=rows)
