@@ -65,7 +65,8 @@ enum wamb_epilogue {
   WAMB_EPI_BIAS = 0,     /* out = bf16(A W^T + b) */
   WAMB_EPI_GELU = 1,     /* out = bf16(gelu_tanh(A W^T + b)) */
   WAMB_EPI_RES = 2,      /* out = bf16(res + (A W^T + b)) */
-  WAMB_EPI_RES_GATE = 3  /* out = bf16(res + (A W^T + b) * (table[g] + temb[b, l, g])) */
+  WAMB_EPI_RES_GATE = 3, /* out = bf16(res + (A W^T + b) * (table[g] + temb[b, l, g])) */
+  WAMB_EPI_SILU = 4      /* out = silu(A W^T + b) (timestep embedder) */
 };
 
 /*
@@ -306,6 +307,52 @@ WAMB_API int wamb_block_forward_noalloc(const wamb_block_args* args, void* strea
  * k_out, v_out: [context_batch * context_tokens, dim] bf16.
  */
 WAMB_API int wamb_cross_kv(const wamb_block_args* args, void* k_out, void* v_out, void* stream);
+
+/*
+ * Glue of the whole-model forward (WanTransformer3DModel.forward,
+ * 投机采样/wam-p0-worktree/wan_va/modules/model.py:1060-1116) and of the
+ * flow-match scheduler step (wan_va/utils/scheduler.py:78-89), so that a
+ * denoise step can run end to end on the device. All are asynchronous on
+ * `stream`, allocate nothing and return 0 or a wamb_status.
+ */
+
+/* Sinusoidal timestep features, diffusers Timesteps(num_channels=dim,
+ * flip_sin_to_cos=True, downscale_freq_shift=0) (model.py:213-215):
+ * out[i] = [cos(t_i f), sin(t_i f)], f_k = exp(-ln(10000) k / (dim/2)).
+ * t: [n] fp32, out: [n, dim] bf16, dim even. */
+WAMB_API int wamb_timestep_embedding(const float* t, int32_t n, int32_t dim, void* out, void* stream);
+
+/* out = bf16(silu(x)), x [m, ldx] bf16 or fp32 (x_is_f32), out [m, ldo]. */
+WAMB_API int wamb_silu(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, int32_t n, void* out,
+                       int64_t ldo, void* stream);
+
+/* Patchify gather of the latent / action input embedding (model.py:1064-1077):
+ * x [b, c, f, h, w] bf16 -> out [b, (f/p1)(h/p2)(w/p3), ldo] bf16 with column
+ * (c p1 p2 p3) order and columns [c*p1*p2*p3, ldo) zero (ldo pads K to a
+ * multiple of 64 for wamb_linear). p1 = p2 = p3 = 1 is the action rearrange. */
+WAMB_API int wamb_embed_gather(const void* x, int32_t b, int32_t c, int32_t f, int32_t h, int32_t w,
+                               int32_t p1, int32_t p2, int32_t p3, void* out, int32_t ldo, void* stream);
+
+/* Output norm with its modulation (model.py:1099-1106): out = bf16(LN(x) *
+ * (1 + table[1] + temb) + table[0] + temb), LN without affine in fp32;
+ * x [m, d] bf16 or fp32, table [2, d] fp32, temb [m / rows_per_batch,
+ * temb_len, d] fp32 or bf16 with temb_len 1 or rows_per_batch. */
+WAMB_API int wamb_output_norm(const void* x, int32_t x_is_f32, int32_t m, int32_t d, double eps,
+                              const float* table, const void* temb, int32_t temb_is_f32,
+                              int32_t temb_len, int32_t rows_per_batch, void* out, void* stream);
+
+/* out[r, 0:n_bytes] = x[r, 0:n_bytes] (strided rows, byte counts). */
+WAMB_API int wamb_copy_cols(const void* x, int64_t ldx_bytes, int32_t m, int32_t n_bytes, void* out,
+                            int64_t ldo_bytes, void* stream);
+
+/* torch.repeat_interleave over rows: out[r * repeat + k] = x[r] (row_bytes each). */
+WAMB_API int wamb_repeat_rows(const void* x, int32_t rows, int32_t row_bytes, int32_t repeat, void* out,
+                              void* stream);
+
+/* Flow-match Euler step in place: sample += v * dsigma over n elements
+ * (sample and v bf16 or fp32), dsigma = sigma_next - sigma. */
+WAMB_API int wamb_flow_step(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32,
+                            int64_t n, float dsigma, void* stream);
 
 #ifdef __cplusplus
 }

@@ -10,6 +10,10 @@ Contents:
                  WanTransformerBlock / WanAttention / "original" KV cache /
                  WanRotaryPosEmbed / get_mesh_id, each citing the reference
                  file:line it follows.
+  wan_model.py   the whole-model inference forward around the blocks
+                 (embedders, output norm and projection) and the flow-match
+                 scheduler (model.py:203-240, 797-872, 1028-1116;
+                 scheduler.py:6-89).
   fp8.py         the FP8-E4M3 GEMM path (no reference counterpart): row
                  quantization and a block copy with quantized GEMMs.
 

@@ -1,0 +1,119 @@
+"""The whole-model forward around the blocks (model.py:1028-1116: input
+embedding, text projection, timestep embedding chain, blocks, output norm and
+projection) run by NativeWanModel against the fp32 CPU oracle
+(oracle/wan_model.py, pinned to the reference source by
+tests/golden/model_cases.pt), in action and latent mode, plus the device
+flow-match step against the oracle scheduler.
+
+Gate: the block gate of tests/blockutil.py: cosine >= 0.9999 and max |err|
+<= max(2e-2, E_ref), E_ref the error of the reference model itself run in
+bf16 on the GPU (the oracle modules with bf16 weights, torch ops).
+"""
+import copy
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from blockutil import assert_parity
+from oracle import wan_model as om
+from wam_ops import _lib
+from wam_ops.model import NativeWanModel
+from wam_ops.scheduler import FlowMatchScheduler
+
+sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+from make_model_golden import CFG  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_model(seed=11):
+    torch.manual_seed(seed)
+    m = om.WanTransformer3DModel(**CFG).eval()
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if name.endswith("scale_shift_table"):
+                p.copy_(torch.randn_like(p) / p.shape[-1] ** 0.5)
+            elif "norm" in name and name.endswith("weight"):
+                p.copy_(1.0 + 0.1 * torch.randn_like(p))
+            elif "norm" in name and name.endswith("bias"):
+                p.copy_(0.1 * torch.randn_like(p))
+            elif name.endswith("weight"):
+                p.copy_(torch.randn_like(p) * 0.05)
+            else:
+                p.copy_(0.05 * torch.randn_like(p))
+            p.copy_(p.bfloat16().float())
+    return m
+
+
+def _to_device(m):
+    """Reference dtype policy: fp32 for the modulation tables, norms and the
+    timestep embedder (_keep_in_fp32_modules, model.py:812-825), bf16 else."""
+    g = copy.deepcopy(m)
+    keep32 = ("scale_shift_table", "norm1", "norm2", "norm3", "time_embedder")
+    for name, p in g.named_parameters():
+        fp32 = any(k in name for k in keep32)
+        p.data = p.data.to(device="cuda", dtype=torch.float32 if fp32 else torch.bfloat16).contiguous()
+    return g
+
+
+def _inputs(action_mode, seed):
+    g = torch.Generator().manual_seed(seed)
+    from oracle import wan_block as ob
+    if action_mode:
+        B, f, h, w = 2, 8, 4, 1
+        x = torch.randn(B, CFG["action_dim"], f, h, w, generator=g)
+        grid = ob.get_mesh_id(f, h, w, 0, action=True)
+    else:
+        B, f, h, w = 1, 2, 8, 8
+        x = torch.randn(B, CFG["in_channels"], f, h, w, generator=g)
+        grid = ob.get_mesh_id(f, h // 2, w // 2, 0)
+    x = x.bfloat16().float()
+    text = torch.randn(B, 16, CFG["text_dim"], generator=g).bfloat16().float()
+    steps = torch.rand(B, f, generator=g) * 1000
+    return {"noisy_latents": x, "text_emb": text, "grid_id": grid[None], "timesteps": steps}
+
+
+def _cuda(d, dtype=torch.bfloat16):
+    return {k: (v.cuda().to(dtype) if k in ("noisy_latents", "text_emb") else v.cuda()) for k, v in d.items()}
+
+
+@pytest.mark.parametrize("action_mode", [True, False])
+@pytest.mark.parametrize("prepared", [False, True])
+def test_model_forward(cuda_device, action_mode, prepared):
+    m = _oracle_model()
+    inp = _inputs(action_mode, 50 + int(action_mode))
+    with torch.no_grad():
+        ref = m(inp, action_mode=action_mode)
+        rb = _to_device(m)(_cuda(inp), action_mode=action_mode)
+    dev = _to_device(m)
+    nm = NativeWanModel(dev)
+    with torch.no_grad():
+        if prepared:
+            nm.prepare_context(_cuda(inp)["text_emb"])
+        out = nm(_cuda(inp), action_mode=action_mode)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert out.shape == ref.shape and out.dtype == torch.bfloat16
+    s = assert_parity(out, ref, rb)
+    print("model", "action" if action_mode else "latent", "prepared" if prepared else "", s)
+
+
+@pytest.mark.parametrize("kw,n", [({"shift": 5.0, "sigma_min": 0.0, "extra_one_step": True}, 10), ({}, 50)])
+def test_flow_step(cuda_device, kw, n):
+    so, sn = om.FlowMatchScheduler(**kw), FlowMatchScheduler(**kw)
+    so.set_timesteps(n)
+    sn.set_timesteps(n)
+    assert torch.equal(so.sigmas, sn.sigmas) and torch.equal(so.timesteps, sn.timesteps)
+    g = torch.Generator().manual_seed(n)
+    sample, v = torch.randn(4, 1000, generator=g), torch.randn(4, 1000, generator=g)
+    for t in sn.timesteps[::3]:
+        want = so.step(v, t, sample)
+        got = sn.step(v.cuda(), t, sample.cuda())
+        torch.cuda.synchronize()
+        assert torch.allclose(got.cpu(), want, rtol=1e-6, atol=1e-6)
+    x = sample.cuda().bfloat16()
+    sn.step_(v.cuda().bfloat16(), sn.timesteps[0], x)
+    ref = (sample.bfloat16().float() + v.bfloat16().float() * (float(so.sigmas[1]) - float(so.sigmas[0])))
+    assert torch.allclose(x.float().cpu(), ref, rtol=2 ** -8, atol=1e-2)

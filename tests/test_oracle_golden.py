@@ -59,3 +59,41 @@ def test_rope_split_and_mesh_ids():
     assert g.shape == (4, 8)
     assert torch.all(g[1] == -1) and torch.all(g[3] == 7)
     assert torch.allclose(g[0][:4], torch.tensor([0.2, 0.4, 0.6, 0.8]))
+
+
+# ------------------------------------------------ whole-model forward + scheduler
+MODEL_FIX = Path(__file__).resolve().parent / "golden" / "model_cases.pt"
+
+
+def test_oracle_model_matches_reference_fixture():
+    """oracle.wan_model.WanTransformer3DModel (embedders, 2 blocks, output norm
+    and projection) against the reference's own forward (AST-extracted,
+    tests/golden/make_model_golden.py), action and latent mode."""
+    import sys
+    sys.path.insert(0, str(MODEL_FIX.parent))
+    from make_golden import seeded_params
+    from oracle import wan_model as om
+    fx = torch.load(MODEL_FIX, weights_only=False)
+    torch.manual_seed(0)
+    cfg = dict(fx["config"])
+    model = om.WanTransformer3DModel(**cfg).eval()
+    sums = seeded_params(model, seed=fx["seed"])
+    assert sums.keys() == fx["param_sums"].keys()
+    for k, v in sums.items():
+        assert abs(v[0] - fx["param_sums"][k][0]) < 1e-6 and abs(v[1] - fx["param_sums"][k][1]) < 1e-6, k
+    for case in fx["cases"]:
+        with torch.no_grad():
+            out = model(case["inputs"], update_cache=0, action_mode=case["action_mode"])
+        assert out.shape == case["out"].shape
+        assert torch.allclose(out, case["out"], rtol=1e-5, atol=1e-5), (out - case["out"]).abs().max()
+
+
+def test_oracle_scheduler_matches_reference_fixture():
+    from oracle import wan_model as om
+    fx = torch.load(MODEL_FIX, weights_only=False)
+    for rec in fx["scheduler"]:
+        s = om.FlowMatchScheduler(**rec["kwargs"])
+        s.set_timesteps(rec["n"])
+        assert torch.equal(s.sigmas, rec["sigmas"]) and torch.equal(s.timesteps, rec["timesteps"])
+        for t, want in rec["steps"]:
+            assert torch.equal(s.step(rec["v"], t, rec["sample"]), want)

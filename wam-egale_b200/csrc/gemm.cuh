@@ -25,6 +25,7 @@ enum GemmEpilogue : int {
   EPI_GELU = 1,      // bf16(gelu_tanh(acc + b))                 FFN1, model.py:733-735
   EPI_RES = 2,       // bf16(res + (acc + b))                    cross-attn residual, model.py:783
   EPI_RES_GATE = 3,  // bf16(res + (acc + b) * (table + temb))   gated residuals, model.py:771,792
+  EPI_SILU = 4,      // silu(acc + b)                            TimestepEmbedding linear_1 (diffusers)
 };
 
 struct GemmParams {
@@ -81,6 +82,14 @@ WAMB_DEV float gelu_tanh(float x) {
   const float u = k0 * fmaf(k1 * x * x, x, x);
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * -2.8853900817779268f));  // -2 log2(e) u
+  return __fdividef(x, 1.f + e);
+}
+
+// x * sigmoid(x) = x / (1 + exp(-x)): one ex2.approx and one approximate
+// reciprocal (relative error ~1e-6); x -> -inf gives x / inf = -0.
+WAMB_DEV float silu(float x) {
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * -1.4426950408889634f));
   return __fdividef(x, 1.f + e);
 }
 
@@ -168,6 +177,9 @@ WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], in
   if (p.epi == EPI_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (p.epi == EPI_SILU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
   } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
     if (p.epi == EPI_RES_GATE) {
 #pragma unroll

@@ -53,11 +53,13 @@ WAMB_DEV void load8f(const float* p, float (&f)[8]) {
   f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 // Modulation row: table[idx, col..col+8] + temb[..., idx, col..col+8] (model.py:751-759).
+// temb_rows: modulation rows per token in temb (6 for the blocks; 1 for the
+// output norm, whose single temb row is added to both table rows, model.py:1100).
 WAMB_DEV void load_mod8(const float* table, const void* temb, int temb_f32, long long temb_off,
-                        int idx, int D, int col, float (&f)[8]) {
+                        int idx, int D, int col, float (&f)[8], int temb_rows = 6) {
   float t[8];
   load8f(table + static_cast<long long>(idx) * D + col, f);
-  const long long o = temb_off + static_cast<long long>(idx) * D + col;
+  const long long o = temb_off + (temb_rows > 1 ? static_cast<long long>(idx) * D : 0) + col;
   if (temb_f32) load8f(static_cast<const float*>(temb) + o, t);
   else load8(static_cast<const __nv_bfloat16*>(temb) + o, t);
 #pragma unroll
@@ -80,8 +82,9 @@ struct LnParams {
   uint8_t* out8;          // non-null: write E4M3 [M, ldo] + out_scale[M] instead of bf16
   float* out_scale;
   const float* table;     // [6, D]
-  const void* temb;       // [B, L, 6, D]
+  const void* temb;       // [B, L, temb_rows, D]
   int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
+  int temb_rows;          // 0 or 6: the blocks' 6 modulation rows; 1: the output norm
 };
 
 // Rows per CTA of ln_kernel: several rows share one load of the modulation
@@ -204,7 +207,7 @@ __global__ void ln_kernel(const LnParams p) {
       const int row = row0 + r < p.M ? row0 + r : p.M - 1;
       const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
       const long long l = p.temb_L == 1 ? 0 : tok;
-      key[r] = (static_cast<long long>(b) * p.temb_L + l) * 6 * p.D;  // temb offset of (b, l)
+      key[r] = (static_cast<long long>(b) * p.temb_L + l) * (p.temb_rows == 1 ? 1 : 6) * p.D;
     }
   }
 #pragma unroll
@@ -218,8 +221,9 @@ __global__ void ln_kernel(const LnParams p) {
           load8f(p.gamma + col, mul);
           load8f(p.beta + col, add);
         } else {
-          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.scale_idx, p.D, col, mul);
-          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.shift_idx, p.D, col, add);
+          const int tr = p.temb_rows == 1 ? 1 : 6;
+          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.scale_idx, p.D, col, mul, tr);
+          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.shift_idx, p.D, col, add, tr);
 #pragma unroll
           for (int j = 0; j < 8; ++j) mul[j] += 1.f;
         }

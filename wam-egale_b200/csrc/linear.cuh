@@ -151,7 +151,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool coun
       WAMB_REQUIRE(a->w_scale[g] && aligned16(a->w_scale[g]), WAMB_ERR_ARG, "w_scale[%d]", g);
   }
   if (f8) WAMB_REQUIRE(a->a_scale != nullptr, WAMB_ERR_ARG, "a_scale");
-  WAMB_REQUIRE(a->epilogue >= 0 && a->epilogue <= 3, WAMB_ERR_ARG, "epilogue");
+  WAMB_REQUIRE(a->epilogue >= 0 && a->epilogue <= 4, WAMB_ERR_ARG, "epilogue");
   if (a->epilogue == WAMB_EPI_RES || a->epilogue == WAMB_EPI_RES_GATE) {
     WAMB_REQUIRE(a->res && aligned16(a->res) && a->ldr >= N && a->ldr % 8 == 0, WAMB_ERR_ARG,
                  "residual");

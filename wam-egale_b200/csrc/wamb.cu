@@ -5,6 +5,7 @@
 #include "host.cuh"
 #include "linear.cuh"
 #include "block.cuh"
+#include "model.cuh"
 
 namespace wamb {
 
@@ -112,6 +113,120 @@ int wamb_block_forward_noalloc(const wamb_block_args* args, void* stream) {
 int wamb_cross_kv(const wamb_block_args* args, void* k_out, void* v_out, void* stream) {
   if (args == nullptr) return wamb::fail(WAMB_ERR_ARG, "null args");
   return wamb::cross_kv_impl(args, k_out, v_out, static_cast<cudaStream_t>(stream));
+}
+
+int wamb_timestep_embedding(const float* t, int32_t n, int32_t dim, void* out, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(n >= 0 && dim > 0 && dim % 2 == 0, WAMB_ERR_SHAPE, "timestep embedding: n >= 0, even dim");
+  if (n == 0) return WAMB_OK;
+  WAMB_REQUIRE(t && out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  timestep_embed_kernel<<<elem_grid(static_cast<long long>(n) * dim / 2, di.sms), 256, 0,
+                          static_cast<cudaStream_t>(stream)>>>(t, n, dim, static_cast<__nv_bfloat16*>(out));
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+int wamb_silu(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, int32_t n, void* out, int64_t ldo,
+              void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(m >= 0 && n > 0 && ldx >= n && ldo >= n, WAMB_ERR_SHAPE, "silu shape");
+  if (m == 0) return WAMB_OK;
+  WAMB_REQUIRE(x && out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  silu_kernel<<<elem_grid(static_cast<long long>(m) * n, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, ldx, x_is_f32, m, n, static_cast<__nv_bfloat16*>(out), ldo);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+int wamb_embed_gather(const void* x, int32_t b, int32_t c, int32_t f, int32_t h, int32_t w, int32_t p1,
+                      int32_t p2, int32_t p3, void* out, int32_t ldo, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(b >= 0 && c > 0 && f > 0 && h > 0 && w > 0 && p1 > 0 && p2 > 0 && p3 > 0 &&
+                   f % p1 == 0 && h % p2 == 0 && w % p3 == 0 && ldo >= c * p1 * p2 * p3,
+               WAMB_ERR_SHAPE, "embed gather shape");
+  if (b == 0) return WAMB_OK;
+  WAMB_REQUIRE(x && out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  GatherParams p{static_cast<const __nv_bfloat16*>(x), b, c, f, h, w, p1, p2, p3,
+                 static_cast<__nv_bfloat16*>(out), ldo};
+  const long long total = static_cast<long long>(b) * (f / p1) * (h / p2) * (w / p3) * ldo;
+  embed_gather_kernel<<<elem_grid(total, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+int wamb_output_norm(const void* x, int32_t x_is_f32, int32_t m, int32_t d, double eps, const float* table,
+                     const void* temb, int32_t temb_is_f32, int32_t temb_len, int32_t rows_per_batch,
+                     void* out, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(m >= 0 && rows_per_batch > 0 && (temb_len == 1 || temb_len == rows_per_batch) &&
+                   m % rows_per_batch == 0,
+               WAMB_ERR_SHAPE, "output norm shape");
+  WAMB_REQUIRE(row_vpt(d) > 0, WAMB_ERR_SHAPE, "d=%d unsupported by the row kernels", d);
+  if (m == 0) return WAMB_OK;
+  WAMB_REQUIRE(x && table && temb && out, WAMB_ERR_ARG, "null pointer");
+  LnParams p{};
+  p.x = x; p.x_f32 = x_is_f32; p.ldx = d;
+  p.out = static_cast<__nv_bfloat16*>(out); p.ldo = d;
+  p.M = m; p.D = d; p.eps = static_cast<float>(eps); p.affine = 0;
+  p.table = table; p.temb = temb; p.temb_f32 = temb_is_f32; p.temb_L = temb_len;
+  p.rows_per_batch = rows_per_batch; p.shift_idx = 0; p.scale_idx = 1; p.temb_rows = 1;
+  return launch_ln(p, static_cast<cudaStream_t>(stream));
+}
+
+int wamb_copy_cols(const void* x, int64_t ldx_bytes, int32_t m, int32_t n_bytes, void* out, int64_t ldo_bytes,
+                   void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(m >= 0 && n_bytes > 0 && ldx_bytes >= n_bytes && ldo_bytes >= n_bytes, WAMB_ERR_SHAPE,
+               "copy_cols shape");
+  if (m == 0) return WAMB_OK;
+  WAMB_REQUIRE(x && out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  copy_cols_kernel<<<elem_grid(static_cast<long long>(m) * n_bytes, di.sms), 256, 0,
+                     static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(x), ldx_bytes, m, n_bytes,
+                                                          static_cast<uint8_t*>(out), ldo_bytes);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+int wamb_repeat_rows(const void* x, int32_t rows, int32_t row_bytes, int32_t repeat, void* out, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(rows >= 0 && row_bytes > 0 && repeat >= 1, WAMB_ERR_SHAPE, "repeat_rows shape");
+  if (rows == 0) return WAMB_OK;
+  WAMB_REQUIRE(x && out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  repeat_rows_kernel<<<elem_grid(static_cast<long long>(rows) * repeat * row_bytes, di.sms), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(x), rows, row_bytes, repeat,
+                                                            static_cast<uint8_t*>(out));
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
+int wamb_flow_step(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32, int64_t n, float dsigma,
+                   void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(n >= 0, WAMB_ERR_SHAPE, "flow step size");
+  if (n == 0) return WAMB_OK;
+  WAMB_REQUIRE(sample && v, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  flow_step_kernel<<<elem_grid(n, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(sample, sample_is_f32, v,
+                                                                                      v_is_f32, n, dsigma);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
 }
 
 }  // extern "C"

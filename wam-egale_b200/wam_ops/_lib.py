@@ -32,7 +32,7 @@ class LinearArgs(ctypes.Structure):
     ]
 
 
-EPI_BIAS, EPI_GELU, EPI_RES, EPI_RES_GATE = 0, 1, 2, 3
+EPI_BIAS, EPI_GELU, EPI_RES, EPI_RES_GATE, EPI_SILU = 0, 1, 2, 3, 4
 
 
 class AttentionArgs(ctypes.Structure):
@@ -91,6 +91,8 @@ EXPORTED = (
     "wamb_last_error", "wamb_abi_version", "wamb_device_status", "wamb_linear",
     "wamb_attention", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
     "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc", "wamb_quantize_rows",
+    "wamb_timestep_embedding", "wamb_silu", "wamb_embed_gather", "wamb_output_norm", "wamb_copy_cols",
+    "wamb_flow_step", "wamb_repeat_rows",
 )
 
 # Size of the fixed scratch array behind wamb_block_forward_noalloc.
@@ -125,6 +127,14 @@ def load():
     lib.wamb_block_forward_noalloc.argtypes = [ctypes.POINTER(BlockArgs), c_void_p]
     lib.wamb_quantize_rows.argtypes = [c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p, c_int64,
                                        c_void_p, c_void_p]
+    lib.wamb_timestep_embedding.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p]
+    lib.wamb_silu.argtypes = [c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p]
+    lib.wamb_embed_gather.argtypes = [c_void_p] + [c_int32] * 8 + [c_void_p, c_int32, c_void_p]
+    lib.wamb_output_norm.argtypes = [c_void_p, c_int32, c_int32, c_int32, ctypes.c_double, c_void_p, c_void_p,
+                                     c_int32, c_int32, c_int32, c_void_p, c_void_p]
+    lib.wamb_copy_cols.argtypes = [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p]
+    lib.wamb_repeat_rows.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]
+    lib.wamb_flow_step.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int64, ctypes.c_float, c_void_p]
     if lib.wamb_abi_version() != ABI_VERSION:
         raise WambError(f"{LIB_PATH} has ABI {lib.wamb_abi_version()}, expected {ABI_VERSION}: rebuild")
     _lib = lib

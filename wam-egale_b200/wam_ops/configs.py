@@ -72,7 +72,7 @@ def rope_freqs(grid, head_dim=128, theta=10000.0):
     hw = head_dim // 3
 
     def base(d):
-        return 1.0 / (theta ** (torch.arange(0, d, 2)[: d // 2].double() / d))
+        return 1.0 / (theta ** (torch.arange(0, d, 2, device=grid.device)[: d // 2].double() / d))
 
     parts = [grid[0][:, None].double() * base(f_dim), grid[1][:, None].double() * base(hw),
              grid[2][:, None].double() * base(hw)]
