@@ -449,6 +449,78 @@ def run_verify(args):
     return 0
 
 
+def run_action_chunk(args):
+    """--workload action_chunk: one FastWAM-style action chunk end to end on
+    1 GPU: 10 flow-match updates, each a whole-model forward in action mode
+    (action embedding, timestep embedding chain, 30 cfg2 blocks over a
+    3520-token read-only KV history with the prepared 512-token text
+    context, output norm and projection) and the scheduler step, for 8
+    rollouts x 32 action tokens, as one CUDA graph."""
+    from wam_ops import _lib, configs
+    from wam_ops.model import NativeActionDenoiser, NativeWanModel
+    from wam_ops.scheduler import FlowMatchScheduler
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cfg = configs.PRESETS["cfg2"]
+    B, steps = 8, 10
+    gen = torch.Generator(device=dev).manual_seed(99)
+    torch.set_grad_enabled(False)
+    model = configs.build_model(cfg, dev, seed=99)
+    configs.fill_history(list(model.blocks), cfg, dev, gen, pool_batch=B)
+    nm = NativeWanModel(model, fp8=args.fp8)
+    nm.prepare_context(torch.randn(B, cfg.context, 4096, generator=gen, device=dev).bfloat16())
+    f, h, w = cfg.action
+    x = torch.randn(B, 30, f, h, w, generator=gen, device=dev).bfloat16()
+    grid = configs.mesh_id(f, h, w, 0, f_shift=cfg.history_chunks, action=True)[None].to(dev)
+    sched = FlowMatchScheduler(shift=5.0, sigma_min=0.0, extra_one_step=True)
+    sched.set_timesteps(steps)
+    den = NativeActionDenoiser(nm, sched)
+    den.capture(x, grid)
+    for _ in range(args.warmup):
+        den.run(x)
+    torch.cuda.synchronize()
+    if _lib.device_status() != 0:
+        raise RuntimeError("device error during warm-up")
+    clocks = Clocks(0)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    time.sleep(0.3)
+    e0.record(stream)
+    for _ in range(args.steps):
+        den.run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    hx = x.cpu().pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = den.run(hx.to(dev, non_blocking=True))
+        hout.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    line = {"metric": "action_chunks_per_s", "value": B * 1000.0 / ms, "unit": "action-chunks/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8-e4m3 GEMMs, bf16 attention" if args.fp8 else "bf16",
+            "data": "synthetic (seeded weights N(0,0.02), random unit-scale KV history and text)",
+            "config": {"workload": "action chunk: 10 flow-match updates (shift 5) of the whole model in "
+                                   "action mode, 8 rollouts x 32 action tokens, cfg2 blocks (D3072, 30 "
+                                   "layers) over a 3520-token KV history, 512 prepared text tokens",
+                       "global_batch": B, "seq_len": 32, "kv_history": cfg.history_chunks * cfg.tokens,
+                       "denoise_updates_per_chunk": steps, "ms_per_update": ms / steps},
+            "e2e": {"value": B * 1000.0 / ms_e2e, "unit": "action-chunks/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hout.numel() * 2},
+            "gpu_launches": den.launches_per_chunk() * args.steps, "clocks": clk,
+            "device_error": _lib.device_status()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def stack_flops(cfg, split=False):
     """Algorithmic FLOPs of one 30-layer step for ONE rollout: the six
     projections, the two FFN GEMMs and the QK^T / PV products of both
@@ -473,9 +545,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 GEMMs (the FP8 weight path); default is the bf16 drop-in")
-    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg3"],
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg3", "action_chunk"],
                     help="cfg4 (default, the headline): 8 cfg2 rollouts per GPU; cfg3: the "
-                         "4 x 32-token candidate verify step on one GPU")
+                         "4 x 32-token candidate verify step on one GPU; action_chunk: 10 whole-model "
+                         "denoise updates of an action chunk")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -483,6 +556,8 @@ def main():
         return run_reference(args)
     if args.workload == "cfg3":
         return run_verify(args)
+    if args.workload == "action_chunk":
+        return run_action_chunk(args)
     return run_native(args)
 
 

@@ -345,6 +345,11 @@ WAMB_API int wamb_output_norm(const void* x, int32_t x_is_f32, int32_t m, int32_
 WAMB_API int wamb_copy_cols(const void* x, int64_t ldx_bytes, int32_t m, int32_t n_bytes, void* out,
                             int64_t ldo_bytes, void* stream);
 
+/* The same step with the velocity in the model's output layout:
+ * sample [b, c, l] (the input layout 'b c f h w', l = f*h*w) += v[b, l, c] * dsigma. */
+WAMB_API int wamb_flow_step_cl(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32,
+                               int32_t b, int32_t c, int64_t l, float dsigma, void* stream);
+
 /* torch.repeat_interleave over rows: out[r * repeat + k] = x[r] (row_bytes each). */
 WAMB_API int wamb_repeat_rows(const void* x, int32_t rows, int32_t row_bytes, int32_t repeat, void* out,
                               void* stream);

@@ -16,10 +16,10 @@ from pathlib import Path
 import pytest
 import torch
 
-from blockutil import assert_parity
+from blockutil import assert_parity, stats
 from oracle import wan_model as om
 from wam_ops import _lib
-from wam_ops.model import NativeWanModel
+from wam_ops.model import NativeActionDenoiser, NativeWanModel
 from wam_ops.scheduler import FlowMatchScheduler
 
 sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
@@ -117,3 +117,71 @@ def test_flow_step(cuda_device, kw, n):
     sn.step_(v.cuda().bfloat16(), sn.timesteps[0], x)
     ref = (sample.bfloat16().float() + v.bfloat16().float() * (float(so.sigmas[1]) - float(so.sigmas[0])))
     assert torch.allclose(x.float().cpu(), ref, rtol=2 ** -8, atol=1e-2)
+
+
+def test_action_chunk_denoiser(cuda_device):
+    """Three flow-match updates of an action chunk with a KV history: the
+    captured graph equals the eager native loop bit for bit, and follows the
+    fp32 oracle loop (model + scheduler) within the block gate."""
+    m = _oracle_model(seed=12)
+    inp = _inputs(True, 77)
+    pool, hist = 96, 64
+    g = torch.Generator().manual_seed(3)
+    for blk in m.blocks:
+        blk.attn1.init_kv_cache("pos", pool, 2, 128, "cpu", torch.float32, 2)
+        c = blk.attn1.attn_caches["pos"]
+        c["k"].copy_(torch.randn(c["k"].shape, generator=g).bfloat16().float())
+        c["v"].copy_(torch.randn(c["v"].shape, generator=g).bfloat16().float())
+        c["mask"][:hist] = True
+        c["id"][:hist] = torch.arange(hist) // 32
+    kw = {"shift": 5.0, "sigma_min": 0.0, "extra_one_step": True}
+    so, sn = om.FlowMatchScheduler(**kw), FlowMatchScheduler(**kw)
+    so.set_timesteps(3)
+    sn.set_timesteps(3)
+
+    def run_ref(model, sched, x, dev):
+        for t in sched.timesteps:
+            d = dict(inp, noisy_latents=x, timesteps=torch.full_like(inp["timesteps"], float(t)))
+            d = _cuda(d) if dev else d
+            v = model(d, action_mode=True)
+            B, C = x.shape[:2]
+            v = v.reshape(B, -1, C).permute(0, 2, 1).reshape(x.shape)
+            x = sched.step(v.float(), t, x.float()).to(x.dtype)
+        return x
+
+    def dev_copy():
+        d = _to_device(m)
+        for blk in d.blocks:
+            c = blk.attn1.attn_caches["pos"]
+            for k in list(c):
+                c[k] = c[k].to(device="cuda", dtype=torch.bfloat16 if k in ("k", "v") else c[k].dtype)
+        return d
+
+    with torch.no_grad():
+        ref = run_ref(m, so, inp["noisy_latents"], False)
+        rb = run_ref(dev_copy(), so, inp["noisy_latents"].cuda().bfloat16(), True)
+    dev = dev_copy()
+    nm = NativeWanModel(dev)
+    with torch.no_grad():
+        nm.prepare_context(_cuda(inp)["text_emb"])
+        x0 = _cuda(inp)["noisy_latents"]
+        eager = x0.clone()
+        for t in sn.timesteps:
+            v = nm({"noisy_latents": eager, "grid_id": inp["grid_id"].cuda(),
+                    "timesteps": torch.full((2, 8), float(t), device="cuda")}, action_mode=True)
+            B, C = eager.shape[:2]
+            _lib.check(_lib.load().wamb_flow_step_cl(eager.data_ptr(), 0, v.data_ptr(), 0, B, C, 32,
+                                                     sn.delta(t), _lib.stream_ptr()))
+        den = NativeActionDenoiser(nm, sn)
+        den.capture(x0, inp["grid_id"].cuda())
+        out = den.run(x0).clone()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert torch.equal(out, eager)
+    # Three updates each re-round the sample to bf16, so rounding differences
+    # compound along the loop: the bound is twice the reference's own bf16
+    # loop error here (measured: native 0.030, reference 0.021, cosine
+    # 0.999994); the single-forward tests above hold the plain gate.
+    err_ref = stats(rb, ref)["max_abs"]
+    s = assert_parity(out, ref, None, max_abs=max(2e-2, 2 * err_ref))
+    print("action chunk", s, "reference bf16 loop", err_ref)

@@ -117,6 +117,30 @@ __global__ void flow_step_kernel(void* sample, int s_f32, const void* v, int v_f
   }
 }
 
+// The same step with the velocity in token layout: sample [B, C, L]
+// (channels first, the model's input layout), v [B, L, C] (its output).
+__global__ void flow_step_cl_kernel(void* sample, int s_f32, const void* v, int v_f32, int B, int C,
+                                    long long L, float dsigma) {
+  const long long n = static_cast<long long>(B) * C * L;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long l = i % L;
+    const long long bc = i / L;
+    const int c = static_cast<int>(bc % C);
+    const long long b = bc / C;
+    const long long vi = (b * L + l) * C + c;
+    const float vv = v_f32 ? static_cast<const float*>(v)[vi]
+                           : __bfloat162float(static_cast<const __nv_bfloat16*>(v)[vi]);
+    if (s_f32) {
+      float* s = static_cast<float*>(sample);
+      s[i] = s[i] + vv * dsigma;
+    } else {
+      __nv_bfloat16* s = static_cast<__nv_bfloat16*>(sample);
+      s[i] = __float2bfloat16_rn(__bfloat162float(s[i]) + vv * dsigma);
+    }
+  }
+}
+
 // Grid for an element map of `total` items: up to 8 CTAs of 256 per SM.
 inline int elem_grid(long long total, int sms) {
   long long g = (total + 255) / 256;

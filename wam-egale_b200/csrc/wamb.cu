@@ -214,6 +214,22 @@ int wamb_repeat_rows(const void* x, int32_t rows, int32_t row_bytes, int32_t rep
   return WAMB_OK;
 }
 
+int wamb_flow_step_cl(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32, int32_t b, int32_t c,
+                      int64_t l, float dsigma, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(b >= 0 && c > 0 && l >= 0, WAMB_ERR_SHAPE, "flow step shape");
+  const long long n = static_cast<long long>(b) * c * l;
+  if (n == 0) return WAMB_OK;
+  WAMB_REQUIRE(sample && v, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  flow_step_cl_kernel<<<elem_grid(n, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      sample, sample_is_f32, v, v_is_f32, b, c, l, dsigma);
+  WAMB_CHECK_CUDA(cudaGetLastError());
+  return WAMB_OK;
+}
+
 int wamb_flow_step(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32, int64_t n, float dsigma,
                    void* stream) {
   using namespace wamb;

@@ -92,7 +92,7 @@ EXPORTED = (
     "wamb_attention", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
     "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc", "wamb_quantize_rows",
     "wamb_timestep_embedding", "wamb_silu", "wamb_embed_gather", "wamb_output_norm", "wamb_copy_cols",
-    "wamb_flow_step", "wamb_repeat_rows",
+    "wamb_flow_step", "wamb_repeat_rows", "wamb_flow_step_cl",
 )
 
 # Size of the fixed scratch array behind wamb_block_forward_noalloc.
@@ -133,6 +133,8 @@ def load():
     lib.wamb_output_norm.argtypes = [c_void_p, c_int32, c_int32, c_int32, ctypes.c_double, c_void_p, c_void_p,
                                      c_int32, c_int32, c_int32, c_void_p, c_void_p]
     lib.wamb_copy_cols.argtypes = [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p]
+    lib.wamb_flow_step_cl.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_int32, c_int64,
+                                      ctypes.c_float, c_void_p]
     lib.wamb_repeat_rows.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]
     lib.wamb_flow_step.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int64, ctypes.c_float, c_void_p]
     if lib.wamb_abi_version() != ABI_VERSION:

@@ -152,3 +152,30 @@ def fill_history(blocks, cfg, device, gen, pool_batch):
         c["mask"][:hist] = True
         c["id"][:hist] = torch.arange(hist, device=device) // Q
     return pool, hist
+
+
+def build_model(cfg, device, seed=0, text_dim=4096, action_dim=30, in_channels=48):
+    """A WanModel container (embedders, cfg.layers blocks, output head) with
+    seeded weights on `device`: Linear weights N(0, 0.02) bf16, biases 0,
+    tables randn / sqrt(D) fp32, norm gains 1 (the timestep embedder fp32, as
+    the reference keeps it, model.py:812-825)."""
+    from .model import WanModel
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    with torch.device("meta"):
+        m = WanModel(num_attention_heads=cfg.heads, in_channels=in_channels, out_channels=in_channels,
+                     action_dim=action_dim, text_dim=text_dim, ffn_dim=cfg.ffn, num_layers=cfg.layers)
+    m = m.to_empty(device=device)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            fp32 = name.endswith("scale_shift_table") or "norm2" in name or "time_embedder" in name
+            if name.endswith("scale_shift_table"):
+                v = torch.randn(p.shape, generator=gen, device=device) / cfg.dim ** 0.5
+            elif "norm" in name and name.endswith("weight"):
+                v = torch.ones(p.shape, device=device)
+            elif name.endswith("weight"):
+                v = torch.randn(p.shape, generator=gen, device=device) * 0.02
+            else:
+                v = torch.zeros(p.shape, device=device)
+            p.data = v.to(torch.float32 if fp32 else torch.bfloat16).contiguous()
+    return m.eval()

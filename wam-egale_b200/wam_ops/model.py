@@ -183,7 +183,9 @@ class NativeWanModel:
         ctx = None
         if self.text is None:
             ctx = self.embed_text(input_dict["text_emb"])
-        rope = rope_freqs(input_dict["grid_id"][0].to(device=x.device, dtype=torch.float64))
+        rope = input_dict.get("rotary_emb")
+        if rope is None:
+            rope = rope_freqs(input_dict["grid_id"][0].to(device=x.device, dtype=torch.float64))
         ph, pw = (1, 1) if action_mode else (p2, p3)
         temb, tproj = self.embed_time(input_dict["timesteps"], (H // ph) * (W // pw), action_mode)
         h = self.stack.forward(h, ctx, tproj, rope, update_cache, cache_name, candidate_cache_rows)
@@ -203,3 +205,68 @@ class NativeWanModel:
         return y.reshape(B, L * n_patch, n_real // n_patch)     # 'b l (n c) -> b (l n) c'
 
     __call__ = forward
+
+
+class NativeActionDenoiser:
+    """The action denoise loop of one chunk as one CUDA graph: `steps`
+    updates, each a NativeWanModel forward in action mode with
+    update_cache=0 (the KV history stays read-only) followed by the
+    flow-match step of the sample in place (FastWAM runs 10 such updates per
+    action chunk, fastwam-base/fullcode-v1/real_speculative.py:33,107). The
+    context must be prepared first (NativeWanModel.prepare_context)."""
+
+    def __init__(self, native_model, scheduler):
+        self.nm, self.sched = native_model, scheduler
+        self.graph, self.static = None, None
+
+    def capture(self, noisy_latents, grid_id, steps=None, frames_per_step=None):
+        """Record the chunk for inputs shaped like `noisy_latents`
+        ([B, action_dim, F, H, W]); each update k uses the scheduler's
+        timestep k for every frame."""
+        nm, sc = self.nm, self.sched
+        if nm.text is None:
+            raise RuntimeError("prepare_context() first")
+        steps = len(sc.timesteps) if steps is None else steps
+        x = noisy_latents.to(torch.bfloat16).contiguous().clone()
+        B, C, Fr, H, W = x.shape
+        L = Fr * H * W
+        ts = [torch.full((B, Fr), float(sc.timesteps[k]), device=x.device) for k in range(steps)]
+        rope = rope_freqs(grid_id[0].to(device=x.device, dtype=torch.float64))   # once per chunk
+        deltas = [sc.delta(sc.timesteps[k]) for k in range(steps)]
+        lib = _lib.load()
+
+        def chunk():
+            for k in range(steps):
+                v = nm.forward({"noisy_latents": x, "rotary_emb": rope, "timesteps": ts[k]}, 0, "pos", True)
+                _lib.check(lib.wamb_flow_step_cl(x.data_ptr(), 0, v.data_ptr(), 0, B, C, L, deltas[k],
+                                                 _lib.stream_ptr()))
+
+        with torch.no_grad():
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            saved = x.clone()
+            with torch.cuda.stream(s):
+                chunk()                       # warm-up (allocations, first-use setup)
+            torch.cuda.current_stream().wait_stream(s)
+            x.copy_(saved)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                chunk()
+        self.graph, self.static = g, {"x": x, "timesteps": ts, "steps": steps}
+        return self.static
+
+    def run(self, noisy_latents=None):
+        """Denoise one chunk: copy new noise in (if given), replay, return the sample."""
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        if noisy_latents is not None:
+            self.static["x"].copy_(noisy_latents, non_blocking=True)
+        self.graph.replay()
+        return self.static["x"]
+
+    def launches_per_chunk(self, with_cache=True):
+        """Kernel launches of one chunk: per update the stack's launches plus
+        gather, input GEMM, timestep features, 3 embedding GEMMs, SiLU,
+        output norm, output GEMM and the step (= 10), + 2 row repeats when
+        frames repeat over tokens, + 1 column copy for the 30-wide output."""
+        return self.static["steps"] * (self.nm.stack.launches_per_step(with_cache) + 13)
