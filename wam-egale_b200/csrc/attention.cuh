@@ -194,6 +194,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  pdl_wait();   // the tile list and Q/K/V of the previous kernels are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y;
   const int q0 = blockIdx.x * 256;

@@ -78,9 +78,8 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream) {
     configured[dev] = true;
   }
   dim3 grid((a->q_rows + 255) / 256, a->heads, a->batch);
-  attn_tc_kernel<<<grid, ATT_THREADS, AttnSmem::TOTAL, stream>>>(tq, tk0, tv0, tk1, tv1, p);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
+  return launch_kernel(attn_tc_kernel, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
+                       tv1, p);
 }
 
 // -------------------------------------------------------------- row kernels
@@ -116,17 +115,13 @@ inline int launch_ln(const LnParams& p, cudaStream_t s) {
   const int threads = p.D / (8 * vpt);
   return dispatch_vpt(vpt, [&](auto v) {
     constexpr int R = ln_rows(decltype(v)::value);
-    ln_kernel<decltype(v)::value><<<(p.M + R - 1) / R, threads, 0, s>>>(p);
-    WAMB_CHECK_CUDA(cudaGetLastError());
-    return static_cast<int>(WAMB_OK);
+    return launch_kernel(ln_kernel<decltype(v)::value>, dim3((p.M + R - 1) / R), dim3(threads), 0, s, p);
   });
 }
 
 inline int launch_quant(const QuantParams& p, cudaStream_t s) {
   if (p.M == 0) return WAMB_OK;
-  quant_rows_kernel<<<p.M, 256, 0, s>>>(p);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
+  return launch_kernel(quant_rows_kernel, dim3(p.M), dim3(256), 0, s, p);
 }
 
 inline int launch_rms(const RmsParams& p, cudaStream_t s) {
@@ -135,9 +130,7 @@ inline int launch_rms(const RmsParams& p, cudaStream_t s) {
   WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
   const int threads = p.D / (8 * vpt);
   return dispatch_vpt(vpt, [&](auto v) {
-    rms_rope_kernel<decltype(v)::value><<<p.M, threads, 0, s>>>(p);
-    WAMB_CHECK_CUDA(cudaGetLastError());
-    return static_cast<int>(WAMB_OK);
+    return launch_kernel(rms_rope_kernel<decltype(v)::value>, dim3(p.M), dim3(threads), 0, s, p);
   });
 }
 
@@ -350,8 +343,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     k.rows = reinterpret_cast<const long long*>(a->candidate_rows);
     k.batch = B; k.pool_batch = a->pool_batch;
     k.new_slots = slots; k.tiles = reinterpret_cast<int2*>(tiles); k.counts = counts;
-    kv_layout_kernel<<<1, KV_THREADS, 0, s>>>(k);
-    WAMB_CHECK_CUDA(cudaGetLastError());
+    if ((rc = launch_kernel(kv_layout_kernel, dim3(1), dim3(KV_THREADS), 0, s, k))) return rc;
   }
   // 2. LN1 + modulation (shift 0, scale 1)
   LnParams ln{};

@@ -93,6 +93,7 @@ __host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 2 ? 4 : (vpt 
 
 template <int VPT>
 __global__ void ln_kernel(const LnParams p) {
+  pdl_wait();
   constexpr int R = ln_rows(VPT);
   __shared__ float red[32 * R];
   const int row0 = blockIdx.x * R;
@@ -250,6 +251,7 @@ struct QuantParams {
 // One CTA per row: amax over the row (pass 1), then E4M3(x * 448 / amax)
 // (pass 2, re-reading the row from L1/L2).
 __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantParams p) {
+  pdl_wait();
   __shared__ float red[8];
   const long long row = blockIdx.x;
   float am = 0.f;
@@ -299,6 +301,7 @@ struct RmsParams {
 
 template <int VPT>
 __global__ void rms_rope_kernel(const RmsParams p) {
+  pdl_wait();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nthr = blockDim.x;
@@ -447,6 +450,7 @@ WAMB_DEV long long block_max_ll(long long v, long long* sh) {
 }
 
 __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams p) {
+  pdl_wait();
   __shared__ uint8_t m[KV_MAX_POOL];
   __shared__ int sh[33];
   __shared__ long long shl[32];

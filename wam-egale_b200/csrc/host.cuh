@@ -9,7 +9,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
+#include <utility>
 #include <string>
 
 #include "../../include/wamb.h"
@@ -87,6 +89,33 @@ inline int make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t rows, uint64
 inline int make_tmap_e4m3(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols,
                           uint64_t ld, uint32_t box_rows) {
   return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols, ld, box_rows, 128);
+}
+
+// Launch with programmatic stream serialization (see pdl_wait in
+// common.cuh); WAMB_PDL=0 in the environment turns it off (plain launches).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WAMB_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                         Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+  return WAMB_OK;
 }
 
 struct DeviceInfo {

@@ -21,9 +21,8 @@ inline int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap* tb, const Ge
   }
   const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * (p.N / BN) * (p.splits > 1 ? p.splits : 1);
   const int grid = tiles < sms ? tiles : sms;
-  gemm_tc_kernel<BN, STAGES, F8><<<grid, GEMM_THREADS, L::TOTAL, stream>>>(ta, tb[0], tb[1], tb[2], p);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
+  return launch_kernel(gemm_tc_kernel<BN, STAGES, F8>, dim3(grid), dim3(GEMM_THREADS), L::TOTAL, stream, ta, tb[0],
+                       tb[1], tb[2], p);
 }
 
 // Two-CTA launch: clusters of 2 along x, one cluster per pair of SMs.
@@ -37,11 +36,13 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
   cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = Gemm2Smem::TOTAL;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (resident[dev] == 0) {
@@ -55,6 +56,7 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
   const int tiles = ((p.M + 255) / 256) * (p.N / 256);
   const int pairs = tiles < resident[dev] ? tiles : resident[dev];
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<F8>, ta, tb[0], tb[1], tb[2], p));
   return WAMB_OK;
 }

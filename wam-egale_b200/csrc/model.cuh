@@ -21,6 +21,7 @@
 namespace wamb {
 
 __global__ void timestep_embed_kernel(const float* t, int n, int dim, __nv_bfloat16* out) {
+  pdl_wait();
   const int half = dim / 2;
   const long long total = static_cast<long long>(n) * half;
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
@@ -37,6 +38,7 @@ __global__ void timestep_embed_kernel(const float* t, int n, int dim, __nv_bfloa
 
 __global__ void silu_kernel(const void* x, long long ldx, int x_f32, int m, int n, __nv_bfloat16* out,
                             long long ldo) {
+  pdl_wait();
   const long long total = static_cast<long long>(m) * n;
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -56,6 +58,7 @@ struct GatherParams {
 };
 
 __global__ void embed_gather_kernel(const GatherParams p) {
+  pdl_wait();
   const int Fn = p.F / p.p1, Hn = p.H / p.p2, Wn = p.W / p.p3;
   const long long L = static_cast<long long>(Fn) * Hn * Wn;
   const int K = p.C * p.p1 * p.p2 * p.p3;
@@ -82,6 +85,7 @@ __global__ void embed_gather_kernel(const GatherParams p) {
 
 __global__ void copy_cols_kernel(const uint8_t* x, long long ldx_bytes, int m, int n_bytes, uint8_t* out,
                                  long long ldo_bytes) {
+  pdl_wait();
   const long long total = static_cast<long long>(m) * n_bytes;
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -92,6 +96,7 @@ __global__ void copy_cols_kernel(const uint8_t* x, long long ldx_bytes, int m, i
 }
 
 __global__ void repeat_rows_kernel(const uint8_t* x, int rows, int row_bytes, int repeat, uint8_t* out) {
+  pdl_wait();
   const long long total = static_cast<long long>(rows) * repeat * row_bytes;
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -103,6 +108,7 @@ __global__ void repeat_rows_kernel(const uint8_t* x, int rows, int row_bytes, in
 
 __global__ void flow_step_kernel(void* sample, int s_f32, const void* v, int v_f32, long long n,
                                  float dsigma) {
+  pdl_wait();
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const float vv = v_f32 ? static_cast<const float*>(v)[i]
@@ -121,6 +127,7 @@ __global__ void flow_step_kernel(void* sample, int s_f32, const void* v, int v_f
 // (channels first, the model's input layout), v [B, L, C] (its output).
 __global__ void flow_step_cl_kernel(void* sample, int s_f32, const void* v, int v_f32, int B, int C,
                                     long long L, float dsigma) {
+  pdl_wait();
   const long long n = static_cast<long long>(B) * C * L;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {

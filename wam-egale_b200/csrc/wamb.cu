@@ -123,10 +123,8 @@ int wamb_timestep_embedding(const float* t, int32_t n, int32_t dim, void* out, v
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  timestep_embed_kernel<<<elem_grid(static_cast<long long>(n) * dim / 2, di.sms), 256, 0,
-                          static_cast<cudaStream_t>(stream)>>>(t, n, dim, static_cast<__nv_bfloat16*>(out));
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
+  return launch_kernel(timestep_embed_kernel, dim3(elem_grid(static_cast<long long>(n) * dim / 2, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       t, n, dim, static_cast<__nv_bfloat16*>(out));
 }
 
 int wamb_silu(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, int32_t n, void* out, int64_t ldo,
@@ -138,10 +136,9 @@ int wamb_silu(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, int32_t n
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  silu_kernel<<<elem_grid(static_cast<long long>(m) * n, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  return launch_kernel(silu_kernel, dim3(elem_grid(static_cast<long long>(m) * n, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       
       x, ldx, x_is_f32, m, n, static_cast<__nv_bfloat16*>(out), ldo);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
 }
 
 int wamb_embed_gather(const void* x, int32_t b, int32_t c, int32_t f, int32_t h, int32_t w, int32_t p1,
@@ -158,9 +155,8 @@ int wamb_embed_gather(const void* x, int32_t b, int32_t c, int32_t f, int32_t h,
   GatherParams p{static_cast<const __nv_bfloat16*>(x), b, c, f, h, w, p1, p2, p3,
                  static_cast<__nv_bfloat16*>(out), ldo};
   const long long total = static_cast<long long>(b) * (f / p1) * (h / p2) * (w / p3) * ldo;
-  embed_gather_kernel<<<elem_grid(total, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
+  return launch_kernel(embed_gather_kernel, dim3(elem_grid(total, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       p);
 }
 
 int wamb_output_norm(const void* x, int32_t x_is_f32, int32_t m, int32_t d, double eps, const float* table,
@@ -192,11 +188,9 @@ int wamb_copy_cols(const void* x, int64_t ldx_bytes, int32_t m, int32_t n_bytes,
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  copy_cols_kernel<<<elem_grid(static_cast<long long>(m) * n_bytes, di.sms), 256, 0,
-                     static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(x), ldx_bytes, m, n_bytes,
+  return launch_kernel(copy_cols_kernel, dim3(elem_grid(static_cast<long long>(m) * n_bytes, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const uint8_t*>(x), ldx_bytes, m, n_bytes,
                                                           static_cast<uint8_t*>(out), ldo_bytes);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
 }
 
 int wamb_repeat_rows(const void* x, int32_t rows, int32_t row_bytes, int32_t repeat, void* out, void* stream) {
@@ -207,11 +201,9 @@ int wamb_repeat_rows(const void* x, int32_t rows, int32_t row_bytes, int32_t rep
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  repeat_rows_kernel<<<elem_grid(static_cast<long long>(rows) * repeat * row_bytes, di.sms), 256, 0,
-                       static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(x), rows, row_bytes, repeat,
+  return launch_kernel(repeat_rows_kernel, dim3(elem_grid(static_cast<long long>(rows) * repeat * row_bytes, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const uint8_t*>(x), rows, row_bytes, repeat,
                                                             static_cast<uint8_t*>(out));
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
 }
 
 int wamb_flow_step_cl(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32, int32_t b, int32_t c,
@@ -224,10 +216,9 @@ int wamb_flow_step_cl(void* sample, int32_t sample_is_f32, const void* v, int32_
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  flow_step_cl_kernel<<<elem_grid(n, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  return launch_kernel(flow_step_cl_kernel, dim3(elem_grid(n, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       
       sample, sample_is_f32, v, v_is_f32, b, c, l, dsigma);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
 }
 
 int wamb_flow_step(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32, int64_t n, float dsigma,
@@ -239,10 +230,9 @@ int wamb_flow_step(void* sample, int32_t sample_is_f32, const void* v, int32_t v
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  flow_step_kernel<<<elem_grid(n, di.sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(sample, sample_is_f32, v,
+  return launch_kernel(flow_step_kernel, dim3(elem_grid(n, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       sample, sample_is_f32, v,
                                                                                       v_is_f32, n, dsigma);
-  WAMB_CHECK_CUDA(cudaGetLastError());
-  return WAMB_OK;
 }
 
 }  // extern "C"
