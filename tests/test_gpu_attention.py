@@ -114,3 +114,25 @@ def test_broadcast_source(cuda_device):
     ref = _sdpa_ref(q.view(B, Q, H, 128), k.view(1, C, H, 128).expand(B, -1, -1, -1),
                     v.view(1, C, H, 128).expand(B, -1, -1, -1))
     _check(out.view(B, Q, H, 128), ref)
+
+
+@pytest.mark.parametrize("Sq,Sk,hot", [(100, 1000, "first"), (100, 1000, "second"), (128, 3553, "last"),
+                                       (77, 257, "none"), (384, 1900, "second")])
+def test_split_kv_single_tile(cuda_device, Sq, Sk, hot):
+    """A CTA holding one query tile runs the first half of the key tiles on
+    TMEM slot A and the second half on slot B, then merges the two partial
+    softmaxes. Keys scaled up in one half put the row max (and the 2^8 rescale
+    steps) in that half only, so a wrong merge weight shows."""
+    g = torch.Generator(device="cuda").manual_seed(Sq * 31 + Sk)
+    B, H = 2, 2
+    q = torch.randn(B, Sq, H, 128, device="cuda", generator=g)
+    k = torch.randn(B, Sk, H, 128, device="cuda", generator=g)
+    v = torch.randn(B, Sk, H, 128, device="cuda", generator=g)
+    if hot == "first":
+        k[:, : Sk // 4] *= 3
+    elif hot == "second":
+        k[:, -Sk // 4:] *= 3
+    elif hot == "last":
+        k[:, -5:] *= 4
+    q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    _check(ops.sdpa(q, k, v), _sdpa_ref(q, k, v))

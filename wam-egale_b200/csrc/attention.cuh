@@ -23,6 +23,10 @@
 //               softmax runs the tensor core works on the other tile.
 //               S = Q K^T reads both operands from SMEM; O += P V reads P
 //               from TMEM and V from SMEM as an MN-major operand.
+// A CTA with a single query tile (q_rows <= 128, or the last 128 rows of a
+// longer query) would leave slot B idle and lose the ping-pong, so it splits
+// its keys instead: slot A takes key tiles [0, ceil(n/2)), slot B the rest,
+// both against Q_A, and the epilogue merges the two partial softmaxes.
 // TMEM columns: S/P of A [0,128), S/P of B [128,256), O_A [256,384), O_B [384,512).
 // SMEM: Q_A, Q_B and a 5-slot K/V ring of 128 rows x 128 bf16 tiles (224 KB).
 //
@@ -186,7 +190,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t p_full = bar0 + 104;     // [2] by query tile
   const uint32_t o_done = bar0 + 120;
   const uint32_t drain = bar0 + 128;
-  // Load L (K_j: L = 2j, V_j: L = 2j+1) lives in slot L % 5; its phase is (L / 5) & 1.
+  // Ring load L (the L-th K or V tile in consumption order; K_j = 2j and
+  // V_j = 2j+1 without split-KV) lives in slot L % 5, phase (L / 5) & 1.
   auto slot_addr = [&](int L) { return sRing + (L % ATT_SLOTS) * ATT_TILE_BYTES; };
   auto slot_full = [&](int L) { return full + 8 * (L % ATT_SLOTS); };
   auto slot_empty = [&](int L) { return empty + 8 * (L % ATT_SLOTS); };
@@ -202,6 +207,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const int n0 = p.tiles != nullptr ? *p.n_tiles : (p.src0_len + 127) / 128;
   const int n1 = p.has_src1 ? (p.q_rows + 127) / 128 : 0;
   const int n = n0 + n1;
+  // Split-KV: a CTA with one query tile runs its keys as two halves, [0, nA)
+  // in TMEM slot A and [nA, n) in slot B (both against Q_A), so the two-slot
+  // ping-pong still overlaps softmax with MMAs; the epilogue merges the halves.
+  const bool split = !has_b && n >= 2;
+  const int nA = split ? (n + 1) >> 1 : n;
+  const int nB = split ? n - nA : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -247,19 +258,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         vc = (t.src ? p.v1_col : p.v0_col) + h * 128;
       };
       int issued = 0;   // ring loads issued
-      for (int L = 0; L < 2 * n; ++L) {
-        const int j = L >> 1;
+      bool go = true;
+      auto emit = [&](int j, bool is_v) {
+        if (!go) return;
+        const int L = issued;
         const KvTile t = att_tile(p, j, n0, b);
         const CUtensorMap *mk, *mv;
         int kc, vc;
         src_of(t, mk, mv, kc, vc);
-        if (!mbar_wait(slot_empty(L), slot_phase(L) ^ 1, abort_flag)) break;
-        const CUtensorMap* m = (L & 1) ? mv : mk;
-        const int col = (L & 1) ? vc : kc;
+        if (!mbar_wait(slot_empty(L), slot_phase(L) ^ 1, abort_flag)) { go = false; return; }
+        const CUtensorMap* m = is_v ? mv : mk;
+        const int col = is_v ? vc : kc;
         mbar_arrive_expect_tx(slot_full(L), ATT_TILE_BYTES);
         tma_load_2d(slot_addr(L), m, slot_full(L), col, t.row);
         tma_load_2d(slot_addr(L) + ATT_ATOM, m, slot_full(L), col + 64, t.row);
         issued = L + 1;
+      };
+      if (split) {
+        // K_A(0), K_B(0), then V_A(j), K_A(j+1), V_B(j), K_B(j+1): the MMA order.
+        emit(0, false);
+        emit(nA, false);
+        for (int j = 0; j < nA; ++j) {
+          emit(j, true);
+          if (j + 1 < nA) emit(j + 1, false);
+          if (j < nB) {
+            emit(nA + j, true);
+            if (j + 1 < nB) emit(nA + j + 1, false);
+          }
+        }
+      } else {
+        for (int j = 0; j < n; ++j) {
+          emit(j, false);
+          emit(j, true);
+        }
       }
       // Teardown: loads still in flight must land before the CTA exits.
       mbar_wait_teardown(q_full, 0);
@@ -272,46 +303,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0);
     constexpr uint32_t IDESC_O = idesc_bf16(128, 128, 1);
     const int ntq = has_b ? 2 : 1;
-    // S_t = Q_t K_j^T (ring load 2j) into TMEM columns [t*128, t*128+128).
-    auto issue_s = [&](int t, int j) {
-      {
-        const uint32_t qb = sQ + t * ATT_TILE_BYTES;
-        const uint32_t kb = slot_addr(2 * j);
+    // S_t = Q K^T into TMEM columns [t*128, t*128+128); Q at qb, K at ring address kb.
+    auto issue_s = [&](int t, uint32_t qb, uint32_t kb) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * ATT_ATOM + (kk & 3) * 32;
-          umma_bf16(tmem + t * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
-                    IDESC_S, kk > 0);
-        }
-        umma_commit(s_full + 8 * t);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * ATT_ATOM + (kk & 3) * 32;
+        umma_bf16(tmem + t * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
+                  IDESC_S, kk > 0);
       }
+      umma_commit(s_full + 8 * t);
     };
-    // O_t += P_t V_j (ring load 2j+1); P_t is packed bf16 in TMEM columns [t*128, t*128+64).
-    auto issue_pv = [&](int t, int j, int ksteps, bool acc) {
-      {
-        const uint32_t vb = slot_addr(2 * j + 1);
-        for (int kk = 0; kk < ksteps; ++kk)
-          umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                       sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, acc || kk > 0);
-      }
+    // O_t += P_t V (V at ring address vb); P_t is packed bf16 in TMEM columns [t*128, t*128+64).
+    auto issue_pv = [&](int t, uint32_t vb, int ksteps, bool acc) {
+      for (int kk = 0; kk < ksteps; ++kk)
+        umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                     sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, acc || kk > 0);
     };
-    bool ok = mbar_wait(q_full, 0, abort_flag);
-    if (ok && n > 0) {
-      ok = mbar_wait(slot_full(0), slot_phase(0), abort_flag);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < ntq; ++t) issue_s(t, 0);
-        umma_commit(slot_empty(0));
-      }
-    }
-    for (int j = 0; ok && j < n; ++j) {
-      const KvTile tl = att_tile(p, j, n0, b);
-      const int ksteps = (tl.len + 15) >> 4;
-      if (!mbar_wait(slot_full(2 * j + 1), slot_phase(2 * j + 1), abort_flag)) break;
-      if (tl.len & 15) {
-        // Zero V rows [len, 16*ksteps) in both 64-column halves.
-        uint8_t* vt = smem + L::RING_OFF + ((2 * j + 1) % ATT_SLOTS) * ATT_TILE_BYTES;
-        const int r0 = tl.len, r1 = ksteps * 16;
+    // Zero V rows [len, 16*ceil(len/16)) of ring load L in both 64-column halves.
+    auto zero_v_tail = [&](int L, int len) {
+      if (len & 15) {
+        uint8_t* vt = smem + L::RING_OFF + (L % ATT_SLOTS) * ATT_TILE_BYTES;
+        const int r0 = len, r1 = ((len + 15) >> 4) * 16;
         for (int i = 0; i < (r1 - r0) * 16; ++i) {
           const int r = r0 + (i >> 4), c = i & 15;
           uint8_t* dst = vt + (c >> 3) * ATT_ATOM + r * 128 + (c & 7) * 16;
@@ -319,20 +331,69 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         fence_proxy_async();
       }
+    };
+    auto wait_full = [&](int L) { return mbar_wait(slot_full(L), slot_phase(L), abort_flag); };
+    bool ok = mbar_wait(q_full, 0, abort_flag);
+    if (split) {
+      // Loads: K_A(0) = 0, K_B(0) = 1, then V_A(j), K_A(j+1), V_B(j), K_B(j+1).
+      for (int t = 0; ok && t < 2; ++t) {
+        ok = wait_full(t);
+        if (ok) {
+          tc_fence_after();
+          issue_s(t, sQ, slot_addr(t));
+          umma_commit(slot_empty(t));
+        }
+      }
+      int Lc = 2;
+      for (int j = 0; ok && j < nA; ++j) {
+        for (int t = 0; ok && t < 2; ++t) {
+          const int nt = t ? nB : nA;
+          if (j >= nt) break;
+          const int len = att_tile(p, t ? nA + j : j, n0, b).len;
+          if (!wait_full(Lc)) { ok = false; break; }
+          zero_v_tail(Lc, len);
+          if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, slot_addr(Lc), (len + 15) >> 4, j > 0);
+          umma_commit(slot_empty(Lc));
+          ++Lc;
+          if (j + 1 < nt) {
+            if (!wait_full(Lc)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(t, sQ, slot_addr(Lc));
+            umma_commit(slot_empty(Lc));
+            ++Lc;
+          }
+        }
+      }
+    }
+    if (!split && ok && n > 0) {
+      ok = wait_full(0);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < ntq; ++t) issue_s(t, sQ + t * ATT_TILE_BYTES, slot_addr(0));
+        umma_commit(slot_empty(0));
+      }
+    }
+    for (int j = 0; !split && ok && j < n; ++j) {
+      const KvTile tl = att_tile(p, j, n0, b);
+      const int ksteps = (tl.len + 15) >> 4;
+      if (!wait_full(2 * j + 1)) break;
+      zero_v_tail(2 * j + 1, tl.len);
       const bool next = j + 1 < n;
       bool knext = false;
       for (int t = 0; t < ntq; ++t) {
         if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(t, j, ksteps, j > 0);
+        issue_pv(t, slot_addr(2 * j + 1), ksteps, j > 0);
         if (t == ntq - 1) umma_commit(slot_empty(2 * j + 1));
         if (next) {
           if (!knext) {
-            if (!mbar_wait(slot_full(2 * j + 2), slot_phase(2 * j + 2), abort_flag)) { ok = false; break; }
+            if (!wait_full(2 * j + 2)) { ok = false; break; }
             tc_fence_after();
             knext = true;
           }
-          issue_s(t, j + 1);
+          issue_s(t, sQ + t * ATT_TILE_BYTES, slot_addr(2 * j + 2));
         }
       }
       if (ok && next) umma_commit(slot_empty(2 * j + 2));
@@ -348,11 +409,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int wq = warp & 3;          // TMEM lane quarter
     const int r = wq * 32 + lane;     // query row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    const bool active = t == 0 || has_b;
+    const bool active = t == 0 || has_b || split;
+    const int nt = split ? (t ? nB : nA) : n;   // key tiles of this slot
+    const int kv0 = split && t ? nA : 0;        // its first key tile
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; active && ok && j < n; ++j) {
-      const int len = att_tile(p, j, n0, b).len;
+    for (int j = 0; active && ok && j < nt; ++j) {
+      const int len = att_tile(p, kv0 + j, n0, b).len;
       if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       float s[128];
@@ -429,7 +492,53 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       l = l * alpha + (sv.x + sv.y);
       m_used = m_new;
     }
-    if (active) {
+    if (split) {
+      // Merge the halves. Each slot's O and l are relative to its own stale
+      // max m; the row's result is (2^(mA-M) O_A + 2^(mB-M) O_B) /
+      // (2^(mA-M) lA + 2^(mB-M) lB), M = max(mA, mB). The (m, l) pairs meet
+      // in the unused Q_B tile; warps of slot A store output columns [0, 64),
+      // warps of slot B columns [64, 128) of the same rows.
+      if (ok) ok = mbar_wait(o_done, 0, abort_flag);
+      tc_fence_after();
+      float* xch = reinterpret_cast<float*>(smem + L::Q_OFF + ATT_TILE_BYTES);
+      xch[t * 256 + r] = m_used;
+      xch[t * 256 + 128 + r] = l;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float m_o = xch[(t ^ 1) * 256 + r], l_o = xch[(t ^ 1) * 256 + 128 + r];
+      const float mA = t ? m_o : m_used, lA = t ? l_o : l;
+      const float mB = t ? m_used : m_o, lB = t ? l : l_o;
+      const float M = fmaxf(mA, mB);
+      const float aA = mA == -INFINITY ? 0.f : exp2f(mA - M);
+      const float aB = mB == -INFINITY ? 0.f : exp2f(mB - M);
+      const float den = aA * lA + aB * lB;
+      const float inv = (ok && !*abort_flag && den > 0.f) ? 1.f / den : 0.f;
+      const float sA = aA * inv, sB = aB * inv;
+      const int qr = q0 + r;
+      const bool store = qr < p.q_rows;
+      __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128 + t * 64;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        float oa[32], ob[32];
+        tmem_ld32(tmem + lane_base + 256 + t * 64 + c * 32, oa);
+        tmem_ld32(tmem + lane_base + 384 + t * 64 + c * 32, ob);
+        tmem_wait_ld();
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = oa[8 * k + i] * sA + ob[8 * k + i] * sB;
+            uint4 w;
+            w.x = pack_bf16(v[0], v[1]);
+            w.y = pack_bf16(v[2], v[3]);
+            w.z = pack_bf16(v[4], v[5]);
+            w.w = pack_bf16(v[6], v[7]);
+            dst[k] = w;
+          }
+        }
+      }
+    } else if (active) {
       if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
       tc_fence_after();
       const int qr = q0 + t * 128 + r;
