@@ -113,14 +113,11 @@ typedef struct wamb_linear_args {
   int32_t a_is_fp8;
   const float* a_scale;
   const float* w_scale[3];
-  /* Optional split-K workspace (NULL: never split). When the output tiles
-   * would leave SMs idle (small M), K is split across CTAs whose fp32
-   * partials meet in this buffer (256-byte aligned); a call that cannot fit
-   * its plan in split_ws_bytes runs unsplit. Contents need not be zero;
-   * calls that overlap on the GPU must not share it. */
-  void* split_ws;
-  int64_t split_ws_bytes;
 } wamb_linear_args;
+/* When the output tiles would leave SMs idle (small M), wamb_linear splits K
+ * across the CTAs of a thread-block cluster: their fp32 partials meet in the
+ * cluster's shared memory and are summed in split order, so the result does
+ * not depend on timing and no workspace is needed. */
 
 WAMB_API int wamb_linear(const wamb_linear_args* args, void* stream);
 
@@ -206,9 +203,6 @@ WAMB_API int wamb_attention(const wamb_attention_args* args, void* stream);
  *
  * Scratch: `workspace` of wamb_block_workspace_bytes() bytes (caller-owned,
  * 256-byte aligned); intermediates stay there after the call (debug taps).
- * For small token counts the size includes split-K scratch for the GEMMs at
- * its end (offset WAMB_TAP_SPLITK of wamb_block_workspace_layout); a
- * workspace that stops at that offset also works, with unsplit GEMMs.
  */
 typedef struct wamb_block_args {
   int32_t batch, tokens, dim, heads, ffn_dim;
@@ -265,8 +259,7 @@ enum wamb_tap {
   WAMB_TAP_KV_COUNTS = 14,  /* [2] int32: tiles, visible slots */
   WAMB_TAP_A8 = 15,         /* fp8 only: [M, F] E4M3, the last quantized GEMM input */
   WAMB_TAP_A8_SCALE = 16,   /* fp8 only: [M] fp32 per-row scales of WAMB_TAP_A8 */
-  WAMB_TAP_SPLITK = 17,     /* small M only: split-K scratch of the GEMMs (not a tap: no meaning after the call) */
-  WAMB_TAP_COUNT = 18
+  WAMB_TAP_COUNT = 17
 };
 
 WAMB_API size_t wamb_block_workspace_bytes(const wamb_block_args* args);

@@ -120,16 +120,17 @@ def test_linear_rejects_bad_shapes():
     assert lib.wamb_linear(a, None) == 2
 
 
-def test_workspace_layout_split_region():
-    """Small token counts reserve split-K scratch at the end of the
-    workspace (optional: the layout's SPLITK offset is enough to run);
-    large ones reserve none."""
+def test_workspace_layout_is_the_taps():
+    """The workspace holds the named intermediates only (small-M GEMMs reduce
+    their split-K partials in cluster shared memory, not in the workspace):
+    the last tap ends the layout, and a 224-row D 3072 verify batch fits the
+    no-allocation entry point's fixed scratch."""
     lib = _lib.load()
-    small = _args(batch=4, tokens=32, dim=3072, heads=24, ffn_dim=14336)
     offs = (ctypes.c_int64 * len(_lib.TAPS))()
+    small = _args(batch=7, tokens=32, dim=3072, heads=24, ffn_dim=14336)
     total = lib.wamb_block_workspace_layout(small, offs)
-    sk = offs[_lib.TAPS.index("splitk")]
-    assert sk > 0 and total > sk and sk == max(o for o in offs if o >= 0)
-    big = _args(batch=8, tokens=880, dim=3072, heads=24, ffn_dim=14336)
-    lib.wamb_block_workspace_layout(big, offs)
-    assert offs[_lib.TAPS.index("splitk")] == -1
+    assert lib.wamb_block_workspace_bytes(small) == total
+    gelu = offs[_lib.TAPS.index("gelu")]
+    assert gelu == max(o for o in offs if o >= 0)          # no cache, bf16: GELU output is last
+    assert total == (gelu + 7 * 32 * 14336 * 2 + 255) // 256 * 256
+    assert total <= _lib.NOALLOC_SCRATCH_BYTES

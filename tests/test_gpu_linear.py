@@ -2,7 +2,8 @@
 
 Shapes with M >= 512, N per group a multiple of 256 and at least 74
 256 x 256 tiles take the two-CTA (cta_group::2) kernel; the others the
-one-CTA kernel with 64/128/256-column tiles.
+one-CTA kernel with 64/128/256-column tiles, split along K across a
+thread-block cluster when the tiles alone would leave SMs idle.
 
 Tolerance: the kernel accumulates in fp32 and rounds once to bf16, so the
 error against an fp32 reference of the same bf16 operands is bounded by the
@@ -107,22 +108,27 @@ def test_linear_pair_epilogues(cuda_device, res_f32):
 @pytest.mark.parametrize("m,k,n,groups,epi", [
     (128, 8192, 3072, 1, "bias"), (128, 14336, 3072, 1, "res_gate"), (224, 8192, 1536, 3, "bias"),
     (100, 4096, 2560, 1, "gelu"), (128, 14336, 3072, 1, "res"),
+    # K 3072: the verify batch's O / cross projections and a 2 x 128-row tile column
+    (128, 3072, 3072, 1, "res_bf16"), (224, 3072, 3072, 1, "res_gate"), (256, 3072, 3072, 3, "bias"),
 ])
 def test_linear_split_k(cuda_device, m, k, n, groups, epi):
-    """Small M with a split-K workspace: K is split across CTAs and the last
-    split of each tile slice sums the partials; the result must meet the
-    same bound as the unsplit GEMM and equal it in split order twice."""
+    """Small M (the output tiles leave SMs idle): K is split across the CTAs
+    of a thread-block cluster, which sum their partials in split order
+    through shared memory; the result meets the unsplit GEMM's bound and is
+    bitwise the same on a second call."""
     g = torch.Generator(device="cuda").manual_seed(m + k + n)
     a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
     ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16() for _ in range(groups)]
     bs = [torch.randn(n, device="cuda", generator=g).bfloat16() for _ in range(groups)]
-    split = torch.empty(16 << 20, dtype=torch.uint8, device="cuda")
-    split.fill_(0xAB)   # garbage counters: the call must zero what it needs
     N = n * groups
     kw, ref = {}, _ref(a, ws, bs)
     if epi == "gelu":
         kw["epilogue"] = _lib.EPI_GELU
         ref = torch.nn.functional.gelu(ref, approximate="tanh")
+    elif epi == "res_bf16":
+        res = torch.randn(m, N, device="cuda", generator=g).bfloat16()
+        kw.update(epilogue=_lib.EPI_RES, res=res)
+        ref = res.float() + ref
     elif epi in ("res", "res_gate"):
         res = torch.randn(m, N, device="cuda", generator=g)
         kw.update(epilogue=_lib.EPI_RES if epi == "res" else _lib.EPI_RES_GATE, res=res)
@@ -134,12 +140,10 @@ def test_linear_split_k(cuda_device, m, k, n, groups, epi):
         else:
             ref = res + ref
         kw["out"] = torch.empty(m, N, device="cuda", dtype=torch.float32)
-    out1 = ops.linear(a, ws, bs, split_ws=split, **kw)
+    out1 = ops.linear(a, ws, bs, **kw)
     out1 = out1.clone()
-    out2 = ops.linear(a, ws, bs, split_ws=split, **kw)
+    out2 = ops.linear(a, ws, bs, **kw)
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     _close(out1, ref)
     assert torch.equal(out1, out2)            # deterministic: partials summed in split order
-    tiles = (m + 127) // 128 * (N // 128)
-    assert torch.count_nonzero(split[:tiles * 8 * 4]) == 0   # the tile counters are left at zero

@@ -137,8 +137,7 @@ inline int launch_rms(const RmsParams& p, cudaStream_t s) {
 // ------------------------------------------------------------ block forward
 struct BlockLayout {
   int64_t off[WAMB_TAP_COUNT];
-  size_t total;     // with the optional split-K scratch (WAMB_TAP_SPLITK) at the end
-  size_t minimum;   // without it: enough to run (small-M GEMMs then run unsplit)
+  size_t total;
 };
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -179,11 +178,6 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
     put(WAMB_TAP_KV_TILES, static_cast<size_t>(a->pool) * 8);
     put(WAMB_TAP_KV_COUNTS, 16);
   }
-  L.minimum = o;
-  const int m = static_cast<int>(M), d = a->dim, fd = a->ffn_dim;
-  if (gemm_would_split(m, 3 * d, d, d, f8) || gemm_would_split(m, d, d, d, f8) ||
-      gemm_would_split(m, fd, fd, d, f8) || gemm_would_split(m, d, d, fd, f8))
-    put(WAMB_TAP_SPLITK, kSplitReserveBytes);
   L.total = o;
   return L;
 }
@@ -246,8 +240,8 @@ inline int check_block_args(const wamb_block_args* a) {
                  "candidate verification requires existing read-only KV");
   }
   const BlockLayout L = block_layout(a);
-  WAMB_REQUIRE(a->workspace != nullptr && a->workspace_bytes >= L.minimum, WAMB_ERR_WORKSPACE,
-               "workspace of %zu bytes needed (%zu given)", L.minimum, a->workspace_bytes);
+  WAMB_REQUIRE(a->workspace != nullptr && a->workspace_bytes >= L.total, WAMB_ERR_WORKSPACE,
+               "workspace of %zu bytes needed (%zu given)", L.total, a->workspace_bytes);
   WAMB_REQUIRE(reinterpret_cast<uintptr_t>(a->workspace) % 256 == 0, WAMB_ERR_ALIGN,
                "workspace must be 256-byte aligned");
   return WAMB_OK;
@@ -301,18 +295,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   int* slots = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_SLOTS]) : nullptr;
   int* tiles = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_TILES]) : nullptr;
   int* counts = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_COUNTS]) : nullptr;
-  // Split-K scratch of the small-M GEMMs, when the workspace has room for it;
-  // its counters are zeroed once here and every split GEMM leaves them zero.
-  void* split_ws = nullptr;
-  if (L.off[WAMB_TAP_SPLITK] >= 0 && a->workspace_bytes >= L.total) {
-    split_ws = ws + L.off[WAMB_TAP_SPLITK];
-    WAMB_CHECK_CUDA(cudaMemsetAsync(split_ws, 0, kSplitCounterBytes, s));
-  }
-  auto run_gemm = [&](wamb_linear_args& g) {
-    g.split_ws = split_ws;
-    g.split_ws_bytes = split_ws ? static_cast<int64_t>(kSplitReserveBytes) : 0;
-    return linear_impl(&g, s, true);
-  };
+  auto run_gemm = [&](wamb_linear_args& g) { return linear_impl(&g, s); };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
   const bool f8 = a->fp8 == 1;
   uint8_t* a8 = f8 ? ws + L.off[WAMB_TAP_A8] : nullptr;

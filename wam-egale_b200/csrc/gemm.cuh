@@ -12,6 +12,15 @@
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i+1.
 //
+// Small M (cluster split-K, CL = true): when the output tiles alone would
+// leave SMs idle, each tile is computed by a cluster of `splits` CTAs, one
+// per K range. A split's fp32 partial goes from TMEM into its own shared
+// memory (over the drained TMA ring); after a cluster barrier each CTA sums
+// one row band of the tile over all splits' shared memory (DSMEM, split
+// order) and runs the epilogue on it. Wider tiles and all SMs streaming
+// weights matter at small M: an SM's TMA ring ingests ~90 GB/s, and every
+// k-block of a 64-column tile spends two thirds of that on re-reading A.
+//
 // The output columns may be split into up to three groups that each read a
 // different weight tensor (the separate to_q / to_k / to_v Linear weights of
 // the reference, model.py:318-320), so no concatenated weight copy is needed.
@@ -45,15 +54,11 @@ struct GemmParams {
   // E4M3 operands: acc * a_scale[row] * w_scale[group][col] (null for bf16)
   const float* a_scale;
   const float* w_scale[3];
-  // Split-K (one-CTA kernel, small M): work unit u = tile * splits + s sums
-  // k-blocks [s * kb_per_split, (s + 1) * kb_per_split). Each split writes
-  // its fp32 partial tile to part[(tile * splits + s) * 128 * BN ...]; the
-  // last of the splits to finish a warp's slice (counter cnt[tile * 8 +
-  // slice], left at 0 again) sums the partials in split order and runs the
-  // epilogue, so the result does not depend on which split ends last.
+  // Cluster split-K (one-CTA kernel, small M): CTA u = tile * splits + s of
+  // a cluster of `splits` CTAs sums k-blocks [s * kb_per_split,
+  // (s + 1) * kb_per_split); the cluster reduces its partials through
+  // shared memory (gemm_cluster_reduce). splits = 1: no split.
   int splits, kb_per_split;
-  float* part;
-  int* cnt;
 };
 
 constexpr int GEMM_BM = 128;
@@ -70,6 +75,11 @@ struct GemmSmem {
   static constexpr uint32_t BAR_OFF = STAGES * (A_BYTES + B_BYTES);
   static constexpr uint32_t NBARS = 2 * STAGES + 5;
   static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+  // Cluster split-K: this split's fp32 partial [128][PART_LD] over the ring
+  // once the MMAs are done; the 4-float pad keeps the row-per-thread
+  // stores free of bank conflicts.
+  static constexpr uint32_t PART_LD = BN + 4;
+  static_assert(128 * PART_LD * 4 <= BAR_OFF, "split partial does not fit the ring");
 };
 
 WAMB_DEV float gelu_tanh(float x) {
@@ -127,32 +137,33 @@ WAMB_DEV EpiRow epi_row(const GemmParams& p, int row, int n0) {
   return e;
 }
 
-// Raw residual words of 32 columns starting at `col` (8 x 128 bits for
-// fp32, 4 for bf16).
-WAMB_DEV void epi_fetch_res(const GemmParams& p, int row, int col, uint4 (&r)[8]) {
+// Raw residual words of W columns starting at `col` (W/4 x 128 bits for
+// fp32, W/8 for bf16).
+template <int W>
+WAMB_DEV void epi_fetch_res(const GemmParams& p, int row, int col, uint4 (&r)[W / 4]) {
   if (p.res_f32) {
     const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const float*>(p.res) + row * p.ldr + col);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] = __ldg(rp + j);
+    for (int j = 0; j < W / 4; ++j) r[j] = __ldg(rp + j);
   } else {
     const uint4* rp =
         reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.res) + row * p.ldr + col);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) r[j] = __ldg(rp + j);
+    for (int j = 0; j < W / 8; ++j) r[j] = __ldg(rp + j);
   }
 }
 
-// One 32-column chunk c of the row: accumulator values v -> E4M3 scales,
-// bias, GELU / residual / gate -> bf16 or fp32 stores. `res` holds the
-// chunk's residual words for the residual epilogues.
-WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], int row, int n0, int c,
-                        const uint4 (&res)[8]) {
-  const int col = n0 + c * 32;            // output column
-  const int lcol = e.n_local0 + c * 32;   // column within the weight group
+// W consecutive accumulator values v of the row at output column `col`
+// (column `lcol` of the weight group) -> E4M3 scales, bias, GELU / SiLU /
+// residual / gate -> bf16 or fp32 stores. `res` holds the residual words
+// for the residual epilogues.
+template <int W>
+WAMB_DEV void epi_apply(const GemmParams& p, const EpiRow& e, float (&v)[W], int row, int col, int lcol,
+                        const uint4 (&res)[W / 4]) {
   if (p.a_scale != nullptr) {
     const float4* sp = reinterpret_cast<const float4*>(e.wscale + lcol);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < W / 4; ++j) {
       const float4 w = __ldg(sp + j);
       v[4 * j] *= e.ascale * w.x;
       v[4 * j + 1] *= e.ascale * w.y;
@@ -163,7 +174,7 @@ WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], in
   if (e.bias != nullptr) {
     const uint4* bp = reinterpret_cast<const uint4*>(e.bias + lcol);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < W / 8; ++j) {
       const uint4 w = __ldg(bp + j);
       const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -176,14 +187,14 @@ WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], in
   }
   if (p.epi == EPI_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    for (int j = 0; j < W; ++j) v[j] = gelu_tanh(v[j]);
   } else if (p.epi == EPI_SILU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
+    for (int j = 0; j < W; ++j) v[j] = silu(v[j]);
   } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
     if (p.epi == EPI_RES_GATE) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
+      for (int j = 0; j < W; j += 4) {
         const float4 tb = __ldg(reinterpret_cast<const float4*>(e.gate_tab + col + j));
         float4 te;
         if (e.gate_f32 != nullptr) {
@@ -201,7 +212,7 @@ WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], in
     }
     if (p.res_f32) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < W / 4; ++j) {
         v[4 * j] += __uint_as_float(res[j].x);
         v[4 * j + 1] += __uint_as_float(res[j].y);
         v[4 * j + 2] += __uint_as_float(res[j].z);
@@ -209,7 +220,7 @@ WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], in
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < W / 8; ++j) {
         const uint32_t ws[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
@@ -223,11 +234,11 @@ WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], in
   if (p.out_f32) {
     float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    for (int j = 0; j < W / 4; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   } else {
     uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < W / 8; ++j) {
       uint4 w;
       w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
       w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
@@ -236,6 +247,12 @@ WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], in
       op[j] = w;
     }
   }
+}
+
+// One 32-column chunk c of the tile starting at output column n0.
+WAMB_DEV void epi_chunk(const GemmParams& p, const EpiRow& e, float (&v)[32], int row, int n0, int c,
+                        const uint4 (&res)[8]) {
+  epi_apply<32>(p, e, v, row, n0 + c * 32, e.n_local0 + c * 32, res);
 }
 
 // Epilogue of one output tile for the calling thread's row: 32-column
@@ -249,13 +266,13 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
   // overlaps the previous chunk.
   const bool has_res = e.valid && (p.epi == EPI_RES || p.epi == EPI_RES_GATE);
   uint4 rnext[8];
-  if (has_res) epi_fetch_res(p, row, n0 + c0 * 32, rnext);
+  if (has_res) epi_fetch_res<32>(p, row, n0 + c0 * 32, rnext);
 #pragma unroll 1
   for (int c = c0; c < c1; ++c) {
     uint4 rcur[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) rcur[j] = rnext[j];
-    if (has_res && c + 1 < c1) epi_fetch_res(p, row, n0 + (c + 1) * 32, rnext);
+    if (has_res && c + 1 < c1) epi_fetch_res<32>(p, row, n0 + (c + 1) * 32, rnext);
     float v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
@@ -264,64 +281,70 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
   }
 }
 
-// Split-K, step 1, for one warp slice (rows q*32.., chunks [c0, c1)):
-// this split's fp32 partial from TMEM into its workspace slot.
-// `part_tile` points at split 0 of the tile ([splits][128][BN] fp32).
+// Cluster split-K, step 1, for one warp slice (rows q*32.., chunks [c0, c1)):
+// this split's fp32 partial from TMEM into this CTA's shared memory.
 template <int BN>
-WAMB_DEV void gemm_split_store(uint32_t taddr, float* part_tile, int split, int row_in_tile, int c0,
-                               int c1) {
-  float* mine = part_tile + (static_cast<long long>(split) * 128 + row_in_tile) * BN;
+WAMB_DEV void gemm_part_to_smem(uint32_t taddr, float* part, int row_in_tile, int c0, int c1) {
+  constexpr int LD = BN + 4;
 #pragma unroll 1
   for (int c = c0; c < c1; ++c) {
     float v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
-    float4* dst = reinterpret_cast<float4*>(mine + c * 32);
+    float4* dst = reinterpret_cast<float4*>(part + row_in_tile * LD + c * 32);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) __stcg(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+    for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
 }
 
-// Split-K, step 2: count this split in; the last split to finish the slice
-// sums all partials in split order and runs the epilogue.
+// Cluster split-K, step 2 (after a cluster barrier): CTA `rank` of the
+// `splits` CTAs that computed tile (m_blk, n0) owns rows
+// [rank * R, rank * R + R), R = ceil(128 / splits). Each of its epilogue
+// threads takes 8-column groups of those rows, sums the partials of all
+// splits in split order from their shared memory (DSMEM; the result is
+// independent of timing) and runs the epilogue on them.
 template <int BN>
-WAMB_DEV void gemm_split_finish(const GemmParams& p, const float* part_tile, int row_in_tile, int row,
-                                int n0, int c0, int c1, int* counter) {
-  const int lane = threadIdx.x & 31;
-  __threadfence();   // this lane's partial is visible device-wide before the count
-  __syncwarp();
-  int old = 0;
-  if (lane == 0) old = atomicAdd(counter, 1);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != p.splits - 1) return;
-  __threadfence();   // every other split's partial is visible to this warp
-  if (lane == 0) *counter = 0;  // ready for the next launch
-  const EpiRow e = epi_row(p, row, n0);
-  if (!e.valid) return;
-#pragma unroll 1
-  for (int c = c0; c < c1; ++c) {
-    uint4 res[8];
-    if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) epi_fetch_res(p, row, n0 + c * 32, res);
-    float v[32];
+WAMB_DEV void gemm_cluster_reduce(const GemmParams& p, const float* part, int rank, int m_blk, int n0,
+                                  int etid, int nthreads) {
+  constexpr int LD = BN + 4;
+  constexpr int G = BN / 8;   // 8-column groups per row
+  const int splits = p.splits;
+  const int R = (128 + splits - 1) / splits;
+  const int r0 = rank * R, r1 = min(128, r0 + R);
+  const uint32_t local = smem_u32(part);
+  uint32_t base[8];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    for (int s2 = 0; s2 < p.splits; ++s2) {
-      const float4* src = reinterpret_cast<const float4*>(
-          part_tile + (static_cast<long long>(s2) * 128 + row_in_tile) * BN + c * 32);
+  for (int s2 = 0; s2 < 8; ++s2) base[s2] = s2 < splits ? map_to_rank(local, s2) : 0u;
+  const bool has_res = p.epi == EPI_RES || p.epi == EPI_RES_GATE;
+  for (int it = etid; it < (r1 - r0) * G; it += nthreads) {
+    const int rr = r0 + it / G, g = it - (it / G) * G;
+    const int row = m_blk * GEMM_BM + rr;
+    if (row >= p.M) continue;
+    const uint32_t off = static_cast<uint32_t>((rr * LD + g * 8) * 4);
+    float4 lo[8], hi[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 f = __ldcg(src + j);
-        v[4 * j] += f.x;
-        v[4 * j + 1] += f.y;
-        v[4 * j + 2] += f.z;
-        v[4 * j + 3] += f.w;
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 < splits) {
+        lo[s2] = ld_cluster_f4(base[s2] + off);
+        hi[s2] = ld_cluster_f4(base[s2] + off + 16);
       }
     }
-    epi_chunk(p, e, v, row, n0, c, res);
+    const EpiRow e = epi_row(p, row, n0);
+    uint4 res[2];
+    if (has_res) epi_fetch_res<8>(p, row, n0 + g * 8, res);
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 < splits) {
+        v[0] += lo[s2].x; v[1] += lo[s2].y; v[2] += lo[s2].z; v[3] += lo[s2].w;
+        v[4] += hi[s2].x; v[5] += hi[s2].y; v[6] += hi[s2].z; v[7] += hi[s2].w;
+      }
+    }
+    epi_apply<8>(p, e, v, row, n0 + g * 8, e.n_local0 + g * 8, res);
   }
 }
 
-template <int BN, int STAGES, bool F8>
+template <int BN, int STAGES, bool F8, bool CL>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
@@ -347,7 +370,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int num_tiles = num_m * num_n;
   constexpr int KB = F8 ? GEMM_BK8 : GEMM_BK;
   const int num_kb = p.K / KB;
-  const int splits = p.splits > 1 ? p.splits : 1;
+  const int splits = CL && p.splits > 1 ? p.splits : 1;
   const int num_units = num_tiles * splits;   // unit u: tile u / splits, split u % splits
   auto unit_kb = [&](int u, int& kb0, int& kb1) {
     if (splits == 1) { kb0 = 0; kb1 = num_kb; return; }
@@ -468,23 +491,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       const int row = m_blk * GEMM_BM + row_in_tile;
       const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
-      if (splits == 1) {
-        gemm_epilogue_tile(p, taddr, row, n_blk * BN, c0, c1);
-      } else {
-        float* part_tile = p.part + static_cast<long long>(t) * splits * 128 * BN;
-        gemm_split_store<BN>(taddr, part_tile, u % splits, row_in_tile, c0, c1);
-      }
+      if constexpr (CL) gemm_part_to_smem<BN>(taddr, reinterpret_cast<float*>(smem), row_in_tile, c0, c1);
+      else gemm_epilogue_tile(p, taddr, row, n_blk * BN, c0, c1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty0 + 8 * acc);   // accumulator free for the next unit
-      if (splits > 1) {
-        const float* part_tile = p.part + static_cast<long long>(t) * splits * 128 * BN;
-        gemm_split_finish<BN>(p, part_tile, row_in_tile, row, n_blk * BN, c0, c1,
-                              p.cnt + t * GEMM_EPI_WARPS + (warp - 2));
-      }
     }
   }
 
+  if constexpr (CL) {
+    // One unit per CTA; the cluster's CTAs are the splits of one tile.
+    __syncwarp();
+    cluster_sync_all();   // every split's partial is in its shared memory
+    if (warp >= 2) {
+      const int t = blockIdx.x / splits;
+      gemm_cluster_reduce<BN>(p, reinterpret_cast<const float*>(smem), static_cast<int>(cluster_rank()),
+                              t % num_m, (t / num_m) * BN, threadIdx.x - 64, GEMM_EPI_WARPS * 32);
+    }
+    cluster_sync_all();   // no CTA leaves while another reads its partial
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -5,6 +5,8 @@
 #include "gemm2.cuh"
 #include "host.cuh"
 
+#include <algorithm>
+
 namespace wamb {
 
 template <int BN, int STAGES, bool F8>
@@ -15,14 +17,68 @@ inline int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap* tb, const Ge
   int dev = 0;
   WAMB_CHECK_CUDA(cudaGetDevice(&dev));
   if (!configured[dev]) {
-    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, F8>,
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, F8, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     configured[dev] = true;
   }
   const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * (p.N / BN) * (p.splits > 1 ? p.splits : 1);
   const int grid = tiles < sms ? tiles : sms;
-  return launch_kernel(gemm_tc_kernel<BN, STAGES, F8>, dim3(grid), dim3(GEMM_THREADS), L::TOTAL, stream, ta, tb[0],
-                       tb[1], tb[2], p);
+  return launch_kernel(gemm_tc_kernel<BN, STAGES, F8, false>, dim3(grid), dim3(GEMM_THREADS), L::TOTAL, stream,
+                       ta, tb[0], tb[1], tb[2], p);
+}
+
+// Cluster split-K launch configuration: p.splits CTAs per cluster, one
+// cluster per output tile.
+template <int BN, int STAGES, bool F8>
+inline cudaLaunchConfig_t cluster_config(int splits, int grid, cudaStream_t stream, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = GemmSmem<BN, STAGES>::TOTAL;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Clusters of `splits` CTAs of the cluster split-K kernel that fit on the
+// device at once (1 CTA per SM; the clusters of a GPC must fit its SMs).
+// Queried once per device and size.
+template <int BN, int STAGES, bool F8>
+inline int cluster_capacity(int splits, int sms) {
+  static int cap[64][9] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || splits < 2 || splits > 8) return 0;
+  if (cap[dev][splits] == 0) {
+    int n = 0;
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = cluster_config<BN, STAGES, F8>(splits, splits * (sms / splits), nullptr, attr);
+    if (cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, F8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GemmSmem<BN, STAGES>::TOTAL) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, STAGES, F8, true>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    cap[dev][splits] = n > 0 ? n : -1;
+  }
+  return cap[dev][splits] > 0 ? cap[dev][splits] : 0;
+}
+
+template <int BN, int STAGES, bool F8>
+inline int launch_gemm_cl(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p,
+                          cudaStream_t stream) {
+  const int grid = ((p.M + GEMM_BM - 1) / GEMM_BM) * (p.N / BN) * p.splits;
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = cluster_config<BN, STAGES, F8>(p.splits, grid, stream, attr);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, STAGES, F8, true>, ta, tb[0], tb[1], tb[2], p));
+  return WAMB_OK;
 }
 
 // Two-CTA launch: clusters of 2 along x, one cluster per pair of SMs.
@@ -61,75 +117,63 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
   return WAMB_OK;
 }
 
-// Picks the widest tile (256/128/64 columns) that still gives every SM a
-// tile; falls back to the narrowest legal width for small problems.
-inline int choose_bn(int M, int N, int n_per_group, int sms) {
+// Tile plan of the one-CTA kernel: tile width (256/128/64 columns) and
+// cluster split-K factor, from a cost model measured on B200 at small M:
+//   * the TMA ring of one SM ingests ~90 GB/s of A + weight tiles while
+//     the MMAs consume them, and each k-block moves (128 + BN) x 128 bytes,
+//     so narrow tiles spend most of an SM's ingest on re-reading A;
+//   * the weights stream from HBM at no more than ~6 TB/s in all;
+//   * an output tile's epilogue costs ~1 + BN/128 us; a split tile's
+//     cluster reduction ~1.5 + BN/128 (0.7 + 2/splits) us.
+// Splits need all clusters co-resident (capacity queried per device), at
+// least 4 k-blocks each and splits x tiles <= SMs.
+struct TilePlan {
+  int bn, splits, kb_per_split;
+};
+
+template <bool F8>
+inline int cluster_capacity_bn(int bn, int splits, int sms) {
+  switch (bn) {
+    case 256: return cluster_capacity<256, 4, F8>(splits, sms);
+    case 128: return cluster_capacity<128, 6, F8>(splits, sms);
+    default: return cluster_capacity<64, 8, F8>(splits, sms);
+  }
+}
+
+inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, bool f8) {
+  constexpr double kIngestGBs = 90.0, kDramGBs = 6000.0;
   const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
+  const double t_dram = static_cast<double>(N) * num_kb * 128.0 / (kDramGBs * 1e3);   // us
+  TilePlan best{0, 1, num_kb};
+  double best_t = 1e300;
   const int cands[3] = {256, 128, 64};
-  int best = 0;
-  for (int c : cands) {
-    if (n_per_group % c) continue;
-    if (best == 0) best = c;
-    if (static_cast<long long>(num_m) * (N / c) >= sms) return c;
-    best = c;
+  for (int bn : cands) {
+    if (n_per_group % bn) continue;
+    const long long tiles = static_cast<long long>(num_m) * (N / bn);
+    const double kb_us = (128.0 + bn) * 128.0 / (kIngestGBs * 1e3);   // one k-block of one SM
+    const long long waves = (tiles + sms - 1) / sms;
+    const double t1 = std::max(waves * num_kb * kb_us, t_dram) + 1.0 + bn / 128.0;
+    if (t1 < best_t) {
+      best_t = t1;
+      best = TilePlan{bn, 1, num_kb};
+    }
+    for (int sp = 2; sp <= 8; ++sp) {
+      const int kbps = (num_kb + sp - 1) / sp;
+      const int eff = (num_kb + kbps - 1) / kbps;   // no empty split
+      if (eff != sp || kbps < 4 || tiles * sp > sms) continue;
+      const int cap = f8 ? cluster_capacity_bn<true>(bn, sp, sms) : cluster_capacity_bn<false>(bn, sp, sms);
+      if (tiles > cap) continue;
+      const double t = std::max(kbps * kb_us, t_dram) + 1.5 + bn / 128.0 * (0.7 + 2.0 / sp);
+      if (t < best_t) {
+        best_t = t;
+        best = TilePlan{bn, sp, kbps};
+      }
+    }
   }
   return best;
 }
 
-// Split-K plan of the one-CTA kernel: when the output tiles at the chosen
-// width leave SMs idle (small M: the verify batch, a short chunk), use
-// 128-wide tiles and split K so that tiles x splits fills the SMs, each
-// split keeping at least 32 k-blocks (measured on B200 at M 128: a 6-way
-// split of K 14336 takes the FFN-out GEMM from 66 to 45 us, while 2-3 way
-// splits of K 3072 are slower than the unsplit kernel).
-// Returns splits (1 = none).
-struct SplitPlan {
-  int bn, splits, kb_per_split;
-};
-constexpr int kSplitCounterBytes = 256 * 1024;   // room for 8 counters per tile of up to 8192 tiles
-
-inline SplitPlan plan_split(int M, int N, int n_per_group, int num_kb, int sms, int bn0) {
-  SplitPlan sp{bn0, 1, num_kb};
-  const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
-  if (static_cast<long long>(num_m) * (N / bn0) >= sms) return sp;
-  const int bn = n_per_group % 128 == 0 ? 128 : bn0;
-  const int tiles = num_m * (N / bn);
-  int s = sms / tiles;
-  if (s > num_kb / 32) s = num_kb / 32;
-  if (s < 2) return sp;
-  sp.bn = bn;
-  sp.kb_per_split = (num_kb + s - 1) / s;
-  sp.splits = (num_kb + sp.kb_per_split - 1) / sp.kb_per_split;   // no empty split
-  return sp;
-}
-
-// Workspace bytes a split plan needs: counters, then [tiles][splits][128][bn] fp32.
-inline size_t split_bytes(int M, int N, const SplitPlan& sp) {
-  if (sp.splits <= 1) return 0;
-  const size_t tiles = static_cast<size_t>((M + GEMM_BM - 1) / GEMM_BM) * (N / sp.bn);
-  return kSplitCounterBytes + tiles * sp.splits * 128 * sp.bn * 4;
-}
-
-// Largest split-K scratch any plan can take on a GPU of up to kSplitMaxSms
-// SMs: units = tiles x splits <= SMs, each unit's partial 128 x 128 fp32.
-constexpr int kSplitMaxSms = 160;
-constexpr size_t kSplitReserveBytes =
-    static_cast<size_t>(kSplitCounterBytes) + static_cast<size_t>(kSplitMaxSms) * 128 * 128 * 4;
-
-// Whether a GEMM of this shape would split K on a B200 (148 SMs): the block
-// reserves split-K scratch only when one of its GEMMs would.
-inline bool gemm_would_split(int M, int N, int n_per_group, int K, bool f8) {
-  constexpr int sms = 148;
-  if (M <= 0) return false;
-  const long long pair_tiles = ((M + 255) / 256) * (N / 256);
-  if (M >= 512 && n_per_group % 256 == 0 && pair_tiles >= sms / 2) return false;
-  const int bn0 = choose_bn(M, N, n_per_group, sms);
-  return plan_split(M, N, n_per_group, K / (f8 ? GEMM_BK8 : GEMM_BK), sms, bn0).splits > 1;
-}
-
-// counters_zero: the caller guarantees the workspace's counter area is zero
-// (the block zeroes it once per call; split GEMMs leave it zero).
-inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool counters_zero = false) {
+inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
@@ -177,21 +221,10 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool coun
   // CTA per 128 x BN tile.
   const long long pair_tiles = ((a->m + 255) / 256) * (N / 256);
   const bool pair = a->m >= 512 && a->n_per_group % 256 == 0 && pair_tiles >= di.sms / 2;
-  int bn = pair ? 256 : choose_bn(a->m, static_cast<int>(N), a->n_per_group, di.sms);
-  SplitPlan sp{bn, 1, 0};
-  if (!pair && a->split_ws != nullptr) {
-    sp = plan_split(a->m, static_cast<int>(N), a->n_per_group, a->k / (f8 ? GEMM_BK8 : GEMM_BK), di.sms, bn);
-    if (sp.splits > 1) {
-      WAMB_REQUIRE(reinterpret_cast<uintptr_t>(a->split_ws) % 256 == 0, WAMB_ERR_ALIGN,
-                   "split workspace must be 256-byte aligned");
-      const size_t tiles = static_cast<size_t>((a->m + GEMM_BM - 1) / GEMM_BM) * (N / sp.bn);
-      if (tiles * GEMM_EPI_WARPS * sizeof(int) > static_cast<size_t>(kSplitCounterBytes) ||
-          split_bytes(a->m, static_cast<int>(N), sp) > static_cast<size_t>(a->split_ws_bytes))
-        sp = SplitPlan{bn, 1, 0};   // too little room: no split
-      else
-        bn = sp.bn;
-    }
-  }
+  const int num_kb = a->k / (f8 ? GEMM_BK8 : GEMM_BK);
+  TilePlan tp{256, 1, num_kb};
+  if (!pair) tp = plan_tiles(a->m, static_cast<int>(N), a->n_per_group, num_kb, di.sms, f8);
+  const int bn = tp.bn;
   CUtensorMap ta, tb[3];
   auto tmap = f8 ? make_tmap_e4m3 : make_tmap_bf16;
   rc = tmap(&ta, a->a, a->m, a->k, a->lda, 128);
@@ -226,18 +259,18 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool coun
     p.a_scale = a->a_scale;
     for (int g = 0; g < 3; ++g) p.w_scale[g] = g < a->groups ? a->w_scale[g] : nullptr;
   }
-  p.splits = sp.splits;
-  if (sp.splits > 1) {
-    uint8_t* ws = static_cast<uint8_t*>(a->split_ws);
-    p.kb_per_split = sp.kb_per_split;
-    p.cnt = reinterpret_cast<int*>(ws);
-    p.part = reinterpret_cast<float*>(ws + kSplitCounterBytes);
-    const size_t tiles = static_cast<size_t>((a->m + GEMM_BM - 1) / GEMM_BM) * (N / sp.bn);
-    if (!counters_zero) WAMB_CHECK_CUDA(cudaMemsetAsync(ws, 0, tiles * GEMM_EPI_WARPS * sizeof(int), stream));
-  }
+  p.splits = tp.splits;
+  p.kb_per_split = tp.kb_per_split;
   auto launch = [&](auto f8c) {
     constexpr bool F8 = decltype(f8c)::value;
     if (pair) return launch_gemm2<F8>(ta, tb, p, di.sms, stream);
+    if (tp.splits > 1) {
+      switch (bn) {
+        case 256: return launch_gemm_cl<256, 4, F8>(ta, tb, p, stream);
+        case 128: return launch_gemm_cl<128, 6, F8>(ta, tb, p, stream);
+        default: return launch_gemm_cl<64, 8, F8>(ta, tb, p, stream);
+      }
+    }
     switch (bn) {
       case 256: return launch_gemm_bn<256, 4, F8>(ta, tb, p, di.sms, stream);
       case 128: return launch_gemm_bn<128, 6, F8>(ta, tb, p, di.sms, stream);

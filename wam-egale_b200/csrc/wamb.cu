@@ -39,7 +39,7 @@ extern "C" {
 
 const char* wamb_last_error(void) { return wamb::g_last_error.c_str(); }
 
-int wamb_abi_version(void) { return 102; }
+int wamb_abi_version(void) { return 103; }
 
 int wamb_device_status(void* stream, int* device_code) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -93,9 +93,7 @@ int wamb_block_forward(const wamb_block_args* args, void* stream) {
 
 int wamb_block_forward_noalloc(const wamb_block_args* args, void* stream) {
   if (args == nullptr) return wamb::fail(WAMB_ERR_ARG, "null args");
-  // The block's minimum workspace must fit; the optional split-K scratch is
-  // used when the array has room for it too.
-  const size_t need = wamb::block_layout(args).minimum;
+  const size_t need = wamb::block_layout(args).total;
   if (need > WAMB_NOALLOC_SCRATCH_BYTES)
     return wamb::fail(WAMB_ERR_WORKSPACE,
                       "this block call needs %zu bytes of scratch; the no-allocation entry point "

@@ -28,7 +28,6 @@ class LinearArgs(ctypes.Structure):
         ("temb_len", c_int32), ("rows_per_batch", c_int32), ("gate_index", c_int32),
         ("dim", c_int32),
         ("a_is_fp8", c_int32), ("a_scale", c_void_p), ("w_scale", c_void_p * 3),
-        ("split_ws", c_void_p), ("split_ws_bytes", c_int64),
     ]
 
 
@@ -79,12 +78,12 @@ class BlockArgs(ctypes.Structure):
 # Workspace taps (enum wamb_tap).
 TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", "cross_k",
         "cross_v", "cross_attention", "residual2", "modulated3", "gelu", "kv_slots",
-        "kv_tiles", "kv_counts", "a8", "a8_scale", "splitk")
+        "kv_tiles", "kv_counts", "a8", "a8_scale")
 
 # Weight slots the FP8 path reads as E4M3 (self q/k/v/out, cross q/out, FFN).
 FP8_WEIGHTS = (3, 5, 7, 9, 13, 19, 23, 25)
 
-ABI_VERSION = 102
+ABI_VERSION = 103
 
 # Every symbol include/wamb.h declares; tests check the library exports them.
 EXPORTED = (

@@ -228,7 +228,7 @@ class NativeBlock:
             o = offs[i]
             if o < 0:
                 continue
-            if name.startswith("a8") or name == "splitk":
+            if name.startswith("a8"):
                 continue
             if name.startswith("kv_"):
                 n = {"kv_slots": Q, "kv_tiles": 2 * a.pool, "kv_counts": 2}[name]

@@ -17,8 +17,7 @@ def _bf16_2d(t, name):
 
 
 def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
-           table=None, temb=None, rows_per_batch=None, gate_index=0, a_scale=None, w_scales=None,
-           split_ws=None):
+           table=None, temb=None, rows_per_batch=None, gate_index=0, a_scale=None, w_scales=None):
     """out = epilogue(a @ cat(weights).T + cat(biases)) on the tcgen05 GEMM.
 
     `weights` is one [N, K] bf16 tensor or a list of up to three equally
@@ -29,8 +28,9 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
     scales) and `w_scales` (one [N] fp32 per weight) are required and the
     product is a_scale[m] * w_scale[n] * (a8 @ w8.T) (see quantize_rows).
 
-    split_ws: optional uint8 CUDA buffer; with it, small-M calls may split K
-    across CTAs (wamb_linear_args.split_ws).
+    Small M: when the output tiles would leave SMs idle, K is split across
+    the CTAs of a thread-block cluster (partials summed in split order in
+    shared memory, so results do not depend on timing).
     """
     out_f32 = out is not None and out.dtype == torch.float32
     if isinstance(weights, torch.Tensor):
@@ -75,8 +75,6 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
     args.ldo = out.stride(0)
     args.out_is_f32 = int(out_f32)
     args.epilogue = epilogue
-    if split_ws is not None:
-        args.split_ws, args.split_ws_bytes = split_ws.data_ptr(), split_ws.numel()
     if fp8:
         args.a_is_fp8 = 1
         args.a_scale = a_scale.data_ptr()

@@ -4,12 +4,16 @@ hundred MB on the device, 3 warm-up launches then `--launches` more).
   python wam-egale_b200/wam_ops/profile_cases.py ffn1 [--m 2048] [--launches 1] [--fp8]
   python wam-egale_b200/wam_ops/profile_cases.py attention [--q 880] [--pool 4400] [--batch 8]
   python wam-egale_b200/wam_ops/profile_cases.py rms | ln
+  python wam-egale_b200/wam_ops/profile_cases.py small [--m 128] [--n 3072] [--k 14336]
 
 ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (cfg2 weights); --fp8: E4M3
            operands (quantized once before the timed launches)
 attention  self attention of `batch` cfg2 rollouts over 4400-key pools (24 heads)
 rms        RMSNorm + RoPE of the q/k/v projection output, K/V into the pool
 ln         LayerNorm + adaLN modulation
+small      small-M GEMM + residual epilogue (the verify batch's O / FFN-out
+           projections; cluster split-K where the tiles leave SMs idle); 12
+           weight copies rotate so every launch streams its weights from HBM
 """
 import argparse
 import sys
@@ -24,8 +28,10 @@ from wam_ops import _lib, configs, ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["ffn1", "attention", "rms", "ln"])
+    ap.add_argument("case", choices=["ffn1", "attention", "rms", "ln", "small"])
     ap.add_argument("--m", type=int, default=2048)
+    ap.add_argument("--n", type=int, default=3072)
+    ap.add_argument("--k", type=int, default=14336)
     ap.add_argument("--q", type=int, default=880)
     ap.add_argument("--pool", type=int, default=4400)
     ap.add_argument("--batch", type=int, default=8)
@@ -48,6 +54,15 @@ def main():
                                      a_scale=sx, w_scales=sw)
         else:
             run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_GELU, out=out)  # noqa: E731
+    elif a.case == "small":
+        x = torch.randn(a.m, a.k, generator=g, device=dev).bfloat16()
+        ws = [(torch.randn(a.n, a.k, generator=g, device=dev) * 0.02).bfloat16() for _ in range(12)]
+        b = torch.zeros(a.n, device=dev, dtype=torch.bfloat16)
+        res = torch.randn(a.m, a.n, generator=g, device=dev).bfloat16()
+        out = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
+        it = iter(range(1 << 30))
+        run = lambda: ops.linear(x, ws[next(it) % 12], b, epilogue=_lib.EPI_RES, out=out,  # noqa: E731
+                                 res=res)
     elif a.case == "attention":
         q = torch.randn(a.batch * a.q, D, generator=g, device=dev).bfloat16()
         kp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
