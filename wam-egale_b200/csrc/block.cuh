@@ -113,9 +113,15 @@ inline int launch_ln(const LnParams& p, cudaStream_t s) {
   const int vpt = row_vpt(p.D);
   WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
   const int threads = p.D / (8 * vpt);
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
   return dispatch_vpt(vpt, [&](auto v) {
-    constexpr int R = ln_rows(decltype(v)::value);
-    return launch_kernel(ln_kernel<decltype(v)::value>, dim3((p.M + R - 1) / R), dim3(threads), 0, s, p);
+    constexpr int V = decltype(v)::value;
+    constexpr int R = ln_rows(V);
+    if (R > 1 && (p.M + R - 1) / R < di.sms)   // small M: one row per CTA
+      return launch_kernel(ln_kernel<V, 1>, dim3(p.M), dim3(threads), 0, s, p);
+    return launch_kernel(ln_kernel<V, R>, dim3((p.M + R - 1) / R), dim3(threads), 0, s, p);
   });
 }
 
@@ -295,7 +301,9 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   int* slots = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_SLOTS]) : nullptr;
   int* tiles = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_TILES]) : nullptr;
   int* counts = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_COUNTS]) : nullptr;
-  auto run_gemm = [&](wamb_linear_args& g) { return linear_impl(&g, s); };
+  // Every GEMM of the block follows at least one other kernel of the block,
+  // so its weights may be requested before griddepcontrol.wait.
+  auto run_gemm = [&](wamb_linear_args& g) { return linear_impl(&g, s, true); };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
   const bool f8 = a->fp8 == 1;
   uint8_t* a8 = f8 ? ws + L.off[WAMB_TAP_A8] : nullptr;

@@ -54,6 +54,11 @@ struct GemmParams {
   // E4M3 operands: acc * a_scale[row] * w_scale[group][col] (null for bf16)
   const float* a_scale;
   const float* w_scale[3];
+  // 1: the weights were last written two or more kernels before this one
+  // in the stream (the block forward), so the one-CTA kernel requests the
+  // weight tiles of its first ring stages before griddepcontrol.wait; with
+  // implicit triggers, that writer finished before the previous kernel began.
+  int w_early;
   // Cluster split-K (one-CTA kernel, small M): CTA u = tile * splits + s of
   // a cluster of `splits` CTAs sums k-blocks [s * kb_per_split,
   // (s + 1) * kb_per_split); the cluster reduces its partials through
@@ -403,6 +408,27 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Weight tile source of unit u: tensor map and first row.
+  auto unit_b = [&](int u, const CUtensorMap*& mb, int& n_local) {
+    const int n0 = (u / splits / num_m) * BN;
+    const int g = n0 / p.n_per_group;
+    n_local = n0 - g * p.n_per_group;
+    mb = g == 0 ? &tmB0 : (g == 1 ? &tmB1 : &tmB2);
+  };
+  // Early weight loads: the first ring stages of this CTA's first unit (the
+  // stages are free, so no empty wait); their A halves follow the wait.
+  int pre = 0;
+  if (p.w_early && warp == 0 && lane == 0 && static_cast<int>(blockIdx.x) < num_units) {
+    const CUtensorMap* mb;
+    int n_local, kb0, kb1;
+    unit_b(blockIdx.x, mb, n_local);
+    unit_kb(blockIdx.x, kb0, kb1);
+    pre = min(STAGES, kb1 - kb0);
+    for (int s = 0; s < pre; ++s) {
+      mbar_arrive_expect_tx(full0 + 8 * s, L::A_BYTES + L::B_BYTES);
+      tma_load_2d(smem_u32(sB + s * L::B_BYTES), mb, full0 + 8 * s, (kb0 + s) * KB, n_local);
+    }
+  }
   pdl_wait();   // inputs of the previous kernel are complete from here on
 
   if (warp == 0) {
@@ -410,18 +436,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // ------------------------------------------------------ TMA producer
       int it = 0;
       for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
-        const int t = u / splits;
-        const int m_blk = t % num_m, n_blk = t / num_m;
-        const int n0 = n_blk * BN;
-        const int g = n0 / p.n_per_group;
-        const int n_local = n0 - g * p.n_per_group;
-        const CUtensorMap* mb = g == 0 ? &tmB0 : (g == 1 ? &tmB1 : &tmB2);
+        const int m_blk = (u / splits) % num_m;
+        const CUtensorMap* mb;
+        int n_local;
+        unit_b(u, mb, n_local);
         int kb0, kb1;
         unit_kb(u, kb0, kb1);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          if (it < pre) {   // weight half already requested
+            tma_load_2d(smem_u32(sA + s * L::A_BYTES), &tmA, full0 + 8 * s, kb * KB, m_blk * GEMM_BM);
+            continue;
+          }
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(full0 + 8 * s, L::A_BYTES + L::B_BYTES);
           tma_load_2d(smem_u32(sA + s * L::A_BYTES), &tmA, full0 + 8 * s, kb * KB, m_blk * GEMM_BM);
@@ -429,7 +457,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (!ok) break;
       }
-      // Teardown: wait for the last load issued into each stage to land.
+      // Teardown: wait for the last load issued into each stage to land
+      // (early weight loads included when an abort stopped the loop first).
+      if (it < pre) it = pre;
       for (int s = 0; s < STAGES; ++s) {
         if (it > s) {
           const int last = s + ((it - 1 - s) / STAGES) * STAGES;

@@ -87,14 +87,15 @@ struct LnParams {
   int temb_rows;          // 0 or 6: the blocks' 6 modulation rows; 1: the output norm
 };
 
-// Rows per CTA of ln_kernel: several rows share one load of the modulation
-// (or gamma / beta) vectors and one pair of barriers per reduction.
+// Rows per CTA of ln_kernel for large M: several rows share one load of the
+// modulation (or gamma / beta) vectors and one pair of barriers per
+// reduction. Small M (fewer CTAs than SMs at that count) runs one row per
+// CTA, with the modulation loads issued before the reductions.
 __host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 2 ? 4 : (vpt <= 4 ? 2 : 1); }
 
-template <int VPT>
+template <int VPT, int R>
 __global__ void ln_kernel(const LnParams p) {
   pdl_wait();
-  constexpr int R = ln_rows(VPT);
   __shared__ float red[32 * R];
   const int row0 = blockIdx.x * R;
   const int nthr = blockDim.x;
@@ -174,6 +175,37 @@ __global__ void ln_kernel(const LnParams p) {
     emit();
     return;
   }
+  // Per-column multiplier / offset: gamma / beta (affine), or 1 + scale /
+  // shift of the row's (batch, token) modulation, reloaded only when it
+  // changes between consecutive rows.
+  long long key[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    key[r] = 0;
+    if (p.affine == 0) {
+      const int row = row0 + r < p.M ? row0 + r : p.M - 1;
+      const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
+      const long long l = p.temb_L == 1 ? 0 : tok;
+      key[r] = (static_cast<long long>(b) * p.temb_L + l) * (p.temb_rows == 1 ? 1 : 6) * p.D;
+    }
+  }
+  auto load_mul_add = [&](int r, int col, float (&mul)[8], float (&add)[8]) {
+    if (p.affine) {
+      load8f(p.gamma + col, mul);
+      load8f(p.beta + col, add);
+    } else {
+      const int tr = p.temb_rows == 1 ? 1 : 6;
+      load_mod8(p.table, p.temb, p.temb_f32, key[r], p.scale_idx, p.D, col, mul, tr);
+      load_mod8(p.table, p.temb, p.temb_f32, key[r], p.shift_idx, p.D, col, add, tr);
+    }
+  };
+  // One row per CTA: fetch the row's vectors now, so that their latency
+  // overlaps the two reductions.
+  float mul1[R == 1 ? VPT : 1][8], add1[R == 1 ? VPT : 1][8];
+  if constexpr (R == 1) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) load_mul_add(0, (i * nthr + threadIdx.x) * 8, mul1[i], add1[i]);
+  }
   float mean[R], var[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -197,41 +229,25 @@ __global__ void ln_kernel(const LnParams p) {
       }
   }
   reduce(var, false);
-  // Per-column multiplier / offset: gamma / beta (affine), or 1 + scale /
-  // shift of the row's (batch, token) modulation, reloaded only when it
-  // changes between consecutive rows.
-  long long key[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    key[r] = 0;
-    if (p.affine == 0) {
-      const int row = row0 + r < p.M ? row0 + r : p.M - 1;
-      const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
-      const long long l = p.temb_L == 1 ? 0 : tok;
-      key[r] = (static_cast<long long>(b) * p.temb_L + l) * (p.temb_rows == 1 ? 1 : 6) * p.D;
-    }
-  }
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int col = (i * nthr + threadIdx.x) * 8;
     float mul[8], add[8];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      if (r == 0 || key[r] != key[r - 1]) {
-        if (p.affine) {
-          load8f(p.gamma + col, mul);
-          load8f(p.beta + col, add);
-        } else {
-          const int tr = p.temb_rows == 1 ? 1 : 6;
-          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.scale_idx, p.D, col, mul, tr);
-          load_mod8(p.table, p.temb, p.temb_f32, key[r], p.shift_idx, p.D, col, add, tr);
+      if constexpr (R == 1) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) mul[j] += 1.f;
+        for (int j = 0; j < 8; ++j) {
+          mul[j] = mul1[i][j];
+          add[j] = add1[i][j];
         }
+      } else if (r == 0 || key[r] != key[r - 1]) {
+        load_mul_add(r, col, mul, add);
       }
+      const float one = p.affine ? 0.f : 1.f;   // the modulation multiplies by 1 + scale
       const float rstd = rsqrtf(var[r] / p.D + p.eps);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[r][i][j] = (v[r][i][j] - mean[r]) * rstd * mul[j] + add[j];
+      for (int j = 0; j < 8; ++j) v[r][i][j] = (v[r][i][j] - mean[r]) * rstd * (mul[j] + one) + add[j];
     }
   }
   emit();
@@ -449,9 +465,19 @@ WAMB_DEV long long block_max_ll(long long v, long long* sh) {
   return r;
 }
 
+// Nonzero bytes of a 32-bit word -> 1, zero bytes -> 0 (bit 8k of the
+// shifted ORs covers bits 8k..8k+7 of x).
+WAMB_DEV uint32_t bytes_nonzero(uint32_t x) {
+  x |= x >> 4;
+  x |= x >> 2;
+  x |= x >> 1;
+  return x & 0x01010101u;
+}
+
 __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams p) {
   pdl_wait();
-  __shared__ uint8_t m[KV_MAX_POOL];
+  constexpr int SEG_MAX = KV_MAX_POOL / KV_THREADS;   // slots per thread at most
+  __shared__ __align__(16) uint8_t m[KV_MAX_POOL];
   __shared__ int sh[33];
   __shared__ long long shl[32];
   __shared__ int s_err;
@@ -459,7 +485,24 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams
   const int lo = threadIdx.x * seg;
   const int hi = min(p.pool, lo + seg);
   if (threadIdx.x == 0) s_err = 0;
-  for (int i = threadIdx.x; i < p.pool; i += KV_THREADS) m[i] = p.mask[i] ? 1 : 0;
+  // Stage the mask as 0/1 bytes, 16 per load when the base allows it (one
+  // round trip for pools up to 16 K slots).
+  int vec_end = 0;
+  if ((reinterpret_cast<uintptr_t>(p.mask) & 15) == 0) {
+    vec_end = p.pool & ~15;
+    for (int i = threadIdx.x; i < (vec_end >> 4); i += KV_THREADS) {
+      const uint4 w = reinterpret_cast<const uint4*>(p.mask)[i];
+      reinterpret_cast<uint4*>(m)[i] =
+          make_uint4(bytes_nonzero(w.x), bytes_nonzero(w.y), bytes_nonzero(w.z), bytes_nonzero(w.w));
+    }
+  }
+  for (int i = vec_end + threadIdx.x; i < p.pool; i += KV_THREADS) m[i] = p.mask[i] ? 1 : 0;
+  // This thread's slot ids, all loads in flight at once (allocation only).
+  long long idr[SEG_MAX];
+  if (!p.candidate) {
+#pragma unroll
+    for (int k = 0; k < SEG_MAX; ++k) idr[k] = lo + k < hi ? p.ids[lo + k] : -1;
+  }
   __syncthreads();
   int total = 0;
 
@@ -475,22 +518,26 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams
     // Evict the smallest ids, lowest slot first among equal ids (model.py:553-563).
     for (int iter = 0; need > 0 && iter <= p.pool; ++iter) {
       long long mn = LLONG_MAX;
-      for (int i = lo; i < hi; ++i)
-        if (m[i] && p.ids[i] < mn) mn = p.ids[i];
+#pragma unroll
+      for (int k = 0; k < SEG_MAX; ++k)
+        if (lo + k < hi && m[lo + k] && idr[k] < mn) mn = idr[k];
       mn = block_min_ll(mn, shl);
       if (mn == LLONG_MAX) {
         if (threadIdx.x == 0) s_err = 4;
         break;
       }
       int c = 0;
-      for (int i = lo; i < hi; ++i) c += (m[i] && p.ids[i] == mn);
+#pragma unroll
+      for (int k = 0; k < SEG_MAX; ++k) c += lo + k < hi && m[lo + k] && idr[k] == mn;
       const int before = block_excl_scan(c, sh, &total);
       int r = before;
-      for (int i = lo; i < hi; ++i) {
-        if (m[i] && p.ids[i] == mn) {
+#pragma unroll
+      for (int k = 0; k < SEG_MAX; ++k) {
+        if (lo + k < hi && m[lo + k] && idr[k] == mn) {
           if (r < need) {
-            m[i] = 0;
-            p.ids[i] = -1;
+            m[lo + k] = 0;
+            idr[k] = -1;
+            p.ids[lo + k] = -1;
           }
           ++r;
         }
@@ -502,8 +549,9 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams
     if (s_err == 0) {
       // next id = max(valid ids) + 1, or 0 (model.py:565-571)
       long long mx = -1;
-      for (int i = lo; i < hi; ++i)
-        if (m[i] && p.ids[i] > mx) mx = p.ids[i];
+#pragma unroll
+      for (int k = 0; k < SEG_MAX; ++k)
+        if (lo + k < hi && m[lo + k] && idr[k] > mx) mx = idr[k];
       mx = block_max_ll(mx, shl);
       const long long next = mx < 0 ? 0 : mx + 1;
       // first q free slots in physical order (model.py:551, 564)

@@ -173,7 +173,9 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
   return best;
 }
 
-inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
+// w_early: the caller guarantees that the weights were last written two or
+// more kernels before this GEMM in the stream (GemmParams::w_early).
+inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_early = false) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
@@ -259,6 +261,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream) {
     p.a_scale = a->a_scale;
     for (int g = 0; g < 3; ++g) p.w_scale[g] = g < a->groups ? a->w_scale[g] : nullptr;
   }
+  p.w_early = w_early ? 1 : 0;
   p.splits = tp.splits;
   p.kb_per_split = tp.kb_per_split;
   auto launch = [&](auto f8c) {
