@@ -112,6 +112,7 @@ WAMB_DEV uint64_t ex2_poly2(uint64_t x2) {
             __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
 }
 struct AttnParams {
+  int trigger;              // 1: trigger the dependent grid early (a GEMM follows)
   int heads;
   int q_rows;               // query rows per batch row
   __nv_bfloat16* out;       // [B * q_rows, ldo], head h at columns [h*128, h*128+128)
@@ -199,6 +200,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  if (p.trigger) pdl_trigger();
   pdl_wait();   // the tile list and Q/K/V of the previous kernels are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y;

@@ -18,7 +18,8 @@
 namespace wamb {
 
 // ---------------------------------------------------------------- attention
-inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream) {
+// trigger: a GEMM that requests weights before its pdl_wait follows.
+inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, bool trigger = false) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->batch >= 0 && a->heads > 0 && a->q_rows >= 0, WAMB_ERR_SHAPE, "bad dims");
   if (a->batch == 0 || a->q_rows == 0) return WAMB_OK;
@@ -41,6 +42,7 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream) {
   if ((rc = make_tmap_bf16(&tk0, a->k0, a->src0_total_rows, a->ld0, a->ld0, 128))) return rc;
   if ((rc = make_tmap_bf16(&tv0, a->v0, a->src0_total_rows, a->ld0, a->ld0, 128))) return rc;
   AttnParams p{};
+  p.trigger = trigger ? 1 : 0;
   p.heads = a->heads;
   p.q_rows = a->q_rows;
   p.out = static_cast<__nv_bfloat16*>(a->out);
@@ -303,7 +305,10 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   int* counts = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_COUNTS]) : nullptr;
   // Every GEMM of the block follows at least one other kernel of the block,
   // so its weights may be requested before griddepcontrol.wait.
-  auto run_gemm = [&](wamb_linear_args& g) { return linear_impl(&g, s, true); };
+  auto run_gemm = [&](wamb_linear_args& g, bool trigger = false) { return linear_impl(&g, s, true, trigger); };
+  // Early triggers pay only before a one-CTA GEMM, whose weight loads can
+  // start before its pdl_wait (N columns, N per weight group).
+  auto early = [&](long long n, int n_per_group) { return !gemm_is_pair(static_cast<int>(M), n, n_per_group, di.sms); };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
   const bool f8 = a->fp8 == 1;
   uint8_t* a8 = f8 ? ws + L.off[WAMB_TAP_A8] : nullptr;
@@ -340,6 +345,10 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   LnParams ln{};
   ln.x = a->x; ln.x_f32 = a->x_is_f32; ln.ldx = D; ln.out = h1; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[0]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
+  // LN1 triggers early only after the KV layout kernel: the block's first
+  // kernel keeps the implicit trigger, so writes of the kernels before the
+  // block are complete before any GEMM of the block reads weights early.
+  ln.trigger = cache && early(3 * D, D) ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -378,7 +387,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     at.k0 = qkv; at.v0 = qkv; at.ld0 = 3LL * D; at.k0_col = D; at.v0_col = 2 * D;
     at.src0_total_rows = M; at.src0_batch_stride = Q; at.src0_len = Q;
   }
-  if ((rc = attention_impl(&at, s))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D)))) return rc;
   if (f8 && (rc = quantize(attn, D, D))) return rc;
   // 6. O projection + gated residual (gate 2): h2 = x + o * gate_msa
   g = wamb_linear_args{};
@@ -394,6 +403,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln = LnParams{};
   ln.x = h2; ln.x_f32 = 1; ln.ldx = D; ln.out = n2; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[1]); ln.affine = a->weights[1] != nullptr ? 1 : 2;
+  ln.trigger = early(D, D) ? 1 : 0;
   ln.gamma = static_cast<const float*>(a->weights[1]); ln.beta = static_cast<const float*>(a->weights[2]);
   ln.rows_per_batch = Q;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -429,7 +439,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   at.src0_map = a->context_rows;
   at.src0_broadcast = a->context_rows == nullptr && a->context_batch == 1 && B > 1;
   at.out = ca; at.ldo = D;
-  if ((rc = attention_impl(&at, s))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D)))) return rc;
   if (f8 && (rc = quantize(ca, D, D))) return rc;
   // 12. cross O projection + residual: h3 = h2 + o
   g = wamb_linear_args{};
@@ -442,6 +452,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln = LnParams{};
   ln.x = h3; ln.x_f32 = 1; ln.ldx = D; ln.out = f0; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[2]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
+  ln.trigger = early(F, F) ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 3; ln.scale_idx = 4;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -452,7 +463,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   gemm_input(g, f0, 23);
   g.bias[0] = a->weights[24]; g.out = act; g.ldo = F;
   g.epilogue = WAMB_EPI_GELU;
-  if ((rc = run_gemm(g))) return rc;
+  if ((rc = run_gemm(g, !f8 && early(D, D)))) return rc;   // bf16: FFN2 follows directly
   if (f8 && (rc = quantize(act, F, F))) return rc;
   // 15. FFN2 + gated residual (gate 5): out = h3 + f * c_gate_msa
   g = wamb_linear_args{};

@@ -38,13 +38,16 @@ WAMB_DEV void record_error(int code) { atomicCAS(&g_error, 0, code); }
 
 // Programmatic dependent launch: every kernel of the library is launched
 // with programmatic stream serialization and waits for its predecessor's
-// completion and memory (pdl_wait) before it touches any global memory, so
-// only the launch itself and the prologue (barrier init, TMEM allocation)
-// overlap the predecessor's exit. No kernel triggers its dependents early:
-// on B200 an early trigger (dependent CTAs resident while the predecessor
-// still runs) measured 1-12% slower, the implicit trigger at exit 0-2%
-// faster than plain launches. A no-op without a programmatic dependency.
+// completion and memory (pdl_wait) before it touches global memory that an
+// earlier kernel may write, so the launch and the prologue (barrier init,
+// TMEM allocation, a GEMM's first weight tiles) overlap the predecessor.
+// A no-op without a programmatic dependency.
 WAMB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Early trigger: the dependent grid may launch once every CTA of this grid
+// has issued it (so it never takes an SM from a CTA of this grid that has
+// not started). Used only where a GEMM that requests weights before its
+// pdl_wait follows; elsewhere the implicit trigger at exit measured faster.
+WAMB_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ----------------------------------------------------------------- mbarrier
 WAMB_DEV void mbar_init(uint32_t bar, uint32_t count) {

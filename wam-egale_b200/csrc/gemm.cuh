@@ -59,6 +59,7 @@ struct GemmParams {
   // weight tiles of its first ring stages before griddepcontrol.wait; with
   // implicit triggers, that writer finished before the previous kernel began.
   int w_early;
+  int trigger;   // 1: trigger the dependent grid early (a GEMM with w_early follows)
   // Cluster split-K (one-CTA kernel, small M): CTA u = tile * splits + s of
   // a cluster of `splits` CTAs sums k-blocks [s * kb_per_split,
   // (s + 1) * kb_per_split); the cluster reduces its partials through
@@ -429,6 +430,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tma_load_2d(smem_u32(sB + s * L::B_BYTES), mb, full0 + 8 * s, (kb0 + s) * KB, n_local);
     }
   }
+  if (p.trigger) pdl_trigger();
   pdl_wait();   // inputs of the previous kernel are complete from here on
 
   if (warp == 0) {

@@ -85,6 +85,7 @@ struct LnParams {
   const void* temb;       // [B, L, temb_rows, D]
   int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
   int temb_rows;          // 0 or 6: the blocks' 6 modulation rows; 1: the output norm
+  int trigger;            // 1: trigger the dependent grid early (a GEMM follows)
 };
 
 // Rows per CTA of ln_kernel for large M: several rows share one load of the
@@ -95,6 +96,7 @@ __host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 2 ? 4 : (vpt 
 
 template <int VPT, int R>
 __global__ void ln_kernel(const LnParams p) {
+  if (p.trigger) pdl_trigger();
   pdl_wait();
   __shared__ float red[32 * R];
   const int row0 = blockIdx.x * R;

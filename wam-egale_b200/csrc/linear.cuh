@@ -173,9 +173,19 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
   return best;
 }
 
+// Whether a GEMM of this shape takes the 2-CTA kernel: 256 x 256 tiles when
+// the weight groups split into 256-wide tiles and there are enough of them
+// to give every SM pair one.
+inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms) {
+  const long long pair_tiles = ((M + 255) / 256) * (N / 256);
+  return M >= 512 && n_per_group % 256 == 0 && pair_tiles >= sms / 2;
+}
+
 // w_early: the caller guarantees that the weights were last written two or
 // more kernels before this GEMM in the stream (GemmParams::w_early).
-inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_early = false) {
+// trigger: the next kernel is a GEMM with w_early (GemmParams::trigger).
+inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_early = false,
+                       bool trigger = false) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
@@ -218,11 +228,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   int rc = device_info(&di);
   if (rc) return rc;
 
-  // 2-CTA 256 x 256 tiles when the weight groups split into 256-wide tiles
-  // and there are enough of them to give every SM pair one; otherwise one
-  // CTA per 128 x BN tile.
-  const long long pair_tiles = ((a->m + 255) / 256) * (N / 256);
-  const bool pair = a->m >= 512 && a->n_per_group % 256 == 0 && pair_tiles >= di.sms / 2;
+  const bool pair = gemm_is_pair(a->m, N, a->n_per_group, di.sms);
   const int num_kb = a->k / (f8 ? GEMM_BK8 : GEMM_BK);
   TilePlan tp{256, 1, num_kb};
   if (!pair) tp = plan_tiles(a->m, static_cast<int>(N), a->n_per_group, num_kb, di.sms, f8);
@@ -262,6 +268,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
     for (int g = 0; g < 3; ++g) p.w_scale[g] = g < a->groups ? a->w_scale[g] : nullptr;
   }
   p.w_early = w_early ? 1 : 0;
+  p.trigger = trigger ? 1 : 0;
   p.splits = tp.splits;
   p.kb_per_split = tp.kb_per_split;
   auto launch = [&](auto f8c) {
