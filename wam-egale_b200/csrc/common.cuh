@@ -125,6 +125,26 @@ WAMB_DEV void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }
+// Split cluster barrier: arrive (release: this thread's prior writes,
+// shared::cluster stores included, become visible to the cluster) and wait
+// (acquire), so that independent work can run between the two.
+WAMB_DEV void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+WAMB_DEV void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into another CTA's of the cluster by the
+// TMA engine; completes as transaction bytes on that CTA's mbarrier
+// (dst and bar from map_to_rank). No multicast.
+WAMB_DEV void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "r"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// 16 bytes into shared memory of a CTA of the cluster (address from map_to_rank).
+WAMB_DEV void st_cluster_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
 // 16 bytes from shared memory of a CTA of the cluster (address from map_to_rank).
 WAMB_DEV float4 ld_cluster_f4(uint32_t addr) {
   float4 v;

@@ -79,13 +79,16 @@ struct GemmSmem {
   static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr uint32_t BAR_OFF = STAGES * (A_BYTES + B_BYTES);
-  static constexpr uint32_t NBARS = 2 * STAGES + 5;
+  static constexpr uint32_t NBARS = 2 * STAGES + 6;
   static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
-  // Cluster split-K: this split's fp32 partial [128][PART_LD] over the ring
-  // once the MMAs are done; the 4-float pad keeps the row-per-thread
-  // stores free of bank conflicts.
+  // Cluster split-K (64/128-column tiles): over the ring once the MMAs are
+  // done, this split's fp32 partial [128][PART_LD] and the receive slots
+  // [splits][R][PART_LD] of the other splits' rows of this CTA's band (R =
+  // ceil(128 / splits); splits * R <= 133 for splits <= 8). The 4-float pad
+  // keeps the row-per-thread stores free of bank conflicts.
   static constexpr uint32_t PART_LD = BN + 4;
-  static_assert(128 * PART_LD * 4 <= BAR_OFF, "split partial does not fit the ring");
+  static constexpr uint32_t PART_BYTES = 128 * PART_LD * 4;
+  static constexpr bool CL_FITS = PART_BYTES + 133 * PART_LD * 4 <= BAR_OFF;
 };
 
 WAMB_DEV float gelu_tanh(float x) {
@@ -287,8 +290,9 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
   }
 }
 
-// Cluster split-K, step 1, for one warp slice (rows q*32.., chunks [c0, c1)):
-// this split's fp32 partial from TMEM into this CTA's shared memory.
+// Cluster split-K, step 1, for one warp slice (rows q*32.., chunks
+// [c0, c1)): this split's fp32 accumulator rows from TMEM into its local
+// partial, then made visible to the bulk-copy (async) proxy.
 template <int BN>
 WAMB_DEV void gemm_part_to_smem(uint32_t taddr, float* part, int row_in_tile, int c0, int c1) {
   constexpr int LD = BN + 4;
@@ -301,52 +305,164 @@ WAMB_DEV void gemm_part_to_smem(uint32_t taddr, float* part, int row_in_tile, in
 #pragma unroll
     for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
+  fence_proxy_async();
 }
 
-// Cluster split-K, step 2 (after a cluster barrier): CTA `rank` of the
-// `splits` CTAs that computed tile (m_blk, n0) owns rows
-// [rank * R, rank * R + R), R = ceil(128 / splits). Each of its epilogue
-// threads takes 8-column groups of those rows, sums the partials of all
-// splits in split order from their shared memory (DSMEM; the result is
-// independent of timing) and runs the epilogue on them.
+// Epilogue operands of 8 consecutive output columns of one row, requested
+// ahead of the accumulator values (epi_load8: loads only, nothing that waits
+// for them) and applied in epi_apply's order (epi_finish8).
+struct EpiOps8 {
+  uint4 bias;        // 8 bf16 (has_bias)
+  float4 w[2];       // w_scale (E4M3 operands)
+  float ascale;
+  float4 tab[2];     // gate table row (EPI_RES_GATE)
+  float4 tef[2];     // fp32 temb gate row, or
+  uint4 teb;         // bf16 temb gate row
+  uint4 res[2];      // raw residual words
+  bool has_bias;
+};
+
+WAMB_DEV void epi_load8(const GemmParams& p, const EpiRow& e, int row, int col, int lcol, EpiOps8& o) {
+  o.has_bias = e.bias != nullptr;
+  if (o.has_bias) o.bias = __ldg(reinterpret_cast<const uint4*>(e.bias + lcol));
+  o.ascale = e.ascale;
+  if (p.a_scale != nullptr) {
+    const float4* sp = reinterpret_cast<const float4*>(e.wscale + lcol);
+    o.w[0] = __ldg(sp);
+    o.w[1] = __ldg(sp + 1);
+  }
+  if (p.epi == EPI_RES_GATE) {
+    o.tab[0] = __ldg(reinterpret_cast<const float4*>(e.gate_tab + col));
+    o.tab[1] = __ldg(reinterpret_cast<const float4*>(e.gate_tab + col + 4));
+    if (e.gate_f32 != nullptr) {
+      o.tef[0] = __ldg(reinterpret_cast<const float4*>(e.gate_f32 + col));
+      o.tef[1] = __ldg(reinterpret_cast<const float4*>(e.gate_f32 + col + 4));
+    } else {
+      o.teb = __ldg(reinterpret_cast<const uint4*>(e.gate_bf + col));
+    }
+  }
+  if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) epi_fetch_res<8>(p, row, col, o.res);
+}
+
+WAMB_DEV void epi_finish8(const GemmParams& p, const EpiOps8& o, float (&v)[8], int row, int col) {
+  if (p.a_scale != nullptr) {
+    const float ws[8] = {o.w[0].x, o.w[0].y, o.w[0].z, o.w[0].w, o.w[1].x, o.w[1].y, o.w[1].z, o.w[1].w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= o.ascale * ws[j];
+  }
+  if (o.has_bias) {
+    const uint32_t ws[4] = {o.bias.x, o.bias.y, o.bias.z, o.bias.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float2 f = unpack_bf16(ws[h]);
+      v[2 * h] += f.x;
+      v[2 * h + 1] += f.y;
+    }
+  }
+  if (p.epi == EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (p.epi == EPI_SILU) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = silu(v[j]);
+  } else if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
+    if (p.epi == EPI_RES_GATE) {
+      const float tb[8] = {o.tab[0].x, o.tab[0].y, o.tab[0].z, o.tab[0].w,
+                           o.tab[1].x, o.tab[1].y, o.tab[1].z, o.tab[1].w};
+      float te[8];
+      if (p.temb_f32) {
+        te[0] = o.tef[0].x; te[1] = o.tef[0].y; te[2] = o.tef[0].z; te[3] = o.tef[0].w;
+        te[4] = o.tef[1].x; te[5] = o.tef[1].y; te[6] = o.tef[1].z; te[7] = o.tef[1].w;
+      } else {
+        const uint32_t ws[4] = {o.teb.x, o.teb.y, o.teb.z, o.teb.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = unpack_bf16(ws[h]);
+          te[2 * h] = f.x;
+          te[2 * h + 1] = f.y;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= tb[j] + te[j];
+    }
+    if (p.res_f32) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        v[4 * j] += __uint_as_float(o.res[j].x);
+        v[4 * j + 1] += __uint_as_float(o.res[j].y);
+        v[4 * j + 2] += __uint_as_float(o.res[j].z);
+        v[4 * j + 3] += __uint_as_float(o.res[j].w);
+      }
+    } else {
+      const uint32_t ws[4] = {o.res[0].x, o.res[0].y, o.res[0].z, o.res[0].w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16(ws[h]);
+        v[2 * h] += f.x;
+        v[2 * h + 1] += f.y;
+      }
+    }
+  }
+  if (p.out_f32) {
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
+    op[0] = make_float4(v[0], v[1], v[2], v[3]);
+    op[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 w;
+    w.x = pack_bf16(v[0], v[1]);
+    w.y = pack_bf16(v[2], v[3]);
+    w.z = pack_bf16(v[4], v[5]);
+    w.w = pack_bf16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col) = w;
+  }
+}
+
+// Cluster split-K, step 3, for the epilogue threads, once the other
+// splits' rows of this CTA's band [rank * R, rank * R + R) arrived in its
+// receive slots (recv_bar): each thread takes 8-column groups of the band,
+// requests the group's epilogue operands, sums the splits in split order
+// (its own from the local partial; the result does not depend on timing)
+// and runs the epilogue. The next group's operands are requested before the
+// current group is summed.
 template <int BN>
-WAMB_DEV void gemm_cluster_reduce(const GemmParams& p, const float* part, int rank, int m_blk, int n0,
-                                  int etid, int nthreads) {
+WAMB_DEV void gemm_cluster_reduce(const GemmParams& p, const float* part, const float* recv, uint32_t recv_bar,
+                                  volatile int* abort_flag, int rank, int m_blk, int n0, int etid,
+                                  int nthreads) {
   constexpr int LD = BN + 4;
   constexpr int G = BN / 8;   // 8-column groups per row
   const int splits = p.splits;
   const int R = (128 + splits - 1) / splits;
   const int r0 = rank * R, r1 = min(128, r0 + R);
-  const uint32_t local = smem_u32(part);
-  uint32_t base[8];
-#pragma unroll
-  for (int s2 = 0; s2 < 8; ++s2) base[s2] = s2 < splits ? map_to_rank(local, s2) : 0u;
-  const bool has_res = p.epi == EPI_RES || p.epi == EPI_RES_GATE;
-  for (int it = etid; it < (r1 - r0) * G; it += nthreads) {
+  const int items = (r1 - r0) * G;
+  EpiOps8 nxt;
+  auto prefetch = [&](int it) {
     const int rr = r0 + it / G, g = it - (it / G) * G;
     const int row = m_blk * GEMM_BM + rr;
-    if (row >= p.M) continue;
-    const uint32_t off = static_cast<uint32_t>((rr * LD + g * 8) * 4);
-    float4 lo[8], hi[8];
-#pragma unroll
-    for (int s2 = 0; s2 < 8; ++s2) {
-      if (s2 < splits) {
-        lo[s2] = ld_cluster_f4(base[s2] + off);
-        hi[s2] = ld_cluster_f4(base[s2] + off + 16);
-      }
+    if (row < p.M) {
+      const EpiRow e = epi_row(p, row, n0);
+      epi_load8(p, e, row, n0 + g * 8, e.n_local0 + g * 8, nxt);
     }
-    const EpiRow e = epi_row(p, row, n0);
-    uint4 res[2];
-    if (has_res) epi_fetch_res<8>(p, row, n0 + g * 8, res);
+  };
+  if (etid < items) prefetch(etid);
+  mbar_wait(recv_bar, 0, abort_flag);   // bounded; on abort the sums are garbage
+  for (int it = etid; it < items; it += nthreads) {
+    const int rr = r0 + it / G, g = it - (it / G) * G;
+    const int row = m_blk * GEMM_BM + rr;
+    const EpiOps8 cur = nxt;
+    if (it + nthreads < items) prefetch(it + nthreads);
+    if (row >= p.M) continue;
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int s2 = 0; s2 < 8; ++s2) {
       if (s2 < splits) {
-        v[0] += lo[s2].x; v[1] += lo[s2].y; v[2] += lo[s2].z; v[3] += lo[s2].w;
-        v[4] += hi[s2].x; v[5] += hi[s2].y; v[6] += hi[s2].z; v[7] += hi[s2].w;
+        const float* src = s2 == rank ? part + rr * LD + g * 8 : recv + (s2 * R + rr - r0) * LD + g * 8;
+        const float4 lo = *reinterpret_cast<const float4*>(src);
+        const float4 hi = *reinterpret_cast<const float4*>(src + 4);
+        v[0] += lo.x; v[1] += lo.y; v[2] += lo.z; v[3] += lo.w;
+        v[4] += hi.x; v[5] += hi.y; v[6] += hi.z; v[7] += hi.w;
       }
     }
-    epi_apply<8>(p, e, v, row, n0 + g * 8, e.n_local0 + g * 8, res);
+    epi_finish8(p, cur, v, row, n0 + g * 8);
   }
 }
 
@@ -367,6 +483,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tfull0 = empty0 + 8 * STAGES;
   const uint32_t tempty0 = tfull0 + 16;
   const uint32_t drain = tempty0 + 16;
+  const uint32_t recv_bar = drain + 8;   // cluster split-K: the band's incoming rows
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -394,6 +511,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(tempty0 + 8 * a, GEMM_EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -409,6 +527,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  bool cl_ok = false;   // cluster split-K: this thread saw the accumulator complete
   // Weight tile source of unit u: tensor map and first row.
   auto unit_b = [&](int u, const CUtensorMap*& mb, int& n_local) {
     const int n0 = (u / splits / num_m) * BN;
@@ -513,7 +632,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     int tc = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++tc) {
+    if constexpr (CL) {
+      // One unit per CTA (accumulator 0, phase 0); the push and reduction
+      // follow the role branches, where every thread takes the cluster
+      // barriers whatever happened here.
+      cl_ok = static_cast<int>(blockIdx.x) < num_units && mbar_wait(tfull0, 0, abort_flag);
+      tc_fence_after();
+    }
+    for (int u = blockIdx.x; !CL && u < num_units; u += gridDim.x, ++tc) {
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
       if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) break;
@@ -523,8 +649,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       const int row = m_blk * GEMM_BM + row_in_tile;
       const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
-      if constexpr (CL) gemm_part_to_smem<BN>(taddr, reinterpret_cast<float*>(smem), row_in_tile, c0, c1);
-      else gemm_epilogue_tile(p, taddr, row, n_blk * BN, c0, c1);
+      gemm_epilogue_tile(p, taddr, row, n_blk * BN, c0, c1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty0 + 8 * acc);   // accumulator free for the next unit
@@ -532,15 +657,42 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 
   if constexpr (CL) {
-    // One unit per CTA; the cluster's CTAs are the splits of one tile.
+    static_assert(!CL || L::CL_FITS, "cluster split-K buffers do not fit the ring");
+    // The cluster's CTAs are the splits of one tile; CTA r owns rows
+    // [r * R, r * R + R). Each writes its partial locally and announces the
+    // bytes its band will receive; after barrier A (every split's MMAs are
+    // done and its partial written, so every ring is free) one thread sends
+    // each other CTA its band by bulk copy; owners reduce; barrier C keeps
+    // every CTA alive until the copies out of its partial have landed.
+    float* part = reinterpret_cast<float*>(smem);
+    float* recv = reinterpret_cast<float*>(smem + L::PART_BYTES);
+    const int rank = static_cast<int>(cluster_rank());
+    const int R = (128 + splits - 1) / splits;
+    auto band_rows = [&](int r) { return max(0, min(128, r * R + R) - r * R); };
+    if (warp >= 2 && __all_sync(0xffffffffu, cl_ok)) {
+      const int q = warp & 3, half = (warp - 2) >> 2;
+      gemm_part_to_smem<BN>(tmem_base + (static_cast<uint32_t>(q * 32) << 16), part, q * 32 + lane,
+                            half * (BN / 64), (half + 1) * (BN / 64));
+    }
+    if (threadIdx.x == 64)
+      mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((splits - 1) * band_rows(rank) * L::PART_LD * 4));
     __syncwarp();
-    cluster_sync_all();   // every split's partial is in its shared memory
+    cluster_sync_all();   // barrier A
+    if (threadIdx.x == 32) {
+      for (int o = 0; o < splits; ++o) {
+        if (o == rank || band_rows(o) == 0) continue;
+        bulk_copy_to_peer(map_to_rank(smem_u32(recv) + static_cast<uint32_t>(rank * R * L::PART_LD * 4), o),
+                          smem_u32(part) + static_cast<uint32_t>(o * R * L::PART_LD * 4),
+                          static_cast<uint32_t>(band_rows(o) * L::PART_LD * 4), map_to_rank(recv_bar, o));
+      }
+    }
     if (warp >= 2) {
       const int t = blockIdx.x / splits;
-      gemm_cluster_reduce<BN>(p, reinterpret_cast<const float*>(smem), static_cast<int>(cluster_rank()),
-                              t % num_m, (t / num_m) * BN, threadIdx.x - 64, GEMM_EPI_WARPS * 32);
+      gemm_cluster_reduce<BN>(p, part, recv, recv_bar, abort_flag, rank, t % num_m, (t / num_m) * BN,
+                              threadIdx.x - 64, GEMM_EPI_WARPS * 32);
     }
-    cluster_sync_all();   // no CTA leaves while another reads its partial
+    __syncwarp();
+    cluster_sync_all();   // barrier C
   }
   tc_fence_before();
   __syncthreads();

@@ -124,19 +124,22 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
 //     so narrow tiles spend most of an SM's ingest on re-reading A;
 //   * the weights stream from HBM at no more than ~6 TB/s in all;
 //   * an output tile's epilogue costs ~1 + BN/128 us; a split tile's
-//     cluster reduction ~1.5 + BN/128 (0.7 + 2/splits) us.
+//     cluster reduction ~1.5 + BN/128 (0.7 + 2/splits) us;
+//   * split plans use 64- or 128-column tiles (cluster_capacity_bn).
 // Splits need all clusters co-resident (capacity queried per device), at
 // least 4 k-blocks each and splits x tiles <= SMs.
 struct TilePlan {
   int bn, splits, kb_per_split;
 };
 
+// Split plans use 64- or 128-column tiles: a 256-column tile's fp32
+// partial and receive slots do not fit its ring.
 template <bool F8>
 inline int cluster_capacity_bn(int bn, int splits, int sms) {
   switch (bn) {
-    case 256: return cluster_capacity<256, 4, F8>(splits, sms);
     case 128: return cluster_capacity<128, 6, F8>(splits, sms);
-    default: return cluster_capacity<64, 8, F8>(splits, sms);
+    case 64: return cluster_capacity<64, 8, F8>(splits, sms);
+    default: return 0;
   }
 }
 
@@ -275,11 +278,8 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
     constexpr bool F8 = decltype(f8c)::value;
     if (pair) return launch_gemm2<F8>(ta, tb, p, di.sms, stream);
     if (tp.splits > 1) {
-      switch (bn) {
-        case 256: return launch_gemm_cl<256, 4, F8>(ta, tb, p, stream);
-        case 128: return launch_gemm_cl<128, 6, F8>(ta, tb, p, stream);
-        default: return launch_gemm_cl<64, 8, F8>(ta, tb, p, stream);
-      }
+      if (bn == 128) return launch_gemm_cl<128, 6, F8>(ta, tb, p, stream);
+      return launch_gemm_cl<64, 8, F8>(ta, tb, p, stream);
     }
     switch (bn) {
       case 256: return launch_gemm_bn<256, 4, F8>(ta, tb, p, di.sms, stream);
