@@ -136,3 +136,43 @@ def test_split_kv_single_tile(cuda_device, Sq, Sk, hot):
         k[:, -5:] *= 4
     q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
     _check(ops.sdpa(q, k, v), _sdpa_ref(q, k, v))
+
+
+@pytest.mark.parametrize("Q,rows,pool,vis", [
+    (32, [0, 0, 0, 0], 700, 600),              # G 4: one cluster, one shared history row
+    (32, [1, 1, 1, 1, 0, 0, 0, 0], 700, 650),  # two clusters, each with its own history row
+    (64, [1, 1], 1000, 930),                   # G 2
+    (16, [0] * 8, 500, 420),                   # G 8
+    (32, [0, 0, 0, 0], 200, 60),               # two key tiles for four CTAs: some take none
+])
+def test_candidate_grouped(cuda_device, Q, rows, pool, vis):
+    """Candidates that share one history row attend as one 128-row query
+    group per head: a cluster of 128 / Q CTAs splits the history tiles and
+    the block-diagonal tile of the candidates' own keys, then merges
+    (m, l, O) across the cluster. Each candidate must still see only the
+    history plus its own keys (model.py:654-660)."""
+    g = torch.Generator(device="cuda").manual_seed(Q * 100 + pool)
+    Bp, B, H = 2, len(rows), 2
+    kp = torch.randn(Bp, pool, H, 128, device="cuda", generator=g).bfloat16()
+    vp = torch.randn(Bp, pool, H, 128, device="cuda", generator=g).bfloat16()
+    mask = torch.zeros(pool, dtype=torch.bool, device="cuda")
+    mask[torch.randperm(pool, generator=g, device="cuda")[:vis]] = True
+    kp[:, ~mask] = float("nan")
+    vp[:, ~mask] = float("nan")
+    r = torch.tensor(rows, dtype=torch.int64, device="cuda")
+    D = H * 128
+    qkv = torch.randn(B * Q, 3 * D, device="cuda", generator=g).bfloat16()
+    tl = _tiles(mask)
+    tiles = torch.tensor(tl, dtype=torch.int32, device="cuda").view(-1, 2)
+    n = torch.tensor([len(tl)], dtype=torch.int32, device="cuda")
+    out = ops.attention(qkv, kp.view(Bp * pool, -1), vp.view(Bp * pool, -1), heads=H, q_rows=Q,
+                        src0_batch_stride=pool, tiles=tiles, n_tiles=n, src0_map=r,
+                        k1=qkv, v1=qkv, k1_col=D, v1_col=2 * D)
+    idx = mask.nonzero().squeeze(-1)
+    q = qkv[:, :D].view(B, Q, H, 128)
+    k = torch.cat([kp[:, idx].index_select(0, r), qkv[:, D:2 * D].view(B, Q, H, 128)], 1)
+    v = torch.cat([vp[:, idx].index_select(0, r), qkv[:, 2 * D:].view(B, Q, H, 128)], 1)
+    torch.cuda.synchronize()
+    from wam_ops import _lib
+    assert _lib.device_status() == 0
+    _check(out.view(B, Q, H, 128), _sdpa_ref(q, k, v))

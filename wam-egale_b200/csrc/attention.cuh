@@ -130,14 +130,29 @@ struct AttnParams {
   // source 1 (own rows of this call)
   int has_src1;
   int k1_col, v1_col;
+  // Grouped candidates (G > 1; launched as clusters of G CTAs along z,
+  // G * q_rows = 128, source-0 rows by src0_map): when the G batch rows of
+  // a cluster read the same source-0 row, its CTAs share one 128-row query
+  // tile holding all G candidates, split the key tiles (source 0, then the
+  // G candidates' own keys as one block-diagonal tile) and merge (m, l, O).
+  int group;
 };
 
 struct AttnSmem {
   static constexpr uint32_t Q_OFF = 0;                                    // Q_A, Q_B
   static constexpr uint32_t RING_OFF = Q_OFF + 2 * ATT_TILE_BYTES;        // K/V ring
   static constexpr uint32_t BAR_OFF = RING_OFF + ATT_SLOTS * ATT_TILE_BYTES;
-  // q_full, full[5], empty[5], s_full[2], p_full[2], o_done, drain
-  static constexpr uint32_t NBARS = 17;
+  // q_full, full[5], empty[5], s_full[2], p_full[2], o_done, drain, recv
+  static constexpr uint32_t NBARS = 18;
+  // Grouped candidates, over the ring once the MMAs are done: this CTA's
+  // partial O [128][PART_LD] fp32, m [128], l [128], then one receive slot
+  // per sender of q_rows x (PART_LD + 2) floats (128 rows in all).
+  static constexpr uint32_t PART_LD = 132;
+  static constexpr uint32_t PART_O = RING_OFF;
+  static constexpr uint32_t PART_M = PART_O + 128 * PART_LD * 4;
+  static constexpr uint32_t PART_L = PART_M + 128 * 4;
+  static constexpr uint32_t RECV = PART_L + 128 * 4;
+  static_assert(RECV + 128 * (PART_LD + 2) * 4 <= BAR_OFF, "grouped exchange does not fit the ring");
   static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
   static_assert(TOTAL <= 232448, "attention shared memory exceeds 227 KB");
 };
@@ -173,6 +188,9 @@ WAMB_DEV KvTile att_tile(const AttnParams& p, int j, int n0, int b) {
   return t;
 }
 
+// GROUPED: the grouped-candidate variant (cluster launch); false compiles
+// the kernel without any of that code.
+template <bool GROUPED>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
                    const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
@@ -191,6 +209,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t p_full = bar0 + 104;     // [2] by query tile
   const uint32_t o_done = bar0 + 120;
   const uint32_t drain = bar0 + 128;
+  const uint32_t recv_bar = bar0 + 136;   // grouped: the other CTAs' partials of this CTA's rows
   // Ring load L (the L-th K or V tile in consumption order; K_j = 2j and
   // V_j = 2j+1 without split-KV) lives in slot L % 5, phase (L / 5) & 1.
   auto slot_addr = [&](int L) { return sRing + (L % ATT_SLOTS) * ATT_TILE_BYTES; };
@@ -205,10 +224,30 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y;
   const int q0 = blockIdx.x * 256;
-  const bool has_b = q0 + 128 < p.q_rows;   // the second query tile holds rows
   const int n0 = p.tiles != nullptr ? *p.n_tiles : (p.src0_len + 127) / 128;
-  const int n1 = p.has_src1 ? (p.q_rows + 127) / 128 : 0;
-  const int n = n0 + n1;
+  // Grouped candidates: the cluster's G batch rows share their source-0 row
+  // (checked here, so every CTA of the cluster decides alike).
+  const int G = GROUPED && p.group > 1 ? p.group : 1;
+  const int b0 = b - b % G, rank = b - b0;
+  bool grouped = GROUPED && G > 1;
+  for (int i = 1; grouped && i < G; ++i) grouped = p.src0_map[b0 + i] == p.src0_map[b0];
+  // Key tiles of this CTA: [kv_lo, kv_lo + n) of the tile space (source 0,
+  // then source 1; grouped: source 0, then the group's own-key tile n0).
+  const int n_all = grouped ? n0 + 1 : n0 + (p.has_src1 ? (p.q_rows + 127) / 128 : 0);
+  const int kv_lo = grouped ? rank * n_all / G : 0;
+  const int n = grouped ? (rank + 1) * n_all / G - kv_lo : n_all;
+  const bool has_b = !grouped && q0 + 128 < p.q_rows;   // the second query tile holds rows
+  auto tile_of = [&](int j) {   // this CTA's j-th key tile
+    const int jj = kv_lo + j;
+    if (grouped && jj == n0) {
+      KvTile t;
+      t.row = b0 * p.q_rows;
+      t.len = G * p.q_rows;
+      t.src = 1;
+      return t;
+    }
+    return att_tile(p, jj, n0, b);
+  };
   // Split-KV: a CTA with one query tile runs its keys as two halves, [0, nA)
   // in TMEM slot A and [nA, n) in slot B (both against Q_A), so the two-slot
   // ping-pong still overlaps softmax with MMAs; the epilogue merges the halves.
@@ -228,6 +267,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -243,7 +283,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   if (warp == ATT_PRODUCER_WARP) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
-      const int qrow = b * p.q_rows + q0;
+      const int qrow = grouped ? b0 * p.q_rows : b * p.q_rows + q0;
       const int qcol = p.q_col + h * 128;
       mbar_arrive_expect_tx(q_full, (has_b ? 2 : 1) * ATT_TILE_BYTES);
       tma_load_2d(sQ, &tmQ, q_full, qcol, qrow);
@@ -264,7 +304,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       auto emit = [&](int j, bool is_v) {
         if (!go) return;
         const int L = issued;
-        const KvTile t = att_tile(p, j, n0, b);
+        const KvTile t = tile_of(j);
         const CUtensorMap *mk, *mv;
         int kc, vc;
         src_of(t, mk, mv, kc, vc);
@@ -351,7 +391,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int t = 0; ok && t < 2; ++t) {
           const int nt = t ? nB : nA;
           if (j >= nt) break;
-          const int len = att_tile(p, t ? nA + j : j, n0, b).len;
+          const int len = tile_of(t ? nA + j : j).len;
           if (!wait_full(Lc)) { ok = false; break; }
           zero_v_tail(Lc, len);
           if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
@@ -378,7 +418,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
     }
     for (int j = 0; !split && ok && j < n; ++j) {
-      const KvTile tl = att_tile(p, j, n0, b);
+      const KvTile tl = tile_of(j);
       const int ksteps = (tl.len + 15) >> 4;
       if (!wait_full(2 * j + 1)) break;
       zero_v_tail(2 * j + 1, tl.len);
@@ -417,7 +457,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; active && ok && j < nt; ++j) {
-      const int len = att_tile(p, kv0 + j, n0, b).len;
+      // Valid key columns [lo, hi): the tile's length, or in the group's own
+      // keys only the row's candidate (a row sees only its own keys).
+      int lo = 0, hi = tile_of(kv0 + j).len;
+      if (grouped && kv_lo + kv0 + j == n0) {
+        lo = (r / p.q_rows) * p.q_rows;
+        hi = lo + p.q_rows;
+      }
       if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       float s[128];
@@ -429,10 +475,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = t32[i];
       }
       tmem_wait_ld();
-      if (len < 128) {
+      if (lo > 0 || hi < 128) {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
-          if (i >= len) s[i] = -INFINITY;
+          if (i < lo || i >= hi) s[i] = -INFINITY;
       }
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
@@ -513,13 +559,33 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const float aA = mA == -INFINITY ? 0.f : exp2f(mA - M);
       const float aB = mB == -INFINITY ? 0.f : exp2f(mB - M);
       const float den = aA * lA + aB * lB;
+      if (grouped) {
+        // This CTA's partial of the row: O relative to M, unnormalized.
+        float* po = reinterpret_cast<float*>(smem + L::PART_O) + r * L::PART_LD + t * 64;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float oa[32], ob[32];
+          tmem_ld32(tmem + lane_base + 256 + t * 64 + c * 32, oa);
+          tmem_ld32(tmem + lane_base + 384 + t * 64 + c * 32, ob);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            reinterpret_cast<float4*>(po + c * 32)[k] =
+                make_float4(oa[4 * k] * aA + ob[4 * k] * aB, oa[4 * k + 1] * aA + ob[4 * k + 1] * aB,
+                            oa[4 * k + 2] * aA + ob[4 * k + 2] * aB, oa[4 * k + 3] * aA + ob[4 * k + 3] * aB);
+        }
+        if (t == 0) {
+          reinterpret_cast<float*>(smem + L::PART_M)[r] = ok ? M : -INFINITY;
+          reinterpret_cast<float*>(smem + L::PART_L)[r] = ok ? den : 0.f;
+        }
+      }
       const float inv = (ok && !*abort_flag && den > 0.f) ? 1.f / den : 0.f;
       const float sA = aA * inv, sB = aB * inv;
       const int qr = q0 + r;
-      const bool store = qr < p.q_rows;
+      const bool store = !grouped && qr < p.q_rows;
       __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128 + t * 64;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; !grouped && c < 2; ++c) {
         float oa[32], ob[32];
         tmem_ld32(tmem + lane_base + 256 + t * 64 + c * 32, oa);
         tmem_ld32(tmem + lane_base + 384 + t * 64 + c * 32, ob);
@@ -540,6 +606,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           }
         }
       }
+    } else if (active && grouped) {
+      // One key tile (or none): this CTA's partial is slot A's O, m, l.
+      if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
+      tc_fence_after();
+      float* po = reinterpret_cast<float*>(smem + L::PART_O) + r * L::PART_LD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        if (n > 0) {
+          tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          reinterpret_cast<float4*>(po + c * 32)[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+      }
+      reinterpret_cast<float*>(smem + L::PART_M)[r] = ok && n > 0 ? m_used : -INFINITY;
+      reinterpret_cast<float*>(smem + L::PART_L)[r] = ok && n > 0 ? l : 0.f;
     } else if (active) {
       if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
       tc_fence_after();
@@ -568,6 +655,91 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   }
 
+  if (grouped) {
+    // Exchange: CTA `rank` owns the rows of candidate b0 + rank. Each CTA
+    // announces the bytes its rows will receive, barrier A (every partial is
+    // written; every CTA's MMAs and loads are done, so its ring is free),
+    // one thread sends each owner its rows (O, m, l) by bulk copy into slot
+    // `rank`, owners merge in sender order (the result does not depend on
+    // timing), barrier C keeps every CTA alive until its copies out landed.
+    const int qr = p.q_rows;
+    const uint32_t slot_bytes = static_cast<uint32_t>(qr * (L::PART_LD + 2) * 4);
+    const float* part_o = reinterpret_cast<const float*>(smem + L::PART_O);
+    const float* part_m = reinterpret_cast<const float*>(smem + L::PART_M);
+    const float* part_l = reinterpret_cast<const float*>(smem + L::PART_L);
+    const uint8_t* recv = smem + L::RECV;
+    if (threadIdx.x < 256) fence_proxy_async();
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(G - 1) * slot_bytes);
+    __syncwarp();
+    cluster_sync_all();   // barrier A
+    if (threadIdx.x == ATT_MMA_WARP * 32) {
+      for (int o = 0; o < G; ++o) {
+        if (o == rank) continue;
+        const uint32_t dst = map_to_rank(smem_u32(recv) + static_cast<uint32_t>(rank) * slot_bytes, o);
+        const uint32_t bar = map_to_rank(recv_bar, o);
+        bulk_copy_to_peer(dst, smem_u32(part_o + o * qr * L::PART_LD), qr * L::PART_LD * 4, bar);
+        bulk_copy_to_peer(dst + qr * L::PART_LD * 4, smem_u32(part_m + o * qr), qr * 4, bar);
+        bulk_copy_to_peer(dst + qr * L::PART_LD * 4 + qr * 4, smem_u32(part_l + o * qr), qr * 4, bar);
+      }
+    }
+    if (threadIdx.x < 256) {
+      const bool ok = mbar_wait(recv_bar, 0, abort_flag);
+      // 16-column groups of this candidate's rows.
+      for (int it = threadIdx.x; it < qr * 8; it += 256) {
+        const int rr = it >> 3, cg = (it & 7) * 16;
+        const int own = rank * qr + rr;
+        float ms[8], ls[8];
+        float M = -INFINITY;
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+          ms[s2] = -INFINITY;
+          ls[s2] = 0.f;
+          if (s2 < G) {
+            const float* rm = reinterpret_cast<const float*>(recv + s2 * slot_bytes) + qr * L::PART_LD;
+            ms[s2] = s2 == rank ? part_m[own] : rm[rr];
+            ls[s2] = s2 == rank ? part_l[own] : rm[qr + rr];
+            M = fmaxf(M, ms[s2]);
+          }
+        }
+        float acc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+        float den = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+          if (s2 < G) {
+            const float w = ms[s2] == -INFINITY ? 0.f : exp2f(ms[s2] - M);
+            den += w * ls[s2];
+            const float* src = s2 == rank
+                                   ? part_o + own * L::PART_LD + cg
+                                   : reinterpret_cast<const float*>(recv + s2 * slot_bytes) + rr * L::PART_LD + cg;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float4 v = reinterpret_cast<const float4*>(src)[k];
+              acc[4 * k] += w * v.x;
+              acc[4 * k + 1] += w * v.y;
+              acc[4 * k + 2] += w * v.z;
+              acc[4 * k + 3] += w * v.w;
+            }
+          }
+        }
+        const float inv = (ok && !*abort_flag && den > 0.f) ? 1.f / den : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(
+            p.out + (static_cast<long long>(b) * qr + rr) * p.ldo + h * 128 + cg);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          uint4 w;
+          w.x = pack_bf16(acc[8 * k + 0] * inv, acc[8 * k + 1] * inv);
+          w.y = pack_bf16(acc[8 * k + 2] * inv, acc[8 * k + 3] * inv);
+          w.z = pack_bf16(acc[8 * k + 4] * inv, acc[8 * k + 5] * inv);
+          w.w = pack_bf16(acc[8 * k + 6] * inv, acc[8 * k + 7] * inv);
+          dst[k] = w;
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();   // barrier C
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == ATT_MMA_WARP) {

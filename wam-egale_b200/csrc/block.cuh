@@ -75,12 +75,37 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
   int dev = 0;
   WAMB_CHECK_CUDA(cudaGetDevice(&dev));
   if (!configured[dev]) {
-    WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnSmem::TOTAL));
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnSmem::TOTAL));
     configured[dev] = true;
   }
   dim3 grid((a->q_rows + 255) / 256, a->heads, a->batch);
-  return launch_kernel(attn_tc_kernel, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
+  // Candidate verification with short chunks: G = 128 / q_rows batch rows
+  // per cluster (the kernel checks that they share their history row).
+  const int G = a->q_rows >= 16 && 128 % a->q_rows == 0 ? 128 / a->q_rows : 1;
+  if (p.src0_map != nullptr && p.has_src1 && G >= 2 && G <= 8 && a->batch % G == 0) {
+    p.group = G;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(ATT_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = AttnSmem::TOTAL;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = G;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<true>, tq, tk0, tv0, tk1, tv1, p));
+    return WAMB_OK;
+  }
+  p.group = 1;
+  return launch_kernel(attn_tc_kernel<false>, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
                        tv1, p);
 }
 
