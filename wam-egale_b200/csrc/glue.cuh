@@ -577,25 +577,33 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams
   __syncthreads();
 
   // Run-tile list: maximal runs of visible slots inside each 128-slot window.
+  // A tile starts at a visible slot whose predecessor is hidden or in the
+  // previous window, and ends at a visible slot whose successor is hidden or
+  // in the next window; the k-th start and the k-th end (in slot order)
+  // belong to tile k, so two scans pair them without walking the runs.
   {
-    int nt = 0, nv = 0;
+    auto is_start = [&](int i) { return m[i] && (i % KV_TILE == 0 || !m[i - 1]); };
+    auto is_end = [&](int i) { return m[i] && ((i + 1) % KV_TILE == 0 || i + 1 == p.pool || !m[i + 1]); };
+    int nt = 0, ne = 0, nv = 0;
     for (int i = lo; i < hi; ++i) {
       nv += m[i];
-      nt += m[i] && (i % KV_TILE == 0 || !m[i - 1]);
+      nt += is_start(i);
+      ne += is_end(i);
     }
-    int vis = 0;
-    const int t0 = block_excl_scan(nt, sh, &total);
-    const int ntiles = total;
+    int vis = 0, ntiles = 0, nends = 0;
+    const int t0 = block_excl_scan(nt, sh, &ntiles);
+    const int e0 = block_excl_scan(ne, sh, &nends);
     block_excl_scan(nv, sh, &vis);
     int t = t0;
-    for (int i = lo; i < hi; ++i) {
-      if (m[i] && (i % KV_TILE == 0 || !m[i - 1])) {
-        int e = i + 1;
-        const int wend = min(p.pool, (i / KV_TILE + 1) * KV_TILE);
-        while (e < wend && m[e]) ++e;
-        p.tiles[t++] = make_int2(i, e - i);
+    for (int i = lo; i < hi; ++i)
+      if (is_start(i)) p.tiles[t++].x = i;
+    __syncthreads();   // every start is written (block-scope global visibility)
+    int e = e0;
+    for (int i = lo; i < hi; ++i)
+      if (is_end(i)) {
+        p.tiles[e].y = i + 1 - p.tiles[e].x;
+        ++e;
       }
-    }
     if (s_err && !p.candidate)
       for (int i = threadIdx.x; i < p.q; i += KV_THREADS) p.new_slots[i] = -1;
     if (threadIdx.x == 0) {

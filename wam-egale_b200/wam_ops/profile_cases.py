@@ -5,12 +5,16 @@ hundred MB on the device, 3 warm-up launches then `--launches` more).
   python wam-egale_b200/wam_ops/profile_cases.py attention [--q 880] [--pool 4400] [--batch 8]
   python wam-egale_b200/wam_ops/profile_cases.py rms | ln
   python wam-egale_b200/wam_ops/profile_cases.py small [--m 128] [--n 3072] [--k 14336]
+  python wam-egale_b200/wam_ops/profile_cases.py verify_attention
 
 ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (cfg2 weights); --fp8: E4M3
            operands (quantized once before the timed launches)
 attention  self attention of `batch` cfg2 rollouts over 4400-key pools (24 heads)
 rms        RMSNorm + RoPE of the q/k/v projection output, K/V into the pool
 ln         LayerNorm + adaLN modulation
+verify_attention  cfg3 self attention: 4 candidates x 32 queries sharing one
+           3520-slot history row of a 4400-slot pool (grouped candidates) plus
+           their own keys, 24 heads
 small      small-M GEMM + residual epilogue (the verify batch's O / FFN-out
            projections; cluster split-K where the tiles leave SMs idle); 12
            weight copies rotate so every launch streams its weights from HBM
@@ -28,7 +32,7 @@ from wam_ops import _lib, configs, ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["ffn1", "attention", "rms", "ln", "small"])
+    ap.add_argument("case", choices=["ffn1", "attention", "rms", "ln", "small", "verify_attention"])
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=14336)
@@ -63,6 +67,19 @@ def main():
         it = iter(range(1 << 30))
         run = lambda: ops.linear(x, ws[next(it) % 12], b, epilogue=_lib.EPI_RES, out=out,  # noqa: E731
                                  res=res)
+    elif a.case == "verify_attention":
+        B, Q, pool, hist = 4, 32, 4400, 3520
+        kp = torch.randn(2 * pool, D, generator=g, device=dev).bfloat16()
+        vp = torch.randn(2 * pool, D, generator=g, device=dev).bfloat16()
+        qkv = torch.randn(B * Q, 3 * D, generator=g, device=dev).bfloat16()
+        tl = [(s0, min(128, hist - s0)) for s0 in range(0, hist, 128)]
+        tiles = torch.tensor(tl, dtype=torch.int32, device=dev).view(-1, 2)
+        n = torch.tensor([len(tl)], dtype=torch.int32, device=dev)
+        rows = torch.zeros(B, dtype=torch.int64, device=dev)
+        out = torch.empty(B * Q, D, device=dev, dtype=torch.bfloat16)
+        run = lambda: ops.attention(qkv, kp, vp, heads=H, q_rows=Q, src0_batch_stride=pool,  # noqa: E731
+                                    tiles=tiles, n_tiles=n, src0_map=rows, k1=qkv, v1=qkv, k1_col=D,
+                                    v1_col=2 * D, out=out)
     elif a.case == "attention":
         q = torch.randn(a.batch * a.q, D, generator=g, device=dev).bfloat16()
         kp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
