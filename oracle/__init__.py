@@ -16,6 +16,12 @@ Contents:
                  scheduler.py:6-89).
   fp8.py         the FP8-E4M3 GEMM path (no reference counterpart): row
                  quantization and a block copy with quantized GEMMs.
+  speculative.py speculative action decoding around the target model: the
+                 FastWAM draft predictor, weighted-L2 edge scores, the K2/B2
+                 and K3/B2 route rules and the K2/B2 loop
+                 (fastwam-base/fullcode-v1/draft.py, real_speculative.py;
+                 wam-p0-worktree/wan_va/utils/p0_k3_b2.py), pinned by
+                 tests/golden/make_spec_golden.py.
 
 Parity pin: tests/golden/make_golden.py runs the reference's own model.py
 source (AST-extracted, in the build container where the reference is
