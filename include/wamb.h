@@ -352,6 +352,73 @@ WAMB_API int wamb_repeat_rows(const void* x, int32_t rows, int32_t row_bytes, in
 WAMB_API int wamb_flow_step(void* sample, int32_t sample_is_f32, const void* v, int32_t v_is_f32,
                             int64_t n, float dsigma, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Speculative action decoding around the target model (the reference's K2/B2
+ * loop, fastwam-base/fullcode-v1/real_speculative.py:32-109): the draft
+ * predictor, the tree states, edge scores, route choice and commit. States and
+ * directions are row-major [rows, n] (n = positions x action channels), bf16
+ * or fp32 (io_is_f32). The element maps round as torch's ops on those dtypes.
+ * ------------------------------------------------------------------------ */
+
+/* FastWAM DirectionPredictor weights (fullcode-v1/draft.py:10-20), fp32, with
+ * the reference's state_dict layout: embed [width, 2A+3], position [tokens,
+ * width], TransformerEncoderLayer(width, heads, ffn, GELU, pre-norm) with
+ * in_proj [3 width, width], out_proj, linear1 [ffn, width], linear2 [width,
+ * ffn], norm1 / norm2, head [2A, width], and the normalization buffers.
+ * Supported shape: tokens 32, width 64, heads 4, ffn 256, channels A <= 16. */
+typedef struct wamb_draft_params {
+  int32_t tokens, channels, width, heads, ffn;
+  float ln_eps;
+  const float* embed_w; const float* embed_b; const float* position;
+  const float* in_proj_w; const float* in_proj_b; const float* out_proj_w; const float* out_proj_b;
+  const float* linear1_w; const float* linear1_b; const float* linear2_w; const float* linear2_b;
+  const float* norm1_w; const float* norm1_b; const float* norm2_w; const float* norm2_b;
+  const float* head_w; const float* head_b;
+  const float* feature_mean; const float* feature_std;     /* [2 tokens A + 3] */
+  const float* residual_mean; const float* residual_std;   /* [tokens A] */
+} wamb_draft_params;
+
+/* DirectionPredictor.decode (draft.py:26-36) for `batch` rows: state and
+ * previous [batch, tokens*A] (time-major, io dtype), scalars [batch, 3] fp32
+ * -> out [batch, 2, tokens*A] (io dtype): the two candidate directions. */
+WAMB_API int wamb_draft_forward(const wamb_draft_params* p, const void* state, const void* previous,
+                                int32_t io_is_f32, const float* scalars, int32_t batch, void* out, void* stream);
+
+/* Weighted L2 per tree edge k < edges (at most 16): scores[k] =
+ * ||draft[draft_rows[k]] - target[target_rows[k]]|| * |scales[k]|, or with
+ * scale_inside = 1 ||(draft - target) * scales[k]|| (p0_k3_b2.py:220-232).
+ * The row and scale arrays are host memory; scores fp32 on the device. */
+WAMB_API int wamb_spec_scores(const void* draft, const void* target, int32_t io_is_f32, int64_t n, int32_t edges,
+                              const int32_t* draft_rows, const int32_t* target_rows, const float* scales,
+                              int32_t scale_inside, float* scores, void* stream);
+
+/* Route on the device, route [4] int32:
+ *   mode 0: K2/B2 (real_speculative.py:13-23) over scores first[2],
+ *           second[4] (2 + 2 parent + child) and threshold tau ->
+ *           (depth, parent, child, 0)
+ *   mode 1 / 2: K3/B2 greedy / global (p0_k3_b2.py:258-283) over first[2],
+ *           second[2][2], third[2][2][2] -> (3, parent, child, grandchild) */
+WAMB_API int wamb_spec_route(const float* scores, int32_t mode, double tau, int32_t* route, void* stream);
+
+/* Tree states: out[r] = base[r / fan] + dirs[r] * delta, r < rows. */
+WAMB_API int wamb_spec_expand(const void* base, const void* dirs, int32_t io_is_f32, int32_t rows, int32_t fan,
+                              int64_t n, float delta, void* out, void* stream);
+
+/* K2/B2 commit from a device route (depth, parent, child): row sel = 0,
+ * 1 + parent or 3 + 2 parent + child of the packed tree [7, n] (state,
+ * parents, leaves) and of the target values [7, n]:
+ * state_out = tree[sel] + values[sel] * delta_depth, previous_out =
+ * values[sel] (state_out may be tree row 0). */
+WAMB_API int wamb_spec_commit(const int32_t* route, const void* values, const void* tree, int32_t io_is_f32,
+                              int64_t n, float delta0, float delta1, float delta2, void* state_out,
+                              void* previous_out, void* stream);
+
+/* Classifier-free guidance of packed [conditional | unconditional] rows
+ * (wan_va_server.py:1936-1941): out = uncond + scale * (cond - uncond) when
+ * scale > 1, else cond. */
+WAMB_API int wamb_cfg_combine(const void* cond, const void* uncond, int32_t io_is_f32, int64_t n, float scale,
+                              void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

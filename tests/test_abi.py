@@ -25,7 +25,8 @@ def test_header_symbols_exported():
 
 @pytest.mark.parametrize("cname,pyname", [("wamb_linear_args", "LinearArgs"),
                                             ("wamb_attention_args", "AttentionArgs"),
-                                            ("wamb_block_args", "BlockArgs")])
+                                            ("wamb_block_args", "BlockArgs"),
+                                            ("wamb_draft_params", "DraftParams")])
 def test_struct_layout_matches_header(tmp_path, cname, pyname):
     """Every field offset of the ctypes mirror equals the C compiler's."""
     cc = shutil.which("gcc") or shutil.which("cc")

@@ -6,6 +6,9 @@
 #include "linear.cuh"
 #include "block.cuh"
 #include "model.cuh"
+#include "speculative.cuh"
+
+#include <cmath>
 
 namespace wamb {
 
@@ -39,7 +42,7 @@ extern "C" {
 
 const char* wamb_last_error(void) { return wamb::g_last_error.c_str(); }
 
-int wamb_abi_version(void) { return 103; }
+int wamb_abi_version(void) { return 104; }
 
 int wamb_device_status(void* stream, int* device_code) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -229,8 +232,120 @@ int wamb_flow_step(void* sample, int32_t sample_is_f32, const void* v, int32_t v
   int rc = device_info(&di);
   if (rc) return rc;
   return launch_kernel(flow_step_kernel, dim3(elem_grid(n, di.sms)), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                       sample, sample_is_f32, v,
-                                                                                      v_is_f32, n, dsigma);
+                       sample, sample_is_f32, v, v_is_f32, n, dsigma);
+}
+
+// ------------------------------------------------- speculative decoding
+int wamb_draft_forward(const wamb_draft_params* p, const void* state, const void* previous, int32_t io_is_f32,
+                       const float* scalars, int32_t batch, void* out, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(p != nullptr, WAMB_ERR_ARG, "null draft params");
+  WAMB_REQUIRE(p->tokens == DR_T && p->width == DR_E && p->heads == DR_H && p->ffn == DR_F, WAMB_ERR_SHAPE,
+               "draft shape tokens %d width %d heads %d ffn %d (supported: %d, %d, %d, %d)", p->tokens, p->width,
+               p->heads, p->ffn, DR_T, DR_E, DR_H, DR_F);
+  WAMB_REQUIRE(p->channels >= 1 && p->channels <= DR_AMAX, WAMB_ERR_SHAPE, "draft channels %d (1..%d)",
+               p->channels, DR_AMAX);
+  WAMB_REQUIRE(batch >= 0 && (io_is_f32 == 0 || io_is_f32 == 1), WAMB_ERR_ARG, "batch / dtype");
+  if (batch == 0) return WAMB_OK;
+  const float* w[] = {p->embed_w, p->embed_b, p->position, p->in_proj_w, p->in_proj_b, p->out_proj_w,
+                      p->out_proj_b, p->linear1_w, p->linear1_b, p->linear2_w, p->linear2_b, p->norm1_w,
+                      p->norm1_b, p->norm2_w, p->norm2_b, p->head_w, p->head_b, p->feature_mean,
+                      p->feature_std, p->residual_mean, p->residual_std};
+  for (const float* x : w) WAMB_REQUIRE(x != nullptr, WAMB_ERR_ARG, "null draft weight");
+  WAMB_REQUIRE(state && previous && scalars && out, WAMB_ERR_ARG, "null draft input / output");
+  static bool configured[64] = {};
+  int dev = 0;
+  WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+  WAMB_REQUIRE(dev >= 0 && dev < 64, WAMB_ERR_CUDA, "device index %d", dev);
+  if (!configured[dev]) {
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(draft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         DraftSmem::BYTES));
+    configured[dev] = true;
+  }
+  DraftArgs a{};
+  a.A = p->channels;
+  a.eps = p->ln_eps;
+  a.embed_w = p->embed_w; a.embed_b = p->embed_b; a.position = p->position;
+  a.ln1_w = p->norm1_w; a.ln1_b = p->norm1_b; a.in_w = p->in_proj_w; a.in_b = p->in_proj_b;
+  a.out_w = p->out_proj_w; a.out_b = p->out_proj_b; a.ln2_w = p->norm2_w; a.ln2_b = p->norm2_b;
+  a.l1_w = p->linear1_w; a.l1_b = p->linear1_b; a.l2_w = p->linear2_w; a.l2_b = p->linear2_b;
+  a.head_w = p->head_w; a.head_b = p->head_b;
+  a.fmean = p->feature_mean; a.fstd = p->feature_std; a.rmean = p->residual_mean; a.rstd = p->residual_std;
+  a.state = state; a.previous = previous; a.io_f32 = io_is_f32; a.scalars = scalars; a.out = out;
+  return launch_kernel(draft_kernel, dim3(batch), dim3(DR_THREADS), DraftSmem::BYTES,
+                       static_cast<cudaStream_t>(stream), a);
+}
+
+int wamb_spec_scores(const void* draft, const void* target, int32_t io_is_f32, int64_t n, int32_t edges,
+                     const int32_t* draft_rows, const int32_t* target_rows, const float* scales,
+                     int32_t scale_inside, float* scores, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(edges >= 0 && edges <= SPEC_MAX_EDGES && n > 0, WAMB_ERR_SHAPE, "edges %d (0..%d), n %lld", edges,
+               SPEC_MAX_EDGES, static_cast<long long>(n));
+  if (edges == 0) return WAMB_OK;
+  WAMB_REQUIRE(draft && target && draft_rows && target_rows && scales && scores, WAMB_ERR_ARG, "null pointer");
+  SpecEdges e{};
+  e.n = edges;
+  e.scale_inside = scale_inside ? 1 : 0;
+  for (int k = 0; k < edges; ++k) {
+    WAMB_REQUIRE(draft_rows[k] >= 0 && target_rows[k] >= 0, WAMB_ERR_ARG, "negative row");
+    e.d[k] = draft_rows[k];
+    e.t[k] = target_rows[k];
+    e.scale[k] = scales[k];
+  }
+  return launch_kernel(spec_scores_kernel, dim3(edges), dim3(256), 0, static_cast<cudaStream_t>(stream), draft,
+                       target, io_is_f32, static_cast<long long>(n), e, scores);
+}
+
+int wamb_spec_route(const float* scores, int32_t mode, double tau, int32_t* route, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(mode >= 0 && mode <= 2, WAMB_ERR_ARG, "route mode %d", mode);
+  WAMB_REQUIRE(mode != 0 || (std::isfinite(tau) && tau >= 0.0), WAMB_ERR_ARG, "tau must be finite and >= 0");
+  WAMB_REQUIRE(scores && route, WAMB_ERR_ARG, "null pointer");
+  return launch_kernel(spec_route_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), scores, mode,
+                       tau, route);
+}
+
+int wamb_spec_expand(const void* base, const void* dirs, int32_t io_is_f32, int32_t rows, int32_t fan, int64_t n,
+                     float delta, void* out, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(rows >= 0 && fan >= 1 && n >= 0, WAMB_ERR_SHAPE, "rows / fan / n");
+  if (rows == 0 || n == 0) return WAMB_OK;
+  WAMB_REQUIRE(base && dirs && out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  return launch_kernel(spec_expand_kernel, dim3(elem_grid(static_cast<long long>(rows) * n, di.sms)), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), base, dirs, out, io_is_f32, rows, fan,
+                       static_cast<long long>(n), delta);
+}
+
+int wamb_spec_commit(const int32_t* route, const void* values, const void* tree, int32_t io_is_f32, int64_t n,
+                     float delta0, float delta1, float delta2, void* state_out, void* previous_out, void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(n >= 0, WAMB_ERR_SHAPE, "n");
+  if (n == 0) return WAMB_OK;
+  WAMB_REQUIRE(route && values && tree && state_out && previous_out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  return launch_kernel(spec_commit_kernel, dim3(elem_grid(n, di.sms)), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), route, values, tree, io_is_f32, static_cast<long long>(n),
+                       delta0, delta1, delta2, state_out, previous_out);
+}
+
+int wamb_cfg_combine(const void* cond, const void* uncond, int32_t io_is_f32, int64_t n, float scale, void* out,
+                     void* stream) {
+  using namespace wamb;
+  WAMB_REQUIRE(n >= 0, WAMB_ERR_SHAPE, "n");
+  if (n == 0) return WAMB_OK;
+  WAMB_REQUIRE(cond && uncond && out, WAMB_ERR_ARG, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  return launch_kernel(cfg_combine_kernel, dim3(elem_grid(n, di.sms)), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), cond, uncond, out, io_is_f32, static_cast<long long>(n),
+                       scale);
 }
 
 }  // extern "C"

@@ -51,6 +51,21 @@ class AttentionArgs(ctypes.Structure):
     ]
 
 
+class DraftParams(ctypes.Structure):
+    """Mirror of `wamb_draft_params` (include/wamb.h)."""
+    _fields_ = [
+        ("tokens", c_int32), ("channels", c_int32), ("width", c_int32), ("heads", c_int32), ("ffn", c_int32),
+        ("ln_eps", ctypes.c_float),
+        ("embed_w", c_void_p), ("embed_b", c_void_p), ("position", c_void_p),
+        ("in_proj_w", c_void_p), ("in_proj_b", c_void_p), ("out_proj_w", c_void_p), ("out_proj_b", c_void_p),
+        ("linear1_w", c_void_p), ("linear1_b", c_void_p), ("linear2_w", c_void_p), ("linear2_b", c_void_p),
+        ("norm1_w", c_void_p), ("norm1_b", c_void_p), ("norm2_w", c_void_p), ("norm2_b", c_void_p),
+        ("head_w", c_void_p), ("head_b", c_void_p),
+        ("feature_mean", c_void_p), ("feature_std", c_void_p),
+        ("residual_mean", c_void_p), ("residual_std", c_void_p),
+    ]
+
+
 class BlockArgs(ctypes.Structure):
     """Mirror of `wamb_block_args` (include/wamb.h)."""
     _fields_ = [
@@ -83,7 +98,7 @@ TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", 
 # Weight slots the FP8 path reads as E4M3 (self q/k/v/out, cross q/out, FFN).
 FP8_WEIGHTS = (3, 5, 7, 9, 13, 19, 23, 25)
 
-ABI_VERSION = 103
+ABI_VERSION = 104
 
 # Every symbol include/wamb.h declares; tests check the library exports them.
 EXPORTED = (
@@ -92,6 +107,8 @@ EXPORTED = (
     "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc", "wamb_quantize_rows",
     "wamb_timestep_embedding", "wamb_silu", "wamb_embed_gather", "wamb_output_norm", "wamb_copy_cols",
     "wamb_flow_step", "wamb_repeat_rows", "wamb_flow_step_cl",
+    "wamb_draft_forward", "wamb_spec_scores", "wamb_spec_route", "wamb_spec_expand", "wamb_spec_commit",
+    "wamb_cfg_combine",
 )
 
 # Size of the fixed scratch array behind wamb_block_forward_noalloc.
@@ -136,6 +153,17 @@ def load():
                                       ctypes.c_float, c_void_p]
     lib.wamb_repeat_rows.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]
     lib.wamb_flow_step.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int64, ctypes.c_float, c_void_p]
+    lib.wamb_draft_forward.argtypes = [ctypes.POINTER(DraftParams), c_void_p, c_void_p, c_int32, c_void_p, c_int32,
+                                       c_void_p, c_void_p]
+    lib.wamb_spec_scores.argtypes = [c_void_p, c_void_p, c_int32, c_int64, c_int32, ctypes.POINTER(c_int32),
+                                     ctypes.POINTER(c_int32), ctypes.POINTER(ctypes.c_float), c_int32, c_void_p,
+                                     c_void_p]
+    lib.wamb_spec_route.argtypes = [c_void_p, c_int32, ctypes.c_double, c_void_p, c_void_p]
+    lib.wamb_spec_expand.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, ctypes.c_float,
+                                     c_void_p, c_void_p]
+    lib.wamb_spec_commit.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int64, ctypes.c_float,
+                                     ctypes.c_float, ctypes.c_float, c_void_p, c_void_p, c_void_p]
+    lib.wamb_cfg_combine.argtypes = [c_void_p, c_void_p, c_int32, c_int64, ctypes.c_float, c_void_p, c_void_p]
     if lib.wamb_abi_version() != ABI_VERSION:
         raise WambError(f"{LIB_PATH} has ABI {lib.wamb_abi_version()}, expected {ABI_VERSION}: rebuild")
     _lib = lib

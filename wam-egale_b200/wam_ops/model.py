@@ -122,6 +122,7 @@ class NativeWanModel:
         self.emb = _Embedders(model.condition_embedder)
         self.emb_action = _Embedders(model.condition_embedder_action)
         self.text = None
+        self._token_bufs = {}   # zero-padded input rows of action_tokens, by shape
 
     # -------------------------------------------------------------- pieces
     def embed_text(self, text_emb):
@@ -162,23 +163,49 @@ class NativeWanModel:
 
     # ------------------------------------------------------------- forward
     def forward(self, input_dict, update_cache=0, cache_name="pos", action_mode=False,
-                candidate_cache_rows=None):
+                candidate_cache_rows=None, context_rows=None):
+        """input_dict as the reference's (noisy_latents [B, C, F, H, W],
+        timesteps [B, F], text_emb or a prepared context, grid_id or
+        rotary_emb). Action mode also takes action_tokens [B, L, C]
+        (time-major, L = F H W) in place of noisy_latents, with
+        action_grid = (F, H, W). context_rows ([B] int64): prepared-context
+        row of each batch row (CFG rows over a [conditional, negative]
+        context)."""
         if torch.is_grad_enabled():
             raise RuntimeError("NativeWanModel is inference-only; use no_grad/inference_mode")
         if candidate_cache_rows is not None and update_cache != 0:
             raise ValueError("candidate read-only forward requires inference and update_cache=0")
-        x = input_dict["noisy_latents"]
-        if x.dim() != 5 or not x.is_cuda:
-            raise ValueError("noisy_latents must be a CUDA [B, C, F, H, W] tensor")
-        x = x.to(torch.bfloat16).contiguous()
-        B, C, Fr, H, W = x.shape
-        p1, p2, p3 = (1, 1, 1) if action_mode else self.patch_size
-        L = (Fr // p1) * (H // p2) * (W // p3)
-        w_in, b_in = self.action_in if action_mode else self.patch_in
         lib, st = _lib.load(), _lib.stream_ptr()
-        xa = torch.empty(B * L, w_in.shape[1], dtype=torch.bfloat16, device=x.device)
-        _lib.check(lib.wamb_embed_gather(x.data_ptr(), B, C, Fr, H, W, p1, p2, p3, xa.data_ptr(),
-                                         w_in.shape[1], st))
+        tokens = input_dict.get("action_tokens") if action_mode else None
+        if tokens is not None:
+            # Time-major action states: the input GEMM reads them through a
+            # zero-padded copy (one row per token, the padding stays zero).
+            if tokens.dim() != 3 or not tokens.is_cuda or tokens.dtype != torch.bfloat16:
+                raise ValueError("action_tokens must be a CUDA bf16 [B, L, C] tensor")
+            x = tokens.contiguous()
+            B, L, C = x.shape
+            Fr, H, W = input_dict["action_grid"]
+            if Fr * H * W != L:
+                raise ValueError("action_grid does not match the token count")
+            w_in, b_in = self.action_in
+            key = (B * L, w_in.shape[1])
+            xa = self._token_bufs.get(key)
+            if xa is None:
+                xa = self._token_bufs[key] = torch.zeros(key, dtype=torch.bfloat16, device=x.device)
+            _lib.check(lib.wamb_copy_cols(x.data_ptr(), C * 2, B * L, C * 2, xa.data_ptr(), w_in.shape[1] * 2, st))
+            p1, p2, p3 = 1, 1, 1
+        else:
+            x = input_dict["noisy_latents"]
+            if x.dim() != 5 or not x.is_cuda:
+                raise ValueError("noisy_latents must be a CUDA [B, C, F, H, W] tensor")
+            x = x.to(torch.bfloat16).contiguous()
+            B, C, Fr, H, W = x.shape
+            p1, p2, p3 = (1, 1, 1) if action_mode else self.patch_size
+            L = (Fr // p1) * (H // p2) * (W // p3)
+            w_in, b_in = self.action_in if action_mode else self.patch_in
+            xa = torch.empty(B * L, w_in.shape[1], dtype=torch.bfloat16, device=x.device)
+            _lib.check(lib.wamb_embed_gather(x.data_ptr(), B, C, Fr, H, W, p1, p2, p3, xa.data_ptr(),
+                                             w_in.shape[1], st))
         h = ops.linear(xa, w_in, b_in).reshape(B, L, self.dim)
         ctx = None
         if self.text is None:
@@ -188,7 +215,8 @@ class NativeWanModel:
             rope = rope_freqs(input_dict["grid_id"][0].to(device=x.device, dtype=torch.float64))
         ph, pw = (1, 1) if action_mode else (p2, p3)
         temb, tproj = self.embed_time(input_dict["timesteps"], (H // ph) * (W // pw), action_mode)
-        h = self.stack.forward(h, ctx, tproj, rope, update_cache, cache_name, candidate_cache_rows)
+        h = self.stack.forward(h, ctx, tproj, rope, update_cache, cache_name, candidate_cache_rows,
+                               context_rows=context_rows)
         n = torch.empty(B * L, self.dim, dtype=torch.bfloat16, device=x.device)
         _lib.check(lib.wamb_output_norm(h.data_ptr(), 0, B * L, self.dim, self.eps, self.table.data_ptr(),
                                         temb.data_ptr(), 1, L, L, n.data_ptr(), st))

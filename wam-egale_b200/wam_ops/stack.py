@@ -32,8 +32,9 @@ class NativeStack:
                 layer.prepare_context(context, precompute=True)
 
     def forward(self, hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache=0,
-                cache_name="pos", candidate_cache_rows=None, out=None):
-        """One denoise step through every layer; returns bf16 [B, Q, D]."""
+                cache_name="pos", candidate_cache_rows=None, out=None, context_rows=None):
+        """One denoise step through every layer; returns bf16 [B, Q, D].
+        context_rows: per-call prepared-context row of each batch row."""
         if torch.is_grad_enabled():
             raise RuntimeError("NativeStack is inference-only; use no_grad/inference_mode")
         B, Q, D = hidden_states.shape
@@ -46,7 +47,7 @@ class NativeStack:
             dst = (out if out is not None else torch.empty(B, Q, D, dtype=torch.bfloat16, device=dev)) \
                 if last else bufs[i % 2]
             layer(h, encoder_hidden_states, temb, rotary_emb, update_cache, cache_name,
-                  candidate_cache_rows, out=dst)
+                  candidate_cache_rows, out=dst, context_rows=context_rows)
             h = dst
         return h
 
