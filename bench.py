@@ -521,6 +521,137 @@ def run_action_chunk(args):
     return 0
 
 
+def _random_draft(dev, channels=7, seed=5):
+    """A seeded random-weight FastWAM DirectionPredictor state_dict (the
+    reference's names and shapes; no trained checkpoint is available)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    A, E, F = channels, 64, 256
+    shapes = {"embed.weight": (E, 2 * A + 3), "embed.bias": (E,), "position": (1, 32, E),
+              "block.self_attn.in_proj_weight": (3 * E, E), "block.self_attn.in_proj_bias": (3 * E,),
+              "block.self_attn.out_proj.weight": (E, E), "block.self_attn.out_proj.bias": (E,),
+              "block.linear1.weight": (F, E), "block.linear1.bias": (F,), "block.linear2.weight": (E, F),
+              "block.linear2.bias": (E,), "block.norm1.weight": (E,), "block.norm1.bias": (E,),
+              "block.norm2.weight": (E,), "block.norm2.bias": (E,), "head.weight": (2 * A, E),
+              "head.bias": (2 * A,)}
+    sd = {k: torch.randn(v, generator=g, device=dev) * 0.1 for k, v in shapes.items()}
+    for k in ("block.norm1.weight", "block.norm2.weight"):
+        sd[k] += 1.0
+    n = 2 * 32 * A + 3
+    sd.update(feature_mean=torch.zeros(n, device=dev), feature_std=torch.ones(n, device=dev),
+              residual_mean=torch.zeros(32 * A, device=dev), residual_std=torch.full((32 * A,), 0.05, device=dev))
+    return sd
+
+
+def run_spec_chunk(args):
+    """--workload spec_chunk: one action chunk (10 flow-match updates) of one
+    rollout through the speculative K2/B2 loop of the reference
+    (fastwam-base/fullcode-v1/real_speculative.py:32-109): the device draft
+    predictor proposes a 7-state tree, ONE target forward (the whole model in
+    action mode, 30 cfg2 blocks over a 3520-token read-only KV history with
+    the prepared 512-token text context, 7 candidate rows) verifies it, the
+    device scores and route commit 1-3 updates. Target forwards replay CUDA
+    graphs (1 and 7 rows); the draft is random-weight (no trained
+    checkpoint), so the line reports the two ends of acceptance: every tree
+    accepted at depth 2 (tau above every score; the headline value) and
+    every tree rejected (tau 0), beside the plain 10-update chunk."""
+    from wam_ops import _lib, configs
+    from wam_ops import speculative as sp
+    from wam_ops.model import NativeWanModel
+    from wam_ops.scheduler import FlowMatchScheduler
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cfg = configs.PRESETS["cfg2"]
+    A, steps = 7, 10
+    gen = torch.Generator(device=dev).manual_seed(98)
+    torch.set_grad_enabled(False)
+    model = configs.build_model(cfg, dev, seed=98, action_dim=A)
+    configs.fill_history(list(model.blocks), cfg, dev, gen, pool_batch=1)
+    nm = NativeWanModel(model)
+    nm.prepare_context(torch.randn(1, cfg.context, 4096, generator=gen, device=dev).bfloat16())
+    f, h, w = cfg.action
+    rope = configs.rope_freqs(configs.mesh_id(f, h, w, 0, f_shift=cfg.history_chunks, action=True)
+                              .to(device=dev, dtype=torch.float64))
+    target = sp.GraphedTarget(sp.NativeActionTarget(nm, (f, h, w), rope))
+    draft = sp.DraftPredictor(_random_draft(dev, A))
+    sched = FlowMatchScheduler(shift=5.0, sigma_min=0.0, extra_one_step=True)
+    sched.set_timesteps(steps)
+    ts = [float(t) for t in sched.timesteps[:steps]]
+    ds = [sched.delta(t) for t in sched.timesteps[:steps]]
+    state0 = torch.randn(1, 32, A, generator=gen, device=dev).bfloat16()
+    times = torch.tensor(ts, dtype=torch.float32, device=dev)
+    lib, n = _lib.load(), 32 * A
+
+    def plain():
+        x = state0.clone()
+        for k in range(steps):
+            v = target(x, times[k:k + 1])
+            _lib.check(lib.wamb_spec_expand(x.data_ptr(), v.data_ptr(), 0, 1, 1, n, ds[k], x.data_ptr(),
+                                            _lib.stream_ptr()))
+        return x
+
+    arms = {"accept_all": sp.K2B2Speculative(target, draft, 1e30), "reject_all": sp.K2B2Speculative(target, draft, 0.0)}
+    runs = {name: (lambda s=spec: s.loop(state0, ts, ds)) for name, spec in arms.items()}
+    runs["plain"] = plain
+    for _ in range(args.warmup):
+        for r in runs.values():
+            r()
+    torch.cuda.synchronize()
+    if _lib.device_status() != 0:
+        raise RuntimeError("device error during warm-up")
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ms, clk = {}, None
+    for name, r in runs.items():
+        clocks = Clocks(0)
+        clocks.start()
+        time.sleep(0.3)
+        e0.record(stream)
+        for _ in range(args.steps):
+            r()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        c = clocks.stop()
+        clk = c if name == "accept_all" else clk
+        ms[name] = e0.elapsed_time(e1) / args.steps
+    hx = state0.cpu().pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = arms["accept_all"].loop(hx.to(dev, non_blocking=True), ts, ds)
+        hout.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    calls = {k: len(s.rounds) for k, s in arms.items()}
+    per_forward = nm.stack.launches_per_step(with_cache=True) + 12   # blocks + embedders / head
+    line = {"metric": "spec_action_chunks_per_s", "value": 1000.0 / ms["accept_all"], "unit": "action-chunks/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms["accept_all"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded model weights N(0,0.02), random unit-scale KV history and text, "
+                    "random-weight draft predictor)",
+            "config": {"workload": "speculative action chunk (K2/B2): 10 flow-match updates (shift 5) of one "
+                                   "rollout, 32 x 7 action tokens, cfg2 blocks (D3072, 30 layers) over a "
+                                   "3520-token read-only KV history, 512 prepared text tokens; 7-row tree "
+                                   "verification per round",
+                       "global_batch": 1, "seq_len": 32, "kv_history": cfg.history_chunks * cfg.tokens,
+                       "denoise_updates_per_chunk": steps,
+                       "rounds": {k: [r[1] for r in s.rounds] for k, s in arms.items()},
+                       "target_forwards_per_chunk": calls,
+                       "ms_per_chunk": ms, "plain_chunks_per_s": 1000.0 / ms["plain"],
+                       "reject_all_chunks_per_s": 1000.0 / ms["reject_all"],
+                       "speedup_accept_all_vs_plain": ms["plain"] / ms["accept_all"]},
+            "e2e": {"value": 1000.0 / ms_e2e, "unit": "action-chunks/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hout.numel() * 2},
+            # per chunk: target forwards, 7 kernels per tree round (2 draft, 2 expand, scores, route,
+            # commit), 1 step per ordinary round
+            "gpu_launches": args.steps * sum(per_forward + (7 if r[1] is not None else 1)
+                                             for r in arms["accept_all"].rounds),
+            "clocks": clk, "device_error": _lib.device_status()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def stack_flops(cfg, split=False):
     """Algorithmic FLOPs of one 30-layer step for ONE rollout: the six
     projections, the two FFN GEMMs and the QK^T / PV products of both
@@ -545,10 +676,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 GEMMs (the FP8 weight path); default is the bf16 drop-in")
-    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg3", "action_chunk"],
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg3", "action_chunk", "spec_chunk"],
                     help="cfg4 (default, the headline): 8 cfg2 rollouts per GPU; cfg3: the "
                          "4 x 32-token candidate verify step on one GPU; action_chunk: 10 whole-model "
-                         "denoise updates of an action chunk")
+                         "denoise updates of an action chunk; spec_chunk: the same chunk for one rollout "
+                         "through the speculative K2/B2 loop")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -558,6 +690,8 @@ def main():
         return run_verify(args)
     if args.workload == "action_chunk":
         return run_action_chunk(args)
+    if args.workload == "spec_chunk":
+        return run_spec_chunk(args)
     return run_native(args)
 
 

@@ -315,7 +315,8 @@ __global__ void spec_expand_kernel(const void* base, const void* dirs, void* out
 __global__ void spec_commit_kernel(const int* route, const void* values, const void* tree, int io_f32, long long n,
                                    float d0, float d1, float d2, void* state_out, void* previous_out) {
   pdl_wait();
-  const int depth = route[0], p = route[1], c = route[2];
+  // The route comes from device memory: clamp it to the tree (rows 0..6).
+  const int depth = min(max(route[0], 0), 2), p = route[1] & 1, c = route[2] & 1;
   const int sel = depth <= 0 ? 0 : (depth == 1 ? 1 + p : 3 + 2 * p + c);
   const float delta = depth <= 0 ? d0 : (depth == 1 ? d1 : d2);
   const long long r0 = static_cast<long long>(sel) * n;

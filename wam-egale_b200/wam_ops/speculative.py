@@ -23,6 +23,7 @@ accepted and 1-3 updates are committed. Every piece runs in libwamb.so:
                       (wan_va_server.py:747-780, 1936-1941)
   NativeActionTarget  the target: NativeWanModel in action mode over the
                       read-only KV history (candidate_cache_rows)
+  GraphedTarget       a target replayed from per-batch-size CUDA graphs
 
 The flow-match step is the product's scheduler step (sample + v * delta in
 fp32, one rounding to the state dtype).
@@ -193,6 +194,41 @@ class NativeActionTarget:
                              "rotary_emb": self.rope}, 0, "pos", True, candidate_cache_rows=rows,
                             context_rows=ctx_rows)
         return cfg_combine(y, k, self.scale) if cfg else y
+
+
+class GraphedTarget:
+    """A target callable replayed from CUDA graphs, one per batch size,
+    captured on first use over static input buffers: the loop's 1-row and
+    7-row target forwards without per-call launch overhead. The returned
+    tensor is the graph's static output (valid until the next call)."""
+
+    def __init__(self, target):
+        self.target = target
+        self.graphs = {}
+
+    def _capture(self, states, times):
+        b = states.shape[0]
+        st = states.clone()
+        tt = times.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.target(st, tt)                  # warm-up: allocations, first-use setup
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = self.target(st, tt)
+        self.graphs[b] = (g, st, tt, out)
+
+    def __call__(self, states, times):
+        b = states.shape[0]
+        if b not in self.graphs:
+            self._capture(states, times)
+        g, st, tt, out = self.graphs[b]
+        st.copy_(states)
+        tt.copy_(times)
+        g.replay()
+        return out
 
 
 class K2B2Speculative:
