@@ -469,7 +469,17 @@ def run_action_chunk(args):
     model = configs.build_model(cfg, dev, seed=99)
     configs.fill_history(list(model.blocks), cfg, dev, gen, pool_batch=B)
     nm = NativeWanModel(model, fp8=args.fp8)
-    nm.prepare_context(torch.randn(B, cfg.context, 4096, generator=gen, device=dev).bfloat16())
+    text = torch.randn(B, cfg.context, 4096, generator=gen, device=dev).bfloat16()
+    nm.prepare_context(text)
+    # Cross K/V construction of a new context (text projection + every
+    # layer's K/V projection and RMS), timed apart from the chunk.
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(3):
+        nm.prepare_context(text)
+    c1.record()
+    torch.cuda.synchronize()
+    ctx_ms = c0.elapsed_time(c1) / 3
     f, h, w = cfg.action
     x = torch.randn(B, 30, f, h, w, generator=gen, device=dev).bfloat16()
     grid = configs.mesh_id(f, h, w, 0, f_shift=cfg.history_chunks, action=True)[None].to(dev)
@@ -512,7 +522,8 @@ def run_action_chunk(args):
                                    "action mode, 8 rollouts x 32 action tokens, cfg2 blocks (D3072, 30 "
                                    "layers) over a 3520-token KV history, 512 prepared text tokens",
                        "global_batch": B, "seq_len": 32, "kv_history": cfg.history_chunks * cfg.tokens,
-                       "denoise_updates_per_chunk": steps, "ms_per_update": ms / steps},
+                       "denoise_updates_per_chunk": steps, "ms_per_update": ms / steps,
+                       "context_prepare_ms": ctx_ms},
             "e2e": {"value": B * 1000.0 / ms_e2e, "unit": "action-chunks/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hout.numel() * 2},
             "gpu_launches": den.launches_per_chunk() * args.steps, "clocks": clk,

@@ -185,3 +185,67 @@ def test_action_chunk_denoiser(cuda_device):
     err_ref = stats(rb, ref)["max_abs"]
     s = assert_parity(out, ref, None, max_abs=max(2e-2, 2 * err_ref))
     print("action chunk", s, "reference bf16 loop", err_ref)
+
+
+def test_kv_lifecycle_prefill_denoise_commit(cuda_device):
+    """The KV-cache lifecycle at model level (model.py:547-593, 667-686): two
+    video chunks prefilled in latent mode with update_cache=2 (written into
+    the pool under chunk ids), an action denoise with update_cache=0 over that
+    history (the mask restored after it), a prediction committed with
+    update_cache=1, clear_pred_cache (Attention.clear_pred_cache), and a
+    final read-only action denoise. Every native output follows the fp32
+    oracle model within the block gate and the cache metadata (id, mask,
+    is_pred) matches the oracle's bit for bit after every call."""
+    from oracle import wan_block as ob
+    m = _oracle_model(seed=31)
+    pool = 160
+    for blk in m.blocks:
+        blk.attn1.init_kv_cache("pos", pool, 2, 128, "cpu", torch.float32, 1)
+        c = blk.attn1.attn_caches["pos"]
+        c["k"].zero_()
+        c["v"].zero_()
+
+    def dev_copy():
+        d = _to_device(m)
+        for blk in d.blocks:
+            c = blk.attn1.attn_caches["pos"]
+            for k in list(c):
+                c[k] = c[k].to(device="cuda", dtype=torch.bfloat16 if k in ("k", "v") else c[k].dtype)
+        return d
+
+    rb_model, dev = dev_copy(), dev_copy()
+    nm = NativeWanModel(dev)
+    g = torch.Generator().manual_seed(8)
+    text = torch.randn(1, 16, CFG["text_dim"], generator=g).bfloat16().float()
+
+    def latent(f_shift):
+        x = torch.randn(1, CFG["in_channels"], 2, 8, 8, generator=g).bfloat16().float()
+        return {"noisy_latents": x, "text_emb": text, "grid_id": ob.get_mesh_id(2, 4, 4, 0, f_shift=f_shift)[None],
+                "timesteps": torch.rand(1, 2, generator=g) * 1000}
+
+    def action(f_shift):
+        x = torch.randn(1, CFG["action_dim"], 8, 4, 1, generator=g).bfloat16().float()
+        return {"noisy_latents": x, "text_emb": text,
+                "grid_id": ob.get_mesh_id(8, 4, 1, 0, f_shift=f_shift, action=True)[None],
+                "timesteps": torch.rand(1, 8, generator=g) * 1000}
+
+    calls = [(latent(0), 2, False), (latent(2), 2, False), (action(4), 0, True), (action(4), 1, True),
+             ("clear", None, None), (action(4), 0, True)]
+    for inp, update, action_mode in calls:
+        if inp == "clear":
+            for model in (m, rb_model, dev):
+                for blk in model.blocks:
+                    blk.attn1.clear_pred_cache("pos")
+            continue
+        with torch.no_grad():
+            ref = m(inp, update_cache=update, action_mode=action_mode)
+            rb = rb_model(_cuda(inp), update_cache=update, action_mode=action_mode)
+            out = nm(_cuda(inp), update_cache=update, action_mode=action_mode)
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0
+        s = assert_parity(out, ref, rb)
+        for bo, bn in zip(m.blocks, dev.blocks):
+            co, cn = bo.attn1.attn_caches["pos"], bn.attn1.attn_caches["pos"]
+            for k in ("id", "mask", "is_pred"):
+                assert torch.equal(co[k], cn[k].cpu()), (update, k)
+        print("kv lifecycle", "action" if action_mode else "latent", update, s)

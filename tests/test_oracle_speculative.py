@@ -72,3 +72,15 @@ def test_k2b2_loop_matches_reference(gold):
                                       run["tau"])
         assert [r[:4] for r in rounds] == [tuple(r) for r in run["rounds"]], run["tau"]
         torch.testing.assert_close(final.float(), run["final"].float(), rtol=2 ** -7, atol=2 ** -7)
+
+
+def test_host_draft_scalars_match_reference_fp32():
+    """The speculative loop computes the draft's (sigma, sigma + delta,
+    sigma) on the host in fp32; they must equal the reference's torch fp32
+    arithmetic (draft.py:38-41) bit for bit."""
+    from wam_ops import speculative as sp
+    g = torch.Generator().manual_seed(1)
+    for t, d in zip((torch.rand(200, generator=g) * 1000).tolist(), (-torch.rand(200, generator=g) * 0.2).tolist()):
+        host = torch.tensor(sp.draft_scalars(t, d), dtype=torch.float32)
+        ref = osp.draft_scalars(torch.tensor(t), torch.tensor(d))[0]
+        assert torch.equal(host, ref), (t, d)
