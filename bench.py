@@ -472,14 +472,26 @@ def run_action_chunk(args):
     text = torch.randn(B, cfg.context, 4096, generator=gen, device=dev).bfloat16()
     nm.prepare_context(text)
     # Cross K/V construction of a new context (text projection + every
-    # layer's K/V projection and RMS), timed apart from the chunk.
-    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    c0.record()
-    for _ in range(3):
-        nm.prepare_context(text)
-    c1.record()
-    torch.cuda.synchronize()
-    ctx_ms = c0.elapsed_time(c1) / 3
+    # layer's K/V projection and RMS), timed apart from the chunk: the 8
+    # rollouts' own contexts, and the per-chunk rebuild of one context.
+    D = cfg.dim
+
+    def time_prepare(t):
+        nm.prepare_context(t)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(3):
+            nm.prepare_context(t)
+        c1.record()
+        torch.cuda.synchronize()
+        ms_ = c0.elapsed_time(c1) / 3
+        rows = t.shape[0] * t.shape[1]
+        flops = 2.0 * rows * (4096 * D + D * D) + len(nm.stack.layers) * 2 * 2.0 * rows * D * D
+        return {"contexts": t.shape[0], "tokens": t.shape[1], "ms": ms_,
+                "tflops": flops / ms_ / 1e9, "gflop": flops / 1e9}
+    ctx_one = time_prepare(text[:1].contiguous())
+    ctx_all = time_prepare(text)
+    ctx_ms = ctx_all["ms"]
     f, h, w = cfg.action
     x = torch.randn(B, 30, f, h, w, generator=gen, device=dev).bfloat16()
     grid = configs.mesh_id(f, h, w, 0, f_shift=cfg.history_chunks, action=True)[None].to(dev)
@@ -523,7 +535,7 @@ def run_action_chunk(args):
                                    "layers) over a 3520-token KV history, 512 prepared text tokens",
                        "global_batch": B, "seq_len": 32, "kv_history": cfg.history_chunks * cfg.tokens,
                        "denoise_updates_per_chunk": steps, "ms_per_update": ms / steps,
-                       "context_prepare_ms": ctx_ms},
+                       "context_prepare_ms": ctx_ms, "context_prepare": [ctx_all, ctx_one]},
             "e2e": {"value": B * 1000.0 / ms_e2e, "unit": "action-chunks/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hout.numel() * 2},
             "gpu_launches": den.launches_per_chunk() * args.steps, "clocks": clk,

@@ -165,6 +165,28 @@ def test_whole_layer_prepared_context(cuda_device):
     assert "modulated1" in dbg and "gelu" in dbg
 
 
+@pytest.mark.parametrize("D,C,Bc", [(3072, 512, 1), (1536, 512, 2), (3072, 200, 3)])
+def test_cross_kv_construction(cuda_device, D, C, Bc):
+    """wamb_cross_kv (the prepared cross K/V: RMS(ctx W_k^T + b_k) * gamma_k
+    and ctx W_v^T + b_v, model.py:612-615) against the oracle module's own
+    to_k / norm_k / to_v in fp32: the per-chunk rebuild of one 512-token
+    context at D 3072, two contexts at D 1536, and a ragged token count."""
+    H = D // 128
+    blk = make_oracle_block(D, 256, H, seed=53)
+    ctx = torch.randn(Bc, C, D, generator=torch.Generator().manual_seed(53)).bfloat16().float()
+    at = blk.attn2
+    with torch.no_grad():
+        k_ref, v_ref = at.norm_k(at.to_k(ctx)), at.to_v(ctx)
+        g = to_device_block(blk)
+        k_bf, v_bf = g.attn2.norm_k(g.attn2.to_k(ctx.cuda().bfloat16())), g.attn2.to_v(ctx.cuda().bfloat16())
+        w = WholeLayerBlock(g)
+        w.prepare_context(ctx.cuda().bfloat16(), precompute=True)
+    k, v = w.context_kv
+    assert k.shape == (Bc, C, D) and v.shape == (Bc, C, D)
+    assert_parity(k, k_ref, k_bf)
+    assert_parity(v, v_ref, v_bf)
+
+
 def test_cfg0_single_block(cuda_device):
     """configs[0] shape (D 1536, 12 heads, FFN 8960, 1560 video + 32 action
     tokens, 512 context tokens) against the fp32 oracle."""

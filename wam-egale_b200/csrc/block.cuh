@@ -287,14 +287,19 @@ inline int cross_kv_impl(const wamb_block_args* a, void* k_out, void* v_out, cud
   const int D = a->dim;
   const int rows = a->context_batch * a->context_tokens;
   WAMB_REQUIRE(a->context && k_out && v_out, WAMB_ERR_ARG, "cross K/V needs context and outputs");
-  int rc;
+  WAMB_REQUIRE(aligned16(k_out) && aligned16(v_out), WAMB_ERR_ALIGN, "cross K/V alignment");
+  WAMB_REQUIRE(k_out != v_out, WAMB_ERR_ARG, "cross K and V outputs must differ");
+  // K and V projections as one launch of two weight groups, each group
+  // writing its own output (v_out - k_out elements apart).
   wamb_linear_args g{};
-  g.a = a->context; g.lda = D; g.m = rows; g.k = D; g.groups = 1; g.n_per_group = D;
+  g.a = a->context; g.lda = D; g.m = rows; g.k = D; g.groups = 2; g.n_per_group = D;
   g.ldo = D; g.epilogue = WAMB_EPI_BIAS;
-  g.weight[0] = a->weights[15]; g.bias[0] = a->weights[16]; g.out = k_out;
-  if ((rc = linear_impl(&g, s))) return rc;
-  g.weight[0] = a->weights[17]; g.bias[0] = a->weights[18]; g.out = v_out;
-  if ((rc = linear_impl(&g, s))) return rc;
+  g.weight[0] = a->weights[15]; g.bias[0] = a->weights[16];
+  g.weight[1] = a->weights[17]; g.bias[1] = a->weights[18];
+  g.out = k_out;
+  const long long gstride = static_cast<const bf*>(v_out) - static_cast<const bf*>(k_out);
+  int rc = linear_impl(&g, s, false, false, gstride);
+  if (rc) return rc;
   RmsParams r{};
   r.x = static_cast<bf*>(k_out); r.ld = D; r.M = rows; r.D = D; r.rows_per_batch = rows;
   r.sections = 1; r.gamma[0] = static_cast<const bf*>(a->weights[22]);

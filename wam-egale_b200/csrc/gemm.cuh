@@ -65,6 +65,10 @@ struct GemmParams {
   // (s + 1) * kb_per_split); the cluster reduces its partials through
   // shared memory (gemm_cluster_reduce). splits = 1: no split.
   int splits, kb_per_split;
+  // != 0: the columns of weight group g go to out + g * out_gstride
+  // (elements) at their local column, instead of column g * n_per_group of
+  // one [M, ldo] output (separate K and V outputs of one launch).
+  long long out_gstride;
 };
 
 constexpr int GEMM_BM = 128;
@@ -116,6 +120,7 @@ WAMB_DEV float silu(float x) {
 struct EpiRow {
   bool valid;
   int g, n_local0;
+  long long out_adj;                 // added to row * ldo + col (out_gstride)
   const __nv_bfloat16* bias;
   const float* wscale;
   float ascale;
@@ -129,6 +134,7 @@ WAMB_DEV EpiRow epi_row(const GemmParams& p, int row, int n0) {
   e.valid = row < p.M;
   e.g = n0 / p.n_per_group;
   e.n_local0 = n0 - e.g * p.n_per_group;
+  e.out_adj = p.out_gstride != 0 ? e.g * (p.out_gstride - p.n_per_group) : 0;
   e.bias = e.g == 0 ? p.bias[0] : (e.g == 1 ? p.bias[1] : p.bias[2]);
   e.wscale = e.g == 0 ? p.w_scale[0] : (e.g == 1 ? p.w_scale[1] : p.w_scale[2]);
   e.ascale = p.a_scale != nullptr && e.valid ? __ldg(p.a_scale + row) : 1.f;
@@ -241,11 +247,11 @@ WAMB_DEV void epi_apply(const GemmParams& p, const EpiRow& e, float (&v)[W], int
     }
   }
   if (p.out_f32) {
-    float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col + e.out_adj);
 #pragma unroll
     for (int j = 0; j < W / 4; ++j) op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   } else {
-    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col);
+    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col + e.out_adj);
 #pragma unroll
     for (int j = 0; j < W / 8; ++j) {
       uint4 w;
@@ -319,11 +325,13 @@ struct EpiOps8 {
   float4 tef[2];     // fp32 temb gate row, or
   uint4 teb;         // bf16 temb gate row
   uint4 res[2];      // raw residual words
+  long long out_adj; // EpiRow::out_adj
   bool has_bias;
 };
 
 WAMB_DEV void epi_load8(const GemmParams& p, const EpiRow& e, int row, int col, int lcol, EpiOps8& o) {
   o.has_bias = e.bias != nullptr;
+  o.out_adj = e.out_adj;
   if (o.has_bias) o.bias = __ldg(reinterpret_cast<const uint4*>(e.bias + lcol));
   o.ascale = e.ascale;
   if (p.a_scale != nullptr) {
@@ -404,7 +412,7 @@ WAMB_DEV void epi_finish8(const GemmParams& p, const EpiOps8& o, float (&v)[8], 
     }
   }
   if (p.out_f32) {
-    float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col);
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.ldo + col + o.out_adj);
     op[0] = make_float4(v[0], v[1], v[2], v[3]);
     op[1] = make_float4(v[4], v[5], v[6], v[7]);
   } else {
@@ -413,7 +421,7 @@ WAMB_DEV void epi_finish8(const GemmParams& p, const EpiOps8& o, float (&v)[8], 
     w.y = pack_bf16(v[2], v[3]);
     w.z = pack_bf16(v[4], v[5]);
     w.w = pack_bf16(v[6], v[7]);
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col) = w;
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row * p.ldo + col + o.out_adj) = w;
   }
 }
 

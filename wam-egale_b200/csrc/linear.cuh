@@ -187,8 +187,10 @@ inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms) {
 // w_early: the caller guarantees that the weights were last written two or
 // more kernels before this GEMM in the stream (GemmParams::w_early).
 // trigger: the next kernel is a GEMM with w_early (GemmParams::trigger).
+// out_gstride != 0: weight group g writes its n_per_group columns to
+// out + g * out_gstride elements (separate outputs of one launch, ldo each).
 inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_early = false,
-                       bool trigger = false) {
+                       bool trigger = false, long long out_gstride = 0) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
@@ -200,7 +202,8 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
                a->n_per_group);
   WAMB_REQUIRE(a->lda >= a->k && a->lda % (f8 ? 16 : 8) == 0, WAMB_ERR_ALIGN, "lda");
   const long long N = static_cast<long long>(a->groups) * a->n_per_group;
-  WAMB_REQUIRE(a->ldo >= N && a->ldo % 8 == 0, WAMB_ERR_ALIGN, "ldo");
+  WAMB_REQUIRE(a->ldo >= (out_gstride != 0 ? a->n_per_group : N) && a->ldo % 8 == 0, WAMB_ERR_ALIGN, "ldo");
+  WAMB_REQUIRE(out_gstride % 8 == 0, WAMB_ERR_ALIGN, "group output stride");
   WAMB_REQUIRE(a->out_is_f32 == 0 || a->out_is_f32 == 1, WAMB_ERR_ARG, "out_is_f32");
   WAMB_REQUIRE(a->res_is_f32 == 0 || a->res_is_f32 == 1, WAMB_ERR_ARG, "res_is_f32");
   WAMB_REQUIRE(a->a && a->out, WAMB_ERR_ARG, "null A/out");
@@ -274,6 +277,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   p.trigger = trigger ? 1 : 0;
   p.splits = tp.splits;
   p.kb_per_split = tp.kb_per_split;
+  p.out_gstride = out_gstride;
   auto launch = [&](auto f8c) {
     constexpr bool F8 = decltype(f8c)::value;
     if (pair) return launch_gemm2<F8>(ta, tb, p, di.sms, stream);

@@ -6,6 +6,7 @@ hundred MB on the device, 3 warm-up launches then `--launches` more).
   python wam-egale_b200/wam_ops/profile_cases.py rms | ln
   python wam-egale_b200/wam_ops/profile_cases.py small [--m 128] [--n 3072] [--k 14336]
   python wam-egale_b200/wam_ops/profile_cases.py verify_attention
+  python wam-egale_b200/wam_ops/profile_cases.py res_gate [--m 4096] [--launches 1]
 
 ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (cfg2 weights); --fp8: E4M3
            operands (quantized once before the timed launches)
@@ -15,6 +16,11 @@ ln         LayerNorm + adaLN modulation
 verify_attention  cfg3 self attention: 4 candidates x 32 queries sharing one
            3520-slot history row of a 4400-slot pool (grouped candidates) plus
            their own keys, 24 heads
+res_gate   the block's O projection: M x 3072 x 3072 GEMM with the gated fp32
+           residual epilogue (out fp32 = res + gate * (acc + bias)), per-row
+           modulation of 8 batch rows; prints its CUDA-event time next to the
+           same GEMM with an ungated residual, a bias epilogue with fp32
+           output and one with bf16 output
 small      small-M GEMM + residual epilogue (the verify batch's O / FFN-out
            projections; cluster split-K where the tiles leave SMs idle); 12
            weight copies rotate so every launch streams its weights from HBM
@@ -32,7 +38,7 @@ from wam_ops import _lib, configs, ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["ffn1", "attention", "rms", "ln", "small", "verify_attention"])
+    ap.add_argument("case", choices=["ffn1", "attention", "rms", "ln", "small", "verify_attention", "res_gate"])
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=14336)
@@ -67,6 +73,33 @@ def main():
         it = iter(range(1 << 30))
         run = lambda: ops.linear(x, ws[next(it) % 12], b, epilogue=_lib.EPI_RES, out=out,  # noqa: E731
                                  res=res)
+    elif a.case == "res_gate":
+        cfg = configs.PRESETS["cfg2"]
+        x = torch.randn(a.m, D, generator=g, device=dev).bfloat16()
+        w = (torch.randn(D, D, generator=g, device=dev) * 0.02).bfloat16()
+        b = torch.zeros(D, device=dev, dtype=torch.bfloat16)
+        res = torch.randn(a.m, D, generator=g, device=dev)
+        out = torch.empty(a.m, D, device=dev)
+        out_bf = torch.empty(a.m, D, device=dev, dtype=torch.bfloat16)
+        table = torch.randn(6, D, generator=g, device=dev) / D ** 0.5
+        temb = configs.make_temb(cfg, 8, dev, g)
+        gate = dict(table=table, temb=temb, rows_per_batch=a.m // 8, gate_index=2)
+        run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_RES_GATE, out=out, res=res, **gate)  # noqa: E731
+        variants = (("res_gate", run),
+                    ("res_f32", lambda: ops.linear(x, w, b, epilogue=_lib.EPI_RES, out=out, res=res)),
+                    ("bias_f32", lambda: ops.linear(x, w, b, out=out)),
+                    ("bias_bf16", lambda: ops.linear(x, w, b, out=out_bf)))
+        for name, f in variants:
+            for _ in range(3):
+                f()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / 20 * 1e3
+            print(f"{name}: {us:.1f} us, {2.0 * a.m * D * D / us / 1e6:.1f} TFLOP/s")
     elif a.case == "verify_attention":
         B, Q, pool, hist = 4, 32, 4400, 3520
         kp = torch.randn(2 * pool, D, generator=g, device=dev).bfloat16()

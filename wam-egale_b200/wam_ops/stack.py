@@ -13,7 +13,7 @@ CUDA graph that `replay()` launches with one call.
 import torch
 
 from . import _lib
-from .whole_layer import WholeLayerBlock
+from .whole_layer import WholeLayerBlock, prepared_context
 
 
 class NativeStack:
@@ -28,8 +28,10 @@ class NativeStack:
     def prepare_context(self, context):
         """Cross K/V of every layer for this context (outside timed regions)."""
         with torch.no_grad():
-            for layer in self.layers:
-                layer.prepare_context(context, precompute=True)
+            rows, roots, compact = prepared_context(context)
+            kv = torch.empty(len(self.layers), 2, *compact.shape, dtype=torch.bfloat16, device=compact.device)
+            for layer, kv_l in zip(self.layers, kv):
+                layer.set_context(rows, roots, compact, kv_l)
 
     def forward(self, hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache=0,
                 cache_name="pos", candidate_cache_rows=None, out=None, context_rows=None):

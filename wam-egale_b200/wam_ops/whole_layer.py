@@ -13,6 +13,39 @@ from . import _lib
 from .native import NativeBlock
 
 
+def context_groups(context):
+    """Byte-equal context rows share one prepared row (whole_layer.py:50-58):
+    (rows, roots) with rows[b] the group of batch row b and roots[g] the
+    first batch row of group g. One [B, B] equality matrix on the device and
+    one read-back, instead of one synchronising comparison per pair."""
+    B = context.shape[0]
+    if B == 1:
+        return [0], [0]
+    bits = context.detach().contiguous().view(torch.uint8).reshape(B, -1)
+    eq = torch.stack([(bits == bits[i]).all(dim=1) for i in range(B)]).cpu().tolist()
+    roots, rows = [], []
+    for row in range(B):
+        group = next((g for g, root in enumerate(roots) if eq[root][row]), None)
+        if group is None:
+            group = len(roots)
+            roots.append(row)
+        rows.append(group)
+    return rows, roots
+
+
+def prepared_context(context):
+    """(rows, roots, compact) for set_context: the groups of context_groups
+    as device tensors (None when all rows differ) and the distinct rows."""
+    B = context.shape[0]
+    rows, roots = context_groups(context)
+    if len(roots) == B:
+        return None, None, context.contiguous()
+    dev = context.device
+    roots_t = torch.tensor(roots, dtype=torch.int64, device=dev)
+    return (torch.tensor(rows, dtype=torch.int64, device=dev), roots_t,
+            context.index_select(0, roots_t).contiguous())
+
+
 class WholeLayerBlock:
     production_admitted = True
 
@@ -21,39 +54,39 @@ class WholeLayerBlock:
         self.native = NativeBlock(block, fp8=fp8)
         self.context_rows = self.context_roots = None
         self.context_kv = []
+        self._cross_args = None   # wamb_cross_kv arguments (weights fixed at construction)
 
     def prepare_context(self, context, precompute=False):
-        self.context_rows = self.context_roots = None
+        """Deduplicate the context rows and, with precompute=True, build the
+        cross K/V of the distinct rows (whole_layer.py:41-67)."""
+        rows, roots, compact = prepared_context(context)
+        self.set_context(rows, roots, compact if precompute else None)
+
+    def set_context(self, rows, roots, compact, kv=None):
+        """rows / roots: int64 device tensors of context_groups, or None when
+        every row is distinct; compact: the distinct context rows
+        [Bc, C, D] (None: no prepared cross K/V); kv: optional [2, Bc, C, D]
+        bf16 output buffer."""
+        self.context_rows, self.context_roots = rows, roots
         self.context_kv = []
-        B = context.shape[0]
-        bits = context.detach().contiguous().view(torch.uint8).reshape(B, -1)
-        roots, rows = [], []
-        for row in range(B):
-            group = next((g for g, root in enumerate(roots) if torch.equal(bits[row], bits[root])), None)
-            if group is None:
-                group = len(roots)
-                roots.append(row)
-            rows.append(group)
-        if len(roots) < B:
-            self.context_rows = torch.tensor(rows, dtype=torch.int64, device=context.device)
-            self.context_roots = torch.tensor(roots, dtype=torch.int64, device=context.device)
-        if precompute:
-            compact = context if self.context_roots is None else context.index_select(0, self.context_roots)
-            compact = compact.contiguous()
-            Bc, C, D = compact.shape
-            k = torch.empty(Bc, C, D, dtype=torch.bfloat16, device=context.device)
-            v = torch.empty_like(k)
-            a = _lib.BlockArgs()
+        if compact is None:
+            return
+        Bc, C, D = compact.shape
+        if kv is None:
+            kv = torch.empty(2, Bc, C, D, dtype=torch.bfloat16, device=compact.device)
+        a = self._cross_args
+        if a is None:
+            a = self._cross_args = _lib.BlockArgs()
             a.dim, a.heads = D, self.native.heads
             for i, w in enumerate(self.native.weights):
                 a.weights[i] = None if w is None else w.data_ptr()
             for i, e in enumerate(self.native.eps):
                 a.eps[i] = float(e)
-            a.context = compact.data_ptr()
-            a.context_batch, a.context_tokens = Bc, C
-            with torch.no_grad():
-                _lib.check(_lib.load().wamb_cross_kv(a, k.data_ptr(), v.data_ptr(), _lib.stream_ptr()))
-            self.context_kv = [k, v]
+        a.context = compact.data_ptr()
+        a.context_batch, a.context_tokens = Bc, C
+        with torch.no_grad():
+            _lib.check(_lib.load().wamb_cross_kv(a, kv[0].data_ptr(), kv[1].data_ptr(), _lib.stream_ptr()))
+        self.context_kv = [kv[0], kv[1]]
 
     def __call__(self, hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache=0,
                  cache_name="pos", candidate_cache_rows=None, debug=False, out_dtype=None, out=None,
