@@ -169,12 +169,10 @@ WAMB_DEV void epi_fetch_res(const GemmParams& p, int row, int col, uint4 (&r)[W 
 }
 
 // W consecutive accumulator values v of the row at output column `col`
-// (column `lcol` of the weight group) -> E4M3 scales, bias, GELU / SiLU /
-// residual / gate -> bf16 or fp32 stores. `res` holds the residual words
-// for the residual epilogues.
+// (column `lcol` of the weight group) -> E4M3 scales, bias, then GELU /
+// SiLU or the gate of EPI_RES_GATE: everything before the residual add.
 template <int W>
-WAMB_DEV void epi_apply(const GemmParams& p, const EpiRow& e, float (&v)[W], int row, int col, int lcol,
-                        const uint4 (&res)[W / 4]) {
+WAMB_DEV void epi_value(const GemmParams& p, const EpiRow& e, float (&v)[W], int col, int lcol) {
   if (p.a_scale != nullptr) {
     const float4* sp = reinterpret_cast<const float4*>(e.wscale + lcol);
 #pragma unroll
@@ -225,6 +223,17 @@ WAMB_DEV void epi_apply(const GemmParams& p, const EpiRow& e, float (&v)[W], int
         v[j + 3] *= tb.w + te.w;
       }
     }
+  }
+}
+
+// W consecutive accumulator values v of the row at output column `col`
+// (column `lcol` of the weight group): epi_value, then the residual of the
+// residual epilogues (raw words `res`), then bf16 or fp32 stores.
+template <int W>
+WAMB_DEV void epi_apply(const GemmParams& p, const EpiRow& e, float (&v)[W], int row, int col, int lcol,
+                        const uint4 (&res)[W / 4]) {
+  epi_value<W>(p, e, v, col, lcol);
+  if (p.epi == EPI_RES || p.epi == EPI_RES_GATE) {
     if (p.res_f32) {
 #pragma unroll
       for (int j = 0; j < W / 4; ++j) {
@@ -294,6 +303,130 @@ WAMB_DEV void gemm_epilogue_tile(const GemmParams& p, uint32_t taddr, int row, i
     if (!e.valid) continue;
     epi_chunk(p, e, v, row, n0, c, rcur);
   }
+}
+
+// Epilogue of one output tile through a per-warp staging buffer (32 rows x
+// 32 fp32, 4 KB, 16-byte groups XOR-swizzled by row so that both the
+// row-per-lane and the row-major accesses are free of bank conflicts), for
+// the residual and fp32-output epilogues: the residual reads and the output
+// stores become row-major warp accesses (4 rows x 128 contiguous bytes per
+// instruction) instead of 32 rows x 16 bytes. `row0` is the warp's first
+// row (lane l holds row row0 + l of the accumulator); residual words are
+// requested one chunk ahead and kept raw until they are staged.
+WAMB_DEV void sts4(uint32_t a, float4 x) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x.x), "f"(x.y), "f"(x.z), "f"(x.w)
+               : "memory");
+}
+WAMB_DEV float4 lds4(uint32_t a) {
+  float4 x;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w) : "r"(a)
+               : "memory");
+  return x;
+}
+
+// Four 32-column chunks [c0, c0 + 4) of one tile. The residual of chunks
+// c0 and c0 + 1 is requested before `wait_acc` (the wait for the
+// accumulator: the residual does not depend on it), and each later chunk's
+// two chunks ahead, so its DRAM latency overlaps the accumulator wait and
+// two chunks of work. Residual loads and output stores carry the streaming
+// cache hint (ld/st .cs: evict first), so the streamed rows do not push the
+// mainloop's A and weight tiles out of L2. Returns false if wait_acc gave up.
+template <class WaitAcc>
+WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int row0, int lane, int n0,
+                                        int c0, uint32_t st, WaitAcc&& wait_acc) {
+  const int row = row0 + lane;
+  const EpiRow e = epi_row(p, row, n0);
+  const bool has_res = p.epi == EPI_RES || p.epi == EPI_RES_GATE;
+  const int rs = lane >> 3, f = lane & 7;   // row-major role: rows i*4 + rs, 16-byte group f
+  // Staging byte offsets: row r, group g at r * 128 + ((g ^ (r & 7)) * 16).
+  // Row-major role: rows i*4 + rs have r & 7 = rs + 4 (i & 1).
+  const uint32_t rm_even = st + rs * 128 + ((f ^ rs) << 4);
+  const uint32_t rm_odd = st + rs * 128 + ((f ^ (rs + 4)) << 4);
+  const uint32_t own = st + lane * 128;
+  auto rm = [&](int i) { return ((i & 1) ? rm_odd : rm_even) + i * 512; };
+  auto own_at = [&](int j) { return own + ((j ^ (lane & 7)) << 4); };
+  uint4 ra[8], rb[8];
+  auto fetch = [&](int c, uint4 (&r8)[8]) {
+    const int col = n0 + c * 32 + f * 4;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = row0 + i * 4 + rs;
+      if (r >= p.M) {
+        r8[i] = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      if (p.res_f32) {
+        r8[i] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const float*>(p.res) + r * p.ldr + col));
+      } else {
+        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.res) + r * p.ldr + col));
+        r8[i].x = w.x;
+        r8[i].y = w.y;
+      }
+    }
+  };
+  if (has_res) {
+    fetch(c0, ra);
+    fetch(c0 + 1, rb);
+  }
+  if (!wait_acc()) return false;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int c = c0 + k;
+    uint4 (&rc)[8] = (k & 1) ? rb : ra;
+    if (has_res) {
+      // This chunk's residual into the staging buffer, then the request of
+      // the chunk two ahead into the freed registers.
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float4 x;
+        if (p.res_f32) {
+          x = make_float4(__uint_as_float(rc[i].x), __uint_as_float(rc[i].y), __uint_as_float(rc[i].z),
+                          __uint_as_float(rc[i].w));
+        } else {
+          const float2 a = unpack_bf16(rc[i].x), b = unpack_bf16(rc[i].y);
+          x = make_float4(a.x, a.y, b.x, b.y);
+        }
+        sts4(rm(i), x);
+      }
+      if (k + 2 < 4) fetch(c + 2, rc);
+    }
+    float v[32];
+    tmem_ld32(taddr + c * 32, v);
+    tmem_wait_ld();
+    if (e.valid) epi_value<32>(p, e, v, n0 + c * 32, e.n_local0 + c * 32);
+    if (has_res) {
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 x = lds4(own_at(j));
+        v[4 * j] += x.x;
+        v[4 * j + 1] += x.y;
+        v[4 * j + 2] += x.z;
+        v[4 * j + 3] += x.w;
+      }
+      __syncwarp();
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sts4(own_at(j), make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+    __syncwarp();
+    const long long col = n0 + c * 32 + f * 4 + e.out_adj;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = row0 + i * 4 + rs;
+      if (r >= p.M) continue;
+      const float4 x = lds4(rm(i));
+      if (p.out_f32) {
+        __stcs(reinterpret_cast<float4*>(static_cast<float*>(p.out) + r * p.ldo + col), x);
+      } else {
+        uint2 w;
+        w.x = pack_bf16(x.x, x.y);
+        w.y = pack_bf16(x.z, x.w);
+        __stcs(reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + r * p.ldo + col), w);
+      }
+    }
+    __syncwarp();
+  }
+  return true;
 }
 
 // Cluster split-K, step 1, for one warp slice (rows q*32.., chunks

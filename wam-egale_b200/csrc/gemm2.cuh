@@ -26,7 +26,10 @@ struct Gemm2Smem {
   static constexpr uint32_t B_BYTES = 128 * 128;  // this CTA's 128 of 256 weight rows
   static constexpr uint32_t BAR_OFF = GEMM2_STAGES * (A_BYTES + B_BYTES);
   static constexpr uint32_t NBARS = 2 * GEMM2_STAGES + 6;
-  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+  // Epilogue staging (gemm_epilogue_tile_staged): 4 KB per epilogue warp.
+  static constexpr uint32_t STAGE_OFF = (BAR_OFF + NBARS * 8 + 16 + 15) & ~15u;
+  static constexpr uint32_t TOTAL = 1024 + STAGE_OFF + GEMM_EPI_WARPS * 4096;
+  static_assert(TOTAL <= 232448, "2-CTA GEMM shared memory exceeds 227 KB");
 };
 
 WAMB_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
@@ -218,17 +221,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int half = (warp - 2) >> 2;  // columns [half * 128, half * 128 + 128)
     const int row_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
     const uint32_t tempty_leader0 = map_to_rank(tempty0, 0);
+    // Every tile's epilogue goes through the warp's staging buffer.
+    const uint32_t stage = smem_u32(smem + L::STAGE_OFF + (warp - 2) * 4096);
     int tc = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++tc) {
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
-      if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) break;
-      tc_fence_after();
       const int m_blk = t % num_m, n_blk = t / num_m;
       const int row = m_blk * 256 + row_in_tile;
       const int n0 = n_blk * 256;
-      gemm_epilogue_tile(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256, row, n0,
-                         half * 4, half * 4 + 4);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
+      const bool ok = gemm_epilogue_tile_staged(p, taddr, row - lane, lane, n0, half * 4, stage, [&]() {
+        if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) return false;
+        tc_fence_after();
+        return true;
+      });
+      if (!ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty_leader0 + 8 * acc);
