@@ -38,6 +38,10 @@ METRIC = "chunk_denoise_steps_per_s"
 UNIT = "chunk-steps/s"
 CHUNK_STEPS = 10  # FastWAM denoise updates per action chunk (real_speculative.py:33,107)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) of one FFN1 + GELU launch at the bench shape
+# (M 7040, N 14336, K 3072, bf16), from one ncu capture of the same kernel:
+# 212.1 MB read + 186.6 MB written (algorithmic: 333.3 MB).
+FFN1_TRAFFIC_BYTES = 398.7e6
 
 
 def peaks():
@@ -325,7 +329,9 @@ def run_native(args):
     roof = {"kernel": f"gemm_tc2_kernel<{'E4M3' if args.fp8 else 'bf16'}> (2-CTA 256x256 tiles) "
                       "FFN1+GELU (M 7040, N 14336, K 3072)",
             "bound": "tensor", "achieved": achieved, "peak": kpeak, "unit": "TFLOP/s",
-            "frac": achieved / kpeak, "traffic": None,
+            "frac": achieved / kpeak, "traffic": None if args.fp8 else FFN1_TRAFFIC_BYTES,
+            "traffic_source": None if args.fp8 else "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
+                              "launch of `profile_cases.py ffn1 --m 7040` (same kernel and shape)",
             "peak_source": f"{pk_kind} bf16 burst" + (" x 2 for E4M3" if args.fp8 else ""),
             "ms_per_launch": k_ms, "algorithmic_flops_per_launch": flops}
     gemm_flops, attn_flops = stack_flops(cfg, split=True)

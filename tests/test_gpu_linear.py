@@ -80,10 +80,12 @@ def test_linear_residual_gate(cuda_device, temb_len, temb_f32):
     _close(out2, res.float() + _ref(a, [w], [b]))
 
 
-@pytest.mark.parametrize("res_f32", [False, True])
-def test_linear_pair_epilogues(cuda_device, res_f32):
+@pytest.mark.parametrize("res_f32,per_token", [(False, False), (True, False), (True, True)])
+def test_linear_pair_epilogues(cuda_device, res_f32, per_token):
     """Two-CTA kernel (M 1300, N 4608): GELU, and the gated residual with a
-    bf16 or fp32 residual stream and fp32 output."""
+    bf16 or fp32 residual stream and fp32 output; the gate's modulation row
+    per batch row (650 rows each, so one warp straddles two batch rows) or
+    per token (bf16)."""
     g = torch.Generator(device="cuda").manual_seed(5)
     B, Q, D, K = 2, 650, 4608, 768
     a = torch.randn(B * Q, K, device="cuda", generator=g).bfloat16()
@@ -95,13 +97,15 @@ def test_linear_pair_epilogues(cuda_device, res_f32):
     if not res_f32:
         res = res.bfloat16()
     table = torch.randn(6, D, device="cuda", generator=g)
-    temb = torch.randn(B, 1, 6, D, device="cuda", generator=g)
+    temb = torch.randn(B, Q if per_token else 1, 6, D, device="cuda", generator=g)
+    if per_token:
+        temb = temb.bfloat16()
     out = torch.empty(B * Q, D, device="cuda", dtype=torch.float32)
     ops.linear(a, w, b, epilogue=_lib.EPI_RES_GATE, res=res, table=table, temb=temb,
                rows_per_batch=Q, gate_index=5, out=out)
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
-    gate = (table[5][None, None] + temb[:, :, 5]).expand(B, Q, D).reshape(B * Q, D)
+    gate = (table[5][None, None] + temb[:, :, 5].float()).expand(B, Q, D).reshape(B * Q, D)
     _close(out, res.float() + _ref(a, [w], [b]) * gate)
 
 
