@@ -88,11 +88,13 @@ struct LnParams {
   int trigger;            // 1: trigger the dependent grid early (a GEMM follows)
 };
 
-// Rows per CTA of ln_kernel for large M: several rows share one load of the
+// Rows per CTA of ln_kernel for large M: two rows share one load of the
 // modulation (or gamma / beta) vectors and one pair of barriers per
-// reduction. Small M (fewer CTAs than SMs at that count) runs one row per
-// CTA, with the modulation loads issued before the reductions.
-__host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 2 ? 4 : (vpt <= 4 ? 2 : 1); }
+// reduction (four rows measured slower at D 3072: 128 registers left two
+// CTAs per SM, too few to keep loads in flight through the reductions).
+// Small M (fewer CTAs than SMs at that count) runs one row per CTA, with the
+// modulation loads issued before the reductions.
+__host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 4 ? 2 : 1; }
 
 template <int VPT, int R>
 __global__ void ln_kernel(const LnParams p) {
