@@ -297,7 +297,10 @@ WAMB_API int wamb_block_forward_noalloc(const wamb_block_args* args, void* strea
  * 算子研究/wam_ops/optimized/whole_layer.py:41-67):
  *   k = RMSNorm(context W_k^T + b_k) * gamma_k,  v = context W_v^T + b_v.
  * weights/eps as in wamb_block_args (entries 15..18, 22 and eps[6] are read);
- * k_out, v_out: [context_batch * context_tokens, dim] bf16.
+ * k_out, v_out: [context_batch * context_tokens, dim] bf16, two distinct
+ * 16-byte aligned buffers. Two kernels: the K and V projections as one GEMM
+ * launch (two weight groups, each writing its own output), then the RMSNorm
+ * of K in place.
  */
 WAMB_API int wamb_cross_kv(const wamb_block_args* args, void* k_out, void* v_out, void* stream);
 
