@@ -110,6 +110,22 @@ def test_block_forward_rejects_bad_args(kw, code):
     assert lib.wamb_last_error()
 
 
+def test_cross_kv_rejects_bad_args():
+    """wamb_cross_kv checks its buffers on the host before any launch: a
+    missing context or output (1), K and V outputs that are one buffer (1,
+    its two-group launch would write both into it), unaligned outputs (3)."""
+    lib = _lib.load()
+    lib.wamb_cross_kv.argtypes = [ctypes.POINTER(_lib.BlockArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                  ctypes.c_void_p]
+    a = _args()
+    assert lib.wamb_cross_kv(a, 0x1000, 0x2000, None) == 1        # no context
+    a.context = 0x3000
+    assert lib.wamb_cross_kv(a, None, 0x2000, None) == 1
+    assert lib.wamb_cross_kv(a, 0x1000, 0x1000, None) == 1        # K and V in one buffer
+    assert lib.wamb_cross_kv(a, 0x1008, 0x2000, None) == 3        # K not 16-byte aligned
+    assert lib.wamb_last_error()
+
+
 def test_linear_rejects_bad_shapes():
     lib = _lib.load()
     a = _lib.LinearArgs()
