@@ -379,6 +379,9 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   // kernel keeps the implicit trigger, so writes of the kernels before the
   // block are complete before any GEMM of the block reads weights early.
   ln.trigger = cache && early(3 * D, D) ? 1 : 0;
+  // With a cache, LN1 runs beside the KV layout kernel (which triggers it
+  // after its own wait) and waits for it only before exiting.
+  ln.wait_late = cache ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }

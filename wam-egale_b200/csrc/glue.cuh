@@ -86,6 +86,7 @@ struct LnParams {
   int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
   int temb_rows;          // 0 or 6: the blocks' 6 modulation rows; 1: the output norm
   int trigger;            // 1: trigger the dependent grid early (a GEMM follows)
+  int wait_late;          // 1: griddepcontrol.wait at exit instead of entry (see ln_kernel)
 };
 
 // Rows per CTA of ln_kernel for large M: two rows share one load of the
@@ -97,9 +98,7 @@ struct LnParams {
 __host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 4 ? 2 : 1; }
 
 template <int VPT, int R>
-__global__ void ln_kernel(const LnParams p) {
-  if (p.trigger) pdl_trigger();
-  pdl_wait();
+WAMB_DEV void ln_body(const LnParams& p) {
   __shared__ float red[32 * R];
   const int row0 = blockIdx.x * R;
   const int nthr = blockDim.x;
@@ -255,6 +254,19 @@ __global__ void ln_kernel(const LnParams p) {
     }
   }
   emit();
+}
+
+// wait_late: the preceding kernel (the block's KV layout) triggers this
+// grid right after its own griddepcontrol.wait and this grid reads none of
+// its outputs, so the rows are normalised while it runs; the wait before
+// exit keeps "this grid complete" implying "every earlier grid complete"
+// for the kernels that follow.
+template <int VPT, int R>
+__global__ void ln_kernel(const LnParams p) {
+  if (p.trigger) pdl_trigger();
+  if (!p.wait_late) pdl_wait();
+  ln_body<VPT, R>(p);
+  if (p.wait_late) pdl_wait();
 }
 
 // --------------------------------------------------- row E4M3 quantization
@@ -480,6 +492,9 @@ WAMB_DEV uint32_t bytes_nonzero(uint32_t x) {
 
 __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams p) {
   pdl_wait();
+  // The block's LN1 (ln_kernel with wait_late) reads nothing written here:
+  // let it start on the other SMs now.
+  pdl_trigger();
   constexpr int SEG_MAX = KV_MAX_POOL / KV_THREADS;   // slots per thread at most
   __shared__ __align__(16) uint8_t m[KV_MAX_POOL];
   __shared__ int sh[33];
