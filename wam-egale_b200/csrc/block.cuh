@@ -379,9 +379,6 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   // kernel keeps the implicit trigger, so writes of the kernels before the
   // block are complete before any GEMM of the block reads weights early.
   ln.trigger = cache && early(3 * D, D) ? 1 : 0;
-  // With a cache, LN1 runs beside the KV layout kernel (which triggers it
-  // after its own wait) and waits for it only before exiting.
-  ln.wait_late = cache ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -507,7 +504,9 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   g.out_is_f32 = a->out_is_f32; g.table = table; g.temb = a->temb;
   g.temb_is_f32 = a->temb_is_f32; g.temb_len = a->temb_len; g.rows_per_batch = Q; g.gate_index = 5;
   g.dim = D;
-  return run_gemm(g);
+  // The block's last kernel: trigger the next grid after the wait, so that a
+  // following block's KV layout kernel runs beside this GEMM's last tiles.
+  return linear_impl(&g, s, true, false, 0, true);
 }
 
 }  // namespace wamb

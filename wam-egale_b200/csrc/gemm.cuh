@@ -68,7 +68,11 @@ struct GemmParams {
   // != 0: the columns of weight group g go to out + g * out_gstride
   // (elements) at their local column, instead of column g * n_per_group of
   // one [M, ldo] output (separate K and V outputs of one launch).
-  long long out_gstride;
+  long long out_gstride;  // 1: trigger the dependent grid right after griddepcontrol.wait (every
+  // earlier grid is then complete); the block's last GEMM sets it so that
+  // the next block's KV layout kernel, which waits only before exiting,
+  // overlaps this GEMM's last tiles.
+  int trigger_after;
 };
 
 constexpr int GEMM_BM = 128;
@@ -692,6 +696,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
   if (p.trigger) pdl_trigger();
   pdl_wait();   // inputs of the previous kernel are complete from here on
+  if (p.trigger_after) pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {

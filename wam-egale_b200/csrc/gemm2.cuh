@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();   // inputs of the previous kernel are complete from here on
+  if (p.trigger_after) pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {

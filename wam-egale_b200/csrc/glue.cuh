@@ -86,7 +86,6 @@ struct LnParams {
   int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
   int temb_rows;          // 0 or 6: the blocks' 6 modulation rows; 1: the output norm
   int trigger;            // 1: trigger the dependent grid early (a GEMM follows)
-  int wait_late;          // 1: griddepcontrol.wait at exit instead of entry (see ln_kernel)
 };
 
 // Rows per CTA of ln_kernel for large M: two rows share one load of the
@@ -98,7 +97,9 @@ struct LnParams {
 __host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 4 ? 2 : 1; }
 
 template <int VPT, int R>
-WAMB_DEV void ln_body(const LnParams& p) {
+__global__ void ln_kernel(const LnParams p) {
+  if (p.trigger) pdl_trigger();
+  pdl_wait();
   __shared__ float red[32 * R];
   const int row0 = blockIdx.x * R;
   const int nthr = blockDim.x;
@@ -254,19 +255,6 @@ WAMB_DEV void ln_body(const LnParams& p) {
     }
   }
   emit();
-}
-
-// wait_late: the preceding kernel (the block's KV layout) triggers this
-// grid right after its own griddepcontrol.wait and this grid reads none of
-// its outputs, so the rows are normalised while it runs; the wait before
-// exit keeps "this grid complete" implying "every earlier grid complete"
-// for the kernels that follow.
-template <int VPT, int R>
-__global__ void ln_kernel(const LnParams p) {
-  if (p.trigger) pdl_trigger();
-  if (!p.wait_late) pdl_wait();
-  ln_body<VPT, R>(p);
-  if (p.wait_late) pdl_wait();
 }
 
 // --------------------------------------------------- row E4M3 quantization
@@ -490,10 +478,15 @@ WAMB_DEV uint32_t bytes_nonzero(uint32_t x) {
   return x & 0x01010101u;
 }
 
+// The kernel reads only the cache metadata of its own layer and writes the
+// block's slot / tile scratch, whose readers (the previous block's RMS+RoPE
+// and attention) precede the previous block's last GEMM; that GEMM triggers
+// its dependents only after its own griddepcontrol.wait (trigger_after), so
+// this kernel starts without waiting and runs beside the GEMM's last tiles.
+// It waits before exiting, so its completion still implies every earlier
+// grid's (the next kernel, LN1, reads that GEMM's output); it triggers LN1
+// at once, so LN1's CTAs are resident and start as soon as it exits.
 __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams p) {
-  pdl_wait();
-  // The block's LN1 (ln_kernel with wait_late) reads nothing written here:
-  // let it start on the other SMs now.
   pdl_trigger();
   constexpr int SEG_MAX = KV_MAX_POOL / KV_THREADS;   // slots per thread at most
   __shared__ __align__(16) uint8_t m[KV_MAX_POOL];
@@ -637,6 +630,7 @@ __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams
   __syncthreads();
   if (!p.candidate)
     for (int i = threadIdx.x; i < p.pool; i += KV_THREADS) p.mask[i] = m[i];
+  pdl_wait();
 }
 
 }  // namespace wamb

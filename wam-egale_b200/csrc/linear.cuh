@@ -189,8 +189,9 @@ inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms) {
 // trigger: the next kernel is a GEMM with w_early (GemmParams::trigger).
 // out_gstride != 0: weight group g writes its n_per_group columns to
 // out + g * out_gstride elements (separate outputs of one launch, ldo each).
+// trigger_after: GemmParams::trigger_after.
 inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_early = false,
-                       bool trigger = false, long long out_gstride = 0) {
+                       bool trigger = false, long long out_gstride = 0, bool trigger_after = false) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
@@ -278,6 +279,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   p.splits = tp.splits;
   p.kb_per_split = tp.kb_per_split;
   p.out_gstride = out_gstride;
+  p.trigger_after = trigger_after ? 1 : 0;
   auto launch = [&](auto f8c) {
     constexpr bool F8 = decltype(f8c)::value;
     if (pair) return launch_gemm2<F8>(ta, tb, p, di.sms, stream);
