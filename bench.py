@@ -119,8 +119,11 @@ class Clocks:
 class CpuReference:
     """The reference algorithm on the host cores: the fp32 oracle restatement
     of the block (oracle/wan_block.py) for ONE cfg2 rollout (880 tokens
-    attending to a 3520-token history + itself, 512 context tokens). One
-    sample = `layers` layer forwards, scaled to a 30-layer step."""
+    attending to a 3520-token history + itself, 512 context tokens). A step
+    is a whole 30-layer denoise step of that rollout: the hidden states pass
+    through 30 block forwards (update_cache=0). One block's weights serve all
+    30 layers (same FLOPs and bytes per layer as 30 distinct blocks, without
+    11.7 GB of fp32 host weights)."""
 
     def __init__(self):
         from oracle import wan_block as ob
@@ -146,48 +149,56 @@ class CpuReference:
         self.args = (torch.randn(1, Q, D, generator=g), torch.randn(1, cfg.context, D, generator=g),
                      configs.make_temb(cfg, 1, "cpu", g), configs.chunk_rope(cfg))
 
-    def sample(self, layers=1):
-        """Seconds per layer over `layers` forwards (update_cache=0)."""
+    def step(self, layers=None):
+        """Seconds for `layers` (default all 30) chained block forwards."""
+        x, ctx, temb, rope = self.args
         with torch.no_grad():
             t0 = time.perf_counter()
-            for _ in range(layers):
-                self.blk(*self.args, update_cache=0)
-            return (time.perf_counter() - t0) / layers
+            for _ in range(self.cfg.layers if layers is None else layers):
+                x = self.blk(x, ctx, temb, rope, update_cache=0)
+            return time.perf_counter() - t0
 
-    def describe(self, layers):
-        return (f"{layers} layer forward(s) of one cfg2 rollout (880 tokens, 4400 visible keys, "
-                f"512 context, fp32) per sample, scaled x{self.cfg.layers} layers per step")
+    def describe(self):
+        return (f"one 30-layer denoise step of one cfg2 rollout per sample (880 tokens, 4400 visible "
+                f"keys, 512 context, fp32, {self.cfg.layers} chained block forwards)")
 
 
-def cpu_reference_rate(layers=2):
-    """(chunk-steps/s, threads, seconds per layer, sample text) of the CPU reference."""
+PER_ROLLOUT = ("per-rollout throughput: rollouts are independent and the CPU reference's cost is "
+               "linear in them, so chunk-steps/s of one rollout per step is the comparable unit")
+
+
+def cpu_reference_rate(samples=2):
+    """(chunk-steps/s, threads, seconds per step, sample text) of the CPU
+    reference: `samples` whole 30-layer steps after a one-layer warm-up."""
     ref = CpuReference()
-    ref.sample(1)                       # warm-up
-    dt = ref.sample(layers)
-    return 1.0 / (dt * ref.cfg.layers), torch.get_num_threads(), dt, ref.describe(layers)
+    ref.step(1)
+    dt = sum(ref.step() for _ in range(samples)) / samples
+    return 1.0 / dt, torch.get_num_threads(), dt, ref.describe() + f"; {samples} samples"
 
 
 def run_reference(args):
     """--impl reference: the reference's CPU path on the host (rank 0 only);
-    each step is one layer forward of one rollout, scaled to 30 layers."""
+    each timed step is a whole 30-layer step of one rollout, each warm-up
+    step one layer forward."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     n = args.gpus
     ref = CpuReference()
     for _ in range(args.warmup):
-        ref.sample(1)
+        ref.step(1)
     t0 = time.perf_counter()
-    per_layer = [ref.sample(1) for _ in range(args.steps)]
+    per_step = [ref.step() for _ in range(args.steps)]
     wall = time.perf_counter() - t0
-    step_s = sum(per_layer) / len(per_layer) * ref.cfg.layers
+    step_s = sum(per_step) / len(per_step)
     value = 1.0 / step_s
-    sample = ref.describe(1)
+    sample = ref.describe()
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * step_s,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, cfg2 shapes)",
-            "config": workload_config(n, 1) | {"sample_per_step": sample},
+            "config": workload_config(n, 1) | {"sample_per_step": sample, "unit_note": PER_ROLLOUT,
+                                               "warmup_step": "one layer forward"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
                              "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -197,9 +208,118 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------- GPU side
+def time_graph(run, steps, stream):
+    """ms per call of `run` over `steps` calls, CUDA events on `stream`."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def step_roofline(cfg, batch, ms, fp8=False):
+    """Algorithmic FLOPs of one step of `batch` rollouts against the measured
+    sustained bf16 peak (the E4M3 GEMMs at twice that rate in fp8 mode)."""
+    pk, pk_kind = peaks()
+    gemm_flops, attn_flops = stack_flops(cfg, split=True)
+    sus = pk["bf16_tflops_sustained"] * 1e12
+    tc = 2.0 if fp8 else 1.0
+    floor_s = batch * (gemm_flops / (sus * tc) + attn_flops / sus)
+    flops = (gemm_flops + attn_flops) * batch
+    return {"achieved": flops / (ms / 1000.0) / 1e12, "unit": "TFLOP/s",
+            "peak": pk["bf16_tflops_sustained"] * tc, "frac": floor_s / (ms / 1000.0),
+            "peak_source": f"{pk_kind} bf16 sustained" + (
+                "; frac = (GEMM FLOPs at 2x + attention FLOPs at 1x) / time" if fp8 else ""),
+            "algorithmic_flops_per_step": flops}
+
+
+class ActionGather:
+    """NCCL all_gather of every rollout's action rows after each step, off the
+    compute stream: the step's last kernel copies the rows into a two-slot
+    ring on the compute stream, a side stream runs the collective, and the
+    compute stream waits only before it rewrites a ring slot whose gather
+    (two steps back) may still be reading it. Ranks therefore do not step in
+    lockstep with the slowest one; `drain()` joins the side stream back."""
+
+    def __init__(self, out, action_tokens, world):
+        B, _, D = out.shape
+        self.out, self.A = out, action_tokens
+        self.src = [torch.empty(B, action_tokens, D, dtype=out.dtype, device=out.device) for _ in range(2)]
+        self.dst = [torch.empty(world * B, action_tokens, D, dtype=out.dtype, device=out.device)
+                    for _ in range(2)]
+        self.side = torch.cuda.Stream(device=out.device)
+        self.copied = [torch.cuda.Event() for _ in range(2)]
+        self.gathered = [None, None]
+        self.k = 0
+
+    def __call__(self):
+        import torch.distributed as dist
+        i = self.k % 2
+        cur = torch.cuda.current_stream()
+        if self.gathered[i] is not None:
+            cur.wait_event(self.gathered[i])
+        self.src[i].copy_(self.out[:, -self.A:])
+        self.copied[i].record(cur)
+        self.side.wait_event(self.copied[i])
+        with torch.cuda.stream(self.side):
+            dist.all_gather_into_tensor(self.dst[i], self.src[i])
+            ev = torch.cuda.Event()
+            ev.record(self.side)
+        self.gathered[i] = ev
+        self.k += 1
+
+    def drain(self):
+        torch.cuda.current_stream().wait_stream(self.side)
+
+
+def run_stack_config(name, dev, steps, warmup, fp8=False, seed=0):
+    """One graph-replayed 30-layer step of a 1-GPU config: cfg2 (batch 1,
+    880-token chunk over its 3520-token history) or cfg1 (batch 1, 1592
+    tokens of the D 1536 stack, no self-KV history); prepared cross K/V."""
+    from wam_ops import _lib, configs
+    from wam_ops.stack import NativeStack
+
+    cfg = configs.PRESETS[name]
+    B, Q, D = cfg.batch, cfg.tokens, cfg.dim
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    blocks = configs.build_blocks(cfg, dev, seed=seed)
+    if cfg.history_chunks:
+        configs.fill_history(blocks, cfg, dev, gen, pool_batch=B)
+    stack = NativeStack(blocks, fp8=fp8)
+    ctx = torch.randn(B, cfg.context, D, generator=gen, device=dev).bfloat16()
+    stack.prepare_context(ctx)
+    x = torch.randn(B, Q, D, generator=gen, device=dev).bfloat16()
+    temb = configs.make_temb(cfg, B, dev, gen)
+    rope = configs.chunk_rope(cfg, f_shift=cfg.history_chunks).to(dev)
+    stack.capture(x, ctx, temb, rope, warmup=1)
+    for _ in range(warmup):
+        stack.replay()
+    stream = torch.cuda.current_stream()
+    clocks = Clocks(dev.index)
+    clocks.start()
+    time.sleep(0.3)
+    ms = time_graph(stack.replay, steps, stream)
+    clk = clocks.stop()
+    code = _lib.device_status()
+    hist = cfg.history_chunks * Q
+    line = {"workload": f"{name}: 30-layer Wan-DiT denoise step, D{D} H{cfg.heads}x128 F{cfg.ffn}, batch {B}, "
+                        f"{Q} tokens" + (f" over a {hist}-token self-KV history" if hist else "")
+                        + f", {cfg.context}-token prepared cross-K/V",
+            "dtype": "fp8-e4m3 GEMMs, bf16 attention" if fp8 else "bf16",
+            "ms_per_step": ms, "steps_per_s": 1000.0 / ms,
+            "step_roofline": step_roofline(cfg, B, ms, fp8),
+            "gpu_launches": stack.launches_per_step(with_cache=bool(hist)) * steps,
+            "clocks": clk, "device_error": code}
+    del stack, blocks
+    torch.cuda.empty_cache()
+    return line
+
+
 def run_native(args):
     from wam_ops import _lib, configs, ops
-    from wam_ops.rollouts import gather_actions
     from wam_ops.stack import NativeStack
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -220,52 +340,58 @@ def run_native(args):
 
     blocks = configs.build_blocks(cfg, dev, seed=1234)
     configs.fill_history(blocks, cfg, dev, gen, pool_batch=B)
-    stack = NativeStack(blocks, fp8=args.fp8)
     ctx = torch.randn(B, cfg.context, D, generator=gen, device=dev).bfloat16()
-    stack.prepare_context(ctx)
     x = torch.randn(B, Q, D, generator=gen, device=dev).bfloat16()
     temb = configs.make_temb(cfg, B, dev, gen)
     rope = configs.chunk_rope(cfg).to(dev)
-    torch.cuda.synchronize()
-    if _lib.device_status() != 0:
-        raise RuntimeError("device error during setup")
-
-    static = stack.capture(x, ctx, temb, rope, warmup=1)
     A = 32  # action tokens per rollout
-
-    def step():
-        out = stack.replay()
-        if pg is not None:
-            gather_actions(out, A)  # NCCL all_gather of every rollout's action rows
-        return out
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if _lib.device_status() != 0:
-        raise RuntimeError("device error during warm-up")
-
-    clocks = Clocks(local)
     stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if pg is not None:
-        pg.barrier()
-    torch.cuda.synchronize()
-    clocks.start()
-    time.sleep(0.3)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    if pg is not None:
-        pg.barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev)
-    if pg is not None:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    ms = t.item()
+
+    def measure(fp8):
+        """(ms per step, clocks, stack, static buffers, step function)."""
+        stack = NativeStack(blocks, fp8=fp8)
+        stack.prepare_context(ctx)
+        torch.cuda.synchronize()
+        if _lib.device_status() != 0:
+            raise RuntimeError("device error during setup")
+        static = stack.capture(x, ctx, temb, rope, warmup=1)
+        gather = ActionGather(static["out"], A, world) if pg is not None else None
+
+        def step():
+            out = stack.replay()
+            if gather is not None:
+                gather()
+            return out
+
+        for _ in range(args.warmup):
+            step()
+        if gather is not None:
+            gather.drain()
+        torch.cuda.synchronize()
+        if _lib.device_status() != 0:
+            raise RuntimeError("device error during warm-up")
+        clocks = Clocks(local)
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+        clocks.start()
+        time.sleep(0.3)
+
+        def timed():
+            for _ in range(args.steps):
+                step()
+            if gather is not None:
+                gather.drain()
+        ms = time_graph(timed, 1, stream) / args.steps
+        clk = clocks.stop()
+        if pg is not None:
+            pg.barrier()
+        t = torch.tensor([ms], device=dev)
+        if pg is not None:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return t.item(), clk, stack, static, step, gather
+
+    ms, clk, stack, static, step, gather = measure(False)
     value = B * world / (ms / 1000.0)
     dev_code = _lib.device_status()
 
@@ -276,18 +402,21 @@ def run_native(args):
     for _ in range(2):
         stack.replay(hx.to(dev, non_blocking=True), ht.to(dev, non_blocking=True))
         hout.copy_(static["out"], non_blocking=True)
+    if gather is not None:
+        gather.drain()
     torch.cuda.synchronize()
     if pg is not None:
         pg.barrier()
-    e0.record(stream)
-    for _ in range(args.steps):
-        static["x"].copy_(hx, non_blocking=True)
-        static["temb"].copy_(ht, non_blocking=True)
-        step()
-        hout.copy_(static["out"], non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1) / args.steps
+
+    def e2e_steps():
+        for _ in range(args.steps):
+            static["x"].copy_(hx, non_blocking=True)
+            static["temb"].copy_(ht, non_blocking=True)
+            step()
+            hout.copy_(static["out"], non_blocking=True)
+        if gather is not None:
+            gather.drain()
+    ms_e2e = time_graph(e2e_steps, 1, stream) / args.steps
     t = torch.tensor([ms_e2e], device=dev)
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -295,6 +424,18 @@ def run_native(args):
     e2e = {"value": B * world / (ms_e2e / 1000.0), "unit": UNIT,
            "h2d_bytes_per_step": hx.numel() * 2 + ht.numel() * 4,
            "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": ms_e2e}
+    launches = stack.launches_per_step(with_cache=True) * args.steps
+    del stack, static, step, gather
+    torch.cuda.empty_cache()
+
+    # ---- the same workload with E4M3 GEMMs (configs[4]'s second run)
+    ms8, clk8, stack8, static8, step8, gather8 = measure(True)
+    fp8 = {"value": B * world / (ms8 / 1000.0), "unit": UNIT, "ms_per_step": ms8,
+           "dtype": "fp8-e4m3 GEMMs (per-channel weight / per-token activation scales), bf16 attention",
+           "step_roofline": step_roofline(cfg, B, ms8, fp8=True),
+           "gpu_launches": stack8.launches_per_step(with_cache=True) * args.steps, "clocks": clk8}
+    w8_first = stack8.layers[0].native.w8[23], stack8.layers[0].native.w8_scale[23]
+    del stack8, static8, step8, gather8
 
     # ---- roofline of the dominant kernel (FFN1 GEMM + GELU, M = 8 x 880)
     M, F = B * Q, cfg.ffn
@@ -302,72 +443,83 @@ def run_native(args):
     a = torch.randn(M, D, generator=gen, device=dev).bfloat16()
     w1, b1 = blk0.ffn.net[0].proj.weight, blk0.ffn.net[0].proj.bias
     act = torch.empty(M, F, dtype=torch.bfloat16, device=dev)
-    if args.fp8:
-        a8, sa = ops.quantize_rows(a)
-        w8, sw = stack.layers[0].native.w8[23], stack.layers[0].native.w8_scale[23]
-        run = lambda: ops.linear(a8, w8, b1, epilogue=_lib.EPI_GELU, out=act,  # noqa: E731
-                                 a_scale=sa, w_scales=sw)
-    else:
-        run = lambda: ops.linear(a, w1, b1, epilogue=_lib.EPI_GELU, out=act)  # noqa: E731
-    for _ in range(3):
-        run()
-    reps = 20
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(reps):
-        run()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    k_ms = e0.elapsed_time(e1) / reps
     pk, pk_kind = peaks()
     flops = 2.0 * M * F * D
+
+    def kernel_rate(run):
+        for _ in range(3):
+            run()
+        return time_graph(run, 20, stream)
+    k_ms = kernel_rate(lambda: ops.linear(a, w1, b1, epilogue=_lib.EPI_GELU, out=act))
     achieved = flops / (k_ms / 1000.0) / 1e12
-    # No fp8 GEMM peak is measured on this pool: the E4M3 tensor rate is
-    # twice the bf16 one on B200, so the fp8 denominator is 2x the bf16 burst.
-    tc_mult = 2.0 if args.fp8 else 1.0
-    kpeak = pk["bf16_tflops"] * tc_mult
-    roof = {"kernel": f"gemm_tc2_kernel<{'E4M3' if args.fp8 else 'bf16'}> (2-CTA 256x256 tiles) "
-                      "FFN1+GELU (M 7040, N 14336, K 3072)",
+    kpeak = pk["bf16_tflops"]
+    roof = {"kernel": "gemm_tc2_kernel<bf16> (2-CTA 256x256 tiles) FFN1+GELU (M 7040, N 14336, K 3072)",
             "bound": "tensor", "achieved": achieved, "peak": kpeak, "unit": "TFLOP/s",
-            "frac": achieved / kpeak, "traffic": None if args.fp8 else FFN1_TRAFFIC_BYTES,
-            "traffic_source": None if args.fp8 else "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
-                              "launch of `profile_cases.py ffn1 --m 7040` (same kernel and shape)",
-            "peak_source": f"{pk_kind} bf16 burst" + (" x 2 for E4M3" if args.fp8 else ""),
-            "ms_per_launch": k_ms, "algorithmic_flops_per_launch": flops}
-    gemm_flops, attn_flops = stack_flops(cfg, split=True)
-    step_flops = (gemm_flops + attn_flops) * B
-    sus = pk["bf16_tflops_sustained"] * 1e12
-    floor_s = B * (gemm_flops / (sus * tc_mult) + attn_flops / sus)
-    step_roof = {"achieved": step_flops / (ms / 1000.0) / 1e12, "unit": "TFLOP/s",
-                 "peak": pk["bf16_tflops_sustained"] * (tc_mult if args.fp8 else 1.0),
-                 "frac": floor_s / (ms / 1000.0),
-                 "peak_source": f"{pk_kind} bf16 sustained" + (
-                     "; frac = (GEMM FLOPs at 2x + attention FLOPs at 1x) / time" if args.fp8 else ""),
-                 "algorithmic_flops_per_step": step_flops}
+            "frac": achieved / kpeak, "traffic": FFN1_TRAFFIC_BYTES,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of "
+                              "`bench.py --workload kernel --case ffn1 --m 7040` (same kernel and shape)",
+            "peak_source": f"{pk_kind} bf16 burst", "ms_per_launch": k_ms,
+            "algorithmic_flops_per_launch": flops}
+    a8, sa = ops.quantize_rows(a)
+    k8_ms = kernel_rate(lambda: ops.linear(a8, w8_first[0], b1, epilogue=_lib.EPI_GELU, out=act, a_scale=sa,
+                                           w_scales=w8_first[1]))
+    # No fp8 GEMM peak is measured on this pool: the E4M3 tensor rate is
+    # twice the bf16 one on B200, so its denominator is 2x the bf16 burst.
+    fp8["roofline"] = {"kernel": "gemm_tc2_kernel<E4M3> FFN1+GELU (M 7040, N 14336, K 3072)", "bound": "tensor",
+                       "achieved": flops / (k8_ms / 1000.0) / 1e12, "peak": 2 * kpeak, "unit": "TFLOP/s",
+                       "frac": flops / (k8_ms / 1000.0) / 1e12 / (2 * kpeak),
+                       "peak_source": f"{pk_kind} bf16 burst x 2 for E4M3", "ms_per_launch": k8_ms}
+    del w8_first, a8, sa, act, a
 
     line = None
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None,
-                "dtype": ("fp8-e4m3 GEMMs (per-channel weight / per-token activation scales), "
-                          "bf16 attention" if args.fp8 else "bf16"),
+                "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded weights N(0,0.02), "
                 "zero biases, N(0,1) hidden/context, random unit-scale KV history)",
                 "config": workload_config(world, B) | {"action_chunks_per_s": value / CHUNK_STEPS},
-                "roofline": roof, "step_roofline": step_roof, "e2e": e2e,
-                "gpu_launches": stack.launches_per_step(with_cache=True) * args.steps,
-                "clocks": clk, "device_error": dev_code}
+                "roofline": roof, "step_roofline": step_roofline(cfg, B, ms), "e2e": e2e,
+                "fp8": fp8, "gpu_launches": launches, "clocks": clk, "device_error": dev_code}
+    del blocks
+    torch.cuda.empty_cache()
     if pg is not None:
-        del static, stack
         pg.barrier()
         pg.destroy_process_group()
     if rank == 0:
+        if world == 1:
+            # The configs the north-star target is quoted on, timed on the same GPU.
+            line["configs"] = {n: run_stack_config(n, dev, args.steps, args.warmup, seed=7 + i)
+                               for i, n in enumerate(("cfg2", "cfg1"))}
         if world == 1 and not args.no_cpu_baseline:
             v, th, dt, sample = cpu_reference_rate()
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": th, "kind": "port",
-                                    "sample": sample}
+                                    "sample": sample, "unit_note": PER_ROLLOUT}
         print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_config(args):
+    """--workload cfg2 / cfg1: the 1-GPU config's step as its own line."""
+    from wam_ops import configs
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    torch.set_grad_enabled(False)
+    r = run_stack_config(args.workload, dev, args.steps, args.warmup, fp8=args.fp8, seed=7)
+    cfg = configs.PRESETS[args.workload]
+    line = {"metric": "denoise_steps_per_s", "value": r["steps_per_s"], "unit": "denoise-steps/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": r["dtype"],
+            "data": "synthetic (seeded weights N(0,0.02), zero biases, N(0,1) hidden/context"
+                    + (", random unit-scale KV history)" if cfg.history_chunks else ")"),
+            "config": {"workload": r["workload"], "global_batch": cfg.batch, "seq_len": cfg.tokens,
+                       "kv_history": cfg.history_chunks * cfg.tokens, "context": cfg.context,
+                       "l2": "inputs larger than L2 (weights streamed every step)"},
+            "step_roofline": r["step_roofline"], "roofline": dict(r["step_roofline"], bound="tensor",
+                                                                  kernel="whole step"),
+            "gpu_launches": r["gpu_launches"], "clocks": r["clocks"], "device_error": r["device_error"]}
+    print(json.dumps(line), flush=True)
     return 0
 
 
@@ -681,6 +833,126 @@ def run_spec_chunk(args):
     return 0
 
 
+def run_kernel_case(args):
+    """--workload kernel --case NAME: one kernel (or one block) at a fixed
+    shape, 3 warm-up launches then --launches more, for ncu captures (inputs
+    larger than L2, a few hundred MB to a few GB on the device). Prints one
+    status line; no timing is reported (use the workloads above for that).
+
+    ffn1       FFN1 GEMM + GELU epilogue, M x 14336 x 3072 (--m, cfg2 weights);
+               --fp8: E4M3 operands (quantized once before the launches)
+    small      small-M GEMM + residual epilogue (the verify batch's O / FFN-out
+               projections, --m/--n/--k); 12 weight copies rotate so every
+               launch streams its weights from HBM
+    res_gate   the O projection (M x 3072 x 3072, gated fp32 residual) beside
+               the same GEMM with an ungated residual and bias-only epilogues;
+               prints each one's CUDA-event time
+    attention  self attention of --batch cfg2 rollouts of --q queries over
+               --pool keys (24 heads)
+    verify_attention  cfg3 self attention: 4 candidates x 32 queries sharing
+               one 3520-slot history row plus their own keys (24 heads)
+    quant      row quantization to E4M3 of an --m x --k bf16 matrix
+    block      one cfg2-shape block (no cache) of --batch x --q rows: its
+               LayerNorm and RMS+RoPE launches are the memory-bound kernels
+               to capture (ncu -k regex:ln_kernel / rms_rope_kernel)
+    """
+    from wam_ops import _lib, configs, ops
+
+    torch.set_grad_enabled(False)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    D, H, F = 3072, 24, 14336
+    a = args
+    if a.case == "ffn1":
+        x = torch.randn(a.m, D, generator=g, device=dev).bfloat16()
+        w = (torch.randn(F, D, generator=g, device=dev) * 0.02).bfloat16()
+        b = torch.zeros(F, device=dev, dtype=torch.bfloat16)
+        out = torch.empty(a.m, F, device=dev, dtype=torch.bfloat16)
+        if a.fp8:
+            x8, sx = ops.quantize_rows(x)
+            w8, sw = ops.quantize_rows(w)
+            run = lambda: ops.linear(x8, w8, b, epilogue=_lib.EPI_GELU, out=out,  # noqa: E731
+                                     a_scale=sx, w_scales=sw)
+        else:
+            run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_GELU, out=out)  # noqa: E731
+    elif a.case == "small":
+        x = torch.randn(a.m, a.k, generator=g, device=dev).bfloat16()
+        ws = [(torch.randn(a.n, a.k, generator=g, device=dev) * 0.02).bfloat16() for _ in range(12)]
+        b = torch.zeros(a.n, device=dev, dtype=torch.bfloat16)
+        res = torch.randn(a.m, a.n, generator=g, device=dev).bfloat16()
+        out = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
+        it = iter(range(1 << 30))
+        run = lambda: ops.linear(x, ws[next(it) % 12], b, epilogue=_lib.EPI_RES, out=out,  # noqa: E731
+                                 res=res)
+    elif a.case == "res_gate":
+        cfg = configs.PRESETS["cfg2"]
+        x = torch.randn(a.m, D, generator=g, device=dev).bfloat16()
+        w = (torch.randn(D, D, generator=g, device=dev) * 0.02).bfloat16()
+        b = torch.zeros(D, device=dev, dtype=torch.bfloat16)
+        res = torch.randn(a.m, D, generator=g, device=dev)
+        out = torch.empty(a.m, D, device=dev)
+        out_bf = torch.empty(a.m, D, device=dev, dtype=torch.bfloat16)
+        table = torch.randn(6, D, generator=g, device=dev) / D ** 0.5
+        temb = configs.make_temb(cfg, 8, dev, g)
+        gate = dict(table=table, temb=temb, rows_per_batch=a.m // 8, gate_index=2)
+        run = lambda: ops.linear(x, w, b, epilogue=_lib.EPI_RES_GATE, out=out, res=res, **gate)  # noqa: E731
+        variants = (("res_gate", run),
+                    ("res_f32", lambda: ops.linear(x, w, b, epilogue=_lib.EPI_RES, out=out, res=res)),
+                    ("bias_f32", lambda: ops.linear(x, w, b, out=out)),
+                    ("bias_bf16", lambda: ops.linear(x, w, b, out=out_bf)))
+        for name, f in variants:
+            for _ in range(3):
+                f()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / 20 * 1e3
+            print(f"{name}: {us:.1f} us, {2.0 * a.m * D * D / us / 1e6:.1f} TFLOP/s")
+    elif a.case == "verify_attention":
+        B, Q, pool, hist = 4, 32, 4400, 3520
+        kp = torch.randn(2 * pool, D, generator=g, device=dev).bfloat16()
+        vp = torch.randn(2 * pool, D, generator=g, device=dev).bfloat16()
+        qkv = torch.randn(B * Q, 3 * D, generator=g, device=dev).bfloat16()
+        tl = [(s0, min(128, hist - s0)) for s0 in range(0, hist, 128)]
+        tiles = torch.tensor(tl, dtype=torch.int32, device=dev).view(-1, 2)
+        n = torch.tensor([len(tl)], dtype=torch.int32, device=dev)
+        rows = torch.zeros(B, dtype=torch.int64, device=dev)
+        out = torch.empty(B * Q, D, device=dev, dtype=torch.bfloat16)
+        run = lambda: ops.attention(qkv, kp, vp, heads=H, q_rows=Q, src0_batch_stride=pool,  # noqa: E731
+                                    tiles=tiles, n_tiles=n, src0_map=rows, k1=qkv, v1=qkv, k1_col=D,
+                                    v1_col=2 * D, out=out)
+    elif a.case == "attention":
+        q = torch.randn(a.batch * a.q, D, generator=g, device=dev).bfloat16()
+        kp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
+        vp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
+        out = torch.empty(a.batch * a.q, D, device=dev, dtype=torch.bfloat16)
+        run = lambda: ops.attention(q, kp, vp, heads=H, q_rows=a.q, src0_batch_stride=a.pool,  # noqa: E731
+                                    src0_len=a.pool, out=out)
+    elif a.case == "quant":
+        x = torch.randn(a.m, a.k, generator=g, device=dev).bfloat16()
+        run = lambda: ops.quantize_rows(x)  # noqa: E731
+    else:
+        cfg = configs.PRESETS["cfg2"]
+        blk = configs.build_blocks(configs.Config("p", D, H, F, 1, 1, (1, 16, 53), (8, 4, 1), 8), dev)[0]
+        from wam_ops.native import NativeBlock
+        nb = NativeBlock(blk, fp8=a.fp8)
+        x = torch.randn(a.batch, a.q, D, generator=g, device=dev).bfloat16()
+        ctx = torch.randn(1, 8, D, generator=g, device=dev).bfloat16()
+        temb = configs.make_temb(cfg, a.batch, dev, g)
+        rope = configs.rope_freqs(torch.zeros(3, a.q)).to(dev)
+        run = lambda: nb(x, ctx, temb, rope)  # noqa: E731
+    for _ in range(3 + a.launches):
+        run()
+    torch.cuda.synchronize()
+    code = _lib.device_status()
+    print(f"{a.case}: ok, device status {code}")
+    return 0 if code == 0 else 1
+
+
 def stack_flops(cfg, split=False):
     """Algorithmic FLOPs of one 30-layer step for ONE rollout: the six
     projections, the two FFN GEMMs and the QK^T / PV products of both
@@ -705,7 +977,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 GEMMs (the FP8 weight path); default is the bf16 drop-in")
-    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg3", "action_chunk", "spec_chunk"],
+    ap.add_argument("--case", default="ffn1",
+                    choices=["ffn1", "small", "res_gate", "attention", "verify_attention", "quant", "block"],
+                    help="--workload kernel: which single-kernel case to launch (for ncu captures)")
+    ap.add_argument("--m", type=int, default=2048)
+    ap.add_argument("--n", type=int, default=3072)
+    ap.add_argument("--k", type=int, default=14336)
+    ap.add_argument("--q", type=int, default=880)
+    ap.add_argument("--pool", type=int, default=4400)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--launches", type=int, default=1)
+    ap.add_argument("--workload", default="cfg4",
+                    choices=["cfg4", "cfg3", "cfg2", "cfg1", "action_chunk", "spec_chunk", "kernel"],
                     help="cfg4 (default, the headline): 8 cfg2 rollouts per GPU; cfg3: the "
                          "4 x 32-token candidate verify step on one GPU; action_chunk: 10 whole-model "
                          "denoise updates of an action chunk; spec_chunk: the same chunk for one rollout "
@@ -721,6 +1004,10 @@ def main():
         return run_action_chunk(args)
     if args.workload == "spec_chunk":
         return run_spec_chunk(args)
+    if args.workload == "kernel":
+        return run_kernel_case(args)
+    if args.workload in ("cfg2", "cfg1"):
+        return run_config(args)
     return run_native(args)
 
 

@@ -238,6 +238,15 @@ typedef struct wamb_block_args {
   int32_t fp8;
   const void* w8[27];
   const float* w8_scale[27];
+  /* chained = 1 declares that the work just before this call on `stream` is
+   * a wamb_block_forward (or _noalloc) call with the same batch, tokens,
+   * dims, context shape, cache presence and fp8 mode, i.e. the previous
+   * layer of a stack: the KV bookkeeping kernel (cache only) then starts
+   * beside that call's last GEMM instead of after it. chained = 0 (the
+   * default) makes it wait for all earlier work on the stream first, which
+   * is required when that work may have written this layer's cache
+   * metadata or used a workspace of another layout. */
+  int32_t chained;
 } wamb_block_args;
 
 /* Named intermediates kept in the workspace (byte offsets; -1 = absent). */
@@ -270,11 +279,11 @@ WAMB_API int wamb_block_forward(const wamb_block_args* args, void* stream);
 /*
  * wamb_block_forward without a caller-provided workspace. This entry point
  * has no counterpart in the reference. It is for callers that cannot
- * allocate device memory at the point where they run the block: work being
- * recorded into a CUDA graph (a cudaMalloc during stream capture is an error
- * that invalidates the capture), serving loops that must not hit the device
- * allocator (cudaMalloc can synchronise the device), and hosts that reach
- * the library through a thin FFI and have no device allocator of their own.
+ * allocate device memory where they run the block: serving loops that keep
+ * cudaMalloc / cudaFree off their path (both can synchronise the device and
+ * stall every stream), and hosts that reach the library through a thin FFI
+ * (ctypes, cgo, JNI) and own no device allocator with which to provide a
+ * workspace.
  *
  * The scratch is a fixed array of WAMB_NOALLOC_SCRATCH_BYTES in device
  * memory, defined once in the library; every GPU that loads libwamb.so holds
@@ -282,10 +291,14 @@ WAMB_API int wamb_block_forward(const wamb_block_args* args, void* stream);
  * (wamb_block_workspace_bytes) exceeds it returns WAMB_ERR_WORKSPACE and
  * launches nothing. args->workspace and args->workspace_bytes are ignored;
  * everything else is as for wamb_block_forward. The first call on a device
- * looks up the array's device address (make it before any stream capture on
- * that device). All calls share the one array and it keeps the last call's
- * contents (nothing in it needs to start at zero): calls that can overlap on
- * the GPU, e.g. on two streams without ordering, race on it.
+ * looks up the array's device address with cudaGetSymbolAddress and keeps
+ * it for the life of the process: make that first call before any stream
+ * capture on the device, and do not use the library across a
+ * cudaDeviceReset of it (the kept address would be stale). All calls share
+ * the one array and it keeps the last call's contents (nothing in it needs
+ * to start at zero): calls that can overlap on the GPU, e.g. on two streams
+ * without ordering, race on it; calls ordered on one stream do not, as long
+ * as `chained` is set only as its comment states.
  * Allocates nothing: no cudaMalloc, no cudaFree.
  */
 #define WAMB_NOALLOC_SCRATCH_BYTES (32u << 20)

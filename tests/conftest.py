@@ -28,3 +28,17 @@ def cuda_device():
     if (major, minor) != (10, 0):
         pytest.fail(f"gpu tests need sm_100 (B200); got sm_{major}{minor}")
     return torch.device("cuda", 0)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """Write the parity results the tests recorded (blockutil.RESULTS) to
+    the JSON file named by WAMB_PARITY_OUT, if set."""
+    import json
+    import os
+    path = os.environ.get("WAMB_PARITY_OUT")
+    if not path:
+        return
+    mod = sys.modules.get("blockutil")
+    rows = list(getattr(mod, "RESULTS", []))
+    Path(path).parent.mkdir(parents=True, exist_ok=True)
+    Path(path).write_text(json.dumps(rows, indent=1) + "\n")

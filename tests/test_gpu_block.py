@@ -4,19 +4,20 @@ WanTransformerBlock.forward (model.py:741-794), including the KV-cache
 lifecycle (update_cache 0/1/2, id eviction), candidate verification and the
 prepared cross-K/V variant.
 
-Tolerance (see blockutil.py): cosine >= 0.9999 and
-max |err| <= max(2e-2, E_ref) against the fp32 oracle on identical
-bf16-representable weights and inputs, E_ref being the error of the reference
-block itself run in bf16 on the GPU on the same inputs. Checked for the bf16
-drop-in output and for the block's fp32 output mode. Cache metadata (id,
-mask, is_pred) must match exactly.
+Tolerance (tests/blockutil.py): cosine >= 0.9999 and
+|err| <= 2e-2 against the fp32 oracle on identical bf16-representable
+weights and inputs, plus half a bf16 ulp of the value for outputs stored in
+bf16 (the drop-in output, pool K/V rows, cross K/V). The block's fp32 output
+mode gets no allowance. Cache metadata (id, mask, is_pred) must match
+exactly. The small cases use a stress modulation (temb ~ 0.5 N(0,1): scales
+and gates up to +-2); configs[0] uses its own temb chain.
 """
 import pytest
 import torch
 
 from blockutil import (assert_parity, make_inputs, make_oracle_block, reference_bf16, stats,
                        to_device_block)
-from wam_ops import _lib
+from wam_ops import _lib, configs
 from wam_ops.install import install_block, install_model
 from wam_ops.whole_layer import WholeLayerBlock
 
@@ -53,10 +54,11 @@ def test_block_no_cache(cuda_device, B, Q, C, temb_len, temb_dtype, rope, norm2)
         ref = blk(x, ctx, temb, r)
     g = to_device_block(blk)
     rb = reference_bf16(to_device_block(blk), x, ctx, temb.to(temb_dtype).float(), r)
-    assert_parity(_run_native(g, x, ctx, temb, r, temb_dtype), ref, rb)
+    tag = f"block D256 B{B} Q{Q} C{C} temb_len {temb_len}"
+    assert_parity(_run_native(g, x, ctx, temb, r, temb_dtype), ref, rb, name=tag + " fp32-out")
     out = _run_native(g, x, ctx, temb, r, temb_dtype, out_dtype=torch.bfloat16)
     assert out.dtype == torch.bfloat16
-    assert_parity(out, ref, rb)
+    assert_parity(out, ref, rb, name=tag + " bf16-out")
 
 
 def test_block_context_broadcast(cuda_device):
@@ -66,7 +68,7 @@ def test_block_context_broadcast(cuda_device):
     with torch.no_grad():
         ref = blk(x, ctx.expand(B, -1, -1), temb, r)
     rb = reference_bf16(to_device_block(blk), x, ctx.expand(B, -1, -1), temb, r)
-    assert_parity(_run_native(to_device_block(blk), x, ctx, temb, r), ref, rb)
+    assert_parity(_run_native(to_device_block(blk), x, ctx, temb, r), ref, rb, name="block context broadcast")
 
 
 def _cache_equal(oc, gc, tc):
@@ -97,7 +99,7 @@ def test_block_kv_lifecycle_and_eviction(cuda_device):
             ref = blk(x, ctx, temb, r, update_cache=update)
         rb = reference_bf16(tb, x, ctx, temb, r, update_cache=update)
         out = _run_native(g, x, ctx, temb, r, update_cache=update)
-        assert_parity(out, ref, rb)
+        assert_parity(out, ref, rb, name=f"block KV lifecycle call {step} update {update}")
         _cache_equal(blk.attn1.attn_caches["pos"], g.attn1.attn_caches["pos"], tb.attn1.attn_caches["pos"])
 
 
@@ -129,7 +131,7 @@ def test_block_candidate_verification(cuda_device, rows, Q):
         ref = blk(x, ctx, temb, r, candidate_cache_rows=rows)
     rb = reference_bf16(tb, x, ctx, temb, r, candidate_cache_rows=rows.cuda())
     out = _run_native(g, x, ctx, temb, r, candidate_cache_rows=rows.cuda())
-    assert_parity(out, ref, rb)
+    assert_parity(out, ref, rb, name=f"block candidates rows {rows} Q{Q}")
     for k, v in g.attn1.attn_caches["pos"].items():
         # bitwise (an uninitialised pool may hold NaN patterns)
         assert torch.equal(v.view(torch.uint8), before[k].view(torch.uint8)), f"candidate path wrote the cache ({k})"
@@ -160,7 +162,7 @@ def test_whole_layer_prepared_context(cuda_device):
         assert w.context_roots is not None and w.context_roots.numel() == 2
         out = w(x.cuda().bfloat16(), ctx.cuda().bfloat16(), temb.cuda(), r.cuda())
         dbg = w(x.cuda().bfloat16(), ctx.cuda().bfloat16(), temb.cuda(), r.cuda(), debug=True)
-    assert_parity(out, ref, rb)
+    assert_parity(out, ref, rb, name="whole layer prepared context")
     assert torch.equal(dbg["output"], out)
     assert "modulated1" in dbg and "gelu" in dbg
 
@@ -183,13 +185,47 @@ def test_cross_kv_construction(cuda_device, D, C, Bc):
         w.prepare_context(ctx.cuda().bfloat16(), precompute=True)
     k, v = w.context_kv
     assert k.shape == (Bc, C, D) and v.shape == (Bc, C, D)
-    assert_parity(k, k_ref, k_bf)
-    assert_parity(v, v_ref, v_bf)
+    assert_parity(k, k_ref, k_bf, name=f"cross K D{D} C{C} Bc{Bc}")
+    assert_parity(v, v_ref, v_bf, name=f"cross V D{D} C{C} Bc{Bc}")
 
 
 def test_cfg0_single_block(cuda_device):
-    """configs[0] shape (D 1536, 12 heads, FFN 8960, 1560 video + 32 action
-    tokens, 512 context tokens) against the fp32 oracle."""
+    """D 1536, 12 heads, FFN 8960, 1560 video (2 x 30 x 26) + 32
+    action tokens, 512 context tokens, weights N(0, 0.02), biases 0, temb
+    from t ~ U[0, 1000) through the sinusoidal Linear-SiLU-Linear chain,
+    RoPE from the chunk's grid ids; against the fp32 oracle in both output
+    modes."""
+    cfg = configs.PRESETS["cfg0"]
+    D, H, F, B, Q, C = cfg.dim, cfg.heads, cfg.ffn, 1, cfg.tokens, cfg.context
+    blk = make_oracle_block(D, F, H, seed=0, randomize=False)
+    g0 = torch.Generator().manual_seed(0)
+    x = torch.randn(B, Q, D, generator=g0).bfloat16().float()
+    ctx = torch.randn(B, C, D, generator=g0).bfloat16().float()
+    temb = configs.make_temb(cfg, B, "cpu", g0)
+    r = configs.chunk_rope(cfg)
+    with torch.no_grad():
+        ref = blk(x, ctx, temb, r)
+    g = to_device_block(blk)
+    rb = reference_bf16(to_device_block(blk), x, ctx, temb, r)
+    s32 = assert_parity(_run_native(g, x, ctx, temb, r), ref, rb, name="cfg0 fp32-out")
+    s16 = assert_parity(_run_native(g, x, ctx, temb, r, out_dtype=torch.bfloat16), ref, rb,
+                        name="cfg0 bf16-out")
+    print("cfg0 parity fp32-out", s32, "bf16-out", s16)
+
+
+# Bound of the stress case below: with gates and scales up to +-2 the bf16
+# operands of the two FFN GEMMs alone cost ~0.02 at this shape. A CPU model
+# of the block that rounds every tensor-core operand to bf16 and computes
+# everything else in fp32 (the floor of any bf16-operand datapath) is
+# 0.0206 from the fp32 oracle here; rounding only the LN3 output gives
+# 0.0158, only the GELU output 0.0148, every other operand alone < 0.004.
+STRESS_MAX_ABS = 3e-2
+
+
+def test_cfg0_shape_stress_modulation(cuda_device):
+    """The configs[0] shape with the small cases' stress modulation (temb ~
+    0.5 N(0,1), 14x the configs' temb): outside the configs' distribution,
+    so the bound is the bf16-operand floor above plus margin, not 2e-2."""
     D, H, F, B, Q, C = 1536, 12, 8960, 1, 1592, 512
     blk = make_oracle_block(D, F, H, seed=0, randomize=False)
     x, ctx, temb, r = make_inputs(B, Q, D, C, H, seed=0)
@@ -197,9 +233,9 @@ def test_cfg0_single_block(cuda_device):
         ref = blk(x, ctx, temb, r)
     g = to_device_block(blk)
     rb = reference_bf16(to_device_block(blk), x, ctx, temb, r)
-    s32 = assert_parity(_run_native(g, x, ctx, temb, r), ref, rb)
-    s16 = assert_parity(_run_native(g, x, ctx, temb, r, out_dtype=torch.bfloat16), ref, rb)
-    print("cfg0 parity fp32-out", s32, "bf16-out", s16)
+    s = assert_parity(_run_native(g, x, ctx, temb, r), ref, rb, max_abs=STRESS_MAX_ABS,
+                      name="cfg0 shape, stress temb, fp32-out")
+    print("cfg0-shape stress parity", s)
 
 
 def test_install_model_restores_classes(cuda_device):

@@ -4,6 +4,7 @@ Usage: python wam-egale_b200/build.py   (also called by __graft_entry__.build())
 The output lands in wam-egale_b200/lib/ so that it travels with the source
 tree; nothing is installed into site-packages.
 """
+import hashlib
 import os
 import shutil
 import subprocess
@@ -34,11 +35,24 @@ def sources():
         [ROOT.parent / "include" / "wamb.h"]
 
 
+def fingerprint():
+    """sha256 of the nvcc flags and of every source file's bytes: the build
+    is reused only when this matches the one recorded beside the library
+    (a binary copied from elsewhere, or built from other sources, never is)."""
+    h = hashlib.sha256()
+    h.update("\0".join(NVCC_FLAGS).encode())
+    for p in sources():
+        h.update(p.name.encode() + b"\0" + p.read_bytes() + b"\0")
+    return h.hexdigest()
+
+
+STAMP = OUT.with_suffix(".so.sha256")
+
+
 def up_to_date():
-    if not OUT.exists():
+    if not OUT.exists() or not STAMP.exists():
         return False
-    t = OUT.stat().st_mtime
-    return all(p.stat().st_mtime <= t for p in sources())
+    return STAMP.read_text().strip() == fingerprint()
 
 
 def build(force=False, verbose=False):
@@ -55,6 +69,7 @@ def build(force=False, verbose=False):
     if verbose:
         sys.stderr.write(res.stderr)
     os.replace(tmp, OUT)
+    STAMP.write_text(fingerprint() + "\n")
     return OUT
 
 

@@ -53,7 +53,7 @@ constexpr uint32_t ATT_ATOM = 128 * 128;            // one 64-column half: 128 r
 constexpr float ATT_RESCALE_LOG2 = 8.f;             // rescale O only when the max grows > 2^8
 constexpr int ATT_SLOTS = 5;                        // K/V ring: load L = 2j (K_j) or 2j+1 (V_j)
 // 2^f ~= C0 + f (C1 + f (C2 + f C3)) for f in [-0.5, 0.5]: minimax relative
-// error 7.5e-5 (fit by csrc/exp2_fit.py), far below bf16's 2^-9 for P.
+// error 7.5e-5 (tests/test_host_exp2_cubic.py recomputes the fit), far below bf16's 2^-9 for P.
 constexpr float ATT_EXP2_C0 = 0.9999281167984009f;
 constexpr float ATT_EXP2_C1 = 0.6932609677314758f;
 constexpr float ATT_EXP2_C2 = 0.2426108419895172f;

@@ -247,6 +247,7 @@ inline int check_block_args(const wamb_block_args* a) {
                WAMB_ERR_SHAPE, "freq_batch must be 1 or batch");
   WAMB_REQUIRE(a->update >= 0 && a->update <= 2, WAMB_ERR_ARG, "update must be 0, 1 or 2");
   WAMB_REQUIRE(a->fp8 == 0 || a->fp8 == 1, WAMB_ERR_ARG, "fp8 must be 0 or 1");
+  WAMB_REQUIRE(a->chained == 0 || a->chained == 1, WAMB_ERR_ARG, "chained must be 0 or 1");
   if (a->fp8) {
     WAMB_REQUIRE(a->ffn_dim % 128 == 0, WAMB_ERR_SHAPE, "fp8 needs ffn_dim %% 128 == 0");
     for (int i : kFp8Weights) {
@@ -369,6 +370,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     k.rows = reinterpret_cast<const long long*>(a->candidate_rows);
     k.batch = B; k.pool_batch = a->pool_batch;
     k.new_slots = slots; k.tiles = reinterpret_cast<int2*>(tiles); k.counts = counts;
+    k.early = a->chained;
     if ((rc = launch_kernel(kv_layout_kernel, dim3(1), dim3(KV_THREADS), 0, s, k))) return rc;
   }
   // 2. LN1 + modulation (shift 0, scale 1)

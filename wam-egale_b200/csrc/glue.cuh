@@ -411,6 +411,8 @@ struct KvParams {
   int* new_slots;           // [q]   out: pool slot of each new token
   int2* tiles;              // [pool] out: (first slot, length) of each visible run piece
   int* counts;              // [2]   out: number of tiles, number of visible slots
+  int early;                // 1: start before griddepcontrol.wait (the caller vouches that the
+                            //    previous grid is a same-layout block's last GEMM)
 };
 
 WAMB_DEV int warp_incl_scan(int v) {
@@ -478,16 +480,23 @@ WAMB_DEV uint32_t bytes_nonzero(uint32_t x) {
   return x & 0x01010101u;
 }
 
-// The kernel reads only the cache metadata of its own layer and writes the
-// block's slot / tile scratch, whose readers (the previous block's RMS+RoPE
-// and attention) precede the previous block's last GEMM; that GEMM triggers
-// its dependents only after its own griddepcontrol.wait (trigger_after), so
-// this kernel starts without waiting and runs beside the GEMM's last tiles.
-// It waits before exiting, so its completion still implies every earlier
-// grid's (the next kernel, LN1, reads that GEMM's output); it triggers LN1
-// at once, so LN1's CTAs are resident and start as soon as it exits.
+// With p.early = 1 (a chained block call: the previous grid is the last
+// GEMM of a block call with the same workspace layout) the kernel starts
+// without waiting and runs beside that GEMM's last tiles: it reads only the
+// cache metadata of its own layer and writes that metadata and the block's
+// slot / tile scratch, whose readers in the previous call (RMS+RoPE and
+// attention) precede the previous call's last GEMM, and that GEMM triggers
+// its dependents only after its own griddepcontrol.wait (trigger_after);
+// with the same layout the scratch lies apart from everything that GEMM
+// reads or writes. Otherwise (p.early = 0) it waits first: the previous
+// grid may have written this metadata, or the stream may carry another
+// layout whose buffers overlap this scratch. Either way it waits before
+// exiting, so its completion implies every earlier grid's (the next kernel,
+// LN1, reads that GEMM's output); it triggers LN1 at once, so LN1's CTAs are
+// resident and start as soon as it exits.
 __global__ void __launch_bounds__(KV_THREADS, 1) kv_layout_kernel(const KvParams p) {
   pdl_trigger();
+  if (!p.early) pdl_wait();
   constexpr int SEG_MAX = KV_MAX_POOL / KV_THREADS;   // slots per thread at most
   __shared__ __align__(16) uint8_t m[KV_MAX_POOL];
   __shared__ int sh[33];

@@ -87,6 +87,7 @@ class BlockArgs(ctypes.Structure):
         ("out", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("fp8", c_int32), ("w8", c_void_p * 27), ("w8_scale", c_void_p * 27),
+        ("chained", c_int32),
     ]
 
 
@@ -98,7 +99,7 @@ TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", 
 # Weight slots the FP8 path reads as E4M3 (self q/k/v/out, cross q/out, FFN).
 FP8_WEIGHTS = (3, 5, 7, 9, 13, 19, 23, 25)
 
-ABI_VERSION = 104
+ABI_VERSION = 105
 
 # Every symbol include/wamb.h declares; tests check the library exports them.
 EXPORTED = (

@@ -115,7 +115,7 @@ class NativeBlock:
     # --------------------------------------------------------------- args
     def make_args(self, hidden_states, encoder_hidden_states, temb, rotary_emb, cache,
                   candidate_cache_rows, update_cache, out, cross_kv=None, context_rows=None,
-                  keep=None):
+                  keep=None, chained=False):
         keep = [] if keep is None else keep
         x = hidden_states
         if not (x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and x.is_contiguous()
@@ -188,14 +188,18 @@ class NativeBlock:
             raise RuntimeError("out must be a contiguous bf16/fp32 tensor shaped like hidden_states")
         a.out = out.data_ptr()
         a.out_is_f32 = int(out.dtype == torch.float32)
+        a.chained = int(bool(chained))
         return a
 
     def __call__(self, hidden_states, encoder_hidden_states, temb, rotary_emb,
                  update_cache=0, cache_name="pos", candidate_cache_rows=None, debug=False,
-                 cross_kv=None, context_rows=None, out_dtype=None, out=None):
+                 cross_kv=None, context_rows=None, out_dtype=None, out=None, chained=False):
         """Runs the block; returns hidden_states' dtype by default. out_dtype /
         out select an fp32 output (the residual stream without the final bf16
-        rounding), which multi-layer stacks use between blocks."""
+        rounding), which multi-layer stacks use between blocks. chained=True
+        declares that the previous work on the current stream is a block call
+        of the same shape (the previous layer of a stack), so that the KV
+        bookkeeping may start beside its last GEMM."""
         if torch.is_grad_enabled():
             raise RuntimeError("NativeBlock is inference-only; use no_grad/inference_mode")
         block = self.block()
@@ -207,7 +211,8 @@ class NativeBlock:
             out = torch.empty_like(hidden_states, dtype=out_dtype or hidden_states.dtype)
         keep = []
         a = self.make_args(hidden_states, encoder_hidden_states, temb, rotary_emb, cache,
-                           candidate_cache_rows, update_cache, out, cross_kv, context_rows, keep)
+                           candidate_cache_rows, update_cache, out, cross_kv, context_rows, keep,
+                           chained)
         lib = _lib.load()
         nbytes = lib.wamb_block_workspace_bytes(a)
         ws = workspace(hidden_states.device, nbytes)
@@ -224,12 +229,12 @@ class NativeBlock:
         M = B * Q
         C = a.context_batch * a.context_tokens
         shapes = {"qkv": (M, 3 * D), "gelu": (M, F), "cross_k": (C, D), "cross_v": (C, D)}
+        result = {}
         if a.fp8:
             o8, os_ = offs[_lib.TAPS.index("a8")], offs[_lib.TAPS.index("a8_scale")]
             result["a8"] = ws[o8:o8 + M * max(D, F)].clone()  # last quantized GEMM input, raw E4M3
             result["a8_scale"] = ws[os_:os_ + 4 * M].view(torch.float32).clone()
         fp32 = ("residual1", "residual2")
-        result = {}
         for i, name in enumerate(_lib.TAPS):
             o = offs[i]
             if o < 0:

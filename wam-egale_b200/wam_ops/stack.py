@@ -48,8 +48,10 @@ class NativeStack:
             last = i == n - 1
             dst = (out if out is not None else torch.empty(B, Q, D, dtype=torch.bfloat16, device=dev)) \
                 if last else bufs[i % 2]
+            # Layers after the first follow a block call of the same shape on
+            # this stream, so their KV bookkeeping may start beside its last GEMM.
             layer(h, encoder_hidden_states, temb, rotary_emb, update_cache, cache_name,
-                  candidate_cache_rows, out=dst, context_rows=context_rows)
+                  candidate_cache_rows, out=dst, context_rows=context_rows, chained=i > 0)
             h = dst
         return h
 

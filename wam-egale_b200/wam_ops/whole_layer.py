@@ -90,7 +90,7 @@ class WholeLayerBlock:
 
     def __call__(self, hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache=0,
                  cache_name="pos", candidate_cache_rows=None, debug=False, out_dtype=None, out=None,
-                 context_rows=None):
+                 context_rows=None, chained=False):
         """context_rows ([batch] int64, optional): the prepared context row of
         each batch row for this call (e.g. [0]*K + [1]*K for CFG rows over a
         [conditional, negative] context), instead of the rows found at
@@ -100,4 +100,4 @@ class WholeLayerBlock:
         return self.native(hidden_states, encoder_hidden_states, temb, rotary_emb, update_cache,
                            cache_name, candidate_cache_rows, debug, cross_kv=cross,
                            context_rows=rows if cross is not None else None,
-                           out_dtype=out_dtype, out=out)
+                           out_dtype=out_dtype, out=out, chained=chained)
