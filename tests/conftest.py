@@ -30,9 +30,25 @@ def cuda_device():
     return torch.device("cuda", 0)
 
 
+def parity_markdown(rows):
+    """The recorded parity results as a markdown table."""
+    out = ["| case | output | cos | max abs err | allowance at the max | E_ref (reference in bf16) |",
+           "|---|---|---|---|---|---|"]
+    for r in rows:
+        if "vs_unquantized" in r:
+            extra = f"vs fp8 model; vs fp32: cos {r['vs_unquantized']['cos']:.6f}, max {r['vs_unquantized']['max_abs']:.4f}"
+            out.append(f"| {r['name']} | fp8 | {r['cos']:.7f} | {r['max_abs']:.5f} | {extra} | |")
+            continue
+        e = f"{r['E_ref']:.4f}" if "E_ref" in r else ""
+        out.append(f"| {r['name']} | {r['dtype']} | {r['cos']:.7f} | {r['max_abs']:.5f} | "
+                   f"{r['bound_at_max']:.5f} | {e} |")
+    return "\n".join(out) + "\n"
+
+
 def pytest_sessionfinish(session, exitstatus):
     """Write the parity results the tests recorded (blockutil.RESULTS) to
-    the JSON file named by WAMB_PARITY_OUT, if set."""
+    the file named by WAMB_PARITY_OUT, if set: JSON, or a markdown table
+    when the name ends in .md."""
     import json
     import os
     path = os.environ.get("WAMB_PARITY_OUT")
@@ -41,4 +57,5 @@ def pytest_sessionfinish(session, exitstatus):
     mod = sys.modules.get("blockutil")
     rows = list(getattr(mod, "RESULTS", []))
     Path(path).parent.mkdir(parents=True, exist_ok=True)
-    Path(path).write_text(json.dumps(rows, indent=1) + "\n")
+    text = parity_markdown(rows) if path.endswith(".md") else json.dumps(rows, indent=1) + "\n"
+    Path(path).write_text(text)

@@ -131,7 +131,7 @@ def test_block_candidate_verification(cuda_device, rows, Q):
         ref = blk(x, ctx, temb, r, candidate_cache_rows=rows)
     rb = reference_bf16(tb, x, ctx, temb, r, candidate_cache_rows=rows.cuda())
     out = _run_native(g, x, ctx, temb, r, candidate_cache_rows=rows.cuda())
-    assert_parity(out, ref, rb, name=f"block candidates rows {rows} Q{Q}")
+    assert_parity(out, ref, rb, name=f"block candidates rows {rows.tolist()} Q{Q}")
     for k, v in g.attn1.attn_caches["pos"].items():
         # bitwise (an uninitialised pool may hold NaN patterns)
         assert torch.equal(v.view(torch.uint8), before[k].view(torch.uint8)), f"candidate path wrote the cache ({k})"
