@@ -7,6 +7,7 @@
 //   cross attention -> cross-O GEMM + residual -> LN3+mod -> FFN1 GEMM+GELU ->
 //   FFN2 GEMM + gated residual.
 #pragma once
+#include <algorithm>
 #include <cmath>
 #include <type_traits>
 
@@ -135,14 +136,55 @@ inline int dispatch_vpt(int vpt, F&& f) {
   return fail(WAMB_ERR_SHAPE, "row width not supported");
 }
 
+// NV = D / 256 values per lane per 256-column group of the warp-per-row
+// LayerNorm (D <= 4096).
+template <typename F>
+inline int dispatch_nv(int nv, F&& f) {
+  switch (nv) {
+    case 1: return f(std::integral_constant<int, 1>{});
+    case 2: return f(std::integral_constant<int, 2>{});
+    case 3: return f(std::integral_constant<int, 3>{});
+    case 4: return f(std::integral_constant<int, 4>{});
+    case 5: return f(std::integral_constant<int, 5>{});
+    case 6: return f(std::integral_constant<int, 6>{});
+    case 8: return f(std::integral_constant<int, 8>{});
+    case 10: return f(std::integral_constant<int, 10>{});
+    case 12: return f(std::integral_constant<int, 12>{});
+  }
+  return -1;
+}
+
 inline int launch_ln(const LnParams& p, cudaStream_t s) {
   if (p.M == 0) return WAMB_OK;
-  const int vpt = row_vpt(p.D);
-  WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
-  const int threads = p.D / (8 * vpt);
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
+  const size_t lsm = ln_warp_smem(p.D, p.x_f32);
+  if (p.D % 256 == 0 && lsm <= 227 * 1024 && aligned16(p.x) && (p.ldx * (p.x_f32 ? 4 : 2)) % 16 == 0) {
+    // Warp-per-row kernel, one CTA of 8 warps per SM: the CTAs of each
+    // batch row of the modulation split its rows evenly, and all CTAs fit
+    // one wave (no SM runs a second CTA while others idle).
+    const int rpb = p.affine ? p.M : p.rows_per_batch;
+    const int nb = (p.M + rpb - 1) / rpb;
+    const int cpb = std::max(1, std::min(rpb, di.sms / nb));
+    const int rpc = (rpb + cpb - 1) / cpb;
+    rc = dispatch_nv(p.D / 256, [&](auto v) {
+      constexpr int NV = decltype(v)::value;
+      static bool configured[64] = {};
+      int dev = 0;
+      WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+      if (!configured[dev]) {
+        WAMB_CHECK_CUDA(cudaFuncSetAttribute(ln_warp_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024));
+        configured[dev] = true;
+      }
+      return launch_kernel(ln_warp_kernel<NV>, dim3(nb * cpb), dim3(LNW_WARPS * 32), lsm, s, p, rpc, cpb);
+    });
+    if (rc >= 0) return rc;
+  }
+  const int vpt = row_vpt(p.D);
+  WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
+  const int threads = p.D / (8 * vpt);
   return dispatch_vpt(vpt, [&](auto v) {
     constexpr int V = decltype(v)::value;
     constexpr int R = ln_rows(V);

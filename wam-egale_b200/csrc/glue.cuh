@@ -257,6 +257,232 @@ __global__ void ln_kernel(const LnParams p) {
   emit();
 }
 
+// Warp-per-row LayerNorm for D % 256 == 0 (the block's widths), one CTA
+// of 8 warps per SM. Rows reach shared memory by bulk copies (TMA engine,
+// completing on one mbarrier per slot): every warp keeps two row slots and
+// requests its next row as soon as it has taken the current one into
+// registers, so two rows per warp (16 per SM, 192 KB of fp32 rows) are in
+// flight while the warp normalizes. Each lane holds 8 values of each
+// 256-column group of its row: both reductions are warp shuffles over
+// eight independent partial sums, with no block barrier on a row's path.
+// The CTA's `rpc` rows lie in one batch row of the modulation, whose
+// per-column multiplier and offset (1 + scale and shift, or gamma and beta)
+// are staged in shared memory once instead of every row re-reading four
+// fp32 D-vectors from L2; per-token modulation (temb_L > 1) stages the
+// table part and adds each row's temb. Grid: batch rows x `cpb` CTAs (the
+// affine modes: one batch of M rows).
+WAMB_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+WAMB_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// Four consecutive temb values (fp32 or bf16) as fp32.
+WAMB_DEV float4 load_temb4(const void* temb, int f32, long long off) {
+  if (f32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(temb) + off));
+  const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(temb) + off));
+  const float2 a = unpack_bf16(w.x), b = unpack_bf16(w.y);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+// `bytes` (a multiple of 16; both addresses 16-byte aligned) from global
+// into this CTA's shared memory by the TMA engine, completing as
+// transaction bytes on the mbarrier `bar`.
+WAMB_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+constexpr int LNW_WARPS = 8;
+
+// Dynamic shared memory of ln_warp_kernel: multiplier and offset [2][D]
+// fp32, two row slots per warp, one mbarrier per slot, the abort flag.
+__host__ __device__ constexpr size_t ln_warp_smem(int D, int x_f32) {
+  return 8ull * D + 2ull * LNW_WARPS * D * (x_f32 ? 4 : 2) + 16ull * LNW_WARPS + 16;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnParams p, int rpc, int cpb) {
+  extern __shared__ __align__(16) uint8_t ln_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = p.D;
+  const uint32_t row_bytes = static_cast<uint32_t>(D) * (p.x_f32 ? 4 : 2);
+  float* smul = reinterpret_cast<float*>(ln_smem);
+  float* sadd = smul + D;
+  uint8_t* slots = ln_smem + 8 * D;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(slots + 2 * LNW_WARPS * row_bytes);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * LNW_WARPS);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2 * LNW_WARPS; ++i) mbar_init(smem_u32(bars + i), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (p.trigger) pdl_trigger();
+  pdl_wait();
+  const int rpb = p.affine ? p.M : p.rows_per_batch;
+  const int b = blockIdx.x / cpb, chunk = blockIdx.x - b * cpb;
+  const int r_begin = b * rpb + chunk * rpc;
+  const int r_end = min(min(r_begin + rpc, (b + 1) * rpb), p.M);
+  const int nk = r_end - r_begin > warp ? (r_end - r_begin - warp + LNW_WARPS - 1) / LNW_WARPS : 0;
+  const uint8_t* xb = static_cast<const uint8_t*>(p.x);
+  const long long x_row_bytes = p.ldx * (p.x_f32 ? 4 : 2);
+  const uint32_t slot0 = smem_u32(slots + warp * 2 * row_bytes);
+  const uint32_t bar0 = smem_u32(bars + 2 * warp);
+  auto request = [&](int k) {   // row k of this warp into slot k & 1 (lane 0)
+    const int row = r_begin + warp + k * LNW_WARPS;
+    mbar_arrive_expect_tx(bar0 + 8 * (k & 1), row_bytes);
+    bulk_load(slot0 + (k & 1) * row_bytes, xb + row * x_row_bytes, row_bytes, bar0 + 8 * (k & 1));
+  };
+  int issued = 0;
+  if (lane == 0)
+    for (; issued < 2 && issued < nk; ++issued) request(issued);
+  issued = __shfl_sync(0xffffffffu, issued, 0);
+
+  const int tr = p.temb_rows == 1 ? 1 : 6;
+  const int ts = tr == 1 ? 0 : p.scale_idx, th = tr == 1 ? 0 : p.shift_idx;   // temb rows of scale / shift
+  const bool per_token = p.affine == 0 && p.temb_L > 1;
+  if (p.affine != 2) {
+    const long long toff = static_cast<long long>(b) * p.temb_L * tr * D;   // token 0 of batch row b
+    for (int c = threadIdx.x * 4; c < D; c += LNW_WARPS * 32 * 4) {
+      float4 m, a;
+      if (p.affine == 1) {
+        m = __ldg(reinterpret_cast<const float4*>(p.gamma + c));
+        a = __ldg(reinterpret_cast<const float4*>(p.beta + c));
+      } else {
+        m = __ldg(reinterpret_cast<const float4*>(p.table + static_cast<long long>(p.scale_idx) * D + c));
+        a = __ldg(reinterpret_cast<const float4*>(p.table + static_cast<long long>(p.shift_idx) * D + c));
+        m.x += 1.f; m.y += 1.f; m.z += 1.f; m.w += 1.f;   // the modulation multiplies by 1 + scale
+        if (!per_token) {
+          const float4 tm = load_temb4(p.temb, p.temb_f32, toff + static_cast<long long>(ts) * D + c);
+          const float4 ta = load_temb4(p.temb, p.temb_f32, toff + static_cast<long long>(th) * D + c);
+          m.x += tm.x; m.y += tm.y; m.z += tm.z; m.w += tm.w;
+          a.x += ta.x; a.y += ta.y; a.z += ta.z; a.w += ta.w;
+        }
+      }
+      *reinterpret_cast<float4*>(smul + c) = m;
+      *reinterpret_cast<float4*>(sadd + c) = a;
+    }
+  }
+  __syncthreads();
+
+  // Lane l holds columns [i * 256 + l * 4, +4) and [i * 256 + 128 + l * 4,
+  // +4) of each 256-column group i: every warp access to a row or to the
+  // staged vectors is contiguous (fp32: 512 B, bf16: 256 B), free of bank
+  // conflicts.
+  auto col_of = [&](int i, int h) { return i * 256 + h * 128 + lane * 4; };
+  int k = 0;
+  for (; k < nk; ++k) {
+    const int row = r_begin + warp + k * LNW_WARPS;
+    if (!mbar_wait(bar0 + 8 * (k & 1), (k >> 1) & 1, abort_flag)) break;
+    float v[NV][8];
+    const uint8_t* srow = slots + warp * 2 * row_bytes + (k & 1) * row_bytes;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = col_of(i, h);
+        if (p.x_f32) {
+          const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(srow) + col);
+          v[i][4 * h] = x.x; v[i][4 * h + 1] = x.y; v[i][4 * h + 2] = x.z; v[i][4 * h + 3] = x.w;
+        } else {
+          const uint2 x = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(srow) + col);
+          const float2 a = unpack_bf16(x.x), c = unpack_bf16(x.y);
+          v[i][4 * h] = a.x; v[i][4 * h + 1] = a.y; v[i][4 * h + 2] = c.x; v[i][4 * h + 3] = c.y;
+        }
+      }
+    __syncwarp();
+    if (issued < nk) {   // the slot is free again: request the row two ahead
+      if (lane == 0) {
+        fence_proxy_async();
+        request(issued);
+      }
+      ++issued;
+    }
+    if (p.affine != 2) {
+      // Eight independent partial sums per lane (short dependency chains).
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s8[j] += v[i][j];
+      const float mean = warp_sum(((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))) / D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s8[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float d = v[i][j] - mean;
+          s8[j] = fmaf(d, d, s8[j]);
+        }
+      const float var = warp_sum(((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))) / D;
+      const float rstd = rsqrtf(var + p.eps);
+      long long trow = 0;
+      if (per_token) {
+        const int tok = row - b * rpb;
+        trow = (static_cast<long long>(b) * p.temb_L + tok) * tr * D;
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int col = col_of(i, h);
+          float4 m = *reinterpret_cast<const float4*>(smul + col);
+          float4 a = *reinterpret_cast<const float4*>(sadd + col);
+          if (per_token) {
+            const float4 tm = load_temb4(p.temb, p.temb_f32, trow + static_cast<long long>(ts) * D + col);
+            const float4 ta = load_temb4(p.temb, p.temb_f32, trow + static_cast<long long>(th) * D + col);
+            m.x += tm.x; m.y += tm.y; m.z += tm.z; m.w += tm.w;
+            a.x += ta.x; a.y += ta.y; a.z += ta.z; a.w += ta.w;
+          }
+          float* w = &v[i][4 * h];
+          w[0] = (w[0] - mean) * rstd * m.x + a.x;
+          w[1] = (w[1] - mean) * rstd * m.y + a.y;
+          w[2] = (w[2] - mean) * rstd * m.z + a.z;
+          w[3] = (w[3] - mean) * rstd * m.w + a.w;
+        }
+    }
+    if (p.out8 == nullptr) {
+      __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ldo;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          *reinterpret_cast<uint2*>(orow + col_of(i, h)) =
+              make_uint2(pack_bf16(v[i][4 * h], v[i][4 * h + 1]), pack_bf16(v[i][4 * h + 2], v[i][4 * h + 3]));
+    } else {
+      // E4M3 with the row scale amax / 448 (the quant_rows_kernel rule).
+      float am = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[i][j]));
+      const float amax = fmaxf(warp_max(am), 1e-20f);
+      const float inv = 448.f / amax;
+      if (lane == 0) p.out_scale[row] = amax / 448.f;
+      uint8_t* orow = p.out8 + static_cast<long long>(row) * p.ldo;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = v[i][j] * inv;
+        const uint2 q = pack_e4m3x8(t);   // bytes 0-3: group h = 0, bytes 4-7: h = 1
+        *reinterpret_cast<uint32_t*>(orow + col_of(i, 0)) = q.x;
+        *reinterpret_cast<uint32_t*>(orow + col_of(i, 1)) = q.y;
+      }
+    }
+  }
+  // After an abort, the copies still in flight must land before the CTA's
+  // shared memory goes away.
+  if (lane == 0)
+    for (int j = k; j < issued; ++j) mbar_wait_teardown(bar0 + 8 * (j & 1), (j >> 1) & 1);
+}
+
 // --------------------------------------------------- row E4M3 quantization
 struct QuantParams {
   const void* x;          // [M, ldx] bf16, or fp32 when x_f32
