@@ -113,6 +113,15 @@ typedef struct wamb_linear_args {
   int32_t a_is_fp8;
   const float* a_scale;
   const float* w_scale[3];
+  /* Optional stream-K scratch for M >= 512 (NULL: none) of
+   * wamb_linear_sk_bytes() bytes, 256-byte aligned, zero-filled before its
+   * first use (the library leaves its flags zero after every call). With
+   * it, a GEMM whose 256 x 256 tiles leave the last round over the SM pairs
+   * partly filled shares that round's k-blocks evenly over all pairs; the
+   * partial sums of a shared tile are added in a fixed order, so results do
+   * not depend on timing. Calls that share it must be ordered on one stream. */
+  void* sk_workspace;
+  size_t sk_workspace_bytes;
 } wamb_linear_args;
 /* When the output tiles would leave SMs idle (small M), wamb_linear splits K
  * across the CTAs of a thread-block cluster: their fp32 partials meet in the
@@ -120,6 +129,8 @@ typedef struct wamb_linear_args {
  * not depend on timing and no workspace is needed. */
 
 WAMB_API int wamb_linear(const wamb_linear_args* args, void* stream);
+/* Bytes of wamb_linear_args.sk_workspace on the current device. */
+WAMB_API size_t wamb_linear_sk_bytes(void);
 
 /*
  * Row-wise E4M3 quantization (no counterpart in the reference):
@@ -249,7 +260,11 @@ typedef struct wamb_block_args {
   int32_t chained;
 } wamb_block_args;
 
-/* Named intermediates kept in the workspace (byte offsets; -1 = absent). */
+/* Named intermediates kept in the workspace (byte offsets; -1 = absent).
+ * The workspace must be zero-filled before its first use (cudaMemset once
+ * at allocation): its first bytes hold the stream-K flags of the two-CTA
+ * GEMMs, which every call leaves zero again. Calls of any shape may share
+ * one workspace. After a call that recorded a device error, zero it again. */
 enum wamb_tap {
   WAMB_TAP_MODULATED1 = 0,  /* [M, D]   LN1 + modulation */
   WAMB_TAP_QKV = 1,         /* [M, 3D]  q | k | v (q,k after RMS + RoPE unless in the pool) */
@@ -268,7 +283,9 @@ enum wamb_tap {
   WAMB_TAP_KV_COUNTS = 14,  /* [2] int32: tiles, visible slots */
   WAMB_TAP_A8 = 15,         /* fp8 only: [M, F] E4M3, the last quantized GEMM input */
   WAMB_TAP_A8_SCALE = 16,   /* fp8 only: [M] fp32 per-row scales of WAMB_TAP_A8 */
-  WAMB_TAP_COUNT = 17
+  WAMB_TAP_SK_FLAGS = 17,   /* stream-K flags of the two-CTA GEMMs (offset 0 in every layout) */
+  WAMB_TAP_SK_PART = 18,    /* stream-K fp32 partials (M >= 512 only) */
+  WAMB_TAP_COUNT = 19
 };
 
 WAMB_API size_t wamb_block_workspace_bytes(const wamb_block_args* args);

@@ -62,7 +62,9 @@ def test_workspace_layout():
     total = lib.wamb_block_workspace_layout(a, offs)
     assert total == lib.wamb_block_workspace_bytes(a)
     M, D, F = 48, 256, 512
-    assert offs[_lib.TAPS.index("modulated1")] == 0
+    assert offs[_lib.TAPS.index("sk_flags")] == 0           # stream-K flags first in every layout
+    assert offs[_lib.TAPS.index("modulated1")] == 8192
+    assert offs[_lib.TAPS.index("sk_part")] == -1           # M < 512: no two-CTA GEMM
     assert offs[_lib.TAPS.index("kv_slots")] == -1          # no cache
     assert offs[_lib.TAPS.index("norm2")] >= 0
     assert total >= (12 * M * D + M * F) * 2                # residual stream taps are fp32
@@ -138,10 +140,11 @@ def test_linear_rejects_bad_shapes():
 
 
 def test_workspace_layout_is_the_taps():
-    """The workspace holds the named intermediates only (small-M GEMMs reduce
-    their split-K partials in cluster shared memory, not in the workspace):
-    the last tap ends the layout, and a 224-row D 3072 verify batch fits the
-    no-allocation entry point's fixed scratch."""
+    """Below 512 rows the workspace holds the named intermediates and the
+    stream-K flags only (small-M GEMMs reduce their split-K partials in
+    cluster shared memory, not in the workspace): the last tap ends the
+    layout, and a 224-row D 3072 verify batch fits the no-allocation entry
+    point's fixed scratch."""
     lib = _lib.load()
     offs = (ctypes.c_int64 * len(_lib.TAPS))()
     small = _args(batch=7, tokens=32, dim=3072, heads=24, ffn_dim=14336)

@@ -1,9 +1,11 @@
 """tcgen05 GEMM (wamb_linear) against a torch fp32 reference on the GPU.
 
-Shapes with M >= 512, N per group a multiple of 256 and at least 74
-256 x 256 tiles take the two-CTA (cta_group::2) kernel; the others the
-one-CTA kernel with 64/128/256-column tiles, split along K across a
-thread-block cluster when the tiles alone would leave SMs idle.
+Shapes with M >= 512 and N per group a multiple of 256 take the two-CTA
+(cta_group::2) kernel when they have at least 74 256 x 256 tiles, or when
+the stream-K scratch lets them share a partly filled last round over all
+SM pairs; the others take the one-CTA kernel with 64/128/256-column tiles,
+split along K across a thread-block cluster when the tiles alone would
+leave SMs idle.
 
 Tolerance: the kernel accumulates in fp32 and rounds once to bf16, so the
 error against an fp32 reference of the same bf16 operands is bounded by the
@@ -151,3 +153,77 @@ def test_linear_split_k(cuda_device, m, k, n, groups, epi):
     assert _lib.device_status() == 0
     _close(out1, ref)
     assert torch.equal(out1, out2)            # deterministic: partials summed in split order
+
+
+# ------------------------------------------------------------------ stream-K
+# M >= 512 with a stream-K scratch (ops.linear passes one): when the
+# 256 x 256 tiles leave the last round over the SM pairs partly filled, the
+# two-CTA kernel shares that round's tiles x k-blocks evenly over every
+# pair, and a tile split between pairs is finished from the others' fp32
+# partials.
+def _sk_flags_zero(dev):
+    ws = ops.sk_workspace(dev)
+    return bool((ws[:8192] == 0).all())
+
+
+@pytest.mark.parametrize("m,k,n,groups", [
+    (880, 3072, 3072, 1),      # 48 tiles over 74 pairs: every tile split
+    (880, 14336, 3072, 1),     # FFN2 shape: 224 k-blocks per tile
+    (880, 3072, 3072, 3),      # QKV shape: three weight groups, one full round + 70 tiles
+    (512, 64, 256, 1),         # too few units to share: the one-CTA path
+    (2000, 1536, 1536, 1),     # D 1536 shapes, ragged last row block
+    (7040, 3072, 14336, 1),    # 1568 tiles: 21 full rounds + 14 shared tiles
+])
+def test_linear_stream_k(cuda_device, m, k, n, groups):
+    g = torch.Generator(device="cuda").manual_seed(m + k + n)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.05).bfloat16() for _ in range(groups)]
+    bs = [torch.randn(n, device="cuda", generator=g).bfloat16() for _ in range(groups)]
+    out = ops.linear(a, ws, bs)
+    again = ops.linear(a, ws, bs)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert _sk_flags_zero(a.device)
+    _close(out, _ref(a, ws, bs))
+    assert torch.equal(out, again)   # fixed summation order: no dependence on timing
+
+
+def test_linear_stream_k_epilogues(cuda_device):
+    """Gated fp32 residual (the O projection at M 880) and GELU through the
+    stream-K path, against the fp32 reference."""
+    m, k, n, B = 880, 3072, 3072, 2
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16()
+    b = torch.randn(n, device="cuda", generator=g).bfloat16()
+    res = torch.randn(m, n, device="cuda", generator=g)
+    table = torch.randn(6, n, device="cuda", generator=g) * 0.1
+    temb = torch.randn(B, 1, 6, n, device="cuda", generator=g) * 0.1
+    out = torch.empty(m, n, device="cuda")
+    ops.linear(a, w, b, epilogue=_lib.EPI_RES_GATE, res=res, table=table, temb=temb, rows_per_batch=m // B,
+               gate_index=2, out=out)
+    gelu = ops.linear(a, w, b, epilogue=_lib.EPI_GELU)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert _sk_flags_zero(a.device)
+    base = _ref(a, [w], [b])
+    gate = (table[2][None, None] + temb[:, :, 2]).expand(B, m // B, n).reshape(m, n)
+    err = (out - (res + base * gate)).abs().max().item()
+    assert err <= 2e-3, err
+    _close(gelu, torch.nn.functional.gelu(base, approximate="tanh"))
+
+
+def test_linear_stream_k_fp8(cuda_device):
+    m, k, n = 880, 3072, 3072
+    g = torch.Generator(device="cuda").manual_seed(6)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.05).bfloat16()
+    b = torch.randn(n, device="cuda", generator=g).bfloat16()
+    a8, sa = ops.quantize_rows(a)
+    w8, sw = ops.quantize_rows(w)
+    out = ops.linear(a8, w8, b, a_scale=sa, w_scales=sw)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert _sk_flags_zero(a.device)
+    deq = lambda q, s: q.float() * s[:, None]  # noqa: E731
+    _close(out, deq(a8, sa) @ deq(w8, sw).t() + b.float())

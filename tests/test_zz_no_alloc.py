@@ -52,7 +52,7 @@ def _device_inputs(B, Q, D, C, H, seed):
 def _workspace_call(lib, native, x, ctx, temb, r, cache, update, keep):
     out = torch.empty_like(x)
     a = native.make_args(x, ctx, temb, r, cache, None, update, out, keep=keep)
-    ws = torch.empty(lib.wamb_block_workspace_bytes(a), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(lib.wamb_block_workspace_bytes(a), dtype=torch.uint8, device="cuda")
     keep.append(ws)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _lib.check(lib.wamb_block_forward(a, _lib.stream_ptr()))

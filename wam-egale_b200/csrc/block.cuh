@@ -228,6 +228,9 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
     L.off[tap] = static_cast<int64_t>(o);
     o = align256(o + bytes);
   };
+  // Stream-K flags first, in every layout, so that calls of different
+  // shapes sharing one workspace agree on where the zero flags live.
+  put(WAMB_TAP_SK_FLAGS, SK_FLAG_BYTES);
   const bool f8 = a->fp8 == 1;  // LN outputs go to the E4M3 buffer instead
   if (!f8) put(WAMB_TAP_MODULATED1, MD);
   put(WAMB_TAP_QKV, 3 * MD);
@@ -252,6 +255,12 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
     put(WAMB_TAP_KV_SLOTS, static_cast<size_t>(a->tokens) * 4);
     put(WAMB_TAP_KV_TILES, static_cast<size_t>(a->pool) * 8);
     put(WAMB_TAP_KV_COUNTS, 16);
+  }
+  // Stream-K partials of the two-CTA GEMMs (they run at M >= 512).
+  if (M >= 512) {
+    DeviceInfo di;
+    const int sms = device_info(&di) == WAMB_OK ? di.sms : 148;
+    put(WAMB_TAP_SK_PART, sk_part_bytes(sms));
   }
   L.total = o;
   return L;
@@ -376,12 +385,26 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   int* slots = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_SLOTS]) : nullptr;
   int* tiles = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_TILES]) : nullptr;
   int* counts = cache ? reinterpret_cast<int*>(ws + L.off[WAMB_TAP_KV_COUNTS]) : nullptr;
+  // Stream-K scratch of the two-CTA GEMMs (flags at offset 0, zero between calls).
+  SkBuffers skb;
+  if (L.off[WAMB_TAP_SK_PART] >= 0) {
+    skb.flags = reinterpret_cast<int*>(ws + L.off[WAMB_TAP_SK_FLAGS]);
+    skb.part = reinterpret_cast<float*>(ws + L.off[WAMB_TAP_SK_PART]);
+    skb.part_bytes = sk_part_bytes(di.sms);
+  }
+  const bool has_sk = skb.part != nullptr;
   // Every GEMM of the block follows at least one other kernel of the block,
   // so its weights may be requested before griddepcontrol.wait.
-  auto run_gemm = [&](wamb_linear_args& g, bool trigger = false) { return linear_impl(&g, s, true, trigger); };
+  auto run_gemm = [&](wamb_linear_args& g, bool trigger = false) {
+    return linear_impl(&g, s, true, trigger, 0, false, &skb);
+  };
   // Early triggers pay only before a one-CTA GEMM, whose weight loads can
-  // start before its pdl_wait (N columns, N per weight group).
-  auto early = [&](long long n, int n_per_group) { return !gemm_is_pair(static_cast<int>(M), n, n_per_group, di.sms); };
+  // start before its pdl_wait (N columns, N per weight group, K).
+  auto early = [&](long long n, int n_per_group, int k) {
+    const int kb = k / (a->fp8 == 1 ? GEMM_BK8 : GEMM_BK);
+    return !gemm_is_pair(static_cast<int>(M), n, n_per_group, di.sms,
+                         has_sk && n_per_group % 256 == 0 && gemm_use_sk(M, n, kb, di.sms));
+  };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
   const bool f8 = a->fp8 == 1;
   uint8_t* a8 = f8 ? ws + L.off[WAMB_TAP_A8] : nullptr;
@@ -422,7 +445,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   // LN1 triggers early only after the KV layout kernel: the block's first
   // kernel keeps the implicit trigger, so writes of the kernels before the
   // block are complete before any GEMM of the block reads weights early.
-  ln.trigger = cache && early(3 * D, D) ? 1 : 0;
+  ln.trigger = cache && early(3 * D, D, D) ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -461,7 +484,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     at.k0 = qkv; at.v0 = qkv; at.ld0 = 3LL * D; at.k0_col = D; at.v0_col = 2 * D;
     at.src0_total_rows = M; at.src0_batch_stride = Q; at.src0_len = Q;
   }
-  if ((rc = attention_impl(&at, s, !f8 && early(D, D)))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D)))) return rc;
   if (f8 && (rc = quantize(attn, D, D))) return rc;
   // 6. O projection + gated residual (gate 2): h2 = x + o * gate_msa
   g = wamb_linear_args{};
@@ -477,7 +500,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln = LnParams{};
   ln.x = h2; ln.x_f32 = 1; ln.ldx = D; ln.out = n2; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[1]); ln.affine = a->weights[1] != nullptr ? 1 : 2;
-  ln.trigger = early(D, D) ? 1 : 0;
+  ln.trigger = early(D, D, D) ? 1 : 0;
   ln.gamma = static_cast<const float*>(a->weights[1]); ln.beta = static_cast<const float*>(a->weights[2]);
   ln.rows_per_batch = Q;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -513,7 +536,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   at.src0_map = a->context_rows;
   at.src0_broadcast = a->context_rows == nullptr && a->context_batch == 1 && B > 1;
   at.out = ca; at.ldo = D;
-  if ((rc = attention_impl(&at, s, !f8 && early(D, D)))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D)))) return rc;
   if (f8 && (rc = quantize(ca, D, D))) return rc;
   // 12. cross O projection + residual: h3 = h2 + o
   g = wamb_linear_args{};
@@ -526,7 +549,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln = LnParams{};
   ln.x = h3; ln.x_f32 = 1; ln.ldx = D; ln.out = f0; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[2]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
-  ln.trigger = early(F, F) ? 1 : 0;
+  ln.trigger = early(F, F, D) ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 3; ln.scale_idx = 4;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -537,7 +560,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   gemm_input(g, f0, 23);
   g.bias[0] = a->weights[24]; g.out = act; g.ldo = F;
   g.epilogue = WAMB_EPI_GELU;
-  if ((rc = run_gemm(g, !f8 && early(D, D)))) return rc;   // bf16: FFN2 follows directly
+  if ((rc = run_gemm(g, !f8 && early(D, D, F)))) return rc;   // bf16: FFN2 follows directly
   if (f8 && (rc = quantize(act, F, F))) return rc;
   // 15. FFN2 + gated residual (gate 5): out = h3 + f * c_gate_msa
   g = wamb_linear_args{};
@@ -550,7 +573,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   g.dim = D;
   // The block's last kernel: trigger the next grid after the wait, so that a
   // following block's KV layout kernel runs beside this GEMM's last tiles.
-  return linear_impl(&g, s, true, false, 0, true);
+  return linear_impl(&g, s, true, false, 0, true, &skb);
 }
 
 }  // namespace wamb

@@ -68,11 +68,21 @@ struct GemmParams {
   // != 0: the columns of weight group g go to out + g * out_gstride
   // (elements) at their local column, instead of column g * n_per_group of
   // one [M, ldo] output (separate K and V outputs of one launch).
-  long long out_gstride;  // 1: trigger the dependent grid right after griddepcontrol.wait (every
+  long long out_gstride;
+  // 1: trigger the dependent grid right after griddepcontrol.wait (every
   // earlier grid is then complete); the block's last GEMM sets it so that
   // the next block's KV layout kernel, which waits only before exiting,
   // overlaps this GEMM's last tiles.
   int trigger_after;
+  // Stream-K (two-CTA kernel, gemm2.cuh): sk = 1 shares the last, partly
+  // filled round of tiles evenly over all pairs; a tile shared by several
+  // pairs is finished by the pair holding its last k-block from the other
+  // pairs' fp32 partials in sk_part ([pairs][8 chunks][256 rows][32] fp32),
+  // each announced by one flag per producing warp in sk_flags ([pairs][16],
+  // zero before the launch and zero again after it).
+  int sk;
+  float* sk_part;
+  int* sk_flags;
 };
 
 constexpr int GEMM_BM = 128;
@@ -335,9 +345,15 @@ WAMB_DEV float4 lds4(uint32_t a) {
 // two chunks of work. Residual loads and output stores carry the streaming
 // cache hint (ld/st .cs: evict first), so the streamed rows do not push the
 // mainloop's A and weight tiles out of L2. Returns false if wait_acc gave up.
-template <class WaitAcc>
+struct NoAdjust {
+  WAMB_DEV void operator()(int, float (&)[32]) const {}
+};
+
+// adjust(c, v) runs on each chunk's accumulator values before the epilogue
+// math (the stream-K finisher adds the other pairs' partials there).
+template <class WaitAcc, class Adjust = NoAdjust>
 WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int row0, int lane, int n0,
-                                        int c0, uint32_t st, WaitAcc&& wait_acc) {
+                                        int c0, uint32_t st, WaitAcc&& wait_acc, Adjust&& adjust = Adjust{}) {
   const int row = row0 + lane;
   const EpiRow e = epi_row(p, row, n0);
   const bool has_res = p.epi == EPI_RES || p.epi == EPI_RES_GATE;
@@ -397,6 +413,7 @@ WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int
     float v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
+    adjust(c, v);
     if (e.valid) epi_value<32>(p, e, v, n0 + c * 32, e.n_local0 + c * 32);
     if (has_res) {
       __syncwarp();

@@ -14,6 +14,23 @@
 //   bye        exit handshake: the other CTA arrives once (remote arrive)
 // TMEM: 2 accumulators x 256 columns per CTA (rows 0-127 of the tile in the
 // leader's TMEM, rows 128-255 in the peer's).
+//
+// Stream-K (GemmParams::sk): the full rounds of tiles run as before, one
+// tile per pair per round, in the wave order that keeps few weight column
+// blocks in flight (A and those weights stay in L2). The tiles x k-blocks
+// units of the remaining, partly filled round are cut into one equal
+// contiguous share per pair, so that every SM pair has the same work
+// whatever the tile count (a 880-row GEMM with N 3072 has 48 tiles for 74
+// pairs). A pair walks its share from the highest unit down, in segments
+// cut at tile boundaries. A segment without the tile's last k-block is a
+// producer: its fp32 partial goes to the pair's slot of sk_part and each
+// epilogue warp raises its flag. The segment holding the last k-block (and
+// not the first) finishes the tile: it adds the lower pairs' partials of
+// that tile to its accumulator, in a fixed order, in the epilogue, and
+// clears their flags. Walking down puts a pair's producer segment first
+// and its finisher segment last, and the finisher of a tile is the highest
+// pair on it, so partials are ready when they are needed and no pair waits
+// on a pair that starts after it.
 #pragma once
 #include "gemm.cuh"
 
@@ -79,6 +96,75 @@ WAMB_DEV void umma2_commit_both(uint32_t bar) {
 WAMB_DEV void umma2_commit_local(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
+}
+
+// One output tile's k-block range processed by a pair.
+struct Seg {
+  int t, kb0, kb1;
+  bool producer, finisher;
+};
+
+// The pair's segments: whole tiles pair, pair + npairs, ... for every full
+// round (all tiles without stream-K); with stream-K, then the pair's share
+// [lo, hi) of the remaining tiles' units (tile-major, tiles counted from
+// sk_base) in descending order, cut at tile boundaries. 32-bit: the
+// remaining tiles are fewer than the pairs (< 128), so U < 128 x k-blocks
+// and q * U stay far below 2^31 for any K.
+struct SegIter {
+  int lo, i, U;
+  int t, step, dp_end, sk_base, num_kb;
+  WAMB_DEV SegIter(bool sk, int pair, int npairs, int num_tiles, int num_kb_)
+      : t(pair), step(npairs), num_kb(num_kb_) {
+    dp_end = sk ? (num_tiles / npairs) * npairs : num_tiles;
+    sk_base = dp_end;
+    U = (num_tiles - dp_end) * num_kb_;
+    lo = pair * U / npairs;
+    i = sk ? (pair + 1) * U / npairs - 1 : -1;
+  }
+  // First unit of pair q's stream-K share.
+  WAMB_DEV int share_lo(int q, int npairs) const { return q * U / npairs; }
+  WAMB_DEV bool next(Seg& s) {
+    if (t < dp_end) {
+      s = Seg{t, 0, num_kb, false, false};
+      t += step;
+      return true;
+    }
+    if (i < lo) return false;
+    const int tt = i / num_kb;
+    const int base = tt * num_kb;
+    const int seg_lo = lo > base ? lo : base;
+    s.t = sk_base + tt;
+    s.kb0 = seg_lo - base;
+    s.kb1 = i + 1 - base;
+    s.producer = s.kb1 != num_kb;
+    s.finisher = !s.producer && s.kb0 != 0;
+    i = seg_lo - 1;
+    return true;
+  }
+};
+
+WAMB_DEV void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+WAMB_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait for a stream-K partial's flag.
+WAMB_DEV bool sk_wait_flag(const int* f, volatile int* abort_flag) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if (ld_acquire_gpu(f) != 0) return true;
+    if ((it & 15u) == 15u) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > WAMB_WAIT_TIMEOUT_NS) {
+        *abort_flag = 1;
+        record_error(1);
+        return false;
+      }
+    }
+  }
 }
 
 template <bool F8>
@@ -151,14 +237,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
       int it = 0;
-      for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
+      SegIter segs(p.sk != 0, pair, npairs, num_tiles, num_kb);
+      Seg sg;
+      while (!*abort_flag && segs.next(sg)) {
+        const int t = sg.t;
         const int m_blk = t % num_m, n_blk = t / num_m;
         const int n0 = n_blk * 256;
         const int g = n0 / p.n_per_group;
         const int n_local = n0 - g * p.n_per_group;
         const CUtensorMap* mb = g == 0 ? &tmB0 : (g == 1 ? &tmB1 : &tmB2);
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) { ok = false; break; }
@@ -186,14 +275,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // --------------------------------------------------- MMA issuer (leader)
       constexpr uint32_t IDESC = F8 ? idesc_e4m3(256, 256) : idesc_bf16(256, 256, 0);
       int it = 0, tc = 0;
-      for (int t = pair; t < num_tiles; t += npairs, ++tc) {
+      SegIter segs(p.sk != 0, pair, npairs, num_tiles, num_kb);
+      Seg sg;
+      for (; segs.next(sg); ++tc) {
         const int acc = tc & 1;
         const uint32_t aph = (tc >> 1) & 1;
         if (!mbar_wait(tempty0 + 8 * acc, aph ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * 256;
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) { ok = false; break; }
@@ -204,8 +295,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per k-block
             const uint64_t ad = sw128_desc(a_base + kk * 32, 16, 1024);
             const uint64_t bd = sw128_desc(b_base + kk * 32, 16, 1024);
-            if constexpr (F8) umma2_e4m3(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
-            else umma2_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0);
+            const uint32_t accum = kb > sg.kb0 || kk > 0;
+            if constexpr (F8) umma2_e4m3(d_tmem, ad, bd, IDESC, accum);
+            else umma2_bf16(d_tmem, ad, bd, IDESC, accum);
           }
           umma2_commit_both(empty0 + 8 * s);
         }
@@ -224,19 +316,79 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t tempty_leader0 = map_to_rank(tempty0, 0);
     // Every tile's epilogue goes through the warp's staging buffer.
     const uint32_t stage = smem_u32(smem + L::STAGE_OFF + (warp - 2) * 4096);
+    // Stream-K: this warp's partial rows / chunks in a pair's slot, and its flag.
+    const int wslot = static_cast<int>(rank) * 8 + (warp - 2);
+    auto part_at = [&](int slot, int c) {
+      return p.sk_part + ((static_cast<size_t>(slot) * 8 + c) * 256 + row_in_tile) * 32;
+    };
     int tc = 0;
-    for (int t = pair; t < num_tiles; t += npairs, ++tc) {
+    SegIter segs(p.sk != 0, pair, npairs, num_tiles, num_kb);
+    Seg sg;
+    for (; segs.next(sg); ++tc) {
+      const int t = sg.t;
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
       const int m_blk = t % num_m, n_blk = t / num_m;
       const int row = m_blk * 256 + row_in_tile;
       const int n0 = n_blk * 256;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
-      const bool ok = gemm_epilogue_tile_staged(p, taddr, row - lane, lane, n0, half * 4, stage, [&]() {
-        if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) return false;
-        tc_fence_after();
-        return true;
-      });
+      bool ok;
+      if (sg.producer) {
+        // This pair's partial of the tile into its slot, then the flag.
+        ok = mbar_wait(tfull0 + 8 * acc, aph, abort_flag);
+        if (ok) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = half * 4; c < half * 4 + 4; ++c) {
+            float v[32];
+            tmem_ld32(taddr + c * 32, v);
+            tmem_wait_ld();
+            float4* dst = reinterpret_cast<float4*>(part_at(pair, c));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) st_release_gpu(p.sk_flags + pair * 16 + wslot, 1);
+        }
+      } else {
+        // Finisher: the lower pairs that hold the tile's other k-blocks.
+        const int tile_lo = (t - segs.sk_base) * num_kb;
+        int q_lo = pair;   // producers are pairs [q_lo, pair) (every share is non-empty)
+        if (sg.finisher) {
+          for (int qq = pair - 1; qq >= 0; --qq) {
+            if (segs.share_lo(qq + 1, npairs) <= tile_lo) break;
+            q_lo = qq;
+          }
+        }
+        ok = gemm_epilogue_tile_staged(p, taddr, row - lane, lane, n0, half * 4, stage, [&]() {
+          if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) return false;
+          tc_fence_after();
+          // Every lane acquires each producer's flag itself, so that its
+          // own loads of the partial are ordered after the producer's stores.
+          for (int qq = q_lo; qq < pair; ++qq)
+            if (!__all_sync(0xffffffffu, sk_wait_flag(p.sk_flags + qq * 16 + wslot, abort_flag))) return false;
+          return true;
+        }, [&](int c, float (&v)[32]) {
+#pragma unroll 1
+          for (int qq = pair - 1; qq >= q_lo; --qq) {   // fixed order: highest pair first
+            const float4* src = reinterpret_cast<const float4*>(part_at(qq, c));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 x = __ldcg(src + j);
+              v[4 * j] += x.x;
+              v[4 * j + 1] += x.y;
+              v[4 * j + 2] += x.z;
+              v[4 * j + 3] += x.w;
+            }
+          }
+        });
+        if (ok && q_lo < pair) {
+          __syncwarp();
+          if (lane == 0)
+            for (int qq = q_lo; qq < pair; ++qq) p.sk_flags[qq * 16 + wslot] = 0;   // consumed
+        }
+      }
       if (!ok) break;
       tc_fence_before();
       __syncwarp();

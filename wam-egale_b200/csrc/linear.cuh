@@ -82,17 +82,11 @@ inline int launch_gemm_cl(const CUtensorMap& ta, const CUtensorMap* tb, const Ge
 }
 
 // Two-CTA launch: clusters of 2 along x, one cluster per pair of SMs.
-template <bool F8>
-inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p, int sms,
-                        cudaStream_t stream) {
-  static int resident[64] = {};  // co-resident clusters per device, 0 = not queried
-  int dev = 0;
-  WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+inline cudaLaunchConfig_t gemm2_config(cudaStream_t stream, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = Gemm2Smem::TOTAL;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -101,16 +95,59 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Co-resident clusters (SM pairs) of the two-CTA kernel on the current
+// device (queried once per device; 74 on B200). It is also the number of
+// stream-K partial slots a launch needs.
+template <bool F8>
+inline int gemm2_resident(int sms) {
+  static int resident[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (resident[dev] == 0) {
-    WAMB_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<F8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Gemm2Smem::TOTAL));
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = gemm2_config(nullptr, attr);
     cfg.gridDim = dim3(sms, 1, 1);
     int n = 0;
-    WAMB_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<F8>, &cfg));
-    resident[dev] = n > 0 ? n : 1;
+    if (cudaFuncSetAttribute(gemm_tc2_kernel<F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Smem::TOTAL) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<F8>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    resident[dev] = n > 0 ? n : -1;
   }
+  return resident[dev] > 0 ? resident[dev] : 0;
+}
+
+// Stream-K scratch: one flag per epilogue warp of each pair (zero between
+// launches), then one 256 x 256 fp32 partial per pair.
+constexpr size_t SK_FLAG_BYTES = 128 * 16 * 4;    // up to 128 pairs
+constexpr size_t SK_SLOT_BYTES = 256 * 256 * 4;
+inline size_t sk_part_bytes(int sms) {
+  const int r = std::max(gemm2_resident<false>(sms), gemm2_resident<true>(sms));
+  return static_cast<size_t>(r > 0 ? r : sms / 2) * SK_SLOT_BYTES;
+}
+
+struct SkBuffers {
+  int* flags = nullptr;     // SK_FLAG_BYTES, zero
+  float* part = nullptr;    // sk_part_bytes()
+  size_t part_bytes = 0;
+};
+
+template <bool F8>
+inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p, int sms,
+                        cudaStream_t stream) {
+  const int resident = gemm2_resident<F8>(sms);
+  WAMB_REQUIRE(resident > 0, WAMB_ERR_CUDA, "two-CTA GEMM cannot be resident on this device");
+  WAMB_REQUIRE(!p.sk || resident <= 128, WAMB_ERR_CUDA, "stream-K supports at most 128 SM pairs");
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = gemm2_config(stream, attr);
   const int tiles = ((p.M + 255) / 256) * (p.N / 256);
-  const int pairs = tiles < resident[dev] ? tiles : resident[dev];
+  // Stream-K shares the last round over every resident pair (one partial slot each).
+  const int pairs = p.sk ? resident : (tiles < resident ? tiles : resident);
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<F8>, ta, tb[0], tb[1], tb[2], p));
@@ -177,11 +214,21 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
 }
 
 // Whether a GEMM of this shape takes the 2-CTA kernel: 256 x 256 tiles when
-// the weight groups split into 256-wide tiles and there are enough of them
-// to give every SM pair one.
-inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms) {
+// the weight groups split into 256-wide tiles and M >= 512, and either
+// stream-K is used (every pair then gets an equal share of the last round)
+// or there are enough tiles to give every SM pair one.
+inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms, bool sk = false) {
   const long long pair_tiles = ((M + 255) / 256) * (N / 256);
-  return M >= 512 && n_per_group % 256 == 0 && pair_tiles >= sms / 2;
+  return M >= 512 && n_per_group % 256 == 0 && (sk || pair_tiles >= sms / 2);
+}
+
+// Whether stream-K pays for a pair GEMM: when the tiles do not divide
+// evenly over the pairs (a partly filled last round), and the remaining
+// tiles have at least one k-block for every pair (no share is empty).
+inline bool gemm_use_sk(int M, long long N, int num_kb, int sms) {
+  const int r = gemm2_resident<false>(sms);
+  const long long tiles = ((M + 255) / 256) * (N / 256);
+  return M >= 512 && r > 0 && tiles % r != 0 && (tiles % r) * num_kb >= r;
 }
 
 // w_early: the caller guarantees that the weights were last written two or
@@ -190,8 +237,10 @@ inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms) {
 // out_gstride != 0: weight group g writes its n_per_group columns to
 // out + g * out_gstride elements (separate outputs of one launch, ldo each).
 // trigger_after: GemmParams::trigger_after.
+// sk: stream-K scratch (flags zero on entry); null or too small: no stream-K.
 inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_early = false,
-                       bool trigger = false, long long out_gstride = 0, bool trigger_after = false) {
+                       bool trigger = false, long long out_gstride = 0, bool trigger_after = false,
+                       const SkBuffers* sk = nullptr) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->groups >= 1 && a->groups <= 3, WAMB_ERR_ARG, "groups must be 1..3");
   WAMB_REQUIRE(a->m >= 0 && a->k > 0 && a->n_per_group > 0, WAMB_ERR_SHAPE, "bad M/K/N");
@@ -235,7 +284,10 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   int rc = device_info(&di);
   if (rc) return rc;
 
-  const bool pair = gemm_is_pair(a->m, N, a->n_per_group, di.sms);
+  const bool sk_ok = sk != nullptr && sk->flags != nullptr && sk->part != nullptr && a->n_per_group % 256 == 0 &&
+                     sk->part_bytes >= sk_part_bytes(di.sms) &&
+                     gemm_use_sk(a->m, N, a->k / (f8 ? GEMM_BK8 : GEMM_BK), di.sms);
+  const bool pair = gemm_is_pair(a->m, N, a->n_per_group, di.sms, sk_ok);
   const int num_kb = a->k / (f8 ? GEMM_BK8 : GEMM_BK);
   TilePlan tp{256, 1, num_kb};
   if (!pair) tp = plan_tiles(a->m, static_cast<int>(N), a->n_per_group, num_kb, di.sms, f8);
@@ -280,6 +332,11 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   p.kb_per_split = tp.kb_per_split;
   p.out_gstride = out_gstride;
   p.trigger_after = trigger_after ? 1 : 0;
+  if (pair && sk_ok) {
+    p.sk = 1;
+    p.sk_flags = sk->flags;
+    p.sk_part = sk->part;
+  }
   auto launch = [&](auto f8c) {
     constexpr bool F8 = decltype(f8c)::value;
     if (pair) return launch_gemm2<F8>(ta, tb, p, di.sms, stream);

@@ -42,7 +42,7 @@ extern "C" {
 
 const char* wamb_last_error(void) { return wamb::g_last_error.c_str(); }
 
-int wamb_abi_version(void) { return 105; }
+int wamb_abi_version(void) { return 106; }
 
 int wamb_device_status(void* stream, int* device_code) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -56,7 +56,24 @@ int wamb_device_status(void* stream, int* device_code) {
 }
 
 int wamb_linear(const wamb_linear_args* args, void* stream) {
-  return wamb::linear_impl(args, static_cast<cudaStream_t>(stream));
+  using namespace wamb;
+  if (args == nullptr || args->sk_workspace == nullptr) return linear_impl(args, static_cast<cudaStream_t>(stream));
+  WAMB_REQUIRE(reinterpret_cast<uintptr_t>(args->sk_workspace) % 256 == 0, WAMB_ERR_ALIGN,
+               "sk_workspace must be 256-byte aligned");
+  SkBuffers sk;
+  if (args->sk_workspace_bytes >= SK_FLAG_BYTES) {
+    uint8_t* w = static_cast<uint8_t*>(args->sk_workspace);
+    sk.flags = reinterpret_cast<int*>(w);
+    sk.part = reinterpret_cast<float*>(w + SK_FLAG_BYTES);
+    sk.part_bytes = args->sk_workspace_bytes - SK_FLAG_BYTES;
+  }
+  return linear_impl(args, static_cast<cudaStream_t>(stream), false, false, 0, false, &sk);
+}
+
+size_t wamb_linear_sk_bytes(void) {
+  wamb::DeviceInfo di;
+  if (wamb::device_info(&di) != WAMB_OK) return 0;
+  return wamb::SK_FLAG_BYTES + wamb::sk_part_bytes(di.sms);
 }
 
 int wamb_quantize_rows(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, int32_t k, void* out,

@@ -28,6 +28,7 @@ class LinearArgs(ctypes.Structure):
         ("temb_len", c_int32), ("rows_per_batch", c_int32), ("gate_index", c_int32),
         ("dim", c_int32),
         ("a_is_fp8", c_int32), ("a_scale", c_void_p), ("w_scale", c_void_p * 3),
+        ("sk_workspace", c_void_p), ("sk_workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -94,16 +95,16 @@ class BlockArgs(ctypes.Structure):
 # Workspace taps (enum wamb_tap).
 TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", "cross_k",
         "cross_v", "cross_attention", "residual2", "modulated3", "gelu", "kv_slots",
-        "kv_tiles", "kv_counts", "a8", "a8_scale")
+        "kv_tiles", "kv_counts", "a8", "a8_scale", "sk_flags", "sk_part")
 
 # Weight slots the FP8 path reads as E4M3 (self q/k/v/out, cross q/out, FFN).
 FP8_WEIGHTS = (3, 5, 7, 9, 13, 19, 23, 25)
 
-ABI_VERSION = 105
+ABI_VERSION = 106
 
 # Every symbol include/wamb.h declares; tests check the library exports them.
 EXPORTED = (
-    "wamb_last_error", "wamb_abi_version", "wamb_device_status", "wamb_linear",
+    "wamb_last_error", "wamb_abi_version", "wamb_device_status", "wamb_linear", "wamb_linear_sk_bytes",
     "wamb_attention", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
     "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc", "wamb_quantize_rows",
     "wamb_timestep_embedding", "wamb_silu", "wamb_embed_gather", "wamb_output_norm", "wamb_copy_cols",
@@ -134,6 +135,7 @@ def load():
     lib.wamb_abi_version.restype = c_int32
     lib.wamb_device_status.argtypes = [c_void_p, ctypes.POINTER(c_int32)]
     lib.wamb_linear.argtypes = [ctypes.POINTER(LinearArgs), c_void_p]
+    lib.wamb_linear_sk_bytes.restype = ctypes.c_size_t
     lib.wamb_attention.argtypes = [ctypes.POINTER(AttentionArgs), c_void_p]
     lib.wamb_block_workspace_bytes.argtypes = [ctypes.POINTER(BlockArgs)]
     lib.wamb_block_workspace_bytes.restype = ctypes.c_size_t

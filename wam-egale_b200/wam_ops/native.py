@@ -22,13 +22,15 @@ def workspace(device, nbytes):
     run one after another on the stream, so they can reuse it). A buffer that
     is outgrown is retired, never freed: a CUDA graph captured with it (e.g.
     the 1-row target forward of a speculative loop, captured before the
-    7-row one grew the workspace) keeps a valid address."""
+    7-row one grew the workspace) keeps a valid address. New buffers are
+    zero-filled: the library keeps its stream-K flags (the first bytes of
+    every layout) zero between calls."""
     key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
     buf = _WORKSPACES.get(key)
     if buf is None or buf.numel() < nbytes:
         if buf is not None:
             _RETIRED.append(buf)
-        buf = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=torch.device("cuda", key))
+        buf = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=torch.device("cuda", key))
         _WORKSPACES[key] = buf
     return buf
 

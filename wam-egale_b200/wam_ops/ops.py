@@ -16,6 +16,20 @@ def _bf16_2d(t, name):
         raise ValueError(f"{name} must be 2-D with unit column stride")
 
 
+_SK = {}
+
+
+def sk_workspace(device):
+    """Zero-filled stream-K scratch of wamb_linear on `device` (one per
+    device; calls on one stream are ordered, so they share it)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _SK.get(idx)
+    if buf is None:
+        n = _lib.load().wamb_linear_sk_bytes()
+        buf = _SK[idx] = torch.zeros(max(n, 1), dtype=torch.uint8, device=torch.device("cuda", idx))
+    return buf
+
+
 def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
            table=None, temb=None, rows_per_batch=None, gate_index=0, a_scale=None, w_scales=None):
     """out = epilogue(a @ cat(weights).T + cat(biases)) on the tcgen05 GEMM.
@@ -30,7 +44,9 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
 
     Small M: when the output tiles would leave SMs idle, K is split across
     the CTAs of a thread-block cluster (partials summed in split order in
-    shared memory, so results do not depend on timing).
+    shared memory, so results do not depend on timing). M >= 512: the
+    two-CTA kernel, with stream-K over every SM pair when the tiles leave
+    the last round partly filled (scratch from sk_workspace()).
     """
     out_f32 = out is not None and out.dtype == torch.float32
     if isinstance(weights, torch.Tensor):
@@ -75,6 +91,9 @@ def linear(a, weights, biases=None, epilogue=_lib.EPI_BIAS, out=None, res=None,
     args.ldo = out.stride(0)
     args.out_is_f32 = int(out_f32)
     args.epilogue = epilogue
+    if m >= 512:
+        sk = sk_workspace(a.device)
+        args.sk_workspace, args.sk_workspace_bytes = sk.data_ptr(), sk.numel()
     if fp8:
         args.a_is_fp8 = 1
         args.a_scale = a_scale.data_ptr()
