@@ -524,85 +524,139 @@ def run_config(args):
 
 
 def run_verify(args):
-    """--workload cfg3: one 30-layer speculative-verify step on 1 GPU: 4
-    candidate chunks x 32 action tokens attending to a read-only 3520-token
-    history (candidate_cache_rows = [0, 0, 0, 0]) plus their own K/V, 512
+    """--workload cfg3: one 30-layer speculative-verify step: 4 candidate
+    chunks x 32 action tokens attending to a read-only 3520-token history
+    (candidate_cache_rows = 0 for every candidate) plus their own K/V, 512
     prepared context tokens, per-token temb. HBM-bound (weight streaming):
-    the roofline line is bytes / time against the measured copy bandwidth."""
+    the roofline line is bytes / time against the measured copy bandwidth.
+    Under torchrun the candidates are split over the ranks (2 + 2 on 2
+    GPUs): rank 0's KV history is NCCL-broadcast once into every rank's own
+    memory before timing, each rank verifies its candidates, and their
+    outputs are all-gathered after every step on a side stream."""
     from wam_ops import _lib, configs
+    from wam_ops.rollouts import broadcast_cache, shard
     from wam_ops.stack import NativeStack
 
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
     cfg = configs.PRESETS["cfg3"]
-    B, Q, D, F = cfg.candidates, cfg.tokens, cfg.dim, cfg.ffn
+    B_all, Q, D, F = cfg.candidates, cfg.tokens, cfg.dim, cfg.ffn
+    mine = list(shard(B_all, world, rank))
+    B = len(mine)
     gen = torch.Generator(device=dev).manual_seed(4321)
     torch.set_grad_enabled(False)
     blocks = configs.build_blocks(cfg, dev, seed=4321)
     configs.fill_history(blocks, cfg, dev, gen, pool_batch=1)
+    bcast = None
+    if pg is not None:
+        torch.cuda.synchronize()
+        pg.barrier()
+        t0 = time.perf_counter()
+        nbytes = broadcast_cache(blocks, src=0)
+        torch.cuda.synchronize()
+        bcast = {"bytes_per_rank": nbytes, "ms": 1000.0 * (time.perf_counter() - t0)}
     stack = NativeStack(blocks, fp8=args.fp8)
     ctx = torch.randn(1, cfg.context, D, generator=gen, device=dev).bfloat16()
     stack.prepare_context(ctx)
-    x = torch.randn(B, Q, D, generator=gen, device=dev).bfloat16()
-    temb = configs.make_temb(cfg, B, dev, gen, per_token=Q)
+    x_all = torch.randn(B_all, Q, D, generator=gen, device=dev).bfloat16()
+    temb_all = configs.make_temb(cfg, B_all, dev, gen, per_token=Q)
+    x, temb = x_all[mine].contiguous(), temb_all[mine].contiguous()
     rope = configs.chunk_rope(cfg, f_shift=cfg.history_chunks).to(dev)
     rows = torch.zeros(B, dtype=torch.int64, device=dev)
     static = stack.capture(x, ctx, temb, rope, candidate_cache_rows=rows, warmup=1)
-    for _ in range(args.warmup):
+    gather = ActionGather(static["out"], Q, world) if pg is not None else None
+
+    def step():
         stack.replay()
+        if gather is not None:
+            gather()
+
+    for _ in range(args.warmup):
+        step()
+    if gather is not None:
+        gather.drain()
     torch.cuda.synchronize()
     if _lib.device_status() != 0:
         raise RuntimeError("device error during warm-up")
-    clocks = Clocks(0)
+    clocks = Clocks(local)
     stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if pg is not None:
+        pg.barrier()
     clocks.start()
     time.sleep(0.3)
-    e0.record(stream)
-    for _ in range(args.steps):
-        stack.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
+
+    def timed():
+        for _ in range(args.steps):
+            step()
+        if gather is not None:
+            gather.drain()
+    ms = time_graph(timed, 1, stream) / args.steps
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
     hx, ht = x.cpu().pin_memory(), temb.cpu().pin_memory()
     hout = torch.empty(B, Q, D, dtype=torch.bfloat16).pin_memory()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(args.steps):
-        static["x"].copy_(hx, non_blocking=True)
-        static["temb"].copy_(ht, non_blocking=True)
-        stack.replay()
-        hout.copy_(static["out"], non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1) / args.steps
-    # Algorithmic bytes of one step: every GEMM weight once (self q/k/v/out,
-    # cross q/out, FFN), the visible history K/V once, the prepared cross K/V.
+
+    def e2e_steps():
+        for _ in range(args.steps):
+            static["x"].copy_(hx, non_blocking=True)
+            static["temb"].copy_(ht, non_blocking=True)
+            step()
+            hout.copy_(static["out"], non_blocking=True)
+        if gather is not None:
+            gather.drain()
+    if pg is not None:
+        pg.barrier()
+    ms_e2e = time_graph(e2e_steps, 1, stream) / args.steps
+    if pg is not None:
+        t = torch.tensor([ms, ms_e2e], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms, ms_e2e = t.tolist()
+    dev_code = _lib.device_status()
+    # Algorithmic bytes of one step on one GPU: every GEMM weight once (self
+    # q/k/v/out, cross q/out, FFN), the visible history K/V once, the
+    # prepared cross K/V (each GPU streams all of them for its candidates).
     wbytes = 1 if args.fp8 else 2
     hist = cfg.history_chunks * configs.PRESETS["cfg2"].tokens
     per_layer = (6 * D * D + 2 * D * F) * wbytes + hist * D * 2 * 2 + cfg.context * D * 2 * 2
     step_bytes = per_layer * cfg.layers
     pk, pk_kind = peaks()
     achieved = step_bytes / (ms / 1000.0) / 1e9
-    line = {"metric": "verify_steps_per_s", "value": 1000.0 / ms, "unit": "verify-steps/s", "n_gpus": 1,
+    if pg is not None:
+        del gather, static, stack
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {"metric": "verify_steps_per_s", "value": 1000.0 / ms, "unit": "verify-steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "fp8-e4m3 GEMMs, bf16 attention" if args.fp8 else "bf16",
             "data": "synthetic (seeded weights N(0,0.02), random unit-scale KV history)",
             "config": {"workload": "cfg3: 30-layer verify of 4 candidates x 32 action tokens over a "
                                    "read-only 3520-token history, 512 context tokens",
-                       "global_batch": B, "seq_len": Q, "kv_history": hist, "context": cfg.context,
+                       "global_batch": B_all, "seq_len": Q, "kv_history": hist, "context": cfg.context,
+                       "parallelism": (f"candidates split {B}/GPU, history NCCL-broadcast once, "
+                                       "candidate outputs all-gathered each step" if world > 1
+                                       else "one GPU"),
+                       "history_broadcast": bcast,
                        "l2": "inputs larger than L2 (weights streamed every step)"},
-            "roofline": {"kernel": "whole step (GEMM weight streaming dominates)", "bound": "hbm",
+            "roofline": {"kernel": "whole step on one GPU (GEMM weight streaming dominates)", "bound": "hbm",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": None,
                          "peak_source": f"{pk_kind} HBM copy", "algorithmic_bytes_per_step": step_bytes},
             "e2e": {"value": 1000.0 / ms_e2e, "unit": "verify-steps/s", "ms_per_step": ms_e2e,
-                    "h2d_bytes_per_step": hx.numel() * 2 + ht.numel() * 4,
-                    "d2h_bytes_per_step": hout.numel() * 2},
-            "gpu_launches": stack.launches_per_step(with_cache=True) * args.steps,
-            "clocks": clk, "device_error": _lib.device_status()}
+                    "h2d_bytes_per_step": (hx.numel() * 2 + ht.numel() * 4) * world,
+                    "d2h_bytes_per_step": hout.numel() * 2 * world},
+            "gpu_launches": NativeStack.launches_per_layer(True, args.fp8) * cfg.layers * args.steps,
+            "clocks": clk, "device_error": dev_code}
     print(json.dumps(line), flush=True)
     return 0
 

@@ -1,10 +1,17 @@
-"""Rollout sharding across GPUs (one process per GPU).
+"""Rollout and draft-branch sharding across GPUs (one process per GPU).
 
 Independent rollouts (and speculative draft branches) are the only axis the
 denoise step shards on: every rank holds the full weights and its own
 contiguous slice of rollouts with their KV pools, runs the step with no
 data-path collective, and the per-rollout action outputs are all-gathered
 afterwards (NCCL over NVLink on GPUs; gloo works for CPU tests).
+
+Candidate verification on several GPUs (a speculative verify batch split
+across ranks, the candidate path of model.py:624-660 and
+wan_va_server.py:1906-1930) needs the candidates' shared, read-only KV
+history on every rank: broadcast_cache copies each layer's cache from one
+rank into the others' own memory once, and shard() gives each rank its
+candidates.
 """
 import torch
 import torch.distributed as dist
@@ -35,3 +42,24 @@ def gather_actions(hidden, action_tokens, group=None):
     else:
         dist.all_gather(list(out.chunk(world)), local, group=group)
     return out
+
+
+def broadcast_cache(blocks, src=0, cache_name="pos", group=None):
+    """Broadcast every layer's self-attention cache (k, v, id, mask,
+    is_pred) from rank `src` into the same tensors on the other ranks, once
+    (each rank then reads its own copy; nothing crosses the links during a
+    step). The caches must exist on every rank with equal shapes. Returns
+    the bytes received per rank."""
+    nbytes = 0
+    for blk in blocks:
+        cache = blk.attn1.attn_caches[cache_name]
+        for name in ("k", "v", "id", "mask", "is_pred"):
+            t = cache[name]
+            if t.dtype == torch.bool:
+                # gloo has no bool reduction type; the bytes are the same
+                view = t.view(torch.uint8)
+                dist.broadcast(view, src, group=group)
+            else:
+                dist.broadcast(t, src, group=group)
+            nbytes += t.numel() * t.element_size()
+    return nbytes

@@ -96,14 +96,18 @@ class NativeStack:
         self.graph.replay()
         return self._static["out"]
 
+    @staticmethod
+    def launches_per_layer(with_cache, fp8, cross_prepared=True):
+        """Kernel launches of one layer (see launches_per_step)."""
+        return 13 + (1 if with_cache else 0) + (0 if cross_prepared else 3) + (3 if fp8 else 0)
+
     def launches_per_step(self, with_cache, cross_prepared=True):
         """Kernel launches of one step (the count bench.py reports): per layer
         LN1, QKV, RMS+RoPE, attention, O, LN2, cross-Q, RMS, cross attention,
         cross-O, LN3, FFN1, FFN2 = 13, + KV layout with a cache, + 3 when the
         cross K/V is computed per call, + 3 row-quantize passes (self and cross
         attention output, GELU output) in fp8 mode."""
-        per = 13 + (1 if with_cache else 0) + (0 if cross_prepared else 3) + (3 if self.fp8 else 0)
-        return per * len(self.layers)
+        return self.launches_per_layer(with_cache, self.fp8, cross_prepared) * len(self.layers)
 
 
 def device_error():
