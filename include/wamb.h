@@ -173,9 +173,23 @@ typedef struct wamb_attention_args {
   int32_t src0_len;
   const void* k1; const void* v1; int64_t ld1; int32_t k1_col, v1_col;
   void* out; int64_t ldo;
+  /* Optional split-key scratch (NULL: none) of
+   * wamb_attention_split_bytes(args) bytes, 256-byte aligned and zero-filled
+   * before its first use (the library leaves its counters zero after every
+   * call). With it, when the (query tile pair, head, batch row) items alone
+   * would leave SMs idle, each item's keys are split over kv_splits CTAs
+   * (0: chosen by the library, 1: never) whose partial softmax results the
+   * last of them merges in split order (results do not depend on timing).
+   * Not used with candidate rows (src0_map). Calls sharing it must be
+   * ordered on one stream. */
+  void* split_workspace;
+  size_t split_workspace_bytes;
+  int32_t kv_splits;
 } wamb_attention_args;
 
 WAMB_API int wamb_attention(const wamb_attention_args* args, void* stream);
+/* Bytes of split_workspace that this call shape needs (0: it never splits). */
+WAMB_API size_t wamb_attention_split_bytes(const wamb_attention_args* args);
 
 /*
  * One Wan-DiT transformer block forward (WanTransformerBlock.forward,
@@ -283,9 +297,11 @@ enum wamb_tap {
   WAMB_TAP_KV_COUNTS = 14,  /* [2] int32: tiles, visible slots */
   WAMB_TAP_A8 = 15,         /* fp8 only: [M, F] E4M3, the last quantized GEMM input */
   WAMB_TAP_A8_SCALE = 16,   /* fp8 only: [M] fp32 per-row scales of WAMB_TAP_A8 */
-  WAMB_TAP_SK_FLAGS = 17,   /* stream-K flags of the two-CTA GEMMs (offset 0 in every layout) */
+  WAMB_TAP_SK_FLAGS = 17,   /* zero region at offset 0 of every layout: stream-K flags of the
+                               two-CTA GEMMs, then split-key counters of the self attention */
   WAMB_TAP_SK_PART = 18,    /* stream-K fp32 partials (M >= 512 only) */
-  WAMB_TAP_COUNT = 19
+  WAMB_TAP_ATTN_PART = 19,  /* split-key partials of the self attention (small batches only) */
+  WAMB_TAP_COUNT = 20
 };
 
 WAMB_API size_t wamb_block_workspace_bytes(const wamb_block_args* args);

@@ -63,7 +63,7 @@ def test_workspace_layout():
     assert total == lib.wamb_block_workspace_bytes(a)
     M, D, F = 48, 256, 512
     assert offs[_lib.TAPS.index("sk_flags")] == 0           # stream-K flags first in every layout
-    assert offs[_lib.TAPS.index("modulated1")] == 8192
+    assert offs[_lib.TAPS.index("modulated1")] == 16384         # after the 16 KB zero region
     assert offs[_lib.TAPS.index("sk_part")] == -1           # M < 512: no two-CTA GEMM
     assert offs[_lib.TAPS.index("kv_slots")] == -1          # no cache
     assert offs[_lib.TAPS.index("norm2")] >= 0

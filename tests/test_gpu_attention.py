@@ -7,7 +7,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from wam_ops import ops
+from wam_ops import _lib, ops
 
 pytestmark = pytest.mark.gpu
 
@@ -176,3 +176,30 @@ def test_candidate_grouped(cuda_device, Q, rows, pool, vis):
     from wam_ops import _lib
     assert _lib.device_status() == 0
     _check(out.view(B, Q, H, 128), _sdpa_ref(q, k, v))
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk,splits", [
+    (1, 24, 880, 4400, 0),     # one cfg2 chunk: the library picks 3 splits
+    (1, 3, 300, 1000, 2),      # two-tile items and a single-tile item
+    (2, 2, 100, 700, 4),       # single-tile items only, 4 splits
+    (1, 2, 256, 512, 3),       # splits of one or two key tiles
+])
+def test_split_keys(cuda_device, B, H, Sq, Sk, splits):
+    """Split-key attention (the CTAs of one (query tile pair, head) item
+    take consecutive key ranges and the last of them merges the partials)
+    against torch SDPA, bitwise repeatable, with the counters left zero."""
+    g = torch.Generator(device="cuda").manual_seed(Sq * 31 + Sk + splits)
+    q = torch.randn(B, Sq, H, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, Sk, H, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, Sk, H, 128, device="cuda", generator=g).bfloat16()
+    args = dict(heads=H, q_rows=Sq, src0_batch_stride=Sk, src0_len=Sk, kv_splits=splits)
+    run = lambda: ops.attention(q.view(B * Sq, H * 128), k.view(B * Sk, H * 128),  # noqa: E731
+                                v.view(B * Sk, H * 128), **args)
+    out, again = run(), run()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    _check(out.view(B, Sq, H, 128), _sdpa_ref(q, k, v))
+    assert torch.equal(out, again)
+    ws = ops._SPLIT.get(torch.cuda.current_device())
+    if ws is not None:
+        assert bool((ws[:8192] == 0).all())

@@ -167,12 +167,12 @@ def _sk_flags_zero(dev):
 
 
 @pytest.mark.parametrize("m,k,n,groups", [
-    (880, 3072, 3072, 1),      # 48 tiles over 74 pairs: every tile split
-    (880, 14336, 3072, 1),     # FFN2 shape: 224 k-blocks per tile
-    (880, 3072, 3072, 3),      # QKV shape: three weight groups, one full round + 70 tiles
-    (512, 64, 256, 1),         # too few units to share: the one-CTA path
-    (2000, 1536, 1536, 1),     # D 1536 shapes, ragged last row block
-    (7040, 3072, 14336, 1),    # 1568 tiles: 21 full rounds + 14 shared tiles
+    (880, 14336, 3072, 1),     # FFN2 shape: 48 tiles over 74 pairs, 224 k-blocks each
+    (880, 8192, 3072, 3),      # three weight groups: one full round + 70 shared tiles
+    (2000, 8960, 1536, 1),     # D 1536 FFN2 shape, ragged last row block
+    (7040, 14336, 3072, 1),    # 336 tiles: 4 full rounds + 40 shared tiles
+    (880, 3072, 3072, 1),      # K 3072: no stream-K (the one-CTA path)
+    (512, 8192, 256, 1),       # too few tiles to share: no stream-K
 ])
 def test_linear_stream_k(cuda_device, m, k, n, groups):
     g = torch.Generator(device="cuda").manual_seed(m + k + n)
@@ -189,12 +189,12 @@ def test_linear_stream_k(cuda_device, m, k, n, groups):
 
 
 def test_linear_stream_k_epilogues(cuda_device):
-    """Gated fp32 residual (the O projection at M 880) and GELU through the
-    stream-K path, against the fp32 reference."""
-    m, k, n, B = 880, 3072, 3072, 2
+    """Gated fp32 residual (the FFN output projection at M 880) and GELU
+    through the stream-K path, against the fp32 reference."""
+    m, k, n, B = 880, 14336, 3072, 2
     g = torch.Generator(device="cuda").manual_seed(5)
     a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
-    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.01).bfloat16()
     b = torch.randn(n, device="cuda", generator=g).bfloat16()
     res = torch.randn(m, n, device="cuda", generator=g)
     table = torch.randn(6, n, device="cuda", generator=g) * 0.1
@@ -209,12 +209,12 @@ def test_linear_stream_k_epilogues(cuda_device):
     base = _ref(a, [w], [b])
     gate = (table[2][None, None] + temb[:, :, 2]).expand(B, m // B, n).reshape(m, n)
     err = (out - (res + base * gate)).abs().max().item()
-    assert err <= 2e-3, err
+    assert err <= 5e-3, err
     _close(gelu, torch.nn.functional.gelu(base, approximate="tanh"))
 
 
 def test_linear_stream_k_fp8(cuda_device):
-    m, k, n = 880, 3072, 3072
+    m, k, n = 880, 16384, 3072     # 128 E4M3 k-blocks
     g = torch.Generator(device="cuda").manual_seed(6)
     a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
     w = (torch.randn(n, k, device="cuda", generator=g) * 0.05).bfloat16()

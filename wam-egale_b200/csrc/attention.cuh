@@ -136,7 +136,24 @@ struct AttnParams {
   // tile holding all G candidates, split the key tiles (source 0, then the
   // G candidates' own keys as one block-diagonal tile) and merge (m, l, O).
   int group;
+  // Split keys (ungrouped kernel, kv_splits > 1, blockIdx.z = batch row x
+  // kv_splits + split): when the query tiles alone would leave SMs idle,
+  // each (query tile pair, head, batch row) item is computed by kv_splits
+  // CTAs over consecutive key-tile ranges. Each writes its rows' partial
+  // (O relative to its max m, unnormalized, and m, l) to its slot of
+  // kv_part ([item][split] x ATT_PART_BYTES); the CTA that brings the item's
+  // counter in kv_count (zero between launches) to kv_splits merges the
+  // partials in split order, writes the output and resets the counter.
+  int kv_splits;
+  float* kv_part;
+  int* kv_count;
 };
+
+// One split-key partial: O [32 four-column groups][256 rows][4] fp32 (so
+// that for a fixed group the threads of consecutive rows touch one
+// contiguous run), then m [256] and l [256].
+constexpr size_t ATT_PART_FLOATS = 256 * 128 + 2 * 256;
+constexpr size_t ATT_PART_BYTES = ATT_PART_FLOATS * 4;
 
 struct AttnSmem {
   static constexpr uint32_t Q_OFF = 0;                                    // Q_A, Q_B
@@ -218,12 +235,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   auto slot_phase = [&](int L) { return static_cast<uint32_t>((L / ATT_SLOTS) & 1); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_split = reinterpret_cast<volatile int*>(tmem_slot + 2);   // split keys: this CTA merges
 
   if (p.trigger) pdl_trigger();
   pdl_wait();   // the tile list and Q/K/V of the previous kernels are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z, h = blockIdx.y;
+  const int S = !GROUPED && p.kv_splits > 1 ? p.kv_splits : 1;
+  const int b = blockIdx.z / S, sidx = blockIdx.z - b * S, h = blockIdx.y;
   const int q0 = blockIdx.x * 256;
+  const int item = (b * gridDim.y + h) * gridDim.x + blockIdx.x;   // split keys: the item's counter / slots
   const int n0 = p.tiles != nullptr ? *p.n_tiles : (p.src0_len + 127) / 128;
   // Grouped candidates: the cluster's G batch rows share their source-0 row
   // (checked here, so every CTA of the cluster decides alike).
@@ -234,8 +254,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   // Key tiles of this CTA: [kv_lo, kv_lo + n) of the tile space (source 0,
   // then source 1; grouped: source 0, then the group's own-key tile n0).
   const int n_all = grouped ? n0 + 1 : n0 + (p.has_src1 ? (p.q_rows + 127) / 128 : 0);
-  const int kv_lo = grouped ? rank * n_all / G : 0;
-  const int n = grouped ? (rank + 1) * n_all / G - kv_lo : n_all;
+  const int kv_lo = grouped ? rank * n_all / G : sidx * n_all / S;
+  const int n = grouped ? (rank + 1) * n_all / G - kv_lo : (sidx + 1) * n_all / S - kv_lo;
   const bool has_b = !grouped && q0 + 128 < p.q_rows;   // the second query tile holds rows
   auto tile_of = [&](int j) {   // this CTA's j-th key tile
     const int jj = kv_lo + j;
@@ -579,10 +599,32 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           reinterpret_cast<float*>(smem + L::PART_L)[r] = ok ? den : 0.f;
         }
       }
+      if (S > 1) {
+        // Split keys: this CTA's partial of the row (tile A rows only).
+        float* base = p.kv_part + (static_cast<size_t>(item) * S + sidx) * ATT_PART_FLOATS;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float oa[32], ob[32];
+          tmem_ld32(tmem + lane_base + 256 + t * 64 + c * 32, oa);
+          tmem_ld32(tmem + lane_base + 384 + t * 64 + c * 32, ob);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int j = t * 16 + c * 8 + k;   // four-column group
+            reinterpret_cast<float4*>(base)[j * 256 + r] =
+                make_float4(oa[4 * k] * aA + ob[4 * k] * aB, oa[4 * k + 1] * aA + ob[4 * k + 1] * aB,
+                            oa[4 * k + 2] * aA + ob[4 * k + 2] * aB, oa[4 * k + 3] * aA + ob[4 * k + 3] * aB);
+          }
+        }
+        if (t == 0) {
+          base[256 * 128 + r] = ok ? M : -INFINITY;
+          base[256 * 128 + 256 + r] = ok ? den : 0.f;
+        }
+      }
       const float inv = (ok && !*abort_flag && den > 0.f) ? 1.f / den : 0.f;
       const float sA = aA * inv, sB = aB * inv;
       const int qr = q0 + r;
-      const bool store = !grouped && qr < p.q_rows;
+      const bool store = !grouped && S == 1 && qr < p.q_rows;
       __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128 + t * 64;
 #pragma unroll 1
       for (int c = 0; !grouped && c < 2; ++c) {
@@ -627,6 +669,29 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
       reinterpret_cast<float*>(smem + L::PART_M)[r] = ok && n > 0 ? m_used : -INFINITY;
       reinterpret_cast<float*>(smem + L::PART_L)[r] = ok && n > 0 ? l : 0.f;
+    } else if (active && S > 1) {
+      // Split keys: this CTA's partial of tile t's rows (zeros without keys).
+      if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
+      tc_fence_after();
+      float* base = p.kv_part + (static_cast<size_t>(item) * S + sidx) * ATT_PART_FLOATS;
+      const int prow = t * 128 + r;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        if (n > 0) {
+          tmem_ld32(tmem + lane_base + 256 + t * 128 + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          reinterpret_cast<float4*>(base)[(c * 8 + k) * 256 + prow] =
+              make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+      }
+      base[256 * 128 + prow] = ok && n > 0 ? m_used : -INFINITY;
+      base[256 * 128 + 256 + prow] = ok && n > 0 ? l : 0.f;
     } else if (active) {
       if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
       tc_fence_after();
@@ -655,6 +720,55 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   }
 
+  if (S > 1 && warp < 8) {
+    // Split keys: the last of the item's S CTAs to finish merges the S
+    // partials (split order, so the result does not depend on timing).
+    __threadfence();
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    if (threadIdx.x == 0) *last_split = atomicAdd(p.kv_count + item, 1) == S - 1;
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    if (*last_split) {
+      __threadfence();
+      const int prow = threadIdx.x;   // 0..255
+      const int qr = q0 + prow;
+      const bool has_row = (has_b || prow < 128) && qr < p.q_rows;
+      if (has_row) {
+        const float* b0p = p.kv_part + static_cast<size_t>(item) * S * ATT_PART_FLOATS;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(b0p + s2 * ATT_PART_FLOATS + 256 * 128 + prow));
+        float w[8], den = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+          w[s2] = 0.f;
+          if (s2 < S) {
+            const float* bs = b0p + s2 * ATT_PART_FLOATS;
+            const float ms = __ldcg(bs + 256 * 128 + prow);
+            w[s2] = ms == -INFINITY ? 0.f : exp2f(ms - M);
+            den += w[s2] * __ldcg(bs + 256 * 128 + 256 + prow);
+          }
+        }
+        const float inv = (!*abort_flag && den > 0.f) ? 1.f / den : 0.f;
+        __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
+#pragma unroll 1
+        for (int j = 0; j < 32; ++j) {
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int s2 = 0; s2 < 8; ++s2) {
+            if (s2 < S) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(b0p + s2 * ATT_PART_FLOATS) + j * 256 + prow);
+              acc.x += w[s2] * v.x;
+              acc.y += w[s2] * v.y;
+              acc.z += w[s2] * v.z;
+              acc.w += w[s2] * v.w;
+            }
+          }
+          *reinterpret_cast<uint2*>(orow + 4 * j) =
+              make_uint2(pack_bf16(acc.x * inv, acc.y * inv), pack_bf16(acc.z * inv, acc.w * inv));
+        }
+      }
+      if (threadIdx.x == 0) p.kv_count[item] = 0;   // ready for the next launch
+    }
+  }
   if (grouped) {
     // Exchange: CTA `rank` owns the rows of candidate b0 + rank. Each CTA
     // announces the bytes its rows will receive, barrier A (every partial is

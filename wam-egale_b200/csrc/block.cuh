@@ -19,8 +19,51 @@
 namespace wamb {
 
 // ---------------------------------------------------------------- attention
+// Split keys: counters (zero between calls) and partial slots of one call.
+constexpr int ATT_MAX_ITEMS = 2048;
+constexpr size_t ATT_COUNT_BYTES = ATT_MAX_ITEMS * 4;
+struct AttnSplitBuffers {
+  int* count = nullptr;
+  float* part = nullptr;
+  size_t part_bytes = 0;
+};
+
+// Key-split factor of an attention call: 1 unless its (query tile pair,
+// head, batch row) items fill less than one wave of the SMs and a split
+// fills the waves much better (e.g. one 880-row chunk with 24 heads: 96
+// items for 148 SMs, 3 splits make 288 CTAs, 0.97 of two waves), each
+// split keeping at least 4 key tiles. Candidate verification (src0_map)
+// never splits. `force` > 0: that factor (capped by the key tiles).
+inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) {
+  if (a->src0_map != nullptr || a->batch <= 0 || a->q_rows <= 0) return 1;
+  const long long items = static_cast<long long>((a->q_rows + 255) / 256) * a->heads * a->batch;
+  if (items > ATT_MAX_ITEMS) return 1;
+  const long long keys = a->tiles != nullptr ? a->src0_batch_stride : a->src0_len;
+  const int n_est = static_cast<int>((std::max<long long>(keys, 0) + 127) / 128);
+  if (force > 0) return std::max(1, std::min(std::min(force, 8), n_est));
+  if (items >= sms) return 1;
+  auto eff = [&](int S) {
+    const long long ctas = items * S;
+    return static_cast<double>(ctas) / (static_cast<double>((ctas + sms - 1) / sms) * sms);
+  };
+  int best = 1;
+  double best_eff = eff(1);
+  for (int S = 2; S <= 4 && n_est / S >= 4; ++S)
+    if (eff(S) > best_eff + 0.1) {
+      best = S;
+      best_eff = eff(S);
+    }
+  return best;
+}
+inline size_t attn_split_part_bytes(const wamb_attention_args* a, int S) {
+  if (S <= 1) return 0;
+  return static_cast<size_t>((a->q_rows + 255) / 256) * a->heads * a->batch * S * ATT_PART_BYTES;
+}
+
 // trigger: a GEMM that requests weights before its pdl_wait follows.
-inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, bool trigger = false) {
+// split: split-key scratch (counters zero on entry); null: no split.
+inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, bool trigger = false,
+                          const AttnSplitBuffers* split = nullptr) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->batch >= 0 && a->heads > 0 && a->q_rows >= 0, WAMB_ERR_SHAPE, "bad dims");
   if (a->batch == 0 || a->q_rows == 0) return WAMB_OK;
@@ -35,6 +78,7 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
                WAMB_ERR_SHAPE, "row strides too small for the heads");
   WAMB_REQUIRE(a->q_total_rows >= static_cast<int64_t>(a->batch) * a->q_rows, WAMB_ERR_SHAPE,
                "q_total_rows");
+  WAMB_REQUIRE(a->kv_splits >= 0, WAMB_ERR_ARG, "kv_splits must be >= 0");
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -106,6 +150,16 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
     return WAMB_OK;
   }
   p.group = 1;
+  p.kv_splits = 1;
+  if (split != nullptr && split->count != nullptr && split->part != nullptr) {
+    const int S = attn_kv_splits(a, di.sms, a->kv_splits);
+    if (S > 1 && split->part_bytes >= attn_split_part_bytes(a, S)) {
+      p.kv_splits = S;
+      p.kv_part = split->part;
+      p.kv_count = split->count;
+      grid.z = a->batch * S;
+    }
+  }
   return launch_kernel(attn_tc_kernel<false>, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
                        tv1, p);
 }
@@ -217,6 +271,23 @@ struct BlockLayout {
 
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
+// The self attention's shape as attn_kv_splits sees it (the layout and the
+// call must agree on the split factor).
+inline wamb_attention_args self_attention_shape(const wamb_block_args* a) {
+  wamb_attention_args at{};
+  at.batch = a->batch;
+  at.heads = a->heads;
+  at.q_rows = a->tokens;
+  if (a->cache_k != nullptr) {
+    at.tiles = reinterpret_cast<const int32_t*>(1);   // device tile list: keys bounded by the pool
+    at.src0_batch_stride = a->pool;
+    at.src0_map = a->candidate_rows;
+  } else {
+    at.src0_len = a->tokens;
+  }
+  return at;
+}
+
 inline BlockLayout block_layout(const wamb_block_args* a) {
   BlockLayout L;
   for (int i = 0; i < WAMB_TAP_COUNT; ++i) L.off[i] = -1;
@@ -230,7 +301,7 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
   };
   // Stream-K flags first, in every layout, so that calls of different
   // shapes sharing one workspace agree on where the zero flags live.
-  put(WAMB_TAP_SK_FLAGS, SK_FLAG_BYTES);
+  put(WAMB_TAP_SK_FLAGS, SK_FLAG_BYTES + ATT_COUNT_BYTES);
   const bool f8 = a->fp8 == 1;  // LN outputs go to the E4M3 buffer instead
   if (!f8) put(WAMB_TAP_MODULATED1, MD);
   put(WAMB_TAP_QKV, 3 * MD);
@@ -256,12 +327,14 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
     put(WAMB_TAP_KV_TILES, static_cast<size_t>(a->pool) * 8);
     put(WAMB_TAP_KV_COUNTS, 16);
   }
+  DeviceInfo di;
+  const int sms = device_info(&di) == WAMB_OK ? di.sms : 148;
   // Stream-K partials of the two-CTA GEMMs (they run at M >= 512).
-  if (M >= 512) {
-    DeviceInfo di;
-    const int sms = device_info(&di) == WAMB_OK ? di.sms : 148;
-    put(WAMB_TAP_SK_PART, sk_part_bytes(sms));
-  }
+  if (M >= 512) put(WAMB_TAP_SK_PART, sk_part_bytes(sms));
+  // Split-key partials of the self attention.
+  const wamb_attention_args sa = self_attention_shape(a);
+  const int S = attn_kv_splits(&sa, sms);
+  if (S > 1) put(WAMB_TAP_ATTN_PART, attn_split_part_bytes(&sa, S));
   L.total = o;
   return L;
 }
@@ -484,7 +557,13 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     at.k0 = qkv; at.v0 = qkv; at.ld0 = 3LL * D; at.k0_col = D; at.v0_col = 2 * D;
     at.src0_total_rows = M; at.src0_batch_stride = Q; at.src0_len = Q;
   }
-  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D)))) return rc;
+  AttnSplitBuffers asb;
+  if (L.off[WAMB_TAP_ATTN_PART] >= 0) {
+    asb.count = reinterpret_cast<int*>(ws + L.off[WAMB_TAP_SK_FLAGS] + SK_FLAG_BYTES);
+    asb.part = reinterpret_cast<float*>(ws + L.off[WAMB_TAP_ATTN_PART]);
+    asb.part_bytes = attn_split_part_bytes(&at, attn_kv_splits(&at, di.sms));
+  }
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D), &asb))) return rc;
   if (f8 && (rc = quantize(attn, D, D))) return rc;
   // 6. O projection + gated residual (gate 2): h2 = x + o * gate_msa
   g = wamb_linear_args{};

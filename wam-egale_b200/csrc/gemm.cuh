@@ -74,13 +74,13 @@ struct GemmParams {
   // the next block's KV layout kernel, which waits only before exiting,
   // overlaps this GEMM's last tiles.
   int trigger_after;
-  // Stream-K (two-CTA kernel, gemm2.cuh): sk = 1 shares the last, partly
-  // filled round of tiles evenly over all pairs; a tile shared by several
+  // Stream-K (two-CTA kernel, gemm2.cuh): the last sk_tiles tiles (0: none)
+  // are shared evenly over all pairs by k-blocks; a tile shared by several
   // pairs is finished by the pair holding its last k-block from the other
-  // pairs' fp32 partials in sk_part ([pairs][8 chunks][256 rows][32] fp32),
+  // pairs' fp32 partials in sk_part ([pairs][8 chunks][8 groups][256 rows][4]),
   // each announced by one flag per producing warp in sk_flags ([pairs][16],
   // zero before the launch and zero again after it).
-  int sk;
+  int sk_tiles;
   float* sk_part;
   int* sk_flags;
 };
@@ -345,15 +345,9 @@ WAMB_DEV float4 lds4(uint32_t a) {
 // two chunks of work. Residual loads and output stores carry the streaming
 // cache hint (ld/st .cs: evict first), so the streamed rows do not push the
 // mainloop's A and weight tiles out of L2. Returns false if wait_acc gave up.
-struct NoAdjust {
-  WAMB_DEV void operator()(int, float (&)[32]) const {}
-};
-
-// adjust(c, v) runs on each chunk's accumulator values before the epilogue
-// math (the stream-K finisher adds the other pairs' partials there).
-template <class WaitAcc, class Adjust = NoAdjust>
+template <class WaitAcc>
 WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int row0, int lane, int n0,
-                                        int c0, uint32_t st, WaitAcc&& wait_acc, Adjust&& adjust = Adjust{}) {
+                                        int c0, uint32_t st, WaitAcc&& wait_acc) {
   const int row = row0 + lane;
   const EpiRow e = epi_row(p, row, n0);
   const bool has_res = p.epi == EPI_RES || p.epi == EPI_RES_GATE;
@@ -413,7 +407,6 @@ WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int
     float v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
-    adjust(c, v);
     if (e.valid) epi_value<32>(p, e, v, n0 + c * 32, e.n_local0 + c * 32);
     if (has_res) {
       __syncwarp();

@@ -15,22 +15,24 @@
 // TMEM: 2 accumulators x 256 columns per CTA (rows 0-127 of the tile in the
 // leader's TMEM, rows 128-255 in the peer's).
 //
-// Stream-K (GemmParams::sk): the full rounds of tiles run as before, one
-// tile per pair per round, in the wave order that keeps few weight column
-// blocks in flight (A and those weights stay in L2). The tiles x k-blocks
-// units of the remaining, partly filled round are cut into one equal
-// contiguous share per pair, so that every SM pair has the same work
-// whatever the tile count (a 880-row GEMM with N 3072 has 48 tiles for 74
-// pairs). A pair walks its share from the highest unit down, in segments
-// cut at tile boundaries. A segment without the tile's last k-block is a
-// producer: its fp32 partial goes to the pair's slot of sk_part and each
-// epilogue warp raises its flag. The segment holding the last k-block (and
-// not the first) finishes the tile: it adds the lower pairs' partials of
-// that tile to its accumulator, in a fixed order, in the epilogue, and
-// clears their flags. Walking down puts a pair's producer segment first
-// and its finisher segment last, and the finisher of a tile is the highest
-// pair on it, so partials are ready when they are needed and no pair waits
-// on a pair that starts after it.
+// Stream-K (GemmParams::sk_tiles): the first tiles run as before, one tile
+// per pair per round, in the wave order that keeps few weight column blocks
+// in flight (A and those weights stay in L2). The tiles x k-blocks units of
+// the last sk_tiles tiles (the partly filled last round, plus the full
+// round before it when the last one is less than half filled, so that a
+// tile is shared by two or three pairs, not dozens) are cut into one equal
+// contiguous share per pair. A pair walks its share from the highest unit
+// down, in segments cut at tile boundaries. A segment without the tile's
+// last k-block is a producer: its fp32 partial goes to the pair's slot of
+// sk_part and each epilogue warp raises its flag. The segment holding the
+// last k-block (and not the first) finishes the tile: while its own MMAs
+// run, its epilogue warps sum the lower pairs' partials (in a fixed order)
+// into the pair's other TMEM accumulator, free by then, and the epilogue
+// adds that sum to the tile's accumulator; they clear the flags they read.
+// Walking down puts a pair's producer segment first and its finisher
+// segment last, and the finisher of a tile is the highest pair on it, so
+// partials are ready when they are needed and no pair waits on a pair that
+// starts after it.
 #pragma once
 #include "gemm.cuh"
 
@@ -44,7 +46,10 @@ struct Gemm2Smem {
   static constexpr uint32_t BAR_OFF = GEMM2_STAGES * (A_BYTES + B_BYTES);
   static constexpr uint32_t NBARS = 2 * GEMM2_STAGES + 6;
   // Epilogue staging (gemm_epilogue_tile_staged): 4 KB per epilogue warp.
-  static constexpr uint32_t STAGE_OFF = (BAR_OFF + NBARS * 8 + 16 + 15) & ~15u;
+  // After the barriers: the TMEM address, the abort flag, then the pair's
+  // stream-K segment table (SegTable, 64 bytes).
+  static constexpr uint32_t TAB_OFF = BAR_OFF + NBARS * 8 + 16;
+  static constexpr uint32_t STAGE_OFF = (TAB_OFF + 64 + 15) & ~15u;
   static constexpr uint32_t TOTAL = 1024 + STAGE_OFF + GEMM_EPI_WARPS * 4096;
   static_assert(TOTAL <= 232448, "2-CTA GEMM shared memory exceeds 227 KB");
 };
@@ -104,41 +109,59 @@ struct Seg {
   bool producer, finisher;
 };
 
-// The pair's segments: whole tiles pair, pair + npairs, ... for every full
-// round (all tiles without stream-K); with stream-K, then the pair's share
-// [lo, hi) of the remaining tiles' units (tile-major, tiles counted from
-// sk_base) in descending order, cut at tile boundaries. 32-bit: the
-// remaining tiles are fewer than the pairs (< 128), so U < 128 x k-blocks
-// and q * U stay far below 2^31 for any K.
-struct SegIter {
-  int lo, i, U;
-  int t, step, dp_end, sk_base, num_kb;
-  WAMB_DEV SegIter(bool sk, int pair, int npairs, int num_tiles, int num_kb_)
-      : t(pair), step(npairs), num_kb(num_kb_) {
-    dp_end = sk ? (num_tiles / npairs) * npairs : num_tiles;
-    sk_base = dp_end;
-    U = (num_tiles - dp_end) * num_kb_;
-    lo = pair * U / npairs;
-    i = sk ? (pair + 1) * U / npairs - 1 : -1;
+// The pair's stream-K segments (at most three: a share is less than two
+// tiles of k-blocks), computed once per CTA by thread 0 into shared memory
+// so that the roles carry only a tile and a table index through their loops.
+// Share of pair q: units [q U / npairs, (q + 1) U / npairs) of the last
+// sk_tiles tiles (tile-major, counted from dp_end), walked in descending
+// order and cut at tile boundaries. 32-bit: sk_tiles < 2 x pairs (<= 256),
+// so U and q * U stay far below 2^31 for any K up to 2^20.
+struct SegTable {
+  int n;          // segments
+  int dp_end;     // tiles below it run whole, one per pair per round
+  int t[3], kb0[3], kb1[3];
+  int q_lo[3];    // producer pairs [q_lo, pair) of a finisher segment; pair otherwise
+};
+static_assert(sizeof(SegTable) <= 64, "segment table exceeds its shared-memory slot");
+
+WAMB_DEV void sk_table_build(SegTable& tb, int sk_tiles, int pair, int npairs, int num_tiles, int num_kb) {
+  tb.n = 0;
+  tb.dp_end = num_tiles - sk_tiles;
+  const int U = sk_tiles * num_kb;
+  const int lo = pair * U / npairs;
+  for (int i = (pair + 1) * U / npairs - 1; i >= lo && tb.n < 3;) {
+    const int tt = i / num_kb, base = tt * num_kb;
+    const int seg_lo = lo > base ? lo : base;
+    const int k = tb.n++;
+    tb.t[k] = tb.dp_end + tt;
+    tb.kb0[k] = seg_lo - base;
+    tb.kb1[k] = i + 1 - base;
+    int q_lo = pair;
+    if (tb.kb1[k] == num_kb && tb.kb0[k] != 0)   // finisher: the lower pairs on this tile
+      for (int qq = pair - 1; qq >= 0 && (qq + 1) * U / npairs > base; --qq) q_lo = qq;
+    tb.q_lo[k] = q_lo;
+    i = seg_lo - 1;
   }
-  // First unit of pair q's stream-K share.
-  WAMB_DEV int share_lo(int q, int npairs) const { return q * U / npairs; }
-  WAMB_DEV bool next(Seg& s) {
-    if (t < dp_end) {
+}
+
+// Segment s of the pair: whole tiles first, then the table's entries.
+struct SegCursor {
+  int t, k;
+  WAMB_DEV bool next(const SegTable& tb, int npairs, int num_kb, Seg& s, int& q_lo) {
+    if (t < tb.dp_end) {
       s = Seg{t, 0, num_kb, false, false};
-      t += step;
+      q_lo = -1;
+      t += npairs;
       return true;
     }
-    if (i < lo) return false;
-    const int tt = i / num_kb;
-    const int base = tt * num_kb;
-    const int seg_lo = lo > base ? lo : base;
-    s.t = sk_base + tt;
-    s.kb0 = seg_lo - base;
-    s.kb1 = i + 1 - base;
+    if (k >= tb.n) return false;
+    s.t = tb.t[k];
+    s.kb0 = tb.kb0[k];
+    s.kb1 = tb.kb1[k];
     s.producer = s.kb1 != num_kb;
     s.finisher = !s.producer && s.kb0 != 0;
-    i = seg_lo - 1;
+    q_lo = tb.q_lo[k];
+    ++k;
     return true;
   }
 };
@@ -151,20 +174,31 @@ WAMB_DEV int ld_acquire_gpu(const int* p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Bounded wait for a stream-K partial's flag.
+// Bounded wait of a warp for a stream-K partial's flag: lane 0 polls with
+// a growing sleep (hundreds of finisher warps must not flood L2 with
+// acquire loads while the producers' MMAs still run), then every lane
+// acquires the flag itself, so that its own loads of the partial are
+// ordered after the producer's stores. Returns false on abort / timeout.
 WAMB_DEV bool sk_wait_flag(const int* f, volatile int* abort_flag) {
-  const uint64_t t0 = globaltimer();
-  for (uint32_t it = 0;; ++it) {
-    if (ld_acquire_gpu(f) != 0) return true;
-    if ((it & 15u) == 15u) {
-      if (*abort_flag) return false;
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    const uint64_t t0 = globaltimer();
+    uint32_t ns = 64;
+    while (ld_acquire_gpu(f) == 0) {
+      if (*abort_flag) { ok = false; break; }
       if (globaltimer() - t0 > WAMB_WAIT_TIMEOUT_NS) {
         *abort_flag = 1;
         record_error(1);
-        return false;
+        ok = false;
+        break;
       }
+      __nanosleep(ns);
+      ns = ns < 1024 ? 2 * ns : ns;
     }
   }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)ld_acquire_gpu(f);
+  return ok;
 }
 
 template <bool F8>
@@ -188,6 +222,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t bye = drain + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  SegTable& segtab = *reinterpret_cast<SegTable*>(smem + L::TAB_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -211,6 +246,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(bye, 1);
     *abort_flag = 0;
+    sk_table_build(segtab, p.sk_tiles, blockIdx.x >> 1, gridDim.x >> 1, ((p.M + 255) / 256) * (p.N / 256),
+                   p.K / (F8 ? GEMM_BK8 : GEMM_BK));
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -237,9 +274,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
       int it = 0;
-      SegIter segs(p.sk != 0, pair, npairs, num_tiles, num_kb);
+      SegCursor cur{pair, 0};
       Seg sg;
-      while (!*abort_flag && segs.next(sg)) {
+      int q_unused;
+      while (!*abort_flag && cur.next(segtab, npairs, num_kb, sg, q_unused)) {
         const int t = sg.t;
         const int m_blk = t % num_m, n_blk = t / num_m;
         const int n0 = n_blk * 256;
@@ -275,9 +313,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // --------------------------------------------------- MMA issuer (leader)
       constexpr uint32_t IDESC = F8 ? idesc_e4m3(256, 256) : idesc_bf16(256, 256, 0);
       int it = 0, tc = 0;
-      SegIter segs(p.sk != 0, pair, npairs, num_tiles, num_kb);
+      SegCursor cur{pair, 0};
       Seg sg;
-      for (; segs.next(sg); ++tc) {
+      int q_unused;
+      for (; cur.next(segtab, npairs, num_kb, sg, q_unused); ++tc) {
         const int acc = tc & 1;
         const uint32_t aph = (tc >> 1) & 1;
         if (!mbar_wait(tempty0 + 8 * acc, aph ^ 1, abort_flag)) break;
@@ -318,13 +357,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t stage = smem_u32(smem + L::STAGE_OFF + (warp - 2) * 4096);
     // Stream-K: this warp's partial rows / chunks in a pair's slot, and its flag.
     const int wslot = static_cast<int>(rank) * 8 + (warp - 2);
-    auto part_at = [&](int slot, int c) {
-      return p.sk_part + ((static_cast<size_t>(slot) * 8 + c) * 256 + row_in_tile) * 32;
+    // Layout [slot][chunk][4-column group j][256 rows][4]: for a fixed j the
+    // lanes (consecutive rows) of a warp touch one contiguous 512-byte run.
+    auto part_at = [&](int slot, int c, int j) {
+      return reinterpret_cast<float4*>(p.sk_part) + ((static_cast<size_t>(slot) * 8 + c) * 8 + j) * 256 + row_in_tile;
     };
     int tc = 0;
-    SegIter segs(p.sk != 0, pair, npairs, num_tiles, num_kb);
+    SegCursor cur{pair, 0};
     Seg sg;
-    for (; segs.next(sg); ++tc) {
+    int q_lo;
+    for (; cur.next(segtab, npairs, num_kb, sg, q_lo); ++tc) {
       const int t = sg.t;
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
@@ -343,45 +385,70 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             float v[32];
             tmem_ld32(taddr + c * 32, v);
             tmem_wait_ld();
-            float4* dst = reinterpret_cast<float4*>(part_at(pair, c));
 #pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < 8; ++j) *part_at(pair, c, j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           }
           __threadfence();
           __syncwarp();
           if (lane == 0) st_release_gpu(p.sk_flags + pair * 16 + wslot, 1);
         }
       } else {
-        // Finisher: the lower pairs that hold the tile's other k-blocks.
-        const int tile_lo = (t - segs.sk_base) * num_kb;
-        int q_lo = pair;   // producers are pairs [q_lo, pair) (every share is non-empty)
-        if (sg.finisher) {
-          for (int qq = pair - 1; qq >= 0; --qq) {
-            if (segs.share_lo(qq + 1, npairs) <= tile_lo) break;
-            q_lo = qq;
+        // Finisher: the lower pairs [q_lo, pair) hold the tile's other
+        // k-blocks (q_lo = pair: none; whole tiles: -1, none).
+        if (q_lo < 0) q_lo = pair;
+        // The producers' partials, summed in a fixed order (highest pair
+        // first), into the other accumulator of this warp's TMEM slice (the
+        // finisher segment is the pair's last, so its epilogue is done)
+        // while this segment's MMAs still run.
+        const uint32_t tsum = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (acc ^ 1) * 256;
+        bool pre = true;
+        for (int qq = q_lo; pre && qq < pair; ++qq) pre = sk_wait_flag(p.sk_flags + qq * 16 + wslot, abort_flag);
+        if (pre && q_lo < pair) {
+#pragma unroll 1
+          for (int c = half * 4; c < half * 4 + 4; ++c) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+#pragma unroll 1
+            for (int qq = pair - 1; qq >= q_lo; --qq) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 x = __ldcg(part_at(qq, c, j));
+                v[4 * j] += x.x;
+                v[4 * j + 1] += x.y;
+                v[4 * j + 2] += x.z;
+                v[4 * j + 3] += x.w;
+              }
+            }
+            tmem_st32(tsum + c * 32, v);
+          }
+          tmem_wait_st();
+        }
+        bool ready = pre;
+        if (pre && q_lo < pair) {
+          // Once this segment's accumulator is complete, add the sum into it
+          // (TMEM to TMEM), before the epilogue and its residual requests.
+          ready = mbar_wait(tfull0 + 8 * acc, aph, abort_flag);
+          if (ready) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = half * 4; c < half * 4 + 4; ++c) {
+              float v[32], w[32];
+              tmem_ld32(taddr + c * 32, v);
+              tmem_ld32(tsum + c * 32, w);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += w[j];
+              tmem_st32(taddr + c * 32, v);
+            }
+            tmem_wait_st();
           }
         }
-        ok = gemm_epilogue_tile_staged(p, taddr, row - lane, lane, n0, half * 4, stage, [&]() {
+        ok = ready && gemm_epilogue_tile_staged(p, taddr, row - lane, lane, n0, half * 4, stage, [&]() {
+          if (q_lo < pair) return true;   // waited for above
           if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) return false;
           tc_fence_after();
-          // Every lane acquires each producer's flag itself, so that its
-          // own loads of the partial are ordered after the producer's stores.
-          for (int qq = q_lo; qq < pair; ++qq)
-            if (!__all_sync(0xffffffffu, sk_wait_flag(p.sk_flags + qq * 16 + wslot, abort_flag))) return false;
           return true;
-        }, [&](int c, float (&v)[32]) {
-#pragma unroll 1
-          for (int qq = pair - 1; qq >= q_lo; --qq) {   // fixed order: highest pair first
-            const float4* src = reinterpret_cast<const float4*>(part_at(qq, c));
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 x = __ldcg(src + j);
-              v[4 * j] += x.x;
-              v[4 * j + 1] += x.y;
-              v[4 * j + 2] += x.z;
-              v[4 * j + 3] += x.w;
-            }
-          }
         });
         if (ok && q_lo < pair) {
           __syncwarp();

@@ -142,12 +142,12 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
                         cudaStream_t stream) {
   const int resident = gemm2_resident<F8>(sms);
   WAMB_REQUIRE(resident > 0, WAMB_ERR_CUDA, "two-CTA GEMM cannot be resident on this device");
-  WAMB_REQUIRE(!p.sk || resident <= 128, WAMB_ERR_CUDA, "stream-K supports at most 128 SM pairs");
+  WAMB_REQUIRE(!p.sk_tiles || resident <= 128, WAMB_ERR_CUDA, "stream-K supports at most 128 SM pairs");
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = gemm2_config(stream, attr);
   const int tiles = ((p.M + 255) / 256) * (p.N / 256);
   // Stream-K shares the last round over every resident pair (one partial slot each).
-  const int pairs = p.sk ? resident : (tiles < resident ? tiles : resident);
+  const int pairs = p.sk_tiles ? resident : (tiles < resident ? tiles : resident);
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<F8>, ta, tb[0], tb[1], tb[2], p));
@@ -222,14 +222,29 @@ inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms, bool sk =
   return M >= 512 && n_per_group % 256 == 0 && (sk || pair_tiles >= sms / 2);
 }
 
-// Whether stream-K pays for a pair GEMM: when the tiles do not divide
-// evenly over the pairs (a partly filled last round), and the remaining
-// tiles have at least one k-block for every pair (no share is empty).
-inline bool gemm_use_sk(int M, long long N, int num_kb, int sms) {
+// Tiles of a pair GEMM that stream-K shares over the pairs (0: none): the
+// partly filled last round when it holds at least half as many tiles as
+// there are pairs, else that round plus the full one before it (a share is
+// then at least one tile of k-blocks, so that a tile is split between two or
+// three pairs, not dozens); none when the tiles divide evenly, or when a
+// GEMM of less than one round has too few tiles to share that way. Only for
+// long K (>= 128 k-blocks, the FFN output projections): the partial
+// exchange and the split tiles' second epilogue cost a launch ~6 us, which
+// measured more than the idle pairs at K 3072 (M 880: O projection 24 ->
+// 32 us, QKV 43 -> 52 us) and less at K 14336 (M 880: FFN2 93 -> 74 us).
+constexpr int SK_MIN_KB = 128;
+inline int gemm_sk_tiles(int M, long long N, int num_kb, int sms) {
   const int r = gemm2_resident<false>(sms);
+  if (M < 512 || num_kb < SK_MIN_KB || r <= 0 || r > 128) return 0;
   const long long tiles = ((M + 255) / 256) * (N / 256);
-  return M >= 512 && r > 0 && tiles % r != 0 && (tiles % r) * num_kb >= r;
+  const long long rem = tiles % r, full = tiles / r;
+  long long sk = 0;
+  if (rem == 0) sk = 0;
+  else if (2 * rem >= r) sk = rem;
+  else if (full >= 1) sk = rem + r;
+  return sk * num_kb >= r ? static_cast<int>(sk) : 0;
 }
+inline bool gemm_use_sk(int M, long long N, int num_kb, int sms) { return gemm_sk_tiles(M, N, num_kb, sms) > 0; }
 
 // w_early: the caller guarantees that the weights were last written two or
 // more kernels before this GEMM in the stream (GemmParams::w_early).
@@ -333,7 +348,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   p.out_gstride = out_gstride;
   p.trigger_after = trigger_after ? 1 : 0;
   if (pair && sk_ok) {
-    p.sk = 1;
+    p.sk_tiles = gemm_sk_tiles(a->m, N, a->k / (f8 ? GEMM_BK8 : GEMM_BK), di.sms);
     p.sk_flags = sk->flags;
     p.sk_part = sk->part;
   }

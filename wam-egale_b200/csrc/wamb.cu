@@ -42,7 +42,7 @@ extern "C" {
 
 const char* wamb_last_error(void) { return wamb::g_last_error.c_str(); }
 
-int wamb_abi_version(void) { return 106; }
+int wamb_abi_version(void) { return 107; }
 
 int wamb_device_status(void* stream, int* device_code) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -91,7 +91,28 @@ int wamb_quantize_rows(const void* x, int64_t ldx, int32_t x_is_f32, int32_t m, 
 }
 
 int wamb_attention(const wamb_attention_args* args, void* stream) {
-  return wamb::attention_impl(args, static_cast<cudaStream_t>(stream));
+  using namespace wamb;
+  if (args == nullptr || args->split_workspace == nullptr)
+    return attention_impl(args, static_cast<cudaStream_t>(stream));
+  WAMB_REQUIRE(reinterpret_cast<uintptr_t>(args->split_workspace) % 256 == 0, WAMB_ERR_ALIGN,
+               "split_workspace must be 256-byte aligned");
+  AttnSplitBuffers sb;
+  if (args->split_workspace_bytes >= ATT_COUNT_BYTES) {
+    uint8_t* w = static_cast<uint8_t*>(args->split_workspace);
+    sb.count = reinterpret_cast<int*>(w);
+    sb.part = reinterpret_cast<float*>(w + ATT_COUNT_BYTES);
+    sb.part_bytes = args->split_workspace_bytes - ATT_COUNT_BYTES;
+  }
+  return attention_impl(args, static_cast<cudaStream_t>(stream), false, &sb);
+}
+
+size_t wamb_attention_split_bytes(const wamb_attention_args* args) {
+  using namespace wamb;
+  if (args == nullptr) return 0;
+  DeviceInfo di;
+  if (device_info(&di) != WAMB_OK) return 0;
+  const int S = attn_kv_splits(args, di.sms, args->kv_splits);
+  return S > 1 ? ATT_COUNT_BYTES + attn_split_part_bytes(args, S) : 0;
 }
 
 size_t wamb_block_workspace_bytes(const wamb_block_args* args) {

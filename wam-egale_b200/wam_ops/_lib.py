@@ -49,6 +49,7 @@ class AttentionArgs(ctypes.Structure):
         ("src0_len", c_int32),
         ("k1", c_void_p), ("v1", c_void_p), ("ld1", c_int64), ("k1_col", c_int32), ("v1_col", c_int32),
         ("out", c_void_p), ("ldo", c_int64),
+        ("split_workspace", c_void_p), ("split_workspace_bytes", ctypes.c_size_t), ("kv_splits", c_int32),
     ]
 
 
@@ -95,17 +96,17 @@ class BlockArgs(ctypes.Structure):
 # Workspace taps (enum wamb_tap).
 TAPS = ("modulated1", "qkv", "self_attention", "residual1", "norm2", "cross_q", "cross_k",
         "cross_v", "cross_attention", "residual2", "modulated3", "gelu", "kv_slots",
-        "kv_tiles", "kv_counts", "a8", "a8_scale", "sk_flags", "sk_part")
+        "kv_tiles", "kv_counts", "a8", "a8_scale", "sk_flags", "sk_part", "attn_part")
 
 # Weight slots the FP8 path reads as E4M3 (self q/k/v/out, cross q/out, FFN).
 FP8_WEIGHTS = (3, 5, 7, 9, 13, 19, 23, 25)
 
-ABI_VERSION = 106
+ABI_VERSION = 107
 
 # Every symbol include/wamb.h declares; tests check the library exports them.
 EXPORTED = (
     "wamb_last_error", "wamb_abi_version", "wamb_device_status", "wamb_linear", "wamb_linear_sk_bytes",
-    "wamb_attention", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
+    "wamb_attention", "wamb_attention_split_bytes", "wamb_block_workspace_bytes", "wamb_block_workspace_layout",
     "wamb_block_forward", "wamb_cross_kv", "wamb_block_forward_noalloc", "wamb_quantize_rows",
     "wamb_timestep_embedding", "wamb_silu", "wamb_embed_gather", "wamb_output_norm", "wamb_copy_cols",
     "wamb_flow_step", "wamb_repeat_rows", "wamb_flow_step_cl",
@@ -137,6 +138,8 @@ def load():
     lib.wamb_linear.argtypes = [ctypes.POINTER(LinearArgs), c_void_p]
     lib.wamb_linear_sk_bytes.restype = ctypes.c_size_t
     lib.wamb_attention.argtypes = [ctypes.POINTER(AttentionArgs), c_void_p]
+    lib.wamb_attention_split_bytes.argtypes = [ctypes.POINTER(AttentionArgs)]
+    lib.wamb_attention_split_bytes.restype = ctypes.c_size_t
     lib.wamb_block_workspace_bytes.argtypes = [ctypes.POINTER(BlockArgs)]
     lib.wamb_block_workspace_bytes.restype = ctypes.c_size_t
     lib.wamb_block_workspace_layout.argtypes = [ctypes.POINTER(BlockArgs), ctypes.POINTER(c_int64)]

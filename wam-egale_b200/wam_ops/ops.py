@@ -135,13 +135,15 @@ def quantize_rows(x, out=None, scale=None):
 
 def attention(q, k0, v0, *, heads, q_rows, q_col=0, k0_col=0, v0_col=0, src0_batch_stride,
               src0_len=None, tiles=None, n_tiles=None, src0_map=None, src0_broadcast=False,
-              k1=None, v1=None, k1_col=0, v1_col=0, out=None):
+              k1=None, v1=None, k1_col=0, v1_col=0, out=None, kv_splits=None):
     """Flash attention over 2-D row-major views (see wamb_attention_args).
 
     q: [batch*q_rows, ldq] bf16; k0/v0: [rows0, ld0] bf16; optional k1/v1:
     [batch*q_rows, ld1]. tiles: int32 [n, 2] (first row, length) with the
     count in the int32 device tensor n_tiles; otherwise src0_len rows.
-    Returns out [batch*q_rows, heads*128] bf16.
+    kv_splits: None (no split-key scratch), 0 (the library chooses) or a
+    forced split factor; the scratch comes from a zero-filled per-device
+    buffer. Returns out [batch*q_rows, heads*128] bf16.
     """
     for name, t in (("q", q), ("k0", k0), ("v0", v0)):
         _bf16_2d(t, name)
@@ -163,8 +165,30 @@ def attention(q, k0, v0, *, heads, q_rows, q_col=0, k0_col=0, v0_col=0, src0_bat
     if k1 is not None:
         a.k1, a.v1, a.ld1, a.k1_col, a.v1_col = k1.data_ptr(), v1.data_ptr(), k1.stride(0), k1_col, v1_col
     a.out, a.ldo = out.data_ptr(), out.stride(0)
-    _lib.check(_lib.load().wamb_attention(a, _lib.stream_ptr()))
+    lib = _lib.load()
+    if kv_splits is not None:
+        a.kv_splits = kv_splits
+        need = lib.wamb_attention_split_bytes(a)
+        if need:
+            buf = _split_workspace(q.device, need)
+            a.split_workspace, a.split_workspace_bytes = buf.data_ptr(), buf.numel()
+    _lib.check(lib.wamb_attention(a, _lib.stream_ptr()))
     return out
+
+
+_SPLIT = {}
+
+
+def _split_workspace(device, nbytes):
+    """Zero-filled split-key scratch of wamb_attention (one growing buffer
+    per device; outgrown buffers are kept, as captured graphs may use them)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _SPLIT.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            _SPLIT.setdefault("retired", []).append(buf)
+        buf = _SPLIT[idx] = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+    return buf
 
 
 def sdpa(q, k, v):
