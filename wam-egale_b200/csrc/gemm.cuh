@@ -95,7 +95,9 @@ template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK * 2;
   static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
-  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  // tcgen05.alloc takes a power of two of at least 32 columns.
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128
+                                        : 2 * BN <= 256 ? 256 : 512;
   static constexpr uint32_t BAR_OFF = STAGES * (A_BYTES + B_BYTES);
   static constexpr uint32_t NBARS = 2 * STAGES + 6;
   static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;

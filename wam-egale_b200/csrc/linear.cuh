@@ -154,7 +154,7 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
   return WAMB_OK;
 }
 
-// Tile plan of the one-CTA kernel: tile width (256/128/64 columns) and
+// Tile plan of the one-CTA kernel: tile width (256/192/128/64 columns) and
 // cluster split-K factor, from a cost model measured on B200 at small M:
 //   * the TMA ring of one SM ingests ~90 GB/s of A + weight tiles while
 //     the MMAs consume them, and each k-block moves (128 + BN) x 128 bytes,
@@ -186,7 +186,7 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
   const double t_dram = static_cast<double>(N) * num_kb * 128.0 / (kDramGBs * 1e3);   // us
   TilePlan best{0, 1, num_kb};
   double best_t = 1e300;
-  const int cands[3] = {256, 128, 64};
+  const int cands[4] = {256, 192, 128, 64};
   for (int bn : cands) {
     if (n_per_group % bn) continue;
     const long long tiles = static_cast<long long>(num_m) * (N / bn);
@@ -361,6 +361,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
     }
     switch (bn) {
       case 256: return launch_gemm_bn<256, 4, F8>(ta, tb, p, di.sms, stream);
+      case 192: return launch_gemm_bn<192, 5, F8>(ta, tb, p, di.sms, stream);
       case 128: return launch_gemm_bn<128, 6, F8>(ta, tb, p, di.sms, stream);
       default: return launch_gemm_bn<64, 8, F8>(ta, tb, p, di.sms, stream);
     }
