@@ -214,7 +214,12 @@ inline int launch_ln(const LnParams& p, cudaStream_t s) {
   int rc = device_info(&di);
   if (rc) return rc;
   const size_t lsm = ln_warp_smem(p.D, p.x_f32);
-  if (p.D % 256 == 0 && lsm <= 227 * 1024 && aligned16(p.x) && (p.ldx * (p.x_f32 ? 4 : 2)) % 16 == 0) {
+  // The warp-per-row kernel pays at large M; below ~1024 rows a CTA would
+  // hold a row or two and its staging prologue costs more than it saves
+  // (the cfg3 verify step's 128-row LayerNorms took 4.72 -> 5.74 ms per
+  // step), so small M keeps the one-row-per-CTA kernel.
+  if (p.M >= 1024 && p.D % 256 == 0 && lsm <= 227 * 1024 && aligned16(p.x) &&
+      (p.ldx * (p.x_f32 ? 4 : 2)) % 16 == 0) {
     // Warp-per-row kernel, one CTA of 8 warps per SM: the CTAs of each
     // batch row of the modulation split its rows evenly, and all CTAs fit
     // one wave (no SM runs a second CTA while others idle).
