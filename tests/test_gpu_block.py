@@ -44,6 +44,9 @@ def _run_native(g, x, ctx, temb, rope, temb_dtype=torch.float32, out_dtype=torch
     (1, 40, 24, 1, torch.float32, True, True),
     (2, 130, 77, 130, torch.bfloat16, True, True),
     (3, 16, 512, 1, torch.float32, False, False),
+    # M >= 1024: the warp-per-row LayerNorm (per-token bf16 modulation; Identity norm2)
+    (2, 520, 64, 520, torch.bfloat16, True, True),
+    (4, 260, 32, 1, torch.float32, False, False),
 ])
 def test_block_no_cache(cuda_device, B, Q, C, temb_len, temb_dtype, rope, norm2):
     D, H, F = 256, 2, 512

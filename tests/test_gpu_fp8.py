@@ -181,3 +181,20 @@ def test_stack_fp8_cfg2_two_layers(cuda_device):
     assert _lib.device_status() == 0
     s = _gate(out, ref, exact, name="fp8 cfg2 2 layers")
     print("fp8 cfg2 2-layer", s)
+
+
+def test_block_fp8_large_m(cuda_device):
+    """M = 1040 (the warp-per-row LayerNorm writes the E4M3 rows and scales)
+    without a cache, fp8 vs the fp8 model and vs the fp32 block."""
+    D, H, F, B, Q, C = 256, 2, 512, 2, 520, 48
+    blk = make_oracle_block(D, F, H, seed=13)
+    ref_blk = of8.fp8_block(blk)
+    nb = NativeBlock(to_device_block(blk), fp8=True)
+    x, ctx, temb, rope = make_inputs(B, Q, D, C, H, seed=130)
+    with torch.no_grad():
+        ref = ref_blk(x, ctx, temb, rope)
+        exact = blk(x, ctx, temb, rope)
+        out = nb(x.cuda().bfloat16(), ctx.cuda().bfloat16(), temb.cuda(), rope.cuda(), out_dtype=torch.float32)
+    assert _lib.device_status() == 0
+    s = _gate(out, ref, exact, name="fp8 block D256 M1040")
+    print("fp8 block M1040", s)
