@@ -428,6 +428,15 @@ def run_native(args):
     del stack, static, step, gather
     torch.cuda.empty_cache()
 
+    if args.step_only:   # ncu launch lists of the step: skip the sub-runs
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                              "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                              "note": "--step-only: no fp8 / configs / cpu sub-runs"}), flush=True)
+        if pg is not None:
+            pg.barrier()
+            pg.destroy_process_group()
+        return 0
     # ---- the same workload with E4M3 GEMMs (configs[4]'s second run)
     ms8, clk8, stack8, static8, step8, gather8 = measure(True)
     fp8 = {"value": B * world / (ms8 / 1000.0), "unit": UNIT, "ms_per_step": ms8,
@@ -1029,6 +1038,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--step-only", action="store_true",
+                    help="default workload: time the bf16 step only (for ncu launch lists)")
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 GEMMs (the FP8 weight path); default is the bf16 drop-in")
     ap.add_argument("--case", default="ffn1",
