@@ -147,7 +147,6 @@ struct AttnParams {
   int kv_splits;
   float* kv_part;
   int* kv_count;
-  L2Prefetch prefetch;      // the next GEMMs' weights (small M), or nothing
 };
 
 // One split-key partial: O [32 four-column groups][256 rows][4] fp32 (so
@@ -238,7 +237,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_split = reinterpret_cast<volatile int*>(tmem_slot + 2);   // split keys: this CTA merges
 
-  l2_prefetch(p.prefetch);
   if (p.trigger) pdl_trigger();
   pdl_wait();   // the tile list and Q/K/V of the previous kernels are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -9,7 +9,6 @@
 #pragma once
 #include <algorithm>
 #include <cmath>
-#include <initializer_list>
 #include <type_traits>
 
 #include "attention.cuh"
@@ -63,9 +62,8 @@ inline size_t attn_split_part_bytes(const wamb_attention_args* a, int S) {
 
 // trigger: a GEMM that requests weights before its pdl_wait follows.
 // split: split-key scratch (counters zero on entry); null: no split.
-// prefetch: weights of the GEMMs that follow, to bring into L2 (small M).
 inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, bool trigger = false,
-                          const AttnSplitBuffers* split = nullptr, const L2Prefetch* prefetch = nullptr) {
+                          const AttnSplitBuffers* split = nullptr) {
   WAMB_REQUIRE(a != nullptr, WAMB_ERR_ARG, "null args");
   WAMB_REQUIRE(a->batch >= 0 && a->heads > 0 && a->q_rows >= 0, WAMB_ERR_SHAPE, "bad dims");
   if (a->batch == 0 || a->q_rows == 0) return WAMB_OK;
@@ -90,7 +88,6 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
   if ((rc = make_tmap_bf16(&tv0, a->v0, a->src0_total_rows, a->ld0, a->ld0, 128))) return rc;
   AttnParams p{};
   p.trigger = trigger ? 1 : 0;
-  if (prefetch != nullptr) p.prefetch = *prefetch;
   p.heads = a->heads;
   p.q_rows = a->q_rows;
   p.out = static_cast<__nv_bfloat16*>(a->out);
@@ -488,24 +485,6 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
   const bool f8 = a->fp8 == 1;
-  // Small M: the GEMMs stream their weights from HBM while the kernels
-  // between them leave it mostly idle, so those kernels bring the next
-  // GEMM's weights into L2 (LN1: q/k/v; RMS+RoPE: out; self attention:
-  // cross q and out; cross attention: FFN proj). FFN out's weights are not
-  // requested: with FFN proj's they would not fit L2 together.
-  const bool pf_on = M < 512;
-  auto wpf = [&](std::initializer_list<int> idx) {
-    L2Prefetch pf{};
-    if (!pf_on) return pf;
-    int r = 0;
-    for (int i : idx) {
-      const long long n_out = (i == 23) ? F : D, k_in = (i == 25) ? F : D;
-      pf.ptr[r] = f8 ? a->w8[i] : a->weights[i];
-      pf.bytes[r] = static_cast<unsigned long long>(n_out * k_in * (f8 ? 1 : 2));
-      ++r;
-    }
-    return pf;
-  };
   uint8_t* a8 = f8 ? ws + L.off[WAMB_TAP_A8] : nullptr;
   float* a8s = f8 ? reinterpret_cast<float*>(ws + L.off[WAMB_TAP_A8_SCALE]) : nullptr;
   auto gemm_input = [&](wamb_linear_args& g, const void* a_bf16, int widx) {
@@ -548,7 +527,6 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
-  ln.prefetch = wpf({3, 5, 7});
   if ((rc = launch_ln(ln, s))) return rc;
   // 3. QKV projection: three weight groups write q | k | v
   wamb_linear_args g{};
@@ -567,7 +545,6 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     r.pool_k = static_cast<bf*>(a->cache_k); r.pool_v = static_cast<bf*>(a->cache_v);
     r.pool = a->pool; r.slots = slots;
   }
-  r.prefetch = wpf({9});
   if ((rc = launch_rms(r, s))) return rc;
   // 5. self attention
   wamb_attention_args at{};
@@ -591,8 +568,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     asb.part = reinterpret_cast<float*>(ws + L.off[WAMB_TAP_ATTN_PART]);
     asb.part_bytes = attn_split_part_bytes(&at, attn_kv_splits(&at, di.sms));
   }
-  const L2Prefetch pf_self = wpf({13, 19});
-  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D), &asb, &pf_self))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D), &asb))) return rc;
   if (f8 && (rc = quantize(attn, D, D))) return rc;
   // 6. O projection + gated residual (gate 2): h2 = x + o * gate_msa
   g = wamb_linear_args{};
@@ -644,8 +620,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   at.src0_map = a->context_rows;
   at.src0_broadcast = a->context_rows == nullptr && a->context_batch == 1 && B > 1;
   at.out = ca; at.ldo = D;
-  const L2Prefetch pf_cross = wpf({23});
-  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D), nullptr, &pf_cross))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D)))) return rc;
   if (f8 && (rc = quantize(ca, D, D))) return rc;
   // 12. cross O projection + residual: h3 = h2 + o
   g = wamb_linear_args{};

@@ -311,42 +311,6 @@ __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// ------------------------------------------------------------ L2 prefetch
-// Up to three address ranges (16-byte aligned, sizes multiples of 16) that
-// a kernel asks the memory system to bring into L2 while it runs: the next
-// GEMM's weights, for small-M (weight-streaming) GEMMs whose predecessors
-// leave HBM mostly idle. A hint only; nothing waits for it.
-struct L2Prefetch {
-  const void* ptr[3];
-  unsigned long long bytes[3];
-};
-constexpr unsigned long long L2_PREFETCH_CHUNK = 64 * 1024;
-
-// The calling CTA's share of the ranges, 64 KB per instruction, spread
-// over every thread of the grid. Call before griddepcontrol.wait: weights
-// are written long before the kernels that prefetch them.
-WAMB_DEV void l2_prefetch(const L2Prefetch& pf) {
-  const unsigned long long tid = static_cast<unsigned long long>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) *
-                                     (blockDim.x * blockDim.y * blockDim.z) + threadIdx.x;
-  const unsigned long long nthr = static_cast<unsigned long long>(gridDim.x) * gridDim.y * gridDim.z *
-                                  blockDim.x * blockDim.y * blockDim.z;
-  unsigned long long base = 0;
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-    const unsigned long long n = (pf.bytes[r] + L2_PREFETCH_CHUNK - 1) / L2_PREFETCH_CHUNK;
-    if (pf.ptr[r] == nullptr || n == 0) continue;
-    // chunks [base, base + n) of the combined list belong to range r
-    for (unsigned long long c = (tid + nthr - base % nthr) % nthr; c < n; c += nthr) {
-      const unsigned long long off = c * L2_PREFETCH_CHUNK;
-      const unsigned long long len = pf.bytes[r] - off < L2_PREFETCH_CHUNK ? pf.bytes[r] - off : L2_PREFETCH_CHUNK;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const uint8_t*>(pf.ptr[r]) + off),
-                   "r"(static_cast<uint32_t>(len))
-                   : "memory");
-    }
-    base += n;
-  }
-}
-
 // ------------------------------------------------------------- conversions
 // Eight floats -> eight E4M3 bytes (round to nearest even, saturating to +-448).
 WAMB_DEV uint2 pack_e4m3x8(const float (&f)[8]) {

@@ -86,7 +86,6 @@ struct LnParams {
   int temb_f32, temb_L, rows_per_batch, shift_idx, scale_idx;
   int temb_rows;          // 0 or 6: the blocks' 6 modulation rows; 1: the output norm
   int trigger;            // 1: trigger the dependent grid early (a GEMM follows)
-  L2Prefetch prefetch;    // the next GEMM's weights (small M), or nothing
 };
 
 // Rows per CTA of ln_kernel for large M: two rows share one load of the
@@ -99,7 +98,6 @@ __host__ __device__ constexpr int ln_rows(int vpt) { return vpt <= 4 ? 2 : 1; }
 
 template <int VPT, int R>
 __global__ void ln_kernel(const LnParams p) {
-  l2_prefetch(p.prefetch);
   if (p.trigger) pdl_trigger();
   pdl_wait();
   __shared__ float red[32 * R];
@@ -324,7 +322,6 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
     fence_barrier_init();
   }
   __syncthreads();
-  l2_prefetch(p.prefetch);
   if (p.trigger) pdl_trigger();
   pdl_wait();
   const int rpb = p.affine ? p.M : p.rows_per_batch;
@@ -546,12 +543,10 @@ struct RmsParams {
   __nv_bfloat16* pool_v;
   long long pool;          // slots per pool batch row
   const int* slots;        // [rows_per_batch] pool slot of each new token
-  L2Prefetch prefetch;     // the next GEMM's weights (small M), or nothing
 };
 
 template <int VPT>
 __global__ void rms_rope_kernel(const RmsParams p) {
-  l2_prefetch(p.prefetch);
   pdl_wait();
   __shared__ float red[32];
   const int row = blockIdx.x;
