@@ -40,7 +40,7 @@ inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) 
   if (items > ATT_MAX_ITEMS) return 1;
   const long long keys = a->tiles != nullptr ? a->src0_batch_stride : a->src0_len;
   const int n_est = static_cast<int>((std::max<long long>(keys, 0) + 127) / 128);
-  if (force > 0) return std::max(1, std::min(std::min(force, 8), n_est));
+  if (force > 0) return std::max(1, std::min(std::min(force, ATT_MAX_SPLITS), n_est));
   if (items >= sms) return 1;
   auto eff = [&](int S) {
     const long long ctas = items * S;
@@ -48,7 +48,7 @@ inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) 
   };
   int best = 1;
   double best_eff = eff(1);
-  for (int S = 2; S <= 4 && n_est / S >= 4; ++S)
+  for (int S = 2; S <= ATT_MAX_SPLITS && n_est / S >= 4; ++S)
     if (eff(S) > best_eff + 0.1) {
       best = S;
       best_eff = eff(S);
