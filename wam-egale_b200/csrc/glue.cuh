@@ -259,10 +259,10 @@ __global__ void ln_kernel(const LnParams p) {
 
 // Warp-per-row LayerNorm for D % 256 == 0 (the block's widths), one CTA
 // of 8 warps per SM. Rows reach shared memory by bulk copies (TMA engine,
-// completing on one mbarrier per slot): every warp keeps two row slots and
-// requests its next row as soon as it has taken the current one into
-// registers, so two rows per warp (16 per SM, 192 KB of fp32 rows) are in
-// flight while the warp normalizes. Each lane holds 8 values of each
+// completing on one mbarrier per slot): every warp keeps two fp32 or four
+// bf16 row slots and requests the next row for a slot as soon as it has
+// taken that slot's row into registers, so ~192 KB of rows per SM are in
+// flight while the warps normalize. Each lane holds 8 values of each
 // 256-column group of its row: both reductions are warp shuffles over
 // eight independent partial sums, with no block barrier on a row's path.
 // The CTA's `rpc` rows lie in one batch row of the modulation, whose
@@ -299,10 +299,15 @@ WAMB_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t 
 
 constexpr int LNW_WARPS = 8;
 
+// Row slots per warp: two fp32 rows or four bf16 rows (~192 KB of rows in
+// flight per SM at D 3072 either way).
+__host__ __device__ constexpr int ln_warp_slots(int x_f32) { return x_f32 ? 2 : 4; }
+constexpr int LNW_MAX_SLOTS = 4;
 // Dynamic shared memory of ln_warp_kernel: multiplier and offset [2][D]
-// fp32, two row slots per warp, one mbarrier per slot, the abort flag.
+// fp32, the row slots of every warp, one mbarrier per slot, the abort flag.
 __host__ __device__ constexpr size_t ln_warp_smem(int D, int x_f32) {
-  return 8ull * D + 2ull * LNW_WARPS * D * (x_f32 ? 4 : 2) + 16ull * LNW_WARPS + 16;
+  return 8ull * D + static_cast<size_t>(ln_warp_slots(x_f32)) * LNW_WARPS * D * (x_f32 ? 4 : 2) +
+         8ull * LNW_MAX_SLOTS * LNW_WARPS + 16;
 }
 
 template <int NV>
@@ -311,13 +316,14 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = p.D;
   const uint32_t row_bytes = static_cast<uint32_t>(D) * (p.x_f32 ? 4 : 2);
+  const int NS = ln_warp_slots(p.x_f32);
   float* smul = reinterpret_cast<float*>(ln_smem);
   float* sadd = smul + D;
   uint8_t* slots = ln_smem + 8 * D;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(slots + 2 * LNW_WARPS * row_bytes);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * LNW_WARPS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(slots + NS * LNW_WARPS * row_bytes);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + LNW_MAX_SLOTS * LNW_WARPS);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2 * LNW_WARPS; ++i) mbar_init(smem_u32(bars + i), 1);
+    for (int i = 0; i < LNW_MAX_SLOTS * LNW_WARPS; ++i) mbar_init(smem_u32(bars + i), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -331,16 +337,17 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
   const int nk = r_end - r_begin > warp ? (r_end - r_begin - warp + LNW_WARPS - 1) / LNW_WARPS : 0;
   const uint8_t* xb = static_cast<const uint8_t*>(p.x);
   const long long x_row_bytes = p.ldx * (p.x_f32 ? 4 : 2);
-  const uint32_t slot0 = smem_u32(slots + warp * 2 * row_bytes);
-  const uint32_t bar0 = smem_u32(bars + 2 * warp);
-  auto request = [&](int k) {   // row k of this warp into slot k & 1 (lane 0)
+  const uint32_t slot0 = smem_u32(slots + warp * NS * row_bytes);
+  const uint32_t bar0 = smem_u32(bars + LNW_MAX_SLOTS * warp);
+  auto request = [&](int k) {   // row k of this warp into slot k % NS (lane 0)
     const int row = r_begin + warp + k * LNW_WARPS;
-    mbar_arrive_expect_tx(bar0 + 8 * (k & 1), row_bytes);
-    bulk_load(slot0 + (k & 1) * row_bytes, xb + row * x_row_bytes, row_bytes, bar0 + 8 * (k & 1));
+    const int sl = k % NS;
+    mbar_arrive_expect_tx(bar0 + 8 * sl, row_bytes);
+    bulk_load(slot0 + sl * row_bytes, xb + row * x_row_bytes, row_bytes, bar0 + 8 * sl);
   };
   int issued = 0;
   if (lane == 0)
-    for (; issued < 2 && issued < nk; ++issued) request(issued);
+    for (; issued < NS && issued < nk; ++issued) request(issued);
   issued = __shfl_sync(0xffffffffu, issued, 0);
 
   const int tr = p.temb_rows == 1 ? 1 : 6;
@@ -378,9 +385,9 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
   int k = 0;
   for (; k < nk; ++k) {
     const int row = r_begin + warp + k * LNW_WARPS;
-    if (!mbar_wait(bar0 + 8 * (k & 1), (k >> 1) & 1, abort_flag)) break;
+    if (!mbar_wait(bar0 + 8 * (k % NS), (k / NS) & 1, abort_flag)) break;
     float v[NV][8];
-    const uint8_t* srow = slots + warp * 2 * row_bytes + (k & 1) * row_bytes;
+    const uint8_t* srow = slots + (warp * NS + k % NS) * row_bytes;
 #pragma unroll
     for (int i = 0; i < NV; ++i)
 #pragma unroll
@@ -396,7 +403,7 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
         }
       }
     __syncwarp();
-    if (issued < nk) {   // the slot is free again: request the row two ahead
+    if (issued < nk) {   // the slot is free again: request the row NS ahead
       if (lane == 0) {
         fence_proxy_async();
         request(issued);
@@ -480,7 +487,7 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
   // After an abort, the copies still in flight must land before the CTA's
   // shared memory goes away.
   if (lane == 0)
-    for (int j = k; j < issued; ++j) mbar_wait_teardown(bar0 + 8 * (j & 1), (j >> 1) & 1);
+    for (int j = k; j < issued; ++j) mbar_wait_teardown(bar0 + 8 * (j % NS), (j / NS) & 1);
 }
 
 // --------------------------------------------------- row E4M3 quantization
