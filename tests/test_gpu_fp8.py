@@ -189,7 +189,8 @@ def test_block_fp8_large_m(cuda_device):
     D, H, F, B, Q, C = 256, 2, 512, 2, 520, 48
     blk = make_oracle_block(D, F, H, seed=13)
     ref_blk = of8.fp8_block(blk)
-    nb = NativeBlock(to_device_block(blk), fp8=True)
+    dev = to_device_block(blk)          # NativeBlock holds its block weakly
+    nb = NativeBlock(dev, fp8=True)
     x, ctx, temb, rope = make_inputs(B, Q, D, C, H, seed=130)
     with torch.no_grad():
         ref = ref_blk(x, ctx, temb, rope)
