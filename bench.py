@@ -295,12 +295,12 @@ def run_stack_config(name, dev, steps, warmup, fp8=False, seed=0):
     temb = configs.make_temb(cfg, B, dev, gen)
     rope = configs.chunk_rope(cfg, f_shift=cfg.history_chunks).to(dev)
     stack.capture(x, ctx, temb, rope, warmup=1)
-    for _ in range(warmup):
-        stack.replay()
     stream = torch.cuda.current_stream()
     clocks = Clocks(dev.index)
     clocks.start()
-    time.sleep(0.3)
+    time.sleep(0.3)          # the sampler starts; the warm-up then brings the clocks back up
+    for _ in range(warmup):
+        stack.replay()
     ms = time_graph(stack.replay, steps, stream)
     clk = clocks.stop()
     code = _lib.device_status()
@@ -363,6 +363,9 @@ def run_native(args):
                 gather()
             return out
 
+        clocks = Clocks(local)
+        clocks.start()
+        time.sleep(0.3)      # the sampler starts; the warm-up then brings the clocks back up
         for _ in range(args.warmup):
             step()
         if gather is not None:
@@ -370,12 +373,9 @@ def run_native(args):
         torch.cuda.synchronize()
         if _lib.device_status() != 0:
             raise RuntimeError("device error during warm-up")
-        clocks = Clocks(local)
         if pg is not None:
             pg.barrier()
         torch.cuda.synchronize()
-        clocks.start()
-        time.sleep(0.3)
 
         def timed():
             for _ in range(args.steps):
@@ -589,6 +589,9 @@ def run_verify(args):
         if gather is not None:
             gather()
 
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)          # the sampler starts; the warm-up then brings the clocks back up
     for _ in range(args.warmup):
         step()
     if gather is not None:
@@ -596,12 +599,9 @@ def run_verify(args):
     torch.cuda.synchronize()
     if _lib.device_status() != 0:
         raise RuntimeError("device error during warm-up")
-    clocks = Clocks(local)
     stream = torch.cuda.current_stream()
     if pg is not None:
         pg.barrier()
-    clocks.start()
-    time.sleep(0.3)
 
     def timed():
         for _ in range(args.steps):
@@ -720,16 +720,16 @@ def run_action_chunk(args):
     sched.set_timesteps(steps)
     den = NativeActionDenoiser(nm, sched)
     den.capture(x, grid)
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)          # the sampler starts; the warm-up then brings the clocks back up
     for _ in range(args.warmup):
         den.run(x)
     torch.cuda.synchronize()
     if _lib.device_status() != 0:
         raise RuntimeError("device error during warm-up")
-    clocks = Clocks(0)
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks.start()
-    time.sleep(0.3)
     e0.record(stream)
     for _ in range(args.steps):
         den.run()
@@ -849,7 +849,9 @@ def run_spec_chunk(args):
     for name, r in runs.items():
         clocks = Clocks(0)
         clocks.start()
-        time.sleep(0.3)
+        time.sleep(0.3)      # the sampler starts; one untimed run brings the clocks back up
+        r()
+        torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
             r()
@@ -911,7 +913,9 @@ def run_kernel_case(args):
                the same GEMM with an ungated residual and bias-only epilogues;
                prints each one's CUDA-event time
     attention  self attention of --batch cfg2 rollouts of --q queries over
-               --pool keys (24 heads)
+               --pool keys (24 heads), keys split across CTAs as the block
+               does when the (query tile pair, head, batch row) items fill
+               less than one wave
     verify_attention  cfg3 self attention: 4 candidates x 32 queries sharing
                one 3520-slot history row plus their own keys (24 heads)
     quant      row quantization to E4M3 of an --m x --k bf16 matrix
@@ -994,7 +998,7 @@ def run_kernel_case(args):
         vp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
         out = torch.empty(a.batch * a.q, D, device=dev, dtype=torch.bfloat16)
         run = lambda: ops.attention(q, kp, vp, heads=H, q_rows=a.q, src0_batch_stride=a.pool,  # noqa: E731
-                                    src0_len=a.pool, out=out)
+                                    src0_len=a.pool, out=out, kv_splits=0)
     elif a.case == "quant":
         x = torch.randn(a.m, a.k, generator=g, device=dev).bfloat16()
         run = lambda: ops.quantize_rows(x)  # noqa: E731
