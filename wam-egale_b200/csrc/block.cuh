@@ -32,7 +32,10 @@ struct AttnSplitBuffers {
 // head, batch row) items fill less than one wave of the SMs and a split
 // fills the waves much better (e.g. one 880-row chunk with 24 heads: 96
 // items for 148 SMs, 3 splits make 288 CTAs, 0.97 of two waves), each
-// split keeping at least 4 key tiles. Candidate verification (src0_map)
+// split keeping at least 8 key tiles (with fewer, writing and merging the
+// partials costs more than the fuller waves save: 1592 rows over 1592 keys,
+// 12 heads, 3 splits of 4-5 tiles measured 52 us against 42 unsplit).
+// Candidate verification (src0_map)
 // never splits. `force` > 0: that factor (capped by the key tiles).
 inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) {
   if (a->src0_map != nullptr || a->batch <= 0 || a->q_rows <= 0) return 1;
@@ -48,7 +51,7 @@ inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) 
   };
   int best = 1;
   double best_eff = eff(1);
-  for (int S = 2; S <= ATT_MAX_SPLITS && n_est / S >= 4; ++S)
+  for (int S = 2; S <= ATT_MAX_SPLITS && n_est / S >= 8; ++S)
     if (eff(S) > best_eff + 0.1) {
       best = S;
       best_eff = eff(S);
