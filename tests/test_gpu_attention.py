@@ -144,13 +144,18 @@ def test_split_kv_single_tile(cuda_device, Sq, Sk, hot):
     (64, [1, 1], 1000, 930),                   # G 2
     (16, [0] * 8, 500, 420),                   # G 8
     (32, [0, 0, 0, 0], 200, 60),               # two key tiles for four CTAs: some take none
+    (32, [0, 0], 700, 600),                    # G 2, R 4: each CTA merges 8 rows of a candidate
+    (32, [0], 700, 600),                       # one candidate, 8 CTAs of 4 rows each
+    (32, [0, 0, 0], 1000, 900),                # G 3, R 2: a 6-CTA cluster
+    (32, [0, 1], 700, 600),                    # rows differ: each candidate alone, R - 1 CTAs idle
+    (128, [1], 1000, 1000),                    # a 128-row candidate split over 8 CTAs
 ])
 def test_candidate_grouped(cuda_device, Q, rows, pool, vis):
-    """Candidates that share one history row attend as one 128-row query
-    group per head: a cluster of 128 / Q CTAs splits the history tiles and
-    the block-diagonal tile of the candidates' own keys, then merges
-    (m, l, O) across the cluster. Each candidate must still see only the
-    history plus its own keys (model.py:654-660)."""
+    """Candidates that share one history row attend as one query group per
+    head: a cluster of G candidates (G * Q <= 128) and R CTAs per candidate
+    splits the history tiles and the block-diagonal tile of the candidates'
+    own keys, then merges (m, l, O) across the cluster. Each candidate must
+    still see only the history plus its own keys (model.py:654-660)."""
     g = torch.Generator(device="cuda").manual_seed(Q * 100 + pool)
     Bp, B, H = 2, len(rows), 2
     kp = torch.randn(Bp, pool, H, 128, device="cuda", generator=g).bfloat16()

@@ -130,12 +130,16 @@ struct AttnParams {
   // source 1 (own rows of this call)
   int has_src1;
   int k1_col, v1_col;
-  // Grouped candidates (G > 1; launched as clusters of G CTAs along z,
-  // G * q_rows = 128, source-0 rows by src0_map): when the G batch rows of
-  // a cluster read the same source-0 row, its CTAs share one 128-row query
-  // tile holding all G candidates, split the key tiles (source 0, then the
-  // G candidates' own keys as one block-diagonal tile) and merge (m, l, O).
+  // Grouped candidates (launched as clusters of group_ctas = G x R CTAs
+  // along z, G * q_rows <= 128, source-0 rows by src0_map): cluster c holds
+  // batch rows [c G, c G + G) and its CTA k works for row c G + k / R. When
+  // the G rows read the same source-0 row, the CTAs share one query tile
+  // holding all G candidates, split the key tiles (source 0, then the G
+  // candidates' own keys as one block-diagonal tile) into group_ctas
+  // ranges and merge (m, l, O): CTA k owns q_rows / R rows of its
+  // candidate, slice k % R.
   int group;
+  int group_ctas;
   // Split keys (ungrouped kernel, kv_splits > 1, blockIdx.z = batch row x
   // kv_splits + split): when the query tiles alone would leave SMs idle,
   // each (query tile pair, head, batch row) item is computed by kv_splits
@@ -242,21 +246,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   pdl_wait();   // the tile list and Q/K/V of the previous kernels are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = !GROUPED && p.kv_splits > 1 ? p.kv_splits : 1;
-  const int b = blockIdx.z / S, sidx = blockIdx.z - b * S, h = blockIdx.y;
+  const int C = GROUPED && p.group_ctas > 1 ? p.group_ctas : 1;   // CTAs of a cluster
+  const int G = GROUPED && p.group > 1 ? p.group : 1;             // its batch rows
+  const int R = C / G;                                            // CTAs per batch row
+  const int crank = GROUPED ? static_cast<int>(blockIdx.z) % C : 0;
+  const int b = GROUPED ? static_cast<int>(blockIdx.z) / C * G + crank / R : static_cast<int>(blockIdx.z) / S;
+  const int sidx = GROUPED ? 0 : static_cast<int>(blockIdx.z) - b * S, h = blockIdx.y;
   const int q0 = blockIdx.x * 256;
   const int item = (b * gridDim.y + h) * gridDim.x + blockIdx.x;   // split keys: the item's counter / slots
   const int n0 = p.tiles != nullptr ? *p.n_tiles : (p.src0_len + 127) / 128;
   // Grouped candidates: the cluster's G batch rows share their source-0 row
-  // (checked here, so every CTA of the cluster decides alike).
-  const int G = GROUPED && p.group > 1 ? p.group : 1;
-  const int b0 = b - b % G, rank = b - b0;
-  bool grouped = GROUPED && G > 1;
+  // (checked here, so every CTA of the cluster decides alike). Otherwise
+  // each row is computed alone by the first of its R CTAs; the others idle.
+  const int b0 = b - b % G;
+  bool grouped = GROUPED && C > 1;
   for (int i = 1; grouped && i < G; ++i) grouped = p.src0_map[b0 + i] == p.src0_map[b0];
+  const bool idle = GROUPED && !grouped && crank % R != 0;
   // Key tiles of this CTA: [kv_lo, kv_lo + n) of the tile space (source 0,
   // then source 1; grouped: source 0, then the group's own-key tile n0).
   const int n_all = grouped ? n0 + 1 : n0 + (p.has_src1 ? (p.q_rows + 127) / 128 : 0);
-  const int kv_lo = grouped ? rank * n_all / G : sidx * n_all / S;
-  const int n = grouped ? (rank + 1) * n_all / G - kv_lo : (sidx + 1) * n_all / S - kv_lo;
+  const int kv_lo = grouped ? crank * n_all / C : sidx * n_all / S;
+  const int n = idle ? 0 : grouped ? (crank + 1) * n_all / C - kv_lo : (sidx + 1) * n_all / S - kv_lo;
   const bool has_b = !grouped && q0 + 128 < p.q_rows;   // the second query tile holds rows
   auto tile_of = [&](int j) {   // this CTA's j-th key tile
     const int jj = kv_lo + j;
@@ -483,7 +493,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       int lo = 0, hi = tile_of(kv0 + j).len;
       if (grouped && kv_lo + kv0 + j == n0) {
         lo = (r / p.q_rows) * p.q_rows;
-        hi = lo + p.q_rows;
+        hi = min(lo + p.q_rows, hi);   // rows past the G candidates see none
       }
       if (!mbar_wait(s_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
@@ -697,7 +707,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       if (ok && n > 0) ok = mbar_wait(o_done, 0, abort_flag);
       tc_fence_after();
       const int qr = q0 + t * 128 + r;
-      const bool store = qr < p.q_rows;
+      const bool store = qr < p.q_rows && !idle;
       __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
       const float inv = (ok && n > 0 && l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll 1
@@ -781,48 +791,52 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   }
   if (grouped) {
-    // Exchange: CTA `rank` owns the rows of candidate b0 + rank. Each CTA
+    // Exchange: CTA k owns rows [(k % R) ro, + ro) of candidate b0 + k / R
+    // (ro = q_rows / R, rows own0 + [0, ro) of the group tile). Each CTA
     // announces the bytes its rows will receive, barrier A (every partial is
     // written; every CTA's MMAs and loads are done, so its ring is free),
     // one thread sends each owner its rows (O, m, l) by bulk copy into slot
-    // `rank`, owners merge in sender order (the result does not depend on
+    // `crank`, owners merge in sender order (the result does not depend on
     // timing), barrier C keeps every CTA alive until its copies out landed.
     const int qr = p.q_rows;
-    const uint32_t slot_bytes = static_cast<uint32_t>(qr * (L::PART_LD + 2) * 4);
+    const int ro = qr / R;
+    const int own0 = (crank / R) * qr + (crank % R) * ro;
+    const uint32_t slot_bytes = static_cast<uint32_t>(ro * (L::PART_LD + 2) * 4);
     const float* part_o = reinterpret_cast<const float*>(smem + L::PART_O);
     const float* part_m = reinterpret_cast<const float*>(smem + L::PART_M);
     const float* part_l = reinterpret_cast<const float*>(smem + L::PART_L);
     const uint8_t* recv = smem + L::RECV;
     if (threadIdx.x < 256) fence_proxy_async();
-    if (threadIdx.x == 0) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(G - 1) * slot_bytes);
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(C - 1) * slot_bytes);
     __syncwarp();
     cluster_sync_all();   // barrier A
     if (threadIdx.x == ATT_MMA_WARP * 32) {
-      for (int o = 0; o < G; ++o) {
-        if (o == rank) continue;
-        const uint32_t dst = map_to_rank(smem_u32(recv) + static_cast<uint32_t>(rank) * slot_bytes, o);
+      for (int o = 0; o < C; ++o) {
+        if (o == crank) continue;
+        const int orow0 = (o / R) * qr + (o % R) * ro;
+        const uint32_t dst = map_to_rank(smem_u32(recv) + static_cast<uint32_t>(crank) * slot_bytes, o);
         const uint32_t bar = map_to_rank(recv_bar, o);
-        bulk_copy_to_peer(dst, smem_u32(part_o + o * qr * L::PART_LD), qr * L::PART_LD * 4, bar);
-        bulk_copy_to_peer(dst + qr * L::PART_LD * 4, smem_u32(part_m + o * qr), qr * 4, bar);
-        bulk_copy_to_peer(dst + qr * L::PART_LD * 4 + qr * 4, smem_u32(part_l + o * qr), qr * 4, bar);
+        bulk_copy_to_peer(dst, smem_u32(part_o + orow0 * L::PART_LD), ro * L::PART_LD * 4, bar);
+        bulk_copy_to_peer(dst + ro * L::PART_LD * 4, smem_u32(part_m + orow0), ro * 4, bar);
+        bulk_copy_to_peer(dst + ro * L::PART_LD * 4 + ro * 4, smem_u32(part_l + orow0), ro * 4, bar);
       }
     }
     if (threadIdx.x < 256) {
       const bool ok = mbar_wait(recv_bar, 0, abort_flag);
-      // 16-column groups of this candidate's rows.
-      for (int it = threadIdx.x; it < qr * 8; it += 256) {
+      // 16-column groups of this CTA's rows.
+      for (int it = threadIdx.x; it < ro * 8; it += 256) {
         const int rr = it >> 3, cg = (it & 7) * 16;
-        const int own = rank * qr + rr;
+        const int own = own0 + rr;
         float ms[8], ls[8];
         float M = -INFINITY;
 #pragma unroll
         for (int s2 = 0; s2 < 8; ++s2) {
           ms[s2] = -INFINITY;
           ls[s2] = 0.f;
-          if (s2 < G) {
-            const float* rm = reinterpret_cast<const float*>(recv + s2 * slot_bytes) + qr * L::PART_LD;
-            ms[s2] = s2 == rank ? part_m[own] : rm[rr];
-            ls[s2] = s2 == rank ? part_l[own] : rm[qr + rr];
+          if (s2 < C) {
+            const float* rm = reinterpret_cast<const float*>(recv + s2 * slot_bytes) + ro * L::PART_LD;
+            ms[s2] = s2 == crank ? part_m[own] : rm[rr];
+            ls[s2] = s2 == crank ? part_l[own] : rm[ro + rr];
             M = fmaxf(M, ms[s2]);
           }
         }
@@ -832,10 +846,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         float den = 0.f;
 #pragma unroll
         for (int s2 = 0; s2 < 8; ++s2) {
-          if (s2 < G) {
+          if (s2 < C) {
             const float w = ms[s2] == -INFINITY ? 0.f : exp2f(ms[s2] - M);
             den += w * ls[s2];
-            const float* src = s2 == rank
+            const float* src = s2 == crank
                                    ? part_o + own * L::PART_LD + cg
                                    : reinterpret_cast<const float*>(recv + s2 * slot_bytes) + rr * L::PART_LD + cg;
 #pragma unroll
@@ -850,7 +864,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         const float inv = (ok && !*abort_flag && den > 0.f) ? 1.f / den : 0.f;
         uint4* dst = reinterpret_cast<uint4*>(
-            p.out + (static_cast<long long>(b) * qr + rr) * p.ldo + h * 128 + cg);
+            p.out + (static_cast<long long>(b0) * qr + own) * p.ldo + h * 128 + cg);
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           uint4 w;

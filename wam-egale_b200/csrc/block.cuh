@@ -58,6 +58,33 @@ inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) 
     }
   return best;
 }
+// Grouped candidate attention (one query tile per cluster of G = the
+// largest divisor of `batch` with G * q_rows <= 128, R CTAs per candidate):
+// R as large as a cluster of at most 8 CTAs, one wave of CTAs over all
+// heads, and rows a CTA owns (q_rows / R) a multiple of 4 allow (the bulk
+// copies of the exchange move 16-byte multiples). False: no grouping
+// (q_rows must divide 128 and be at least 16; G R = 1 gains nothing).
+inline bool attn_group_shape(int q_rows, int batch, int heads, int sms, int* G_out, int* R_out) {
+  if (q_rows < 16 || 128 % q_rows != 0 || batch <= 0) return false;
+  int G = 1;
+  for (int g = std::min(128 / q_rows, 8); g >= 1; --g)
+    if (batch % g == 0) {
+      G = g;
+      break;
+    }
+  int R = 1;
+  for (int r = 8 / G; r >= 1; --r)
+    if (q_rows % r == 0 && (q_rows / r) % 4 == 0 &&
+        static_cast<long long>(batch / G) * heads * G * r <= sms) {
+      R = r;
+      break;
+    }
+  if (G * R < 2) return false;
+  *G_out = G;
+  *R_out = R;
+  return true;
+}
+
 inline size_t attn_split_part_bytes(const wamb_attention_args* a, int S) {
   if (S <= 1) return 0;
   return static_cast<size_t>((a->q_rows + 255) / 256) * a->heads * a->batch * S * ATT_PART_BYTES;
@@ -130,11 +157,13 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
     configured[dev] = true;
   }
   dim3 grid((a->q_rows + 255) / 256, a->heads, a->batch);
-  // Candidate verification with short chunks: G = 128 / q_rows batch rows
-  // per cluster (the kernel checks that they share their history row).
-  const int G = a->q_rows >= 16 && 128 % a->q_rows == 0 ? 128 / a->q_rows : 1;
-  if (p.src0_map != nullptr && p.has_src1 && G >= 2 && G <= 8 && a->batch % G == 0) {
+  // Candidate verification with short chunks: clusters of G batch rows (the
+  // kernel checks that they share their history row) and R CTAs per row.
+  int G = 0, R = 0;
+  if (p.src0_map != nullptr && p.has_src1 && attn_group_shape(a->q_rows, a->batch, a->heads, di.sms, &G, &R)) {
     p.group = G;
+    p.group_ctas = G * R;
+    grid.z = a->batch / G * (G * R);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(ATT_THREADS, 1, 1);
@@ -144,7 +173,7 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = G;
+    attr[0].val.clusterDim.z = G * R;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
