@@ -512,8 +512,8 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   // start before its pdl_wait (N columns, N per weight group, K).
   auto early = [&](long long n, int n_per_group, int k) {
     const int kb = k / (a->fp8 == 1 ? GEMM_BK8 : GEMM_BK);
-    return !gemm_is_pair(static_cast<int>(M), n, n_per_group, di.sms,
-                         has_sk && n_per_group % 256 == 0 && gemm_use_sk(M, n, kb, di.sms));
+    return gemm_pair_bn(static_cast<int>(M), n, n_per_group, kb, di.sms, a->fp8 == 1,
+                        has_sk && n_per_group % 256 == 0 && gemm_use_sk(M, n, kb, di.sms)) == 0;
   };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
   const bool f8 = a->fp8 == 1;

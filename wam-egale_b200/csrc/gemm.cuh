@@ -340,14 +340,14 @@ WAMB_DEV float4 lds4(uint32_t a) {
   return x;
 }
 
-// Four 32-column chunks [c0, c0 + 4) of one tile. The residual of chunks
+// NC (3 or 4) 32-column chunks [c0, c0 + NC) of one tile. The residual of chunks
 // c0 and c0 + 1 is requested before `wait_acc` (the wait for the
 // accumulator: the residual does not depend on it), and each later chunk's
 // two chunks ahead, so its DRAM latency overlaps the accumulator wait and
 // two chunks of work. Residual loads and output stores carry the streaming
 // cache hint (ld/st .cs: evict first), so the streamed rows do not push the
 // mainloop's A and weight tiles out of L2. Returns false if wait_acc gave up.
-template <class WaitAcc>
+template <int NC, class WaitAcc>
 WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int row0, int lane, int n0,
                                         int c0, uint32_t st, WaitAcc&& wait_acc) {
   const int row = row0 + lane;
@@ -385,8 +385,9 @@ WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int
     fetch(c0 + 1, rb);
   }
   if (!wait_acc()) return false;
+  static_assert(NC >= 2, "the residual of two chunks is requested ahead");
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < NC; ++k) {
     const int c = c0 + k;
     uint4 (&rc)[8] = (k & 1) ? rb : ra;
     if (has_res) {
@@ -404,7 +405,7 @@ WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int
         }
         sts4(rm(i), x);
       }
-      if (k + 2 < 4) fetch(c + 2, rc);
+      if (k + 2 < NC) fetch(c + 2, rc);
     }
     float v[32];
     tmem_ld32(taddr + c * 32, v);

@@ -1,9 +1,10 @@
 // Two-CTA (cta_group::2) variant of the tcgen05 GEMM for large M:
-// a cluster of 2 CTAs computes a 256 x 256 output tile with M=256
-// tcgen05.mma instructions issued by the leader CTA. Each CTA loads its own
-// 128 rows of A and its own 128 of the tile's 256 weight rows, so a CTA
-// moves 32 KB per 64-wide k-block instead of 48 KB for a 128 x 256 tile on
-// one SM: the shared weight tile crosses the L2 -> SM path once per pair.
+// a cluster of 2 CTAs computes a 256 x BN output tile (BN 256 or 192) with
+// M=256 tcgen05.mma instructions issued by the leader CTA. Each CTA loads
+// its own 128 rows of A and its own BN / 2 of the tile's BN weight rows, so
+// a CTA moves 32 KB (BN 256) or 28 KB (BN 192) per 64-wide k-block instead
+// of 48 / 40 KB for a 128 x BN tile on one SM: the shared weight tile
+// crosses the L2 -> SM path once per pair.
 //
 // Barriers (per CTA):
 //   full[s]    leader only: one arrive_expect_tx (both CTAs' bytes); both
@@ -12,7 +13,7 @@
 //   tfull[a]   both CTAs: one arrival from the leader's commit (sent to both)
 //   tempty[a]  leader only: 16 arrivals, one per epilogue warp of either CTA
 //   bye        exit handshake: the other CTA arrives once (remote arrive)
-// TMEM: 2 accumulators x 256 columns per CTA (rows 0-127 of the tile in the
+// TMEM: 2 accumulators x BN columns per CTA (rows 0-127 of the tile in the
 // leader's TMEM, rows 128-255 in the peer's).
 //
 // Stream-K (GemmParams::sk_tiles): the first tiles run as before, one tile
@@ -40,9 +41,11 @@ namespace wamb {
 
 constexpr int GEMM2_STAGES = 6;
 
+template <int BN>
 struct Gemm2Smem {
-  static constexpr uint32_t A_BYTES = 128 * 128;  // this CTA's 128 rows of A x 128 bytes of K
-  static constexpr uint32_t B_BYTES = 128 * 128;  // this CTA's 128 of 256 weight rows
+  static_assert(BN == 256 || BN == 192, "two-CTA tiles are 256 or 192 columns wide");
+  static constexpr uint32_t A_BYTES = 128 * 128;        // this CTA's 128 rows of A x 128 bytes of K
+  static constexpr uint32_t B_BYTES = (BN / 2) * 128;   // this CTA's BN / 2 of BN weight rows
   static constexpr uint32_t BAR_OFF = GEMM2_STAGES * (A_BYTES + B_BYTES);
   static constexpr uint32_t NBARS = 2 * GEMM2_STAGES + 6;
   // Epilogue staging (gemm_epilogue_tile_staged): 4 KB per epilogue warp.
@@ -201,13 +204,16 @@ WAMB_DEV bool sk_wait_flag(const int* f, volatile int* abort_flag) {
   return ok;
 }
 
-template <bool F8>
+// Stream-K (sk_tiles > 0) is used with BN 256 only: the partial slots and
+// their layout hold 256 x 256 tiles.
+template <bool F8, int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
                     const GemmParams p) {
-  using L = Gemm2Smem;
+  using L = Gemm2Smem<BN>;
   constexpr int STAGES = GEMM2_STAGES;
+  constexpr int NCH = BN / 64;   // 32-column chunks per epilogue warp (two warps per lane quarter)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -229,7 +235,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int num_m = (p.M + 255) / 256;
-  const int num_n = p.N / 256;
+  const int num_n = p.N / BN;
   const int num_tiles = num_m * num_n;
   constexpr int KB = F8 ? GEMM_BK8 : GEMM_BK;
   const int num_kb = p.K / KB;
@@ -246,7 +252,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(bye, 1);
     *abort_flag = 0;
-    sk_table_build(segtab, p.sk_tiles, blockIdx.x >> 1, gridDim.x >> 1, ((p.M + 255) / 256) * (p.N / 256),
+    sk_table_build(segtab, p.sk_tiles, blockIdx.x >> 1, gridDim.x >> 1, ((p.M + 255) / 256) * (p.N / BN),
                    p.K / (F8 ? GEMM_BK8 : GEMM_BK));
     fence_barrier_init();
   }
@@ -280,7 +286,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       while (!*abort_flag && cur.next(segtab, npairs, num_kb, sg, q_unused)) {
         const int t = sg.t;
         const int m_blk = t % num_m, n_blk = t / num_m;
-        const int n0 = n_blk * 256;
+        const int n0 = n_blk * BN;
         const int g = n0 / p.n_per_group;
         const int n_local = n0 - g * p.n_per_group;
         const CUtensorMap* mb = g == 0 ? &tmB0 : (g == 1 ? &tmB1 : &tmB2);
@@ -294,7 +300,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tma_load_2d_pair(smem_u32(sA + s * L::A_BYTES), &tmA, full_leader, kb * KB,
                            m_blk * 256 + rank * 128);
           tma_load_2d_pair(smem_u32(sB + s * L::B_BYTES), mb, full_leader, kb * KB,
-                           n_local + rank * 128);
+                           n_local + rank * (BN / 2));
         }
         if (!ok) break;
       }
@@ -311,7 +317,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // --------------------------------------------------- MMA issuer (leader)
-      constexpr uint32_t IDESC = F8 ? idesc_e4m3(256, 256) : idesc_bf16(256, 256, 0);
+      constexpr uint32_t IDESC = F8 ? idesc_e4m3(256, BN) : idesc_bf16(256, BN, 0);
       int it = 0, tc = 0;
       SegCursor cur{pair, 0};
       Seg sg;
@@ -321,7 +327,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const uint32_t aph = (tc >> 1) & 1;
         if (!mbar_wait(tempty0 + 8 * acc, aph ^ 1, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * 256;
+        const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
@@ -350,7 +356,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter accessible to this warp
-    const int half = (warp - 2) >> 2;  // columns [half * 128, half * 128 + 128)
+    const int half = (warp - 2) >> 2;  // columns [half * BN / 2, + BN / 2)
     const int row_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
     const uint32_t tempty_leader0 = map_to_rank(tempty0, 0);
     // Every tile's epilogue goes through the warp's staging buffer.
@@ -372,8 +378,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t aph = (tc >> 1) & 1;
       const int m_blk = t % num_m, n_blk = t / num_m;
       const int row = m_blk * 256 + row_in_tile;
-      const int n0 = n_blk * 256;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
+      const int n0 = n_blk * BN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       bool ok;
       if (sg.producer) {
         // This pair's partial of the tile into its slot, then the flag.
@@ -381,7 +387,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (ok) {
           tc_fence_after();
 #pragma unroll 1
-          for (int c = half * 4; c < half * 4 + 4; ++c) {
+          for (int c = half * NCH; c < half * NCH + NCH; ++c) {
             float v[32];
             tmem_ld32(taddr + c * 32, v);
             tmem_wait_ld();
@@ -400,12 +406,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // first), into the other accumulator of this warp's TMEM slice (the
         // finisher segment is the pair's last, so its epilogue is done)
         // while this segment's MMAs still run.
-        const uint32_t tsum = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (acc ^ 1) * 256;
+        const uint32_t tsum = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (acc ^ 1) * BN;
         bool pre = true;
         for (int qq = q_lo; pre && qq < pair; ++qq) pre = sk_wait_flag(p.sk_flags + qq * 16 + wslot, abort_flag);
         if (pre && q_lo < pair) {
 #pragma unroll 1
-          for (int c = half * 4; c < half * 4 + 4; ++c) {
+          for (int c = half * NCH; c < half * NCH + NCH; ++c) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.f;
@@ -432,7 +438,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (ready) {
             tc_fence_after();
 #pragma unroll 1
-            for (int c = half * 4; c < half * 4 + 4; ++c) {
+            for (int c = half * NCH; c < half * NCH + NCH; ++c) {
               float v[32], w[32];
               tmem_ld32(taddr + c * 32, v);
               tmem_ld32(tsum + c * 32, w);
@@ -444,7 +450,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             tmem_wait_st();
           }
         }
-        ok = ready && gemm_epilogue_tile_staged(p, taddr, row - lane, lane, n0, half * 4, stage, [&]() {
+        ok = ready && gemm_epilogue_tile_staged<NCH>(p, taddr, row - lane, lane, n0, half * NCH, stage, [&]() {
           if (q_lo < pair) return true;   // waited for above
           if (!mbar_wait(tfull0 + 8 * acc, aph, abort_flag)) return false;
           tc_fence_after();

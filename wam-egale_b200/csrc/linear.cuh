@@ -82,10 +82,11 @@ inline int launch_gemm_cl(const CUtensorMap& ta, const CUtensorMap* tb, const Ge
 }
 
 // Two-CTA launch: clusters of 2 along x, one cluster per pair of SMs.
+template <int BN>
 inline cudaLaunchConfig_t gemm2_config(cudaStream_t stream, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = Gemm2Smem::TOTAL;
+  cfg.dynamicSmemBytes = Gemm2Smem<BN>::TOTAL;
   cfg.stream = stream;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -101,19 +102,19 @@ inline cudaLaunchConfig_t gemm2_config(cudaStream_t stream, cudaLaunchAttribute*
 // Co-resident clusters (SM pairs) of the two-CTA kernel on the current
 // device (queried once per device; 74 on B200). It is also the number of
 // stream-K partial slots a launch needs.
-template <bool F8>
+template <bool F8, int BN = 256>
 inline int gemm2_resident(int sms) {
   static int resident[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (resident[dev] == 0) {
     cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = gemm2_config(nullptr, attr);
+    cudaLaunchConfig_t cfg = gemm2_config<BN>(nullptr, attr);
     cfg.gridDim = dim3(sms, 1, 1);
     int n = 0;
-    if (cudaFuncSetAttribute(gemm_tc2_kernel<F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Smem::TOTAL) !=
-            cudaSuccess ||
-        cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<F8>, &cfg) != cudaSuccess) {
+    if (cudaFuncSetAttribute(gemm_tc2_kernel<F8, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Gemm2Smem<BN>::TOTAL) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<F8, BN>, &cfg) != cudaSuccess) {
       (void)cudaGetLastError();
       n = 0;
     }
@@ -137,20 +138,21 @@ struct SkBuffers {
   size_t part_bytes = 0;
 };
 
-template <bool F8>
+template <bool F8, int BN>
 inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const GemmParams& p, int sms,
                         cudaStream_t stream) {
-  const int resident = gemm2_resident<F8>(sms);
+  const int resident = gemm2_resident<F8, BN>(sms);
   WAMB_REQUIRE(resident > 0, WAMB_ERR_CUDA, "two-CTA GEMM cannot be resident on this device");
-  WAMB_REQUIRE(!p.sk_tiles || resident <= 128, WAMB_ERR_CUDA, "stream-K supports at most 128 SM pairs");
+  WAMB_REQUIRE(!p.sk_tiles || (BN == 256 && resident <= 128), WAMB_ERR_CUDA,
+               "stream-K needs 256-column tiles and at most 128 SM pairs");
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = gemm2_config(stream, attr);
-  const int tiles = ((p.M + 255) / 256) * (p.N / 256);
+  cudaLaunchConfig_t cfg = gemm2_config<BN>(stream, attr);
+  const int tiles = ((p.M + 255) / 256) * (p.N / BN);
   // Stream-K shares the last round over every resident pair (one partial slot each).
   const int pairs = p.sk_tiles ? resident : (tiles < resident ? tiles : resident);
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<F8>, ta, tb[0], tb[1], tb[2], p));
+  WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<F8, BN>, ta, tb[0], tb[1], tb[2], p));
   return WAMB_OK;
 }
 
@@ -167,6 +169,7 @@ inline int launch_gemm2(const CUtensorMap& ta, const CUtensorMap* tb, const Gemm
 // least 4 k-blocks each and splits x tiles <= SMs.
 struct TilePlan {
   int bn, splits, kb_per_split;
+  double cost_us = 0.0;   // the cost model's estimate of the plan
 };
 
 // Split plans use 64- or 128-column tiles: a 256-column tile's fp32
@@ -210,16 +213,37 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
       }
     }
   }
+  best.cost_us = best_t;
   return best;
 }
 
-// Whether a GEMM of this shape takes the 2-CTA kernel: 256 x 256 tiles when
-// the weight groups split into 256-wide tiles and M >= 512, and either
-// stream-K is used (every pair then gets an equal share of the last round)
-// or there are enough tiles to give every SM pair one.
-inline bool gemm_is_pair(int M, long long N, int n_per_group, int sms, bool sk = false) {
-  const long long pair_tiles = ((M + 255) / 256) * (N / 256);
-  return M >= 512 && n_per_group % 256 == 0 && (sk || pair_tiles >= sms / 2);
+// Tile width of the 2-CTA kernel for a GEMM of this shape (M >= 512), or 0
+// for the one-CTA kernel. Stream-K (sk: every pair gets an equal share of
+// the last round) needs 256-column tiles. Otherwise 256 x 256 tiles when
+// the weight groups split into them and there are enough to give every SM
+// pair one, and 256 x 192 tiles when plan_tiles' cost model, applied to a
+// pair, rates them faster than that choice: an SM ingests (128 + BN / 2) x
+// 128 bytes per k-block (A rows plus its half of the weight rows) at ~90
+// GB/s, tiles run in rounds over the SM pairs, an epilogue costs ~1 + BN /
+// 128 us. At M 880, N 3072 (the O and cross projections of one cfg2 chunk)
+// that is one round of 64 pair tiles, 28 KB per SM per k-block, against
+// 112 one-CTA 128 x 192 tiles moving 40 KB per k-block.
+inline int gemm_pair_bn(int M, long long N, int n_per_group, int num_kb, int sms, bool f8, bool sk = false) {
+  if (M < 512) return 0;
+  const bool c256 = n_per_group % 256 == 0, c192 = n_per_group % 192 == 0;
+  if (sk) return c256 ? 256 : 0;
+  const int pairs = sms / 2;
+  const double t_dram = static_cast<double>(N) * num_kb * 128.0 / (6000.0 * 1e3);   // us
+  auto cost = [&](int bn) {
+    const long long tiles = static_cast<long long>((M + 255) / 256) * (N / bn);
+    const long long rounds = (tiles + pairs - 1) / pairs;
+    return std::max(rounds * num_kb * ((128.0 + bn / 2) * 128.0 / (90.0 * 1e3)), t_dram) + 1.0 + bn / 128.0;
+  };
+  const long long t256 = c256 ? static_cast<long long>((M + 255) / 256) * (N / 256) : 0;
+  int best = c256 && t256 >= pairs ? 256 : 0;
+  const double best_t = best ? cost(256) : plan_tiles(M, static_cast<int>(N), n_per_group, num_kb, sms, f8).cost_us;
+  if (c192 && cost(192) < best_t) best = 192;
+  return best;
 }
 
 // Tiles of a pair GEMM that stream-K shares over the pairs (0: none): the
@@ -302,9 +326,10 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   const bool sk_ok = sk != nullptr && sk->flags != nullptr && sk->part != nullptr && a->n_per_group % 256 == 0 &&
                      sk->part_bytes >= sk_part_bytes(di.sms) &&
                      gemm_use_sk(a->m, N, a->k / (f8 ? GEMM_BK8 : GEMM_BK), di.sms);
-  const bool pair = gemm_is_pair(a->m, N, a->n_per_group, di.sms, sk_ok);
   const int num_kb = a->k / (f8 ? GEMM_BK8 : GEMM_BK);
-  TilePlan tp{256, 1, num_kb};
+  const int pbn = gemm_pair_bn(a->m, N, a->n_per_group, num_kb, di.sms, f8, sk_ok);
+  const bool pair = pbn != 0;
+  TilePlan tp{pbn, 1, num_kb};
   if (!pair) tp = plan_tiles(a->m, static_cast<int>(N), a->n_per_group, num_kb, di.sms, f8);
   const int bn = tp.bn;
   CUtensorMap ta, tb[3];
@@ -313,7 +338,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   if (rc) return rc;
   for (int g = 0; g < 3; ++g) {
     const int src = g < a->groups ? g : 0;
-    rc = tmap(&tb[g], a->weight[src], a->n_per_group, a->k, a->k, pair ? 128 : bn);
+    rc = tmap(&tb[g], a->weight[src], a->n_per_group, a->k, a->k, pair ? pbn / 2 : bn);
     if (rc) return rc;
   }
   GemmParams p{};
@@ -347,14 +372,15 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   p.kb_per_split = tp.kb_per_split;
   p.out_gstride = out_gstride;
   p.trigger_after = trigger_after ? 1 : 0;
-  if (pair && sk_ok) {
+  if (pair && sk_ok && pbn == 256) {
     p.sk_tiles = gemm_sk_tiles(a->m, N, a->k / (f8 ? GEMM_BK8 : GEMM_BK), di.sms);
     p.sk_flags = sk->flags;
     p.sk_part = sk->part;
   }
   auto launch = [&](auto f8c) {
     constexpr bool F8 = decltype(f8c)::value;
-    if (pair) return launch_gemm2<F8>(ta, tb, p, di.sms, stream);
+    if (pair) return pbn == 256 ? launch_gemm2<F8, 256>(ta, tb, p, di.sms, stream)
+                                : launch_gemm2<F8, 192>(ta, tb, p, di.sms, stream);
     if (tp.splits > 1) {
       if (bn == 128) return launch_gemm_cl<128, 6, F8>(ta, tb, p, stream);
       return launch_gemm_cl<64, 8, F8>(ta, tb, p, stream);
