@@ -3,8 +3,9 @@
 Shapes with M >= 512 and N per group a multiple of 256 take the two-CTA
 (cta_group::2) kernel when they have at least 74 256 x 256 tiles, or when
 the stream-K scratch lets them share a partly filled last round over all
-SM pairs; shapes with N per group a multiple of 192 take it with 256 x 192
-tiles when the cost model rates that faster (the M 880, N 3072 projections);
+SM pairs; residual-epilogue shapes with N per group a multiple of 192 take it with
+256 x 192 tiles when the cost model rates that faster (the M 880, N 3072
+projections);
 the others take the one-CTA kernel with 64/128/192/256-column tiles, split
 along K across a thread-block cluster when the tiles alone would leave SMs
 idle.
@@ -173,7 +174,7 @@ def _sk_flags_zero(dev):
     (880, 8192, 3072, 3),      # three weight groups: one full round + 70 shared tiles
     (2000, 8960, 1536, 1),     # D 1536 FFN2 shape, ragged last row block
     (7040, 14336, 3072, 1),    # 336 tiles: 4 full rounds + 40 shared tiles
-    (880, 3072, 3072, 1),      # K 3072: no stream-K (two-CTA 256 x 192 tiles)
+    (880, 3072, 3072, 1),      # K 3072: no stream-K (the one-CTA path)
     (512, 8192, 256, 1),       # too few tiles to share: no stream-K
 ])
 def test_linear_stream_k(cuda_device, m, k, n, groups):
@@ -231,53 +232,55 @@ def test_linear_stream_k_fp8(cuda_device):
     _close(out, deq(a8, sa) @ deq(w8, sw).t() + b.float())
 
 
-@pytest.mark.parametrize("m,k,n,groups", [
-    (880, 3072, 3072, 1),     # O / cross projections of one cfg2 chunk: 64 pair tiles of 256 x 192
-    (1592, 1536, 1536, 1),    # D 1536 projections: the last pair tile's second half out of range
-    (512, 3072, 3072, 2),     # cross K/V construction: two weight groups of 3072 columns
+
+@pytest.mark.parametrize("m,k,n", [
+    (880, 3072, 3072),     # O / cross-O projections of one cfg2 chunk: 64 pair tiles of 256 x 192
+    (1592, 1536, 1536),    # D 1536 projections: the last pair tile's second half out of range
+    (600, 1536, 3072),     # 3 x 16 pair tiles, a ragged last row block
 ])
-def test_linear_pair192(cuda_device, m, k, n, groups):
+def test_linear_pair192(cuda_device, m, k, n):
     """Two-CTA kernel with 256 x 192 tiles (three 32-column chunks per
-    epilogue warp): bias, GELU, and the gated fp32 residual with fp32 output,
-    bitwise repeatable."""
+    epilogue warp; the residual epilogues of N % 192 == 0 shapes with too
+    few 256 x 256 tiles): the gated fp32 residual with fp32 output and the
+    plain bf16 residual, bitwise repeatable."""
     g = torch.Generator(device="cuda").manual_seed(m + 3 * k + n)
+    B = 2
     a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
-    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.03).bfloat16() for _ in range(groups)]
-    bs = [torch.randn(n, device="cuda", generator=g).bfloat16() for _ in range(groups)]
-    out = ops.linear(a, ws, bs)
-    again = ops.linear(a, ws, bs)
-    gelu = ops.linear(a, ws, bs, epilogue=_lib.EPI_GELU)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.03).bfloat16()
+    b = torch.randn(n, device="cuda", generator=g).bfloat16()
+    res = torch.randn(m, n, device="cuda", generator=g)
+    table = torch.randn(6, n, device="cuda", generator=g) * 0.1
+    temb = torch.randn(B, 1, 6, n, device="cuda", generator=g) * 0.1
+    o32, again = torch.empty(m, n, device="cuda"), torch.empty(m, n, device="cuda")
+    for o in (o32, again):
+        ops.linear(a, w, b, epilogue=_lib.EPI_RES_GATE, res=res, table=table, temb=temb,
+                   rows_per_batch=m // B, gate_index=2, out=o)
+    res16 = res.bfloat16()
+    o16 = ops.linear(a, w, b, epilogue=_lib.EPI_RES, res=res16)
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
-    base = _ref(a, ws, bs)
-    _close(out, base)
-    assert torch.equal(out, again)
-    _close(gelu, torch.nn.functional.gelu(base, approximate="tanh"))
-    if groups == 1:
-        B = 2
-        res = torch.randn(m, n, device="cuda", generator=g)
-        table = torch.randn(6, n, device="cuda", generator=g) * 0.1
-        temb = torch.randn(B, 1, 6, n, device="cuda", generator=g) * 0.1
-        o32 = torch.empty(m, n, device="cuda")
-        ops.linear(a, ws[0], bs[0], epilogue=_lib.EPI_RES_GATE, res=res, table=table, temb=temb,
-                   rows_per_batch=m // B, gate_index=2, out=o32)
-        torch.cuda.synchronize()
-        assert _lib.device_status() == 0
-        gate = (table[2][None, None] + temb[:, :, 2]).expand(B, m // B, n).reshape(m, n)
-        err = (o32 - (res + base * gate)).abs().max().item()
-        assert err <= 5e-3, err
+    base = _ref(a, [w], [b])
+    gate = (table[2][None, None] + temb[:, :, 2]).expand(B, m // B, n).reshape(m, n)
+    err = (o32 - (res + base * gate)).abs().max().item()
+    assert err <= 5e-3, err
+    assert torch.equal(o32, again)
+    _close(o16, res16.float() + base)
 
 
 def test_linear_pair192_fp8(cuda_device):
+    """E4M3 operands through the 256 x 192 pair tiles (fp32 residual)."""
     m, k, n = 880, 3072, 3072
     g = torch.Generator(device="cuda").manual_seed(8)
     a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
     w = (torch.randn(n, k, device="cuda", generator=g) * 0.05).bfloat16()
     b = torch.randn(n, device="cuda", generator=g).bfloat16()
+    res = torch.randn(m, n, device="cuda", generator=g)
     a8, sa = ops.quantize_rows(a)
     w8, sw = ops.quantize_rows(w)
-    out = ops.linear(a8, w8, b, a_scale=sa, w_scales=sw)
+    out = torch.empty(m, n, device="cuda")
+    ops.linear(a8, w8, b, a_scale=sa, w_scales=sw, epilogue=_lib.EPI_RES, res=res, out=out)
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     deq = lambda q, s: q.float() * s[:, None]  # noqa: E731
-    _close(out, deq(a8, sa) @ deq(w8, sw).t() + b.float())
+    err = (out - (res + deq(a8, sa) @ deq(w8, sw).t() + b.float())).abs().max().item()
+    assert err <= 5e-3, err

@@ -550,9 +550,9 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   };
   // Early triggers pay only before a one-CTA GEMM, whose weight loads can
   // start before its pdl_wait (N columns, N per weight group, K).
-  auto early = [&](long long n, int n_per_group, int k) {
+  auto early = [&](long long n, int n_per_group, int k, int epi) {
     const int kb = k / (a->fp8 == 1 ? GEMM_BK8 : GEMM_BK);
-    return gemm_pair_bn(static_cast<int>(M), n, n_per_group, kb, di.sms, a->fp8 == 1,
+    return gemm_pair_bn(static_cast<int>(M), n, n_per_group, kb, di.sms, a->fp8 == 1, epi,
                         has_sk && n_per_group % 256 == 0 && gemm_use_sk(M, n, kb, di.sms)) == 0;
   };
   // FP8 path: every GEMM input is E4M3 in a8 with per-row scales in a8s.
@@ -595,7 +595,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   // LN1 triggers early only after the KV layout kernel: the block's first
   // kernel keeps the implicit trigger, so writes of the kernels before the
   // block are complete before any GEMM of the block reads weights early.
-  ln.trigger = cache && early(3 * D, D, D) ? 1 : 0;
+  ln.trigger = cache && early(3 * D, D, D, WAMB_EPI_BIAS) ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 0; ln.scale_idx = 1;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -640,7 +640,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
     asb.part = reinterpret_cast<float*>(ws + L.off[WAMB_TAP_ATTN_PART]);
     asb.part_bytes = attn_split_part_bytes(&at, attn_kv_splits(&at, di.sms));
   }
-  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D), &asb))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D, WAMB_EPI_RES_GATE), &asb))) return rc;
   if (f8 && (rc = quantize(attn, D, D))) return rc;
   // 6. O projection + gated residual (gate 2): h2 = x + o * gate_msa
   g = wamb_linear_args{};
@@ -656,7 +656,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln = LnParams{};
   ln.x = h2; ln.x_f32 = 1; ln.ldx = D; ln.out = n2; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[1]); ln.affine = a->weights[1] != nullptr ? 1 : 2;
-  ln.trigger = early(D, D, D) ? 1 : 0;
+  ln.trigger = early(D, D, D, WAMB_EPI_BIAS) ? 1 : 0;
   ln.gamma = static_cast<const float*>(a->weights[1]); ln.beta = static_cast<const float*>(a->weights[2]);
   ln.rows_per_batch = Q;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -692,7 +692,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   at.src0_map = a->context_rows;
   at.src0_broadcast = a->context_rows == nullptr && a->context_batch == 1 && B > 1;
   at.out = ca; at.ldo = D;
-  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D)))) return rc;
+  if ((rc = attention_impl(&at, s, !f8 && early(D, D, D, WAMB_EPI_RES)))) return rc;
   if (f8 && (rc = quantize(ca, D, D))) return rc;
   // 12. cross O projection + residual: h3 = h2 + o
   g = wamb_linear_args{};
@@ -705,7 +705,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   ln = LnParams{};
   ln.x = h3; ln.x_f32 = 1; ln.ldx = D; ln.out = f0; ln.ldo = D; ln.M = M; ln.D = D;
   ln.eps = static_cast<float>(a->eps[2]); ln.affine = 0; ln.table = table; ln.temb = a->temb;
-  ln.trigger = early(F, F, D) ? 1 : 0;
+  ln.trigger = early(F, F, D, WAMB_EPI_GELU) ? 1 : 0;
   ln.temb_f32 = a->temb_is_f32; ln.temb_L = a->temb_len; ln.rows_per_batch = Q;
   ln.shift_idx = 3; ln.scale_idx = 4;
   if (f8) { ln.out8 = a8; ln.out_scale = a8s; }
@@ -716,7 +716,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   gemm_input(g, f0, 23);
   g.bias[0] = a->weights[24]; g.out = act; g.ldo = F;
   g.epilogue = WAMB_EPI_GELU;
-  if ((rc = run_gemm(g, !f8 && early(D, D, F)))) return rc;   // bf16: FFN2 follows directly
+  if ((rc = run_gemm(g, !f8 && early(D, D, F, WAMB_EPI_RES_GATE)))) return rc;   // bf16: FFN2 follows directly
   if (f8 && (rc = quantize(act, F, F))) return rc;
   // 15. FFN2 + gated residual (gate 5): out = h3 + f * c_gate_msa
   g = wamb_linear_args{};

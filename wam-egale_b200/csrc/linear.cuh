@@ -221,14 +221,18 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
 // for the one-CTA kernel. Stream-K (sk: every pair gets an equal share of
 // the last round) needs 256-column tiles. Otherwise 256 x 256 tiles when
 // the weight groups split into them and there are enough to give every SM
-// pair one, and 256 x 192 tiles when plan_tiles' cost model, applied to a
-// pair, rates them faster than that choice: an SM ingests (128 + BN / 2) x
-// 128 bytes per k-block (A rows plus its half of the weight rows) at ~90
-// GB/s, tiles run in rounds over the SM pairs, an epilogue costs ~1 + BN /
-// 128 us. At M 880, N 3072 (the O and cross projections of one cfg2 chunk)
-// that is one round of 64 pair tiles, 28 KB per SM per k-block, against
-// 112 one-CTA 128 x 192 tiles moving 40 KB per k-block.
-inline int gemm_pair_bn(int M, long long N, int n_per_group, int num_kb, int sms, bool f8, bool sk = false) {
+// pair one, and, for the residual epilogues, 256 x 192 tiles when
+// plan_tiles' cost model, applied to a pair, rates them faster than that
+// choice: an SM ingests (128 + BN / 2) x 128 bytes per k-block (A rows plus
+// its half of the weight rows) at ~90 GB/s, tiles run in rounds over the SM
+// pairs, an epilogue costs ~1 + BN / 128 us. At M 880, N 3072 that is one
+// round of 64 pair tiles, 28 KB per SM per k-block, against 112 one-CTA
+// 128 x 192 tiles moving 40 KB per k-block. Measured there (CUDA events,
+// weights from HBM): the gated fp32 residual 31.1 -> 28.4 us, whose reads
+// the pair kernel's staged epilogue requests two chunks ahead; a bias-only
+// epilogue 22.4 -> 24.8 us, so those keep the one-CTA plan.
+inline int gemm_pair_bn(int M, long long N, int n_per_group, int num_kb, int sms, bool f8, int epi,
+                        bool sk = false) {
   if (M < 512) return 0;
   const bool c256 = n_per_group % 256 == 0, c192 = n_per_group % 192 == 0;
   if (sk) return c256 ? 256 : 0;
@@ -242,7 +246,8 @@ inline int gemm_pair_bn(int M, long long N, int n_per_group, int num_kb, int sms
   const long long t256 = c256 ? static_cast<long long>((M + 255) / 256) * (N / 256) : 0;
   int best = c256 && t256 >= pairs ? 256 : 0;
   const double best_t = best ? cost(256) : plan_tiles(M, static_cast<int>(N), n_per_group, num_kb, sms, f8).cost_us;
-  if (c192 && cost(192) < best_t) best = 192;
+  const bool res = epi == WAMB_EPI_RES || epi == WAMB_EPI_RES_GATE;
+  if (c192 && res && cost(192) < best_t) best = 192;
   return best;
 }
 
@@ -327,7 +332,7 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
                      sk->part_bytes >= sk_part_bytes(di.sms) &&
                      gemm_use_sk(a->m, N, a->k / (f8 ? GEMM_BK8 : GEMM_BK), di.sms);
   const int num_kb = a->k / (f8 ? GEMM_BK8 : GEMM_BK);
-  const int pbn = gemm_pair_bn(a->m, N, a->n_per_group, num_kb, di.sms, f8, sk_ok);
+  const int pbn = gemm_pair_bn(a->m, N, a->n_per_group, num_kb, di.sms, f8, a->epilogue, sk_ok);
   const bool pair = pbn != 0;
   TilePlan tp{pbn, 1, num_kb};
   if (!pair) tp = plan_tiles(a->m, static_cast<int>(N), a->n_per_group, num_kb, di.sms, f8);
