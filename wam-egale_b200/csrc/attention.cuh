@@ -30,18 +30,6 @@
 // TMEM columns: S/P of A [0,128), S/P of B [128,256), O_A [256,384), O_B [384,512).
 // SMEM: Q_A, Q_B and a 5-slot K/V ring of 128 rows x 128 bf16 tiles (224 KB).
 //
-// CTA pair (PAIR, queries longer than one tile): two CTAs of a cluster, each
-// with its own query tiles A and B, share every K/V tile. The leader's lane
-// 0 of warp 9 issues tcgen05.mma.cta_group::2 (M 256: tile A of both CTAs,
-// then tile B of both), committing to both CTAs' barriers. Each CTA loads
-// only its half of a K tile (64 of its 128 keys: the B operand's N split of
-// S = Q K^T) and of a V tile (64 of the 128 head dims: the N split of O +=
-// P V), so an SM's shared-memory operand reads per key tile drop from 192
-// to 128 KB and its K/V loads from 64 to 32 KB. Each CTA's S, P and O stay
-// in its own TMEM; its softmax warps arrive on the leader's p_full (the
-// peer's remotely); the peer's warp 9 relays "this half landed" (after
-// zeroing V rows past a partial tile's length) to the leader's pfull.
-//
 // Keys come from up to two sources:
 //   source 0  the KV pool (or a contiguous K/V tensor), read as a list of
 //             (first row, length <= 128) tiles: either a device-side tile list
@@ -64,12 +52,6 @@ constexpr uint32_t ATT_TILE_BYTES = 128 * 128 * 2;  // 128 rows x 128 bf16
 constexpr uint32_t ATT_ATOM = 128 * 128;            // one 64-column half: 128 rows x 128 B
 constexpr float ATT_RESCALE_LOG2 = 8.f;             // rescale O only when the max grows > 2^8
 constexpr int ATT_SLOTS = 5;                        // K/V ring: load L = 2j (K_j) or 2j+1 (V_j)
-// CTA-pair variant: each CTA holds half of every K tile (64 keys x 128
-// dims, two 8 KB 64-column atoms) or V tile (128 keys x its 64 dims, one
-// atom) in a ring of 10 slots of 16 KB.
-constexpr int ATT2_SLOTS = 10;
-constexpr uint32_t ATT2_SLOT_BYTES = 16384;
-constexpr uint32_t ATT2_KATOM = 64 * 128;
 // 2^f ~= C0 + f (C1 + f (C2 + f C3)) for f in [-0.5, 0.5]: minimax relative
 // error 7.5e-5 (tests/test_host_exp2_cubic.py recomputes the fit), far below bf16's 2^-9 for P.
 constexpr float ATT_EXP2_C0 = 0.9999281167984009f;
@@ -182,9 +164,8 @@ struct AttnSmem {
   static constexpr uint32_t Q_OFF = 0;                                    // Q_A, Q_B
   static constexpr uint32_t RING_OFF = Q_OFF + 2 * ATT_TILE_BYTES;        // K/V ring
   static constexpr uint32_t BAR_OFF = RING_OFF + ATT_SLOTS * ATT_TILE_BYTES;
-  // q_full, full[S], empty[S], s_full[2], p_full[2], o_done, drain, recv,
-  // then (CTA pair) pfull[S], qpair, bye; S ring slots (5, or 10 for a pair)
-  static constexpr uint32_t NBARS = 3 * ATT2_SLOTS + 10;
+  // q_full, full[5], empty[5], s_full[2], p_full[2], o_done, drain, recv
+  static constexpr uint32_t NBARS = 18;
   // Grouped candidates, over the ring once the MMAs are done: this CTA's
   // partial O [128][PART_LD] fp32, m [128], l [128], then one receive slot
   // per sender of q_rows x (PART_LD + 2) floats (128 rows in all).
@@ -231,15 +212,12 @@ WAMB_DEV KvTile att_tile(const AttnParams& p, int j, int n0, int b) {
 
 // GROUPED: the grouped-candidate variant (cluster launch); false compiles
 // the kernel without any of that code.
-template <bool GROUPED, bool PAIR = false>
+template <bool GROUPED>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
                    const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
                    const __grid_constant__ CUtensorMap tmV1, const AttnParams p) {
-  static_assert(!(GROUPED && PAIR), "grouped candidates run on single CTAs");
   using L = AttnSmem;
-  constexpr int SL = PAIR ? ATT2_SLOTS : ATT_SLOTS;
-  constexpr uint32_t SLOT_BYTES = PAIR ? ATT2_SLOT_BYTES : ATT_TILE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -247,22 +225,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t sRing = smem_u32(smem + L::RING_OFF);
   const uint32_t bar0 = smem_u32(smem + L::BAR_OFF);
   const uint32_t q_full = bar0;
-  const uint32_t full = bar0 + 8;              // [SL] by ring slot
-  const uint32_t empty = full + 8 * SL;        // [SL]
-  const uint32_t s_full = empty + 8 * SL;      // [2] by query tile
-  const uint32_t p_full = s_full + 16;         // [2] by query tile
-  const uint32_t o_done = p_full + 16;
-  const uint32_t drain = o_done + 8;
-  const uint32_t recv_bar = drain + 8;         // grouped: the other CTAs' partials of this CTA's rows
-  const uint32_t pfull = recv_bar + 8;         // [SL] pair (leader): the peer's half of the load is in place
-  const uint32_t qpair = pfull + 8 * SL;       // pair (leader): the peer's query tiles are in place
-  const uint32_t bye = qpair + 8;              // pair: exit handshake
+  const uint32_t full = bar0 + 8;         // [5] by ring slot
+  const uint32_t empty = bar0 + 48;       // [5]
+  const uint32_t s_full = bar0 + 88;      // [2] by query tile
+  const uint32_t p_full = bar0 + 104;     // [2] by query tile
+  const uint32_t o_done = bar0 + 120;
+  const uint32_t drain = bar0 + 128;
+  const uint32_t recv_bar = bar0 + 136;   // grouped: the other CTAs' partials of this CTA's rows
   // Ring load L (the L-th K or V tile in consumption order; K_j = 2j and
-  // V_j = 2j+1 without split-KV) lives in slot L % SL, phase (L / SL) & 1.
-  auto slot_addr = [&](int L) { return sRing + (L % SL) * SLOT_BYTES; };
-  auto slot_full = [&](int L) { return full + 8 * (L % SL); };
-  auto slot_empty = [&](int L) { return empty + 8 * (L % SL); };
-  auto slot_phase = [&](int L) { return static_cast<uint32_t>((L / SL) & 1); };
+  // V_j = 2j+1 without split-KV) lives in slot L % 5, phase (L / 5) & 1.
+  auto slot_addr = [&](int L) { return sRing + (L % ATT_SLOTS) * ATT_TILE_BYTES; };
+  auto slot_full = [&](int L) { return full + 8 * (L % ATT_SLOTS); };
+  auto slot_empty = [&](int L) { return empty + 8 * (L % ATT_SLOTS); };
+  auto slot_phase = [&](int L) { return static_cast<uint32_t>((L / ATT_SLOTS) & 1); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_split = reinterpret_cast<volatile int*>(tmem_slot + 2);   // split keys: this CTA merges
@@ -270,8 +245,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   if (p.trigger) pdl_trigger();
   pdl_wait();   // the tile list and Q/K/V of the previous kernels are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t prank = PAIR ? cluster_rank() : 0;   // pair: 0 = leader (issues the MMAs)
-  const bool leader = prank == 0;
   const int S = !GROUPED && p.kv_splits > 1 ? p.kv_splits : 1;
   const int C = GROUPED && p.group_ctas > 1 ? p.group_ctas : 1;   // CTAs of a cluster
   const int G = GROUPED && p.group > 1 ? p.group : 1;             // its batch rows
@@ -294,9 +267,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const int n_all = grouped ? n0 + 1 : n0 + (p.has_src1 ? (p.q_rows + 127) / 128 : 0);
   const int kv_lo = grouped ? crank * n_all / C : sidx * n_all / S;
   const int n = idle ? 0 : grouped ? (crank + 1) * n_all / C - kv_lo : (sidx + 1) * n_all / S - kv_lo;
-  // The second query tile holds rows (a pair always runs both tiles: the
-  // leader's MMAs cover both CTAs' tiles; rows past q_rows are not stored).
-  const bool has_b = PAIR || (!grouped && q0 + 128 < p.q_rows);
+  const bool has_b = !grouped && q0 + 128 < p.q_rows;   // the second query tile holds rows
   auto tile_of = [&](int j) {   // this CTA's j-th key tile
     const int jj = kv_lo + j;
     if (grouped && jj == n0) {
@@ -317,36 +288,26 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < SL; ++i) {
+    for (int i = 0; i < ATT_SLOTS; ++i) {
       mbar_init(full + 8 * i, 1);
       mbar_init(empty + 8 * i, 1);
-      if (PAIR) mbar_init(pfull + 8 * i, 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + 8 * i, 1);
-      mbar_init(p_full + 8 * i, PAIR ? 8 : 4);   // one arrival per softmax warp of the tile (both CTAs)
+      mbar_init(p_full + 8 * i, 4);   // one arrival per softmax warp of the tile
     }
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     mbar_init(recv_bar, 1);
-    if (PAIR) {
-      mbar_init(qpair, 1);
-      mbar_init(bye, 1);
-    }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == ATT_MMA_WARP) {
-    if constexpr (PAIR) {
-      tmem_alloc_pair(smem_u32(tmem_slot), 512);
-    } else {
-      tmem_alloc(smem_u32(tmem_slot), 512);
-      tmem_relinquish();
-    }
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) cluster_sync_all();   // both CTAs' barriers and TMEM exist before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -381,22 +342,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!mbar_wait(slot_empty(L), slot_phase(L) ^ 1, abort_flag)) { go = false; return; }
         const CUtensorMap* m = is_v ? mv : mk;
         const int col = is_v ? vc : kc;
-        if constexpr (PAIR) {
-          // This CTA's half: keys [64 prank, + 64) of K (64-row boxes), or
-          // dims [64 prank, + 64) of V.
-          mbar_arrive_expect_tx(slot_full(L), ATT2_SLOT_BYTES);
-          if (is_v) {
-            tma_load_2d(slot_addr(L), m, slot_full(L), col + 64 * static_cast<int>(prank), t.row);
-          } else {
-            const int krow = t.row + 64 * static_cast<int>(prank);
-            tma_load_2d(slot_addr(L), m, slot_full(L), col, krow);
-            tma_load_2d(slot_addr(L) + ATT2_KATOM, m, slot_full(L), col + 64, krow);
-          }
-        } else {
-          mbar_arrive_expect_tx(slot_full(L), ATT_TILE_BYTES);
-          tma_load_2d(slot_addr(L), m, slot_full(L), col, t.row);
-          tma_load_2d(slot_addr(L) + ATT_ATOM, m, slot_full(L), col + 64, t.row);
-        }
+        mbar_arrive_expect_tx(slot_full(L), ATT_TILE_BYTES);
+        tma_load_2d(slot_addr(L), m, slot_full(L), col, t.row);
+        tma_load_2d(slot_addr(L) + ATT_ATOM, m, slot_full(L), col + 64, t.row);
         issued = L + 1;
       };
       if (split) {
@@ -419,78 +367,46 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
       // Teardown: loads still in flight must land before the CTA exits.
       mbar_wait_teardown(q_full, 0);
-      for (int L = max(0, issued - SL); L < issued; ++L)
+      for (int L = max(0, issued - ATT_SLOTS); L < issued; ++L)
         mbar_wait_teardown(slot_full(L), slot_phase(L));
     }
   } else if (warp == ATT_MMA_WARP) {
-   // Zero V rows [len, 16*ceil(len/16)) of ring load L (both 64-column
-   // halves; a pair CTA holds one), so that P = 0 there never meets stale rows.
-   auto zero_v_tail = [&](int L, int len) {
-     if (len & 15) {
-       constexpr int CPR = PAIR ? 8 : 16;   // 16-byte chunks per key row
-       uint8_t* vt = smem + L::RING_OFF + (L % SL) * SLOT_BYTES;
-       const int r0 = len, r1 = ((len + 15) >> 4) * 16;
-       for (int i = 0; i < (r1 - r0) * CPR; ++i) {
-         const int r = r0 + i / CPR, c = i % CPR;
-         uint8_t* dst = vt + (c >> 3) * ATT_ATOM + r * 128 + (c & 7) * 16;
-         *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-       }
-       fence_proxy_async();
-     }
-   };
-   if (PAIR && !leader && lane == 0) {
-    // ------------------------------------------- pair relay (peer, lane 0)
-    // Forward "this CTA's half is in place" to the leader's MMA issuer: the
-    // query tiles once, then every K/V load in ring order.
-    bool ok = mbar_wait(q_full, 0, abort_flag);
-    if (ok) mbar_arrive_remote(map_to_rank(qpair, 0));
-    for (int L = 0; ok && L < 2 * n; ++L) {
-      if (!mbar_wait(slot_full(L), slot_phase(L), abort_flag)) break;
-      if (L & 1) zero_v_tail(L, tile_of(L >> 1).len);
-      mbar_arrive_remote(map_to_rank(pfull + 8 * (L % SL), 0));
-    }
-   } else if (lane == 0) {
+   if (lane == 0) {
     // ------------------------------------------------ MMA issuer (lane 0)
-    constexpr uint32_t IDESC_S = idesc_bf16(PAIR ? 256 : 128, 128, 0);
-    constexpr uint32_t IDESC_O = idesc_bf16(PAIR ? 256 : 128, 128, 1);
+    constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0);
+    constexpr uint32_t IDESC_O = idesc_bf16(128, 128, 1);
     const int ntq = has_b ? 2 : 1;
-    auto commit_both = [&](uint32_t bar) {   // arrive on this barrier (of both CTAs of a pair)
-      if constexpr (PAIR) umma2_commit_both(bar);
-      else umma_commit(bar);
-    };
     // S_t = Q K^T into TMEM columns [t*128, t*128+128); Q at qb, K at ring address kb.
     auto issue_s = [&](int t, uint32_t qb, uint32_t kb) {
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t off = (kk >> 2) * ATT_ATOM + (kk & 3) * 32;
-        if constexpr (PAIR) {
-          const uint32_t koff = (kk >> 2) * ATT2_KATOM + (kk & 3) * 32;
-          umma2_bf16(tmem + t * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + koff, 16, 1024),
-                     IDESC_S, kk > 0);
-        } else {
-          umma_bf16(tmem + t * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
-                    IDESC_S, kk > 0);
-        }
+        umma_bf16(tmem + t * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
+                  IDESC_S, kk > 0);
       }
-      commit_both(s_full + 8 * t);
+      umma_commit(s_full + 8 * t);
     };
     // O_t += P_t V (V at ring address vb); P_t is packed bf16 in TMEM columns [t*128, t*128+64).
     auto issue_pv = [&](int t, uint32_t vb, int ksteps, bool acc) {
-      for (int kk = 0; kk < ksteps; ++kk) {
-        if constexpr (PAIR)
-          umma2_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                        sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, acc || kk > 0);
-        else
-          umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                       sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, acc || kk > 0);
+      for (int kk = 0; kk < ksteps; ++kk)
+        umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                     sw128_desc(vb + kk * 2048, ATT_ATOM, 1024), IDESC_O, acc || kk > 0);
+    };
+    // Zero V rows [len, 16*ceil(len/16)) of ring load L in both 64-column halves.
+    auto zero_v_tail = [&](int L, int len) {
+      if (len & 15) {
+        uint8_t* vt = smem + L::RING_OFF + (L % ATT_SLOTS) * ATT_TILE_BYTES;
+        const int r0 = len, r1 = ((len + 15) >> 4) * 16;
+        for (int i = 0; i < (r1 - r0) * 16; ++i) {
+          const int r = r0 + (i >> 4), c = i & 15;
+          uint8_t* dst = vt + (c >> 3) * ATT_ATOM + r * 128 + (c & 7) * 16;
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async();
       }
     };
-    // Load L is in place: this CTA's bytes landed (and, in a pair, the peer relayed its half).
-    auto wait_full = [&](int L) {
-      if (!mbar_wait(slot_full(L), slot_phase(L), abort_flag)) return false;
-      return !PAIR || mbar_wait(pfull + 8 * (L % SL), slot_phase(L), abort_flag);
-    };
-    bool ok = mbar_wait(q_full, 0, abort_flag) && (!PAIR || mbar_wait(qpair, 0, abort_flag));
+    auto wait_full = [&](int L) { return mbar_wait(slot_full(L), slot_phase(L), abort_flag); };
+    bool ok = mbar_wait(q_full, 0, abort_flag);
     if (split) {
       // Loads: K_A(0) = 0, K_B(0) = 1, then V_A(j), K_A(j+1), V_B(j), K_B(j+1).
       for (int t = 0; ok && t < 2; ++t) {
@@ -498,7 +414,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (ok) {
           tc_fence_after();
           issue_s(t, sQ, slot_addr(t));
-          commit_both(slot_empty(t));
+          umma_commit(slot_empty(t));
         }
       }
       int Lc = 2;
@@ -512,13 +428,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           issue_pv(t, slot_addr(Lc), (len + 15) >> 4, j > 0);
-          commit_both(slot_empty(Lc));
+          umma_commit(slot_empty(Lc));
           ++Lc;
           if (j + 1 < nt) {
             if (!wait_full(Lc)) { ok = false; break; }
             tc_fence_after();
             issue_s(t, sQ, slot_addr(Lc));
-            commit_both(slot_empty(Lc));
+            umma_commit(slot_empty(Lc));
             ++Lc;
           }
         }
@@ -529,7 +445,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < ntq; ++t) issue_s(t, sQ + t * ATT_TILE_BYTES, slot_addr(0));
-        commit_both(slot_empty(0));
+        umma_commit(slot_empty(0));
       }
     }
     for (int j = 0; !split && ok && j < n; ++j) {
@@ -543,7 +459,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         issue_pv(t, slot_addr(2 * j + 1), ksteps, j > 0);
-        if (t == ntq - 1) commit_both(slot_empty(2 * j + 1));
+        if (t == ntq - 1) umma_commit(slot_empty(2 * j + 1));
         if (next) {
           if (!knext) {
             if (!wait_full(2 * j + 2)) { ok = false; break; }
@@ -553,11 +469,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           issue_s(t, sQ + t * ATT_TILE_BYTES, slot_addr(2 * j + 2));
         }
       }
-      if (ok && next) commit_both(slot_empty(2 * j + 2));
+      if (ok && next) umma_commit(slot_empty(2 * j + 2));
     }
-    commit_both(o_done);
-    if constexpr (PAIR) umma2_commit_local(drain);
-    else umma_commit(drain);
+    umma_commit(o_done);
+    umma_commit(drain);
     mbar_wait_teardown(drain, 0);
    }
     __syncwarp();
@@ -652,10 +567,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        if (PAIR && !leader) mbar_arrive_remote(map_to_rank(p_full + 8 * t, 0));
-        else mbar_arrive(p_full + 8 * t);
-      }
+      if (lane == 0) mbar_arrive(p_full + 8 * t);
       l = l * alpha + (sv.x + sv.y);
       m_used = m_new;
     }
@@ -969,19 +881,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) {
-    // Exit handshake: neither CTA frees its TMEM or leaves (its shared
-    // memory holding barriers the other signals) before both are done.
-    if (threadIdx.x == 0) {
-      mbar_arrive_remote(map_to_rank(bye, prank ^ 1));
-      mbar_wait_teardown(bye, 0);
-    }
-    __syncthreads();
-  }
   if (warp == ATT_MMA_WARP) {
     tc_fence_after();
-    if constexpr (PAIR) tmem_dealloc_pair(tmem, 512);
-    else tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 512);
   }
 }
 

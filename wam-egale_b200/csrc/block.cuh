@@ -37,17 +37,9 @@ struct AttnSplitBuffers {
 // 12 heads, 3 splits of 4-5 tiles measured 52 us against 42 unsplit).
 // Candidate verification (src0_map)
 // never splits. `force` > 0: that factor (capped by the key tiles).
-// Query-tile-pair CTAs of one (head, batch row): ceil(q_rows / 256), an
-// even count when the CTA-pair kernel runs (q_rows > 128: pairs of CTAs
-// along x, the last CTA of an odd count without rows).
-inline int attn_grid_x(int q_rows) {
-  const int x = (q_rows + 255) / 256;
-  return q_rows > 128 ? (x + 1) & ~1 : x;
-}
-
 inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) {
   if (a->src0_map != nullptr || a->batch <= 0 || a->q_rows <= 0) return 1;
-  const long long items = static_cast<long long>(attn_grid_x(a->q_rows)) * a->heads * a->batch;
+  const long long items = static_cast<long long>((a->q_rows + 255) / 256) * a->heads * a->batch;
   if (items > ATT_MAX_ITEMS) return 1;
   const long long keys = a->tiles != nullptr ? a->src0_batch_stride : a->src0_len;
   const int n_est = static_cast<int>((std::max<long long>(keys, 0) + 127) / 128);
@@ -95,7 +87,7 @@ inline bool attn_group_shape(int q_rows, int batch, int heads, int sms, int* G_o
 
 inline size_t attn_split_part_bytes(const wamb_attention_args* a, int S) {
   if (S <= 1) return 0;
-  return static_cast<size_t>(attn_grid_x(a->q_rows)) * a->heads * a->batch * S * ATT_PART_BYTES;
+  return static_cast<size_t>((a->q_rows + 255) / 256) * a->heads * a->batch * S * ATT_PART_BYTES;
 }
 
 // trigger: a GEMM that requests weights before its pdl_wait follows.
@@ -162,8 +154,6 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
                                          AttnSmem::TOTAL));
     WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnSmem::TOTAL));
-    WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         AttnSmem::TOTAL));
     configured[dev] = true;
   }
   dim3 grid((a->q_rows + 255) / 256, a->heads, a->batch);
@@ -201,36 +191,6 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
       p.kv_count = split->count;
       grid.z = a->batch * S;
     }
-  }
-  if (a->q_rows > 128) {
-    // CTA pairs (clusters of 2 along x): each CTA loads 64-row halves of the
-    // K tiles, so its K maps have 64-row boxes (V keeps 128-row boxes of 64
-    // columns, a CTA loading its 64 of the head's 128 dims).
-    CUtensorMap tk0h, tk1h;
-    if ((rc = make_tmap_bf16(&tk0h, a->k0, a->src0_total_rows, a->ld0, a->ld0, 64))) return rc;
-    if (p.has_src1) {
-      const int64_t rows1 = static_cast<int64_t>(a->batch) * a->q_rows;
-      if ((rc = make_tmap_bf16(&tk1h, a->k1, rows1, a->ld1, a->ld1, 64))) return rc;
-    } else {
-      tk1h = tk0h;
-    }
-    grid.x = attn_grid_x(a->q_rows);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(ATT_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = AttnSmem::TOTAL;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    WAMB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<false, true>, tq, tk0h, tv0, tk1h, tv1, p));
-    return WAMB_OK;
   }
   return launch_kernel(attn_tc_kernel<false>, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
                        tv1, p);

@@ -57,6 +57,10 @@ struct Gemm2Smem {
   static_assert(TOTAL <= 232448, "2-CTA GEMM shared memory exceeds 227 KB");
 };
 
+WAMB_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
 // TMA load into this CTA's shared memory that completes on the mbarrier at
 // `bar_cluster` (the leader CTA's full barrier).
 WAMB_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
@@ -76,6 +80,32 @@ WAMB_DEV void umma2_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+WAMB_DEV void umma2_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at this offset in both CTAs of the pair when
+// all previously issued tcgen05 ops of this thread complete.
+WAMB_DEV void umma2_commit_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+// Same, arriving only on this CTA's barrier (every tcgen05 op of a kernel
+// uses one cta_group, so the teardown drain needs the ::2 form too).
+WAMB_DEV void umma2_commit_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
 // One output tile's k-block range processed by a pair.
 struct Seg {
   int t, kb0, kb1;
