@@ -3,8 +3,7 @@
 Shapes with M >= 512 and N per group a multiple of 256 take the two-CTA
 (cta_group::2) kernel when they have at least 74 256 x 256 tiles, or when
 the stream-K scratch lets them share a partly filled last round over all
-SM pairs (with 256 x 224 tiles when those give shorter rounds, the M 880
-FFN1); residual-epilogue shapes with N per group a multiple of 192 take it with
+SM pairs; residual-epilogue shapes with N per group a multiple of 192 take it with
 256 x 192 tiles when the cost model rates that faster (the M 880, N 3072
 projections);
 the others take the one-CTA kernel with 64/128/192/256-column tiles, split
@@ -286,49 +285,3 @@ def test_linear_pair192_fp8(cuda_device):
     err = (out - (res + deq(a8, sa) @ deq(w8, sw).t() + b.float())).abs().max().item()
     assert err <= 5e-3, err
 
-
-@pytest.mark.parametrize("m,k,n", [
-    (880, 3072, 14336),    # FFN1 of one cfg2 chunk: 256 pair tiles of 256 x 224 (3.46 rounds)
-    (1592, 1536, 8960),    # FFN1 of the D 1536 stack: 280 pair tiles, a ragged last row block
-])
-def test_linear_pair224(cuda_device, m, k, n):
-    """Two-CTA kernel with 256 x 224 tiles (the two epilogue warps of a lane
-    quarter take 4 and 3 chunks of 32 columns): GELU, bias, and the gated
-    fp32 residual, bitwise repeatable."""
-    g = torch.Generator(device="cuda").manual_seed(m + k + 7 * n)
-    B = 2
-    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
-    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16()
-    b = torch.randn(n, device="cuda", generator=g).bfloat16()
-    gelu = ops.linear(a, w, b, epilogue=_lib.EPI_GELU)
-    out, again = ops.linear(a, w, b), ops.linear(a, w, b)
-    res = torch.randn(m, n, device="cuda", generator=g)
-    table = torch.randn(6, n, device="cuda", generator=g) * 0.1
-    temb = torch.randn(B, 1, 6, n, device="cuda", generator=g) * 0.1
-    o32 = torch.empty(m, n, device="cuda")
-    ops.linear(a, w, b, epilogue=_lib.EPI_RES_GATE, res=res, table=table, temb=temb,
-               rows_per_batch=m // B, gate_index=4, out=o32)
-    torch.cuda.synchronize()
-    assert _lib.device_status() == 0
-    base = _ref(a, [w], [b])
-    _close(out, base)
-    assert torch.equal(out, again)
-    _close(gelu, torch.nn.functional.gelu(base, approximate="tanh"))
-    gate = (table[4][None, None] + temb[:, :, 4]).expand(B, m // B, n).reshape(m, n)
-    err = (o32 - (res + base * gate)).abs().max().item()
-    assert err <= 5e-3, err
-
-
-def test_linear_pair224_fp8(cuda_device):
-    m, k, n = 880, 3072, 14336
-    g = torch.Generator(device="cuda").manual_seed(9)
-    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
-    w = (torch.randn(n, k, device="cuda", generator=g) * 0.05).bfloat16()
-    b = torch.randn(n, device="cuda", generator=g).bfloat16()
-    a8, sa = ops.quantize_rows(a)
-    w8, sw = ops.quantize_rows(w)
-    out = ops.linear(a8, w8, b, a_scale=sa, w_scales=sw, epilogue=_lib.EPI_GELU)
-    torch.cuda.synchronize()
-    assert _lib.device_status() == 0
-    deq = lambda q, s: q.float() * s[:, None]  # noqa: E731
-    _close(out, torch.nn.functional.gelu(deq(a8, sa) @ deq(w8, sw).t() + b.float(), approximate="tanh"))

@@ -340,8 +340,7 @@ WAMB_DEV float4 lds4(uint32_t a) {
   return x;
 }
 
-// nc (2 <= nc <= NC, NC 3 or 4) 32-column chunks [c0, c0 + nc) of one tile
-// (one inlined body for the warp halves of a 256 x 224 tile, 4 and 3 chunks). The residual of chunks
+// NC (3 or 4) 32-column chunks [c0, c0 + NC) of one tile. The residual of chunks
 // c0 and c0 + 1 is requested before `wait_acc` (the wait for the
 // accumulator: the residual does not depend on it), and each later chunk's
 // two chunks ahead, so its DRAM latency overlaps the accumulator wait and
@@ -350,7 +349,7 @@ WAMB_DEV float4 lds4(uint32_t a) {
 // mainloop's A and weight tiles out of L2. Returns false if wait_acc gave up.
 template <int NC, class WaitAcc>
 WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int row0, int lane, int n0,
-                                        int c0, int nc, uint32_t st, WaitAcc&& wait_acc) {
+                                        int c0, uint32_t st, WaitAcc&& wait_acc) {
   const int row = row0 + lane;
   const EpiRow e = epi_row(p, row, n0);
   const bool has_res = p.epi == EPI_RES || p.epi == EPI_RES_GATE;
@@ -389,7 +388,6 @@ WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int
   static_assert(NC >= 2, "the residual of two chunks is requested ahead");
 #pragma unroll
   for (int k = 0; k < NC; ++k) {
-    if (k >= nc) break;
     const int c = c0 + k;
     uint4 (&rc)[8] = (k & 1) ? rb : ra;
     if (has_res) {
@@ -407,7 +405,7 @@ WAMB_DEV bool gemm_epilogue_tile_staged(const GemmParams& p, uint32_t taddr, int
         }
         sts4(rm(i), x);
       }
-      if (k + 2 < nc) fetch(c + 2, rc);
+      if (k + 2 < NC) fetch(c + 2, rc);
     }
     float v[32];
     tmem_ld32(taddr + c * 32, v);

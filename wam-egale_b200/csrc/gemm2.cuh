@@ -1,10 +1,10 @@
 // Two-CTA (cta_group::2) variant of the tcgen05 GEMM for large M:
-// a cluster of 2 CTAs computes a 256 x BN output tile (BN 256, 224 or 192) with
+// a cluster of 2 CTAs computes a 256 x BN output tile (BN 256 or 192) with
 // M=256 tcgen05.mma instructions issued by the leader CTA. Each CTA loads
 // its own 128 rows of A and its own BN / 2 of the tile's BN weight rows, so
-// a CTA moves 32 / 30 / 28 KB (BN 256 / 224 / 192) per 64-wide k-block
-// instead of 48 / 44 / 40 KB for a 128 x BN tile on one SM: the shared
-// weight tile crosses the L2 -> SM path once per pair.
+// a CTA moves 32 KB (BN 256) or 28 KB (BN 192) per 64-wide k-block instead
+// of 48 / 40 KB for a 128 x BN tile on one SM: the shared weight tile
+// crosses the L2 -> SM path once per pair.
 //
 // Barriers (per CTA):
 //   full[s]    leader only: one arrive_expect_tx (both CTAs' bytes); both
@@ -43,7 +43,7 @@ constexpr int GEMM2_STAGES = 6;
 
 template <int BN>
 struct Gemm2Smem {
-  static_assert(BN == 256 || BN == 224 || BN == 192, "two-CTA tiles are 256, 224 or 192 columns wide");
+  static_assert(BN == 256 || BN == 192, "two-CTA tiles are 256 or 192 columns wide");
   static constexpr uint32_t A_BYTES = 128 * 128;        // this CTA's 128 rows of A x 128 bytes of K
   static constexpr uint32_t B_BYTES = (BN / 2) * 128;   // this CTA's BN / 2 of BN weight rows
   static constexpr uint32_t BAR_OFF = GEMM2_STAGES * (A_BYTES + B_BYTES);
@@ -213,9 +213,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     const GemmParams p) {
   using L = Gemm2Smem<BN>;
   constexpr int STAGES = GEMM2_STAGES;
-  // 32-column chunks of the two epilogue warps of a lane quarter: [0, NC0)
-  // and [NC0, NC0 + NC1) (4 + 4, 4 + 3 or 3 + 3).
-  constexpr int NC0 = (BN / 32 + 1) / 2, NC1 = BN / 32 - NC0;
+  constexpr int NCH = BN / 64;   // 32-column chunks per epilogue warp (two warps per lane quarter)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -358,8 +356,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter accessible to this warp
-    const int half = (warp - 2) >> 2;  // chunks [c0, c0 + nch) of the tile
-    const int c0 = half * NC0, nch = half ? NC1 : NC0;
+    const int half = (warp - 2) >> 2;  // columns [half * BN / 2, + BN / 2)
+    const int c0 = half * NCH, nch = NCH;
     const int row_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
     const uint32_t tempty_leader0 = map_to_rank(tempty0, 0);
     // Every tile's epilogue goes through the warp's staging buffer.
@@ -459,7 +457,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tc_fence_after();
           return true;
         };
-        ok = ready && gemm_epilogue_tile_staged<NC0>(p, taddr, row - lane, lane, n0, c0, nch, stage, wait_acc);
+        ok = ready && gemm_epilogue_tile_staged<NCH>(p, taddr, row - lane, lane, n0, c0, stage, wait_acc);
         if (ok && q_lo < pair) {
           __syncwarp();
           if (lane == 0)

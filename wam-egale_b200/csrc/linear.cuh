@@ -221,8 +221,7 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
 // for the one-CTA kernel. Stream-K (sk: every pair gets an equal share of
 // the last round) needs 256-column tiles. Otherwise 256 x 256 tiles when
 // the weight groups split into them and there are enough to give every SM
-// pair one (or 256 x 224 ones when they model faster), and, for the
-// residual epilogues, 256 x 192 tiles when
+// pair one, and, for the residual epilogues, 256 x 192 tiles when
 // plan_tiles' cost model, applied to a pair, rates them faster than that
 // choice: an SM ingests (128 + BN / 2) x 128 bytes per k-block (A rows plus
 // its half of the weight rows) at ~90 GB/s, tiles run in rounds over the SM
@@ -235,7 +234,7 @@ inline TilePlan plan_tiles(int M, int N, int n_per_group, int num_kb, int sms, b
 inline int gemm_pair_bn(int M, long long N, int n_per_group, int num_kb, int sms, bool f8, int epi,
                         bool sk = false) {
   if (M < 512) return 0;
-  const bool c256 = n_per_group % 256 == 0, c224 = n_per_group % 224 == 0, c192 = n_per_group % 192 == 0;
+  const bool c256 = n_per_group % 256 == 0, c192 = n_per_group % 192 == 0;
   if (sk) return c256 ? 256 : 0;
   const int pairs = sms / 2;
   const double t_dram = static_cast<double>(N) * num_kb * 128.0 / (6000.0 * 1e3);   // us
@@ -246,14 +245,7 @@ inline int gemm_pair_bn(int M, long long N, int n_per_group, int num_kb, int sms
   };
   const long long t256 = c256 ? static_cast<long long>((M + 255) / 256) * (N / 256) : 0;
   int best = c256 && t256 >= pairs ? 256 : 0;
-  double best_t = best ? cost(256) : plan_tiles(M, static_cast<int>(N), n_per_group, num_kb, sms, f8).cost_us;
-  // 256 x 224 instead of 256 x 256 tiles when the model rates that faster:
-  // FFN1 at M 880 (N 14336) is 3.03 rounds of 256-wide tiles, 3.46 of
-  // 224-wide ones, each 7/8 as long.
-  if (best == 256 && c224 && cost(224) < best_t) {
-    best = 224;
-    best_t = cost(224);
-  }
+  const double best_t = best ? cost(256) : plan_tiles(M, static_cast<int>(N), n_per_group, num_kb, sms, f8).cost_us;
   const bool res = epi == WAMB_EPI_RES || epi == WAMB_EPI_RES_GATE;
   if (c192 && res && cost(192) < best_t) best = 192;
   return best;
@@ -392,11 +384,8 @@ inline int linear_impl(const wamb_linear_args* a, cudaStream_t stream, bool w_ea
   }
   auto launch = [&](auto f8c) {
     constexpr bool F8 = decltype(f8c)::value;
-    if (pair) {
-      if (pbn == 256) return launch_gemm2<F8, 256>(ta, tb, p, di.sms, stream);
-      if (pbn == 224) return launch_gemm2<F8, 224>(ta, tb, p, di.sms, stream);
-      return launch_gemm2<F8, 192>(ta, tb, p, di.sms, stream);
-    }
+    if (pair) return pbn == 256 ? launch_gemm2<F8, 256>(ta, tb, p, di.sms, stream)
+                                : launch_gemm2<F8, 192>(ta, tb, p, di.sms, stream);
     if (tp.splits > 1) {
       if (bn == 128) return launch_gemm_cl<128, 6, F8>(ta, tb, p, stream);
       return launch_gemm_cl<64, 8, F8>(ta, tb, p, stream);
