@@ -500,6 +500,9 @@ def run_native(args):
             # The configs the north-star target is quoted on, timed on the same GPU.
             line["configs"] = {n: run_stack_config(n, dev, args.steps, args.warmup, seed=7 + i)
                                for i, n in enumerate(("cfg2", "cfg1"))}
+            # cfg2 with the E4M3 GEMMs (configs[4]'s second run, at batch 1).
+            line["configs"]["cfg2_fp8"] = run_stack_config("cfg2", dev, args.steps, args.warmup, fp8=True,
+                                                           seed=7)
         if world == 1 and not args.no_cpu_baseline:
             v, th, dt, sample = cpu_reference_rate()
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": th, "kind": "port",
