@@ -386,7 +386,11 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
   for (; k < nk; ++k) {
     const int row = r_begin + warp + k * LNW_WARPS;
     if (!mbar_wait(bar0 + 8 * (k % NS), (k / NS) & 1, abort_flag)) break;
-    float v[NV][8];
+    // The row as fp32 pairs: v[i][2h + e] holds columns col_of(i, h) + 2e,
+    // + 1. The arithmetic below runs on the pairs (sm_100 f32x2), one
+    // instruction per two columns, in the same order and rounding as
+    // separate fp32 operations.
+    uint64_t v[NV][4];
     const uint8_t* srow = slots + (warp * NS + k % NS) * row_bytes;
 #pragma unroll
     for (int i = 0; i < NV; ++i)
@@ -394,12 +398,14 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
       for (int h = 0; h < 2; ++h) {
         const int col = col_of(i, h);
         if (p.x_f32) {
-          const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(srow) + col);
-          v[i][4 * h] = x.x; v[i][4 * h + 1] = x.y; v[i][4 * h + 2] = x.z; v[i][4 * h + 3] = x.w;
+          const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(reinterpret_cast<const float*>(srow) + col);
+          v[i][2 * h] = x.x;
+          v[i][2 * h + 1] = x.y;
         } else {
           const uint2 x = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(srow) + col);
           const float2 a = unpack_bf16(x.x), c = unpack_bf16(x.y);
-          v[i][4 * h] = a.x; v[i][4 * h + 1] = a.y; v[i][4 * h + 2] = c.x; v[i][4 * h + 3] = c.y;
+          v[i][2 * h] = f2(a.x, a.y);
+          v[i][2 * h + 1] = f2(c.x, c.y);
         }
       }
     __syncwarp();
@@ -411,24 +417,31 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
       ++issued;
     }
     if (p.affine != 2) {
-      // Eight independent partial sums per lane (short dependency chains).
-      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // Eight independent partial sums per lane (short dependency chains),
+      // as four pairs.
+      auto row_sum = [&](const uint64_t (&s2)[4]) {
+        const float2 a = f2_split(s2[0]), b = f2_split(s2[1]), c = f2_split(s2[2]), d = f2_split(s2[3]);
+        return warp_sum(((a.x + a.y) + (b.x + b.y)) + ((c.x + c.y) + (d.x + d.y)));
+      };
+      uint64_t s2[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s8[j] += v[i][j];
-      const float mean = warp_sum(((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))) / D;
+        for (int j = 0; j < 4; ++j) s2[j] = fadd2(s2[j], v[i][j]);
+      const float mean = row_sum(s2) / D;
+      const uint64_t mean2 = f2(mean, mean);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s8[j] = 0.f;
+      for (int j = 0; j < 4; ++j) s2[j] = f2(0.f, 0.f);
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float d = v[i][j] - mean;
-          s8[j] = fmaf(d, d, s8[j]);
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t d = fsub2(v[i][j], mean2);
+          s2[j] = ffma2(d, d, s2[j]);
         }
-      const float var = warp_sum(((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))) / D;
+      const float var = row_sum(s2) / D;
       const float rstd = rsqrtf(var + p.eps);
+      const uint64_t rstd2 = f2(rstd, rstd);
       long long trow = 0;
       if (per_token) {
         const int tok = row - b * rpb;
@@ -439,19 +452,19 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int col = col_of(i, h);
-          float4 m = *reinterpret_cast<const float4*>(smul + col);
-          float4 a = *reinterpret_cast<const float4*>(sadd + col);
+          ulonglong2 m = *reinterpret_cast<const ulonglong2*>(smul + col);
+          ulonglong2 a = *reinterpret_cast<const ulonglong2*>(sadd + col);
           if (per_token) {
             const float4 tm = load_temb4(p.temb, p.temb_f32, trow + static_cast<long long>(ts) * D + col);
             const float4 ta = load_temb4(p.temb, p.temb_f32, trow + static_cast<long long>(th) * D + col);
-            m.x += tm.x; m.y += tm.y; m.z += tm.z; m.w += tm.w;
-            a.x += ta.x; a.y += ta.y; a.z += ta.z; a.w += ta.w;
+            m.x = fadd2(m.x, f2(tm.x, tm.y));
+            m.y = fadd2(m.y, f2(tm.z, tm.w));
+            a.x = fadd2(a.x, f2(ta.x, ta.y));
+            a.y = fadd2(a.y, f2(ta.z, ta.w));
           }
-          float* w = &v[i][4 * h];
-          w[0] = (w[0] - mean) * rstd * m.x + a.x;
-          w[1] = (w[1] - mean) * rstd * m.y + a.y;
-          w[2] = (w[2] - mean) * rstd * m.z + a.z;
-          w[3] = (w[3] - mean) * rstd * m.w + a.w;
+          // (x - mean) * rstd * (1 + scale) + shift, or * gamma + beta
+          v[i][2 * h] = ffma2(fmul2(fsub2(v[i][2 * h], mean2), rstd2), m.x, a.x);
+          v[i][2 * h + 1] = ffma2(fmul2(fsub2(v[i][2 * h + 1], mean2), rstd2), m.y, a.y);
         }
     }
     if (p.out8 == nullptr) {
@@ -460,15 +473,20 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
       for (int i = 0; i < NV; ++i)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          *reinterpret_cast<uint2*>(orow + col_of(i, h)) =
-              make_uint2(pack_bf16(v[i][4 * h], v[i][4 * h + 1]), pack_bf16(v[i][4 * h + 2], v[i][4 * h + 3]));
+        {
+          const float2 x = f2_split(v[i][2 * h]), y = f2_split(v[i][2 * h + 1]);
+          *reinterpret_cast<uint2*>(orow + col_of(i, h)) = make_uint2(pack_bf16(x.x, x.y), pack_bf16(y.x, y.y));
+        }
     } else {
       // E4M3 with the row scale amax / 448 (the quant_rows_kernel rule).
       float am = 0.f;
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[i][j]));
+        for (int j = 0; j < 4; ++j) {
+          const float2 x = f2_split(v[i][j]);
+          am = fmaxf(am, fmaxf(fabsf(x.x), fabsf(x.y)));
+        }
       const float amax = fmaxf(warp_max(am), 1e-20f);
       const float inv = 448.f / amax;
       if (lane == 0) p.out_scale[row] = amax / 448.f;
@@ -477,7 +495,11 @@ __global__ void __launch_bounds__(LNW_WARPS * 32, 1) ln_warp_kernel(const LnPara
       for (int i = 0; i < NV; ++i) {
         float t[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = v[i][j] * inv;
+        for (int j = 0; j < 4; ++j) {
+          const float2 x = f2_split(v[i][j]);
+          t[2 * j] = x.x * inv;
+          t[2 * j + 1] = x.y * inv;
+        }
         const uint2 q = pack_e4m3x8(t);   // bytes 0-3: group h = 0, bytes 4-7: h = 1
         *reinterpret_cast<uint32_t*>(orow + col_of(i, 0)) = q.x;
         *reinterpret_cast<uint32_t*>(orow + col_of(i, 1)) = q.y;
