@@ -297,11 +297,15 @@ WAMB_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t 
                : "memory");
 }
 
-constexpr int LNW_WARPS = 8;
+constexpr int LNW_WARPS = 10;
 
-// Row slots per warp: two fp32 rows or four bf16 rows (~192 KB of rows in
-// flight per SM at D 3072 either way).
-__host__ __device__ constexpr int ln_warp_slots(int x_f32) { return x_f32 ? 2 : 4; }
+// Row slots per warp: one fp32 row or three bf16 rows (120 / 180 KB of rows
+// in flight per SM at D 3072). Ten warps of ~168 registers: the kernel is
+// bound by each warp's instruction latency, not by DRAM, so more warps pay
+// more than deeper slots (8 warps with 2 / 4 slots: LN1 28.0, LN2 23.5 us
+// at M 7040; 10 warps: 24.1, 21.6 us; 12 warps with 1 / 2 slots: 24.5,
+// 21.8 us).
+__host__ __device__ constexpr int ln_warp_slots(int x_f32) { return x_f32 ? 1 : 3; }
 constexpr int LNW_MAX_SLOTS = 4;
 // Dynamic shared memory of ln_warp_kernel: multiplier and offset [2][D]
 // fp32, the row slots of every warp, one mbarrier per slot, the abort flag.
