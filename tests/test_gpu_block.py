@@ -86,10 +86,14 @@ def _cache_equal(oc, gc, tc):
         assert_parity(gc[name][:, idx.cuda()], oc[name][:, idx], tc[name][:, idx.cuda()])
 
 
-def test_block_kv_lifecycle_and_eviction(cuda_device):
+@pytest.mark.parametrize("Q,pool", [
+    (40, 100),
+    (520, 1300),   # M 1040: the warp-per-row LayerNorm and RMS, K/V written into pool slots
+])
+def test_block_kv_lifecycle_and_eviction(cuda_device, Q, pool):
     """prefill (update 2) x2, denoise (update 0), commit prediction (update 1)
     with eviction of the oldest chunk, then denoise again."""
-    D, H, F, B, Q, C, pool = 256, 2, 512, 2, 40, 24, 100
+    D, H, F, B, C = 256, 2, 512, 2, 24
     blk = make_oracle_block(D, F, H, seed=11)
     g = to_device_block(blk)
     tb = to_device_block(blk)

@@ -252,7 +252,7 @@ inline int launch_ln(const LnParams& p, cudaStream_t s) {
   // step), so small M keeps the one-row-per-CTA kernel.
   if (p.M >= 1024 && p.D % 256 == 0 && lsm <= 227 * 1024 && aligned16(p.x) &&
       (p.ldx * (p.x_f32 ? 4 : 2)) % 16 == 0) {
-    // Warp-per-row kernel, one CTA of 8 warps per SM: the CTAs of each
+    // Warp-per-row kernel, one CTA of LNW_WARPS warps per SM: the CTAs of each
     // batch row of the modulation split its rows evenly, and all CTAs fit
     // one wave (no SM runs a second CTA while others idle).
     const int rpb = p.affine ? p.M : p.rows_per_batch;
@@ -292,6 +292,30 @@ inline int launch_quant(const QuantParams& p, cudaStream_t s) {
 
 inline int launch_rms(const RmsParams& p, cudaStream_t s) {
   if (p.M == 0) return WAMB_OK;
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const size_t rsm = rmsw_smem(p.D, p.sections);
+  // Warp-per-row kernel at large M (as for the LayerNorm): one CTA of
+  // RMSW_WARPS warps per SM, all in one wave, each on a contiguous range of rows.
+  if (p.M >= 1024 && p.D % 256 == 0 && rsm <= 227 * 1024 && aligned16(p.x) && (p.ld * 2) % 16 == 0 &&
+      (p.freq == nullptr || aligned16(p.freq))) {
+    const int grid = std::min(p.M, di.sms);
+    const int rpc = (p.M + grid - 1) / grid;
+    rc = dispatch_nv(p.D / 256, [&](auto v) {
+      constexpr int NV = decltype(v)::value;
+      static bool configured[64] = {};
+      int dev = 0;
+      WAMB_CHECK_CUDA(cudaGetDevice(&dev));
+      if (!configured[dev]) {
+        WAMB_CHECK_CUDA(cudaFuncSetAttribute(rms_warp_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024));
+        configured[dev] = true;
+      }
+      return launch_kernel(rms_warp_kernel<NV>, dim3((p.M + rpc - 1) / rpc), dim3(RMSW_WARPS * 32), rsm, s, p, rpc);
+    });
+    if (rc != -1) return rc;
+  }
   const int vpt = row_vpt(p.D);
   WAMB_REQUIRE(vpt > 0, WAMB_ERR_SHAPE, "D=%d unsupported by the row kernels", p.D);
   const int threads = p.D / (8 * vpt);

@@ -649,6 +649,142 @@ __global__ void rms_rope_kernel(const RmsParams p) {
   }
 }
 
+// Warp-per-row variant of rms_rope_kernel for large M (the LayerNorm's
+// design): one CTA of RMSW_WARPS warps per SM, a contiguous range of rows
+// per CTA, one warp per row. A row's sections (q | k, adjacent in the row)
+// arrive in a shared-memory slot by one bulk copy, RMSW_SLOTS slots per
+// warp, so the next rows are in flight while one is normalized; gamma is
+// staged in shared memory once per CTA. Lane l holds columns [i*256 + h*128
+// + 4l, +4) of each section, so its two RoPE pairs are the same for every
+// head: one float4 of the row's frequencies per lane. The same arithmetic
+// as rms_rope_kernel per element (x * rstd * gamma, then the rotation);
+// the sum of squares is reduced in another order.
+constexpr int RMSW_WARPS = 10;
+__host__ __device__ constexpr int rmsw_slots(int sections) { return sections == 2 ? 1 : 3; }
+__host__ __device__ constexpr size_t rmsw_smem(int D, int sections) {
+  return 4ull * sections * D + static_cast<size_t>(rmsw_slots(sections)) * RMSW_WARPS * sections * D * 2 +
+         8ull * 3 * RMSW_WARPS + 16;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(RMSW_WARPS * 32, 1) rms_warp_kernel(const RmsParams p, int rpc) {
+  extern __shared__ __align__(16) uint8_t rm_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = p.D, SEC = p.sections;
+  const int NS = rmsw_slots(SEC);
+  const uint32_t row_bytes = static_cast<uint32_t>(SEC) * D * 2;
+  float* sg = reinterpret_cast<float*>(rm_smem);                       // gamma [SEC][D]
+  uint8_t* slots = rm_smem + 4 * SEC * D;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(slots + static_cast<size_t>(NS) * RMSW_WARPS * row_bytes);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * RMSW_WARPS);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 3 * RMSW_WARPS; ++i) mbar_init(smem_u32(bars + i), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  for (int s2 = 0; s2 < SEC; ++s2)
+    for (int c = threadIdx.x * 8; c < D; c += RMSW_WARPS * 32 * 8) {
+      float g[8];
+      load8((s2 == 0 ? p.gamma[0] : p.gamma[1]) + c, g);
+      *reinterpret_cast<float4*>(sg + s2 * D + c) = make_float4(g[0], g[1], g[2], g[3]);
+      *reinterpret_cast<float4*>(sg + s2 * D + c + 4) = make_float4(g[4], g[5], g[6], g[7]);
+    }
+  __syncthreads();
+  pdl_wait();
+  const int r_begin = blockIdx.x * rpc;
+  const int r_end = min(r_begin + rpc, p.M);
+  const int nk = r_end - r_begin > warp ? (r_end - r_begin - warp + RMSW_WARPS - 1) / RMSW_WARPS : 0;
+  const uint32_t slot0 = smem_u32(slots + static_cast<size_t>(warp) * NS * row_bytes);
+  const uint32_t bar0 = smem_u32(bars + 3 * warp);
+  auto request = [&](int k) {   // row k of this warp into slot k % NS (lane 0)
+    const int row = r_begin + warp + k * RMSW_WARPS;
+    const int sl = k % NS;
+    mbar_arrive_expect_tx(bar0 + 8 * sl, row_bytes);
+    bulk_load(slot0 + sl * row_bytes, p.x + static_cast<long long>(row) * p.ld, row_bytes, bar0 + 8 * sl);
+  };
+  int issued = 0;
+  if (lane == 0)
+    for (; issued < NS && issued < nk; ++issued) request(issued);
+  issued = __shfl_sync(0xffffffffu, issued, 0);
+  auto col_of = [&](int i, int h) { return i * 256 + h * 128 + lane * 4; };
+  int k = 0;
+  for (; k < nk; ++k) {
+    const int row = r_begin + warp + k * RMSW_WARPS;
+    const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
+    if (!mbar_wait(bar0 + 8 * (k % NS), (k / NS) & 1, abort_flag)) break;
+    const __nv_bfloat16* srow = reinterpret_cast<const __nv_bfloat16*>(slots + static_cast<size_t>(warp * NS + k % NS) * row_bytes);
+    bool to_pool = p.pool_k != nullptr;
+    long long dst_row = 0;
+    bool skip = false;
+    if (to_pool) {
+      const int slot = p.slots[tok];
+      skip = slot < 0 || slot >= p.pool;   // kv_layout_kernel rejected the call: no pool write
+      dst_row = static_cast<long long>(b) * p.pool + slot;
+    }
+    float4 fr = make_float4(1.f, 0.f, 1.f, 0.f);
+    if (p.freq != nullptr && !skip) {
+      const int fb = p.freq_batch == 1 ? 0 : b;
+      fr = __ldg(reinterpret_cast<const float4*>(p.freq + (static_cast<long long>(fb) * p.rows_per_batch + tok) * 64) + lane);
+    }
+    for (int s2 = 0; s2 < SEC && !skip; ++s2) {
+      float v[NV][8];
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint2 x = *reinterpret_cast<const uint2*>(srow + s2 * D + col_of(i, h));
+          const float2 a = unpack_bf16(x.x), c = unpack_bf16(x.y);
+          v[i][4 * h] = a.x; v[i][4 * h + 1] = a.y; v[i][4 * h + 2] = c.x; v[i][4 * h + 3] = c.y;
+        }
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s8[j] = fmaf(v[i][j], v[i][j], s8[j]);
+      const float ss = warp_sum(((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
+      const float rstd = rsqrtf(ss / D + (s2 == 0 ? p.eps[0] : p.eps[1]));
+      __nv_bfloat16* dst = (s2 == 1 && to_pool) ? p.pool_k + dst_row * D
+                                                : p.x + static_cast<long long>(row) * p.ld + s2 * D;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int col = col_of(i, h);
+          const float4 g = *reinterpret_cast<const float4*>(sg + s2 * D + col);
+          float y[4] = {v[i][4 * h] * rstd * g.x, v[i][4 * h + 1] * rstd * g.y, v[i][4 * h + 2] * rstd * g.z,
+                        v[i][4 * h + 3] * rstd * g.w};
+          if (p.freq != nullptr) {
+            // Pairs (2j, 2j+1) of each 128-wide head rotate by freq[b?, tok, j]
+            // (model.py:614-621, complex multiply).
+            const float a0 = y[0], b0 = y[1], a1 = y[2], b1 = y[3];
+            y[0] = a0 * fr.x - b0 * fr.y;
+            y[1] = a0 * fr.y + b0 * fr.x;
+            y[2] = a1 * fr.z - b1 * fr.w;
+            y[3] = a1 * fr.w + b1 * fr.z;
+          }
+          *reinterpret_cast<uint2*>(dst + col) = make_uint2(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
+        }
+    }
+    __syncwarp();
+    if (issued < nk) {   // the slot is free again: request the row NS ahead
+      if (lane == 0) {
+        fence_proxy_async();
+        request(issued);
+      }
+      ++issued;
+    }
+    if (to_pool && !skip) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<long long>(row) * p.ld + 2LL * D);
+      uint4* vdst = reinterpret_cast<uint4*>(p.pool_v + dst_row * D);
+      for (int i = lane; i < D / 8; i += 32) vdst[i] = src[i];
+    }
+  }
+  // After an abort, the copies still in flight must land before the CTA's
+  // shared memory goes away.
+  if (lane == 0)
+    for (int j = k; j < issued; ++j) mbar_wait_teardown(bar0 + 8 * (j % NS), (j / NS) & 1);
+}
+
 // ------------------------------------------------------------ KV layout
 // One CTA of 1024 threads. The pool mask is staged in shared memory; each
 // thread owns a contiguous segment of slots so that block scans follow the
