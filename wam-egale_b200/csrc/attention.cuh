@@ -184,6 +184,72 @@ WAMB_DEV KvTile att_tile(const AttnParams& p, int j, int n0, int b) {
   return t;
 }
 
+// Split keys: the last of an item's S CTAs to finish merges the S partials
+// (in split order, so the result does not depend on timing), writes the
+// bf16 output and resets the item's counter. Called by the 256 softmax
+// threads (threads 0..255: thread i is row i of the item's 256 query rows)
+// after each wrote its partial.
+WAMB_DEV void att_split_merge(const AttnParams& p, int item, int S, int q0, int b, int h, bool has_b,
+                              volatile int* abort_flag, volatile int* last_split) {
+  // Split keys: the last of the item's S CTAs to finish merges the S
+  // partials (split order, so the result does not depend on timing).
+  __threadfence();
+  asm volatile("bar.sync 2, 256;" ::: "memory");
+  if (threadIdx.x == 0) *last_split = atomicAdd(p.kv_count + item, 1) == S - 1;
+  asm volatile("bar.sync 2, 256;" ::: "memory");
+  if (*last_split) {
+    __threadfence();
+    const int prow = threadIdx.x;   // 0..255
+    const int qr = q0 + prow;
+    const bool has_row = (has_b || prow < 128) && qr < p.q_rows;
+    if (has_row) {
+      const float* b0p = p.kv_part + static_cast<size_t>(item) * S * ATT_PART_FLOATS;
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(b0p + s2 * ATT_PART_FLOATS + 256 * 128 + prow));
+      float w[ATT_MAX_SPLITS], den = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < ATT_MAX_SPLITS; ++s2) {
+        w[s2] = 0.f;
+        if (s2 < S) {
+          const float* bs = b0p + s2 * ATT_PART_FLOATS;
+          const float ms = __ldcg(bs + 256 * 128 + prow);
+          w[s2] = ms == -INFINITY ? 0.f : exp2f(ms - M);
+          den += w[s2] * __ldcg(bs + 256 * 128 + 256 + prow);
+        }
+      }
+      const float inv = (!*abort_flag && den > 0.f) ? 1.f / den : 0.f;
+      __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
+      // Eight four-column groups of every split in flight at once (a
+      // rolled loop of dependent L2 round trips cost ~20 us per item).
+#pragma unroll 1
+      for (int j0 = 0; j0 < 32; j0 += 8) {
+        float4 v[ATT_MAX_SPLITS][8];
+#pragma unroll
+        for (int s2 = 0; s2 < ATT_MAX_SPLITS; ++s2)
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj)
+            v[s2][jj] = s2 < S ? __ldcg(reinterpret_cast<const float4*>(b0p + s2 * ATT_PART_FLOATS) +
+                                        (j0 + jj) * 256 + prow)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int s2 = 0; s2 < ATT_MAX_SPLITS; ++s2) {
+            acc.x += w[s2] * v[s2][jj].x;
+            acc.y += w[s2] * v[s2][jj].y;
+            acc.z += w[s2] * v[s2][jj].z;
+            acc.w += w[s2] * v[s2][jj].w;
+          }
+          *reinterpret_cast<uint2*>(orow + 4 * (j0 + jj)) =
+              make_uint2(pack_bf16(acc.x * inv, acc.y * inv), pack_bf16(acc.z * inv, acc.w * inv));
+        }
+      }
+    }
+    if (threadIdx.x == 0) p.kv_count[item] = 0;   // ready for the next launch
+  }
+}
+
 // GROUPED: the grouped-candidate variant (cluster launch); false compiles
 // the kernel without any of that code.
 template <bool GROUPED>
@@ -705,65 +771,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   }
 
-  if (S > 1 && warp < 8) {
-    // Split keys: the last of the item's S CTAs to finish merges the S
-    // partials (split order, so the result does not depend on timing).
-    __threadfence();
-    asm volatile("bar.sync 2, 256;" ::: "memory");
-    if (threadIdx.x == 0) *last_split = atomicAdd(p.kv_count + item, 1) == S - 1;
-    asm volatile("bar.sync 2, 256;" ::: "memory");
-    if (*last_split) {
-      __threadfence();
-      const int prow = threadIdx.x;   // 0..255
-      const int qr = q0 + prow;
-      const bool has_row = (has_b || prow < 128) && qr < p.q_rows;
-      if (has_row) {
-        const float* b0p = p.kv_part + static_cast<size_t>(item) * S * ATT_PART_FLOATS;
-        float M = -INFINITY;
-        for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(b0p + s2 * ATT_PART_FLOATS + 256 * 128 + prow));
-        float w[ATT_MAX_SPLITS], den = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < ATT_MAX_SPLITS; ++s2) {
-          w[s2] = 0.f;
-          if (s2 < S) {
-            const float* bs = b0p + s2 * ATT_PART_FLOATS;
-            const float ms = __ldcg(bs + 256 * 128 + prow);
-            w[s2] = ms == -INFINITY ? 0.f : exp2f(ms - M);
-            den += w[s2] * __ldcg(bs + 256 * 128 + 256 + prow);
-          }
-        }
-        const float inv = (!*abort_flag && den > 0.f) ? 1.f / den : 0.f;
-        __nv_bfloat16* orow = p.out + (static_cast<long long>(b) * p.q_rows + qr) * p.ldo + h * 128;
-        // Eight four-column groups of every split in flight at once (a
-        // rolled loop of dependent L2 round trips cost ~20 us per item).
-#pragma unroll 1
-        for (int j0 = 0; j0 < 32; j0 += 8) {
-          float4 v[ATT_MAX_SPLITS][8];
-#pragma unroll
-          for (int s2 = 0; s2 < ATT_MAX_SPLITS; ++s2)
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj)
-              v[s2][jj] = s2 < S ? __ldcg(reinterpret_cast<const float4*>(b0p + s2 * ATT_PART_FLOATS) +
-                                          (j0 + jj) * 256 + prow)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int s2 = 0; s2 < ATT_MAX_SPLITS; ++s2) {
-              acc.x += w[s2] * v[s2][jj].x;
-              acc.y += w[s2] * v[s2][jj].y;
-              acc.z += w[s2] * v[s2][jj].z;
-              acc.w += w[s2] * v[s2][jj].w;
-            }
-            *reinterpret_cast<uint2*>(orow + 4 * (j0 + jj)) =
-                make_uint2(pack_bf16(acc.x * inv, acc.y * inv), pack_bf16(acc.z * inv, acc.w * inv));
-          }
-        }
-      }
-      if (threadIdx.x == 0) p.kv_count[item] = 0;   // ready for the next launch
-    }
-  }
+  if (S > 1 && warp < 8) att_split_merge(p, item, S, q0, b, h, has_b, abort_flag, last_split);
   if (grouped) {
     // Exchange: CTA k owns rows [(k % R) ro, + ro) of candidate b0 + k / R
     // (ro = q_rows / R, rows own0 + [0, ro) of the group tile). Each CTA

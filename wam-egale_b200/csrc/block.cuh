@@ -12,6 +12,7 @@
 #include <type_traits>
 
 #include "attention.cuh"
+#include "attention_ot.cuh"
 #include "glue.cuh"
 #include "host.cuh"
 #include "linear.cuh"
@@ -154,6 +155,8 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
                                          AttnSmem::TOTAL));
     WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnSmem::TOTAL));
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_ot_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnOtSmem::TOTAL));
     configured[dev] = true;
   }
   dim3 grid((a->q_rows + 255) / 256, a->heads, a->batch);
@@ -192,6 +195,11 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
       grid.z = a->batch * S;
     }
   }
+  // Queries longer than one tile: the O^T kernel (its P V product as N 256
+  // MMAs over both query tiles of a CTA).
+  if (a->q_rows > 128)
+    return launch_kernel(attn_ot_kernel, grid, dim3(ATT_THREADS), AttnOtSmem::TOTAL, stream, tq, tk0, tv0, tk1,
+                         tv1, p);
   return launch_kernel(attn_tc_kernel<false>, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
                        tv1, p);
 }
@@ -295,10 +303,11 @@ inline int launch_rms(const RmsParams& p, cudaStream_t s) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  const size_t rsm = rmsw_smem(p.D, p.sections);
+  const size_t rsm = rmsw_smem(p.D, p.sections, p.sections + (p.pool_k != nullptr ? 1 : 0));
   // Warp-per-row kernel at large M (as for the LayerNorm): one CTA of
   // RMSW_WARPS warps per SM, all in one wave, each on a contiguous range of rows.
   if (p.M >= 1024 && p.D % 256 == 0 && rsm <= 227 * 1024 && aligned16(p.x) && (p.ld * 2) % 16 == 0 &&
+      (p.pool_k == nullptr || (p.sections == 2 && p.ld >= 3LL * p.D)) &&
       (p.freq == nullptr || aligned16(p.freq))) {
     const int grid = std::min(p.M, di.sms);
     const int rpc = (p.M + grid - 1) / grid;

@@ -651,9 +651,10 @@ __global__ void rms_rope_kernel(const RmsParams p) {
 
 // Warp-per-row variant of rms_rope_kernel for large M (the LayerNorm's
 // design): one CTA of RMSW_WARPS warps per SM, a contiguous range of rows
-// per CTA, one warp per row. A row's sections (q | k, adjacent in the row)
-// arrive in a shared-memory slot by one bulk copy, RMSW_SLOTS slots per
-// warp, so the next rows are in flight while one is normalized; gamma is
+// per CTA, one warp per row. A row's sections (q | k, adjacent in the row,
+// and the V section after them when K and V go to pool slots) arrive in a
+// shared-memory slot by one bulk copy, rmsw_slots() slots per warp, so the
+// next rows are in flight while one is normalized; gamma is
 // staged in shared memory once per CTA. Lane l holds columns [i*256 + h*128
 // + 4l, +4) of each section, so its two RoPE pairs are the same for every
 // head: one float4 of the row's frequencies per lane. The same arithmetic
@@ -661,8 +662,9 @@ __global__ void rms_rope_kernel(const RmsParams p) {
 // the sum of squares is reduced in another order.
 constexpr int RMSW_WARPS = 10;
 __host__ __device__ constexpr int rmsw_slots(int sections) { return sections == 2 ? 1 : 3; }
-__host__ __device__ constexpr size_t rmsw_smem(int D, int sections) {
-  return 4ull * sections * D + static_cast<size_t>(rmsw_slots(sections)) * RMSW_WARPS * sections * D * 2 +
+// row_sections: the sections each slot holds (sections, + 1 for V).
+__host__ __device__ constexpr size_t rmsw_smem(int D, int sections, int row_sections) {
+  return 4ull * sections * D + static_cast<size_t>(rmsw_slots(sections)) * RMSW_WARPS * row_sections * D * 2 +
          8ull * 3 * RMSW_WARPS + 16;
 }
 
@@ -672,7 +674,8 @@ __global__ void __launch_bounds__(RMSW_WARPS * 32, 1) rms_warp_kernel(const RmsP
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = p.D, SEC = p.sections;
   const int NS = rmsw_slots(SEC);
-  const uint32_t row_bytes = static_cast<uint32_t>(SEC) * D * 2;
+  const bool to_pool = p.pool_k != nullptr;
+  const uint32_t row_bytes = static_cast<uint32_t>(SEC + (to_pool ? 1 : 0)) * D * 2;
   float* sg = reinterpret_cast<float*>(rm_smem);                       // gamma [SEC][D]
   uint8_t* slots = rm_smem + 4 * SEC * D;
   uint64_t* bars = reinterpret_cast<uint64_t*>(slots + static_cast<size_t>(NS) * RMSW_WARPS * row_bytes);
@@ -713,7 +716,6 @@ __global__ void __launch_bounds__(RMSW_WARPS * 32, 1) rms_warp_kernel(const RmsP
     const int b = row / p.rows_per_batch, tok = row - b * p.rows_per_batch;
     if (!mbar_wait(bar0 + 8 * (k % NS), (k / NS) & 1, abort_flag)) break;
     const __nv_bfloat16* srow = reinterpret_cast<const __nv_bfloat16*>(slots + static_cast<size_t>(warp * NS + k % NS) * row_bytes);
-    bool to_pool = p.pool_k != nullptr;
     long long dst_row = 0;
     bool skip = false;
     if (to_pool) {
@@ -765,6 +767,16 @@ __global__ void __launch_bounds__(RMSW_WARPS * 32, 1) rms_warp_kernel(const RmsP
           *reinterpret_cast<uint2*>(dst + col) = make_uint2(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
         }
     }
+    if (to_pool && !skip) {
+      // V from the slot into its pool row: every chunk loaded, then stored.
+      const uint4* sv = reinterpret_cast<const uint4*>(srow + 2 * D);
+      uint4* vdst = reinterpret_cast<uint4*>(p.pool_v + dst_row * D);
+      uint4 vv[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) vv[i] = sv[lane + 32 * i];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) vdst[lane + 32 * i] = vv[i];
+    }
     __syncwarp();
     if (issued < nk) {   // the slot is free again: request the row NS ahead
       if (lane == 0) {
@@ -772,11 +784,6 @@ __global__ void __launch_bounds__(RMSW_WARPS * 32, 1) rms_warp_kernel(const RmsP
         request(issued);
       }
       ++issued;
-    }
-    if (to_pool && !skip) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<long long>(row) * p.ld + 2LL * D);
-      uint4* vdst = reinterpret_cast<uint4*>(p.pool_v + dst_row * D);
-      for (int i = lane; i < D / 8; i += 32) vdst[i] = src[i];
     }
   }
   // After an abort, the copies still in flight must land before the CTA's
