@@ -184,7 +184,9 @@ def test_candidate_grouped(cuda_device, Q, rows, pool, vis):
 
 
 @pytest.mark.parametrize("B,H,Sq,Sk,splits", [
-    (1, 24, 880, 4400, 0),     # one cfg2 chunk: the library picks 3 splits
+    (1, 24, 880, 4400, 0),     # one cfg2 chunk: one wave of items, the O^T kernel unsplit
+    (8, 4, 880, 700, 0),       # 128 items: the O^T kernel, partial last key tile
+    (1, 24, 880, 4400, 3),     # forced 3 splits: the split-key kernel
     (1, 3, 300, 1000, 2),      # two-tile items and a single-tile item
     (2, 2, 100, 700, 4),       # single-tile items only, 4 splits
     (1, 2, 256, 512, 3),       # splits of one or two key tiles

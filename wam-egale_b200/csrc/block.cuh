@@ -38,6 +38,18 @@ struct AttnSplitBuffers {
 // 12 heads, 3 splits of 4-5 tiles measured 52 us against 42 unsplit).
 // Candidate verification (src0_map)
 // never splits. `force` > 0: that factor (capped by the key tiles).
+// Whether an unsplit call runs on attn_ot_kernel: queries longer than one
+// tile, not candidate rows, and at most one wave of (query tile pair, head,
+// batch row) items. Measured at one wave or less it beats attn_tc_kernel
+// unsplit and split (one 880-row chunk, 24 heads, 4400 keys: 85.0 us
+// against 95.8 unsplit and 89.3 with 3 key splits; 1592 rows, 12 heads:
+// 38.0 against 41.6 us); with several waves (8 chunks: 493 against 475 us)
+// its 3-slot K/V ring hides less load latency than attn_tc_kernel's 5.
+inline bool attn_use_ot(const wamb_attention_args* a, int sms) {
+  const long long items = static_cast<long long>((a->q_rows + 255) / 256) * a->heads * a->batch;
+  return a->src0_map == nullptr && a->q_rows > 128 && items <= sms;
+}
+
 inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) {
   if (a->src0_map != nullptr || a->batch <= 0 || a->q_rows <= 0) return 1;
   const long long items = static_cast<long long>((a->q_rows + 255) / 256) * a->heads * a->batch;
@@ -45,7 +57,7 @@ inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) 
   const long long keys = a->tiles != nullptr ? a->src0_batch_stride : a->src0_len;
   const int n_est = static_cast<int>((std::max<long long>(keys, 0) + 127) / 128);
   if (force > 0) return std::max(1, std::min(std::min(force, ATT_MAX_SPLITS), n_est));
-  if (items >= sms) return 1;
+  if (items >= sms || attn_use_ot(a, sms)) return 1;
   auto eff = [&](int S) {
     const long long ctas = items * S;
     return static_cast<double>(ctas) / (static_cast<double>((ctas + sms - 1) / sms) * sms);
@@ -195,9 +207,9 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
       grid.z = a->batch * S;
     }
   }
-  // Queries longer than one tile: the O^T kernel (its P V product as N 256
-  // MMAs over both query tiles of a CTA).
-  if (a->q_rows > 128)
+  // One wave or less of long-query items, unsplit: the O^T kernel (its P V
+  // product as N 256 MMAs over both query tiles of a CTA).
+  if (p.kv_splits == 1 && attn_use_ot(a, di.sms))
     return launch_kernel(attn_ot_kernel, grid, dim3(ATT_THREADS), AttnOtSmem::TOTAL, stream, tq, tk0, tv0, tk1,
                          tv1, p);
   return launch_kernel(attn_tc_kernel<false>, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
