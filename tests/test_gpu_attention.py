@@ -138,6 +138,33 @@ def test_split_kv_single_tile(cuda_device, Sq, Sk, hot):
     _check(ops.sdpa(q, k, v), _sdpa_ref(q, k, v))
 
 
+@pytest.mark.parametrize("Sq,Sk,hot", [(300, 1000, "second"), (300, 1000, "last"), (256, 2000, "first"),
+                                       (880, 700, "ramp"), (200, 130, "second")])
+def test_transposed_output_rescale(cuda_device, Sq, Sk, hot):
+    """Queries longer than one tile at one wave run attn_ot_kernel (O^T in
+    TMEM, P V as N 256 MMAs). Keys scaled up late make row maxima grow past
+    the 2^8 threshold after O^T holds earlier tiles, so the rescale of O^T
+    columns by all softmax warps is exercised; "ramp" grows every tile."""
+    g = torch.Generator(device="cuda").manual_seed(Sq * 7 + Sk)
+    B, H = 1, 2
+    q = torch.randn(B, Sq, H, 128, device="cuda", generator=g)
+    k = torch.randn(B, Sk, H, 128, device="cuda", generator=g)
+    v = torch.randn(B, Sk, H, 128, device="cuda", generator=g)
+    if hot == "first":
+        k[:, : Sk // 4] *= 3
+    elif hot == "second":
+        k[:, Sk // 2:] *= 3
+    elif hot == "last":
+        k[:, -7:] *= 5
+    else:
+        k *= torch.linspace(0.5, 4.0, Sk, device="cuda")[None, :, None, None]
+    q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    out = ops.sdpa(q, k, v)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    _check(out, _sdpa_ref(q, k, v))
+
+
 @pytest.mark.parametrize("Q,rows,pool,vis", [
     (32, [0, 0, 0, 0], 700, 600),              # G 4: one cluster, one shared history row
     (32, [1, 1, 1, 1, 0, 0, 0, 0], 700, 650),  # two clusters, each with its own history row
