@@ -237,3 +237,80 @@ def test_split_keys(cuda_device, B, H, Sq, Sk, splits):
     ws = ops._SPLIT.get(torch.cuda.current_device())
     if ws is not None:
         assert bool((ws[:8192] == 0).all())
+
+
+def _split_counters_zero():
+    ws = ops._SPLIT.get(torch.cuda.current_device())
+    return ws is None or bool((ws[:8192] == 0).all())
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk,hot", [
+    (1, 24, 880, 4400, None),      # one cfg2 chunk: 96 items over 148 CTAs, items over 2-3 CTAs
+    (1, 24, 880, 4400, "ramp"),    # maxima grow in every tile: partials with different m
+    (1, 24, 520, 3000, "second"),  # 72 items, up to 4 CTAs per item, last pair tile A only
+    (3, 16, 600, 1900, None),      # 144 items, every third pair tile A only
+    (1, 40, 300, 5000, "last"),    # hot keys in the last segment of each item
+    (3, 24, 880, 2000, None),      # 288 items (1.95 waves), all shared by key tiles
+    (8, 24, 880, 1100, "second"),  # 768 items: 4 whole waves round-robin, then 176 items shared
+    (2, 40, 1592, 1000, None),     # 560 items: 2 whole waves, every seventh pair tile A only
+])
+def test_stream_k(cuda_device, B, H, Sq, Sk, hot):
+    """attn_ot_sk_kernel: whole waves of (query tile pair, head) items
+    round-robin, the key tiles of the rest shared over all SMs, partial
+    segments merged by the last CTA to finish; bitwise repeatable, counters
+    left zero."""
+    g = torch.Generator(device="cuda").manual_seed(Sq * 13 + Sk + H)
+    q = torch.randn(B, Sq, H, 128, device="cuda", generator=g)
+    k = torch.randn(B, Sk, H, 128, device="cuda", generator=g)
+    v = torch.randn(B, Sk, H, 128, device="cuda", generator=g)
+    if hot == "second":
+        k[:, Sk // 2:] *= 3
+    elif hot == "last":
+        k[:, -7:] *= 5
+    elif hot == "ramp":
+        k *= torch.linspace(0.5, 4.0, Sk, device="cuda")[None, :, None, None]
+    q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    args = dict(heads=H, q_rows=Sq, src0_batch_stride=Sk, src0_len=Sk, kv_splits=0)
+    run = lambda: ops.attention(q.view(B * Sq, H * 128), k.view(B * Sk, H * 128),  # noqa: E731
+                                v.view(B * Sk, H * 128), **args)
+    out, again = run(), run()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    _check(out.view(B, Sq, H, 128), _sdpa_ref(q, k, v))
+    assert torch.equal(out, again)
+    assert _split_counters_zero()
+
+
+@pytest.mark.parametrize("visible", ["most", "first300"])
+def test_stream_k_pool_and_own_keys(cuda_device, visible):
+    """Stream-K over a pool tile list (stale slots hold NaN) followed by the
+    call's own K/V as a second source. "first300": the host plans stream-K
+    from the pool size, the device finds 3 pool tiles and runs whole items."""
+    g = torch.Generator(device="cuda").manual_seed(4400 + len(visible))
+    B, H, Q, pool = 1, 24, 880, 4400
+    kp = torch.randn(B, pool, H, 128, device="cuda", generator=g).bfloat16()
+    vp = torch.randn(B, pool, H, 128, device="cuda", generator=g).bfloat16()
+    if visible == "most":
+        mask = torch.rand(pool, device="cuda", generator=g) < 0.8
+    else:
+        mask = torch.zeros(pool, dtype=torch.bool, device="cuda")
+        mask[:300] = True
+    kp[:, ~mask] = float("nan")
+    vp[:, ~mask] = float("nan")
+    q = torch.randn(B, Q, H, 128, device="cuda", generator=g).bfloat16()
+    k1 = torch.randn(B, Q, H, 128, device="cuda", generator=g).bfloat16()
+    v1 = torch.randn(B, Q, H, 128, device="cuda", generator=g).bfloat16()
+    tl = _tiles(mask)
+    tiles = torch.tensor(tl, dtype=torch.int32, device="cuda").view(-1, 2)
+    n = torch.tensor([len(tl)], dtype=torch.int32, device="cuda")
+    run = lambda: ops.attention(q.view(B * Q, -1), kp.view(B * pool, -1), vp.view(B * pool, -1),  # noqa: E731
+                                heads=H, q_rows=Q, src0_batch_stride=pool, tiles=tiles, n_tiles=n,
+                                k1=k1.view(B * Q, -1), v1=v1.view(B * Q, -1), kv_splits=0)
+    out, again = run(), run()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    idx = mask.nonzero().squeeze(-1)
+    ref = _sdpa_ref(q, torch.cat([kp[:, idx], k1], 1), torch.cat([vp[:, idx], v1], 1))
+    _check(out.view(B, Q, H, 128), ref)
+    assert torch.equal(out, again)
+    assert _split_counters_zero()

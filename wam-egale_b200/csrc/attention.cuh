@@ -125,6 +125,13 @@ struct AttnParams {
   int kv_splits;
   float* kv_part;
   int* kv_count;
+  // attn_ot_kernel only (a persistent 1-D grid of G CTAs): items are (query
+  // tile pair, head, batch row) with the pair fastest, ot_items of them,
+  // ot_qpairs pairs per (head, batch row). Items [0, ot_dp_items) go whole
+  // to CTAs round-robin; with ot_sk the key tiles of the rest are shared
+  // evenly over the G CTAs (stream-K), partials in kv_part ([G][2] slots of
+  // ATT_PART_FLOATS) and one counter per item in kv_count.
+  int ot_items, ot_qpairs, ot_dp_items, ot_sk;
 };
 
 // One split-key partial: O [32 four-column groups][256 rows][4] fp32 (so

@@ -12,7 +12,7 @@
 #include <type_traits>
 
 #include "attention.cuh"
-#include "attention_ot.cuh"
+#include "attention_ot_sk.cuh"
 #include "glue.cuh"
 #include "host.cuh"
 #include "linear.cuh"
@@ -48,6 +48,34 @@ struct AttnSplitBuffers {
 inline bool attn_use_ot(const wamb_attention_args* a, int sms) {
   const long long items = static_cast<long long>((a->q_rows + 255) / 256) * a->heads * a->batch;
   return a->src0_map == nullptr && a->q_rows > 128 && items <= sms;
+}
+
+// attn_ot_kernel's round-robin items: all of them when they fill whole
+// waves, none below one wave, else every whole wave but the last (the rest,
+// between one and two waves of items, is shared out by key tiles).
+inline long long attn_ot_dp_items(long long items, int sms) {
+  if (items % sms == 0) return items;
+  if (items < sms) return 0;
+  return (items / sms - 1) * sms;
+}
+
+// Whether a long-query call runs attn_ot_sk_kernel (stream-K over key
+// tiles): whole items would leave SMs idle in their last wave, and each CTA
+// gets at least 8 key tiles by the host's estimate of the keys (the pool
+// size for a tile list); the kernel checks again with the device's tile
+// count. Measured against whole items: one cfg2 chunk (96 items of 35 key
+// tiles) 76.3 us against 83.4 on attn_ot_kernel; 8 chunks (768 items, 4
+// whole waves then stream-K over 176 items) 446 us against 476 on
+// attn_tc_kernel.
+inline bool attn_ot_sk(const wamb_attention_args* a, int sms) {
+  if (a->src0_map != nullptr || a->q_rows <= 128) return false;
+  const long long items = static_cast<long long>((a->q_rows + 255) / 256) * a->heads * a->batch;
+  if (items > ATT_MAX_ITEMS) return false;
+  const long long dp = attn_ot_dp_items(items, sms);
+  if (dp == items) return false;
+  const long long keys = a->tiles != nullptr ? a->src0_batch_stride : a->src0_len;
+  const long long n_est = (std::max<long long>(keys, 0) + 127) / 128 + (a->k1 != nullptr ? (a->q_rows + 127) / 128 : 0);
+  return (items - dp) * n_est / sms >= 8;
 }
 
 inline int attn_kv_splits(const wamb_attention_args* a, int sms, int force = 0) {
@@ -101,6 +129,14 @@ inline bool attn_group_shape(int q_rows, int batch, int heads, int sms, int* G_o
 inline size_t attn_split_part_bytes(const wamb_attention_args* a, int S) {
   if (S <= 1) return 0;
   return static_cast<size_t>((a->q_rows + 255) / 256) * a->heads * a->batch * S * ATT_PART_BYTES;
+}
+
+// Partial bytes of an attention call: its key splits, or two slots per CTA
+// of attn_ot_kernel's stream-K schedule.
+inline size_t attn_part_bytes(const wamb_attention_args* a, int sms, int force = 0) {
+  const int S = attn_kv_splits(a, sms, force);
+  if (S > 1) return attn_split_part_bytes(a, S);
+  return attn_ot_sk(a, sms) ? static_cast<size_t>(2) * sms * ATT_PART_BYTES : 0;
 }
 
 // trigger: a GEMM that requests weights before its pdl_wait follows.
@@ -169,6 +205,8 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
                                          AttnSmem::TOTAL));
     WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_ot_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnOtSmem::TOTAL));
+    WAMB_CHECK_CUDA(cudaFuncSetAttribute(attn_ot_sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnOtSkSmem::TOTAL));
     configured[dev] = true;
   }
   dim3 grid((a->q_rows + 255) / 256, a->heads, a->batch);
@@ -207,11 +245,26 @@ inline int attention_impl(const wamb_attention_args* a, cudaStream_t stream, boo
       grid.z = a->batch * S;
     }
   }
-  // One wave or less of long-query items, unsplit: the O^T kernel (its P V
-  // product as N 256 MMAs over both query tiles of a CTA).
-  if (p.kv_splits == 1 && attn_use_ot(a, di.sms))
-    return launch_kernel(attn_ot_kernel, grid, dim3(ATT_THREADS), AttnOtSmem::TOTAL, stream, tq, tk0, tv0, tk1,
-                         tv1, p);
+  // Long-query items, unsplit: the O^T kernel (its P V product as N 256
+  // MMAs over both query tiles of a CTA), one item per CTA, at one wave or
+  // less; when whole items leave SMs idle and the call has partial slots,
+  // its stream-K variant on one CTA per SM (at any number of waves).
+  const bool sk = p.kv_splits == 1 && attn_ot_sk(a, di.sms) && split != nullptr && split->count != nullptr &&
+                  split->part != nullptr && split->part_bytes >= attn_part_bytes(a, di.sms);
+  if (p.kv_splits == 1 && !sk && attn_use_ot(a, di.sms))
+    return launch_kernel(attn_ot_kernel, grid, dim3(ATT_THREADS), AttnOtSmem::TOTAL, stream, tq, tk0, tv0, tk1, tv1,
+                         p);
+  if (sk) {
+    const long long items = static_cast<long long>(grid.x) * grid.y * grid.z;   // <= ATT_MAX_ITEMS
+    p.ot_items = static_cast<int>(items);
+    p.ot_qpairs = static_cast<int>(grid.x);
+    p.ot_sk = 1;
+    p.ot_dp_items = static_cast<int>(attn_ot_dp_items(items, di.sms));
+    p.kv_part = split->part;
+    p.kv_count = split->count;
+    return launch_kernel(attn_ot_sk_kernel, dim3(di.sms), dim3(ATT_THREADS), AttnOtSkSmem::TOTAL, stream, tq, tk0,
+                         tv0, tk1, tv1, p);
+  }
   return launch_kernel(attn_tc_kernel<false>, grid, dim3(ATT_THREADS), AttnSmem::TOTAL, stream, tq, tk0, tv0, tk1,
                        tv1, p);
 }
@@ -415,8 +468,8 @@ inline BlockLayout block_layout(const wamb_block_args* a) {
   if (M >= 512) put(WAMB_TAP_SK_PART, sk_part_bytes(sms));
   // Split-key partials of the self attention.
   const wamb_attention_args sa = self_attention_shape(a);
-  const int S = attn_kv_splits(&sa, sms);
-  if (S > 1) put(WAMB_TAP_ATTN_PART, attn_split_part_bytes(&sa, S));
+  const size_t apb = attn_part_bytes(&sa, sms);
+  if (apb > 0) put(WAMB_TAP_ATTN_PART, apb);
   L.total = o;
   return L;
 }
@@ -643,7 +696,7 @@ inline int block_forward_impl(const wamb_block_args* a, cudaStream_t s) {
   if (L.off[WAMB_TAP_ATTN_PART] >= 0) {
     asb.count = reinterpret_cast<int*>(ws + L.off[WAMB_TAP_SK_FLAGS] + SK_FLAG_BYTES);
     asb.part = reinterpret_cast<float*>(ws + L.off[WAMB_TAP_ATTN_PART]);
-    asb.part_bytes = attn_split_part_bytes(&at, attn_kv_splits(&at, di.sms));
+    asb.part_bytes = attn_part_bytes(&at, di.sms);
   }
   if ((rc = attention_impl(&at, s, !f8 && early(D, D, D, WAMB_EPI_RES_GATE), &asb))) return rc;
   if (f8 && (rc = quantize(attn, D, D))) return rc;

@@ -111,8 +111,8 @@ size_t wamb_attention_split_bytes(const wamb_attention_args* args) {
   if (args == nullptr) return 0;
   DeviceInfo di;
   if (device_info(&di) != WAMB_OK) return 0;
-  const int S = attn_kv_splits(args, di.sms, args->kv_splits);
-  return S > 1 ? ATT_COUNT_BYTES + attn_split_part_bytes(args, S) : 0;
+  const size_t part = attn_part_bytes(args, di.sms, args->kv_splits);
+  return part > 0 ? ATT_COUNT_BYTES + part : 0;
 }
 
 size_t wamb_block_workspace_bytes(const wamb_block_args* args) {
