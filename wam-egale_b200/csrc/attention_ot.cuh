@@ -34,6 +34,11 @@
 namespace wamb {
 
 constexpr int ATO_SLOTS = 3;
+// exp2 of keys 2i, 2i + 1 of every 32 on the MUFU for i < ATO_MUFU_PAIRS,
+// the rest as the cubic on the FMA pipe: the softmax warps are bound by the
+// MUFU's 16 results per clock per SM, so moving a sixth of the keys off it
+// shortens each key tile's softmax.
+constexpr int ATO_MUFU_PAIRS = 11;
 
 struct AttnOtSmem {
   static constexpr uint32_t Q_OFF = 0;
@@ -44,7 +49,9 @@ struct AttnOtSmem {
   static constexpr uint32_t BAR_OFF = ROW_OFF + 256 * 4;
   // q_full, full[3], empty[3], s_full[2], s_free[2], p_full, p_free, o_done, drain
   static constexpr uint32_t NBARS = 15;
-  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+  // After the barriers: TMEM address, abort flag, split flag, spare, then
+  // the softmax warps' grow flags [2 key-tile parities][8 warps].
+  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16 + 64;
   static_assert(TOTAL <= 232448, "attention shared memory exceeds 227 KB");
   // Epilogue staging over the ring and the P buffer once every MMA is done:
   // fp32 O [256 rows][128] (split keys) or bf16 O [256 rows][128].
@@ -85,7 +92,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_split = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  volatile int* grow_flag = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  volatile int* grow_w = reinterpret_cast<volatile int*>(tmem_slot + 4);   // [2][8]
 
   if (p.trigger) pdl_trigger();
   pdl_wait();   // the tile list and Q/K/V of the previous kernels are complete
@@ -125,7 +132,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
-    *grow_flag = 0;
     fence_barrier_init();
   }
   if (warp == ATT_MMA_WARP) {
@@ -270,13 +276,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= hi) s[i] = -INFINITY;
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
+      for (int i = 0; i < 32; i += 2) {
         mx0 = fmax3(mx0, s[i], s[i + 1]);
-        mx1 = fmax3(mx1, s[64 + i], s[64 + i + 1]);
+        mx1 = fmax3(mx1, s[32 + i], s[32 + i + 1]);
+        mx2 = fmax3(mx2, s[64 + i], s[64 + i + 1]);
+        mx3 = fmax3(mx3, s[96 + i], s[96 + i + 1]);
       }
-      const float mx = fmaxf(mx0, mx1) * p.scale_log2;
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
       // Keep the stale max unless the new one exceeds it by more than 2^8.
       const bool grow = mx > m_used + ATT_RESCALE_LOG2;
       const float m_new = grow ? mx : m_used;
@@ -284,14 +292,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const float alpha = grow ? exp2f(m_used - m_use) : 1.f;
       const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
       const uint64_t neg_m2 = f2(-m_use, -m_use);
-      uint64_t sum2 = f2(0.f, 0.f);
-      // P as packed bf16 pairs: keys 24..31 of every 32 take the cubic, the
-      // rest the MUFU exp2 (as in attn_tc_kernel).
+      uint64_t sum2 = f2(0.f, 0.f), sum2p = f2(0.f, 0.f);
+      // P as packed bf16 pairs: keys 2 ATO_MUFU_PAIRS .. 31 of every 32 take
+      // the cubic, the rest the MUFU exp2.
       uint32_t pk[64];
+      // exp2 of keys [32 c, 32 c + 32) into pk[16 c, 16 c + 16).
+      auto exp_chunk = [&](int c) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-#pragma unroll
-        for (int i = 0; i < 12; ++i) {
+        for (int i = 0; i < ATO_MUFU_PAIRS; ++i) {
           const int k = 32 * c + 2 * i;
           const float2 x = f2_split(ffma2(f2(s[k], s[k + 1]), scale2, neg_m2));
           const float a = ex2_mufu(x.x), bb = ex2_mufu(x.y);
@@ -299,48 +307,65 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           pk[16 * c + i] = pack_bf16(a, bb);
         }
 #pragma unroll
-        for (int i = 12; i < 16; ++i) {
+        for (int i = ATO_MUFU_PAIRS; i < 16; ++i) {
           const int k = 32 * c + 2 * i;
           const uint64_t e = ex2_poly2(ffma2(f2(s[k], s[k + 1]), scale2, neg_m2));
-          sum2 = fadd2(sum2, e);
+          sum2p = fadd2(sum2p, e);
           const float2 ev = f2_split(e);
           pk[16 * c + i] = pack_bf16(ev.x, ev.y);
         }
-      }
-      const float2 sv = f2_split(sum2);
+      };
+      // P row q into the K-major SW128 buffer: 16-byte chunk c of the row's
+      // 64-key atom at ((c ^ (q & 7)) * 16).
+      auto store_p = [&](int c) {
+        const uint32_t addr = sP + (c >> 3) * L::P_ATOM + q * 128 + (((c & 7) ^ (q & 7)) << 4);
+        st_shared_v4(addr, pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      };
+      // The first three quarters of the keys, then (the previous O^T update
+      // having read P) their P goes out while the last quarter is computed,
+      // so most of P's 64 KB of shared-memory stores overlap the exp2s.
+#pragma unroll
+      for (int c = 0; c < 3; ++c) exp_chunk(c);
       if (j > 0) {
         // The previous O^T update has read P and written O^T.
         if (ok) ok = mbar_wait(p_free, (j - 1) & 1, abort_flag);
         tc_fence_after();
         // Rows whose max grew: scale their O^T columns (all 8 warps, each
         // its 32 head dims x its tile's 128 queries) before the next update.
-        row_f[q] = alpha;
-        if (__any_sync(0xffffffffu, grow) && lane == 0) *grow_flag = 1;
+        // One flag per warp, in two sets by key-tile parity (a warp running
+        // a tile ahead writes the other set), so the usual tile without
+        // growth costs one named barrier; a growth costs two more (the
+        // alphas are written, then every warp has read them).
+        volatile int* gw = grow_w + (j & 1) * 8;
+        const bool g_any = __any_sync(0xffffffffu, grow);
+        if (lane == 0) gw[warp] = g_any ? 1 : 0;
         asm volatile("bar.sync 1, 256;" ::: "memory");
-        const bool rescale = *grow_flag != 0;
-        if (rescale && ok) {
+        const bool rescale = (gw[0] | gw[1] | gw[2] | gw[3] | gw[4] | gw[5] | gw[6] | gw[7]) != 0;
+        if (rescale) {
+          row_f[q] = alpha;
+          asm volatile("bar.sync 1, 256;" ::: "memory");
+          if (ok) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            const uint32_t oc = 256 + t * 128 + c * 32;
-            tmem_ld32(tmem + lane_base + oc, o);
-            tmem_wait_ld();
+            for (int c = 0; c < 4; ++c) {
+              float o[32];
+              const uint32_t oc = 256 + t * 128 + c * 32;
+              tmem_ld32(tmem + lane_base + oc, o);
+              tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= row_f[t * 128 + c * 32 + i];
-            tmem_st32(tmem + lane_base + oc, o);
+              for (int i = 0; i < 32; ++i) o[i] *= row_f[t * 128 + c * 32 + i];
+              tmem_st32(tmem + lane_base + oc, o);
+            }
+            tmem_wait_st();
           }
-          tmem_wait_st();
+          asm volatile("bar.sync 1, 256;" ::: "memory");   // every warp read the alphas
         }
-        asm volatile("bar.sync 1, 256;" ::: "memory");   // every warp read the flag and alphas
-        if (rescale && threadIdx.x == 0) *grow_flag = 0;
       }
-      // P row q into the K-major SW128 buffer: 16-byte chunk c of the row's
-      // 64-key atom at ((c ^ (q & 7)) * 16).
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint32_t addr = sP + (c >> 3) * L::P_ATOM + q * 128 + (((c & 7) ^ (q & 7)) << 4);
-        st_shared_v4(addr, pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      }
+      for (int c = 0; c < 12; ++c) store_p(c);
+      exp_chunk(3);
+#pragma unroll
+      for (int c = 12; c < 16; ++c) store_p(c);
+      const float2 sv = f2_split(fadd2(sum2, sum2p));
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();

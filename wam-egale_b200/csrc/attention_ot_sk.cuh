@@ -457,8 +457,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         bool grow;
         float m_new, alpha, lsum;
         uint32_t pk[64];
+        float s[128];
+        uint64_t sum2 = f2(0.f, 0.f), scale2 = 0, neg_m2 = 0;
+        // exp2 of keys [32 c, 32 c + 32) into pk[16 c, 16 c + 16): keys 24..31
+        // of every 32 take the cubic, the rest the MUFU exp2 (as in
+        // attn_tc_kernel).
+        auto exp_chunk = [&](int c) {
+#pragma unroll
+          for (int i = 0; i < 12; ++i) {
+            const int kk = 32 * c + 2 * i;
+            const float2 x = f2_split(ffma2(f2(s[kk], s[kk + 1]), scale2, neg_m2));
+            const float a = ex2_mufu(x.x), bb = ex2_mufu(x.y);
+            sum2 = fadd2(sum2, f2(a, bb));
+            pk[16 * c + i] = pack_bf16(a, bb);
+          }
+#pragma unroll
+          for (int i = 12; i < 16; ++i) {
+            const int kk = 32 * c + 2 * i;
+            const uint64_t e = ex2_poly2(ffma2(f2(s[kk], s[kk + 1]), scale2, neg_m2));
+            sum2 = fadd2(sum2, e);
+            const float2 ev = f2_split(e);
+            pk[16 * c + i] = pack_bf16(ev.x, ev.y);
+          }
+        };
+        // P row q into the K-major SW128 buffer: 16-byte chunk c of the
+        // row's 64-key atom at ((c ^ (q & 7)) * 16).
+        auto store_p = [&](int c) {
+          const uint32_t addr = sP + (c >> 3) * L::P_ATOM + q * 128 + (((c & 7) ^ (q & 7)) << 4);
+          st_shared_v4(addr, pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        };
         {
-          float s[128];
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             float t32[32];
@@ -488,32 +516,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           m_new = grow ? mx : m_used;
           const float m_use = m_new == -INFINITY ? 0.f : m_new;
           alpha = grow ? exp2f(m_used - m_use) : 1.f;
-          const uint64_t scale2 = f2(p.scale_log2, p.scale_log2);
-          const uint64_t neg_m2 = f2(-m_use, -m_use);
-          uint64_t sum2 = f2(0.f, 0.f);
-          // P as packed bf16 pairs: keys 24..31 of every 32 take the cubic,
-          // the rest the MUFU exp2 (as in attn_tc_kernel).
+          scale2 = f2(p.scale_log2, p.scale_log2);
+          neg_m2 = f2(-m_use, -m_use);
+          // The first three quarters of the keys, then (the previous O^T
+          // update having read P) their P goes out while the last quarter is
+          // computed, as in attn_ot_kernel.
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-#pragma unroll
-            for (int i = 0; i < 12; ++i) {
-              const int kk = 32 * c + 2 * i;
-              const float2 x = f2_split(ffma2(f2(s[kk], s[kk + 1]), scale2, neg_m2));
-              const float a = ex2_mufu(x.x), bb = ex2_mufu(x.y);
-              sum2 = fadd2(sum2, f2(a, bb));
-              pk[16 * c + i] = pack_bf16(a, bb);
-            }
-#pragma unroll
-            for (int i = 12; i < 16; ++i) {
-              const int kk = 32 * c + 2 * i;
-              const uint64_t e = ex2_poly2(ffma2(f2(s[kk], s[kk + 1]), scale2, neg_m2));
-              sum2 = fadd2(sum2, e);
-              const float2 ev = f2_split(e);
-              pk[16 * c + i] = pack_bf16(ev.x, ev.y);
-            }
-          }
-          const float2 sv = f2_split(sum2);
-          lsum = sv.x + sv.y;
+          for (int c = 0; c < 3; ++c) exp_chunk(c);
         }
         if (j > 0) {
           // The previous O^T update has read P and written O^T.
@@ -541,12 +550,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           asm volatile("bar.sync 1, 256;" ::: "memory");   // every warp read the flag and alphas
           if (rescale && threadIdx.x == 0) *grow_flag = 0;
         }
-        // P row q into the K-major SW128 buffer: 16-byte chunk c of the
-        // row's 64-key atom at ((c ^ (q & 7)) * 16).
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint32_t addr = sP + (c >> 3) * L::P_ATOM + q * 128 + (((c & 7) ^ (q & 7)) << 4);
-          st_shared_v4(addr, pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        for (int c = 0; c < 12; ++c) store_p(c);
+        exp_chunk(3);
+#pragma unroll
+        for (int c = 12; c < 16; ++c) store_p(c);
+        {
+          const float2 sv = f2_split(sum2);
+          lsum = sv.x + sv.y;
         }
         fence_proxy_async();
         tc_fence_before();
