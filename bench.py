@@ -999,9 +999,12 @@ def run_kernel_case(args):
                the same GEMM with an ungated residual and bias-only epilogues;
                prints each one's CUDA-event time
     attention  self attention of --batch cfg2 rollouts of --q queries over
-               --pool keys (24 heads), keys split across CTAs as the block
-               does when the (query tile pair, head, batch row) items fill
-               less than one wave
+               --pool keys (24 heads) with the block's partial scratch: key
+               tiles shared over the SMs (stream-K) when whole (query tile
+               pair, head, batch row) items would leave SMs idle
+    attention_whole  the same call without partial scratch: one item per CTA
+               (--kv-splits N > 0 with either: that many key splits on
+               attn_tc_kernel instead)
     verify_attention  cfg3 self attention: 4 candidates x 32 queries sharing
                one 3520-slot history row plus their own keys (24 heads)
     quant      row quantization to E4M3 of an --m x --k bf16 matrix
@@ -1078,13 +1081,14 @@ def run_kernel_case(args):
         run = lambda: ops.attention(qkv, kp, vp, heads=H, q_rows=Q, src0_batch_stride=pool,  # noqa: E731
                                     tiles=tiles, n_tiles=n, src0_map=rows, k1=qkv, v1=qkv, k1_col=D,
                                     v1_col=2 * D, out=out)
-    elif a.case == "attention":
+    elif a.case in ("attention", "attention_whole"):
         q = torch.randn(a.batch * a.q, D, generator=g, device=dev).bfloat16()
         kp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
         vp = torch.randn(a.batch * a.pool, D, generator=g, device=dev).bfloat16()
         out = torch.empty(a.batch * a.q, D, device=dev, dtype=torch.bfloat16)
+        ks = a.kv_splits if a.kv_splits > 0 else (0 if a.case == "attention" else None)
         run = lambda: ops.attention(q, kp, vp, heads=H, q_rows=a.q, src0_batch_stride=a.pool,  # noqa: E731
-                                    src0_len=a.pool, out=out, kv_splits=0)
+                                    src0_len=a.pool, out=out, kv_splits=ks)
     elif a.case == "quant":
         x = torch.randn(a.m, a.k, generator=g, device=dev).bfloat16()
         run = lambda: ops.quantize_rows(x)  # noqa: E731
@@ -1133,7 +1137,8 @@ def main():
     ap.add_argument("--fp8", action="store_true",
                     help="E4M3 GEMMs (the FP8 weight path); default is the bf16 drop-in")
     ap.add_argument("--case", default="ffn1",
-                    choices=["ffn1", "small", "res_gate", "attention", "verify_attention", "quant", "block"],
+                    choices=["ffn1", "small", "res_gate", "attention", "attention_whole", "verify_attention", "quant",
+                             "block"],
                     help="--workload kernel: which single-kernel case to launch (for ncu captures)")
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=3072)
@@ -1142,6 +1147,8 @@ def main():
     ap.add_argument("--pool", type=int, default=4400)
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--launches", type=int, default=1)
+    ap.add_argument("--kv-splits", type=int, default=0,
+                    help="--case attention: a forced key-split factor for attn_tc_kernel (0: the library's choice)")
     ap.add_argument("--workload", default="cfg4",
                     choices=["cfg4", "cfg3", "cfg2", "cfg1", "action_chunk", "spec_chunk", "kernel"],
                     help="cfg4 (default, the headline): 8 cfg2 rollouts per GPU; cfg3: the "
