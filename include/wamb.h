@@ -177,11 +177,13 @@ typedef struct wamb_attention_args {
    * wamb_attention_split_bytes(args) bytes, 256-byte aligned and zero-filled
    * before its first use (the library leaves its counters zero after every
    * call). With it, when the (query tile pair, head, batch row) items alone
-   * would leave SMs idle, each item's keys are split over kv_splits CTAs
-   * (0: chosen by the library, 1: never) whose partial softmax results the
-   * last of them merges in split order (results do not depend on timing).
-   * Not used with candidate rows (src0_map). Calls sharing it must be
-   * ordered on one stream. */
+   * would leave SMs idle, their keys are shared out: for queries longer
+   * than 128 rows and kv_splits 0 or 1, key tiles are cut evenly over one
+   * CTA per SM (stream-K); otherwise each item's keys are split over
+   * kv_splits CTAs (0: chosen by the library, 1: never). The CTA that
+   * completes an item merges its partial softmax results in key order
+   * (results do not depend on timing). Not used with candidate rows
+   * (src0_map). Calls sharing it must be ordered on one stream. */
   void* split_workspace;
   size_t split_workspace_bytes;
   int32_t kv_splits;
@@ -300,7 +302,7 @@ enum wamb_tap {
   WAMB_TAP_SK_FLAGS = 17,   /* zero region at offset 0 of every layout: stream-K flags of the
                                two-CTA GEMMs, then split-key counters of the self attention */
   WAMB_TAP_SK_PART = 18,    /* stream-K fp32 partials (M >= 512 only) */
-  WAMB_TAP_ATTN_PART = 19,  /* split-key partials of the self attention (small batches only) */
+  WAMB_TAP_ATTN_PART = 19,  /* partials of the self attention when its items do not fill whole waves */
   WAMB_TAP_COUNT = 20
 };
 
