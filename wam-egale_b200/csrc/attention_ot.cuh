@@ -35,10 +35,9 @@ namespace wamb {
 
 constexpr int ATO_SLOTS = 3;
 // exp2 of keys 2i, 2i + 1 of every 32 on the MUFU for i < ATO_MUFU_PAIRS,
-// the rest as the cubic on the FMA pipe: the softmax warps are bound by the
-// MUFU's 16 results per clock per SM, so moving a sixth of the keys off it
-// shortens each key tile's softmax.
-constexpr int ATO_MUFU_PAIRS = 11;
+// the rest as the cubic on the FMA pipe. One cfg2 chunk (CUDA events): 12
+// pairs 78.5 us, 11 pairs 79.2 us, 10 pairs 81.1 us.
+constexpr int ATO_MUFU_PAIRS = 12;
 
 struct AttnOtSmem {
   static constexpr uint32_t Q_OFF = 0;
