@@ -40,7 +40,9 @@ struct AttnOtSkSmem {
   // q_full, q_empty, full[3], empty[3], s_full[2], s_free[2], p_full, p_free,
   // o_done, o_free, drain
   static constexpr uint32_t NBARS = 17;
-  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16;
+  // After the barriers: TMEM address, abort flag, spare, segment flag, then
+  // the softmax warps' grow flags [2 key-tile parities][8 warps].
+  static constexpr uint32_t TOTAL = 1024 + BAR_OFF + NBARS * 8 + 16 + 64;
   static_assert(TOTAL <= 232448, "attention shared memory exceeds 227 KB");
   // bf16 output staging [256 rows][128] over the P buffer.
   static_assert(256 * 128 * 2 <= 2 * P_ATOM, "output staging does not fit");
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   auto slot_phase = [&](int x) { return static_cast<uint32_t>((x / ATO_SLOTS) & 1); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* grow_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* grow_w = reinterpret_cast<volatile int*>(tmem_slot + 4);   // [2][8]
   volatile int* last_seg = reinterpret_cast<volatile int*>(tmem_slot + 3);
 
   if (p.trigger) pdl_trigger();
@@ -282,7 +284,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     mbar_init(o_free, 8);             // all eight softmax warps read O^T
     mbar_init(drain, 1);
     *abort_flag = 0;
-    *grow_flag = 0;
     fence_barrier_init();
   }
   if (warp == ATT_MMA_WARP) {
@@ -458,7 +459,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         float m_new, alpha, lsum;
         uint32_t pk[64];
         float s[128];
-        uint64_t sum2 = f2(0.f, 0.f), scale2 = 0, neg_m2 = 0;
+        uint64_t sum2 = f2(0.f, 0.f), sum2p = f2(0.f, 0.f), scale2 = 0, neg_m2 = 0;
         // exp2 of keys [32 c, 32 c + 32) into pk[16 c, 16 c + 16): keys 24..31
         // of every 32 take the cubic, the rest the MUFU exp2 (as in
         // attn_tc_kernel).
@@ -475,7 +476,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           for (int i = 12; i < 16; ++i) {
             const int kk = 32 * c + 2 * i;
             const uint64_t e = ex2_poly2(ffma2(f2(s[kk], s[kk + 1]), scale2, neg_m2));
-            sum2 = fadd2(sum2, e);
+            sum2p = fadd2(sum2p, e);
             const float2 ev = f2_split(e);
             pk[16 * c + i] = pack_bf16(ev.x, ev.y);
           }
@@ -504,13 +505,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             for (int i = 0; i < 128; ++i)
               if (i >= hi) s[i] = -INFINITY;
           }
-          float mx0 = -INFINITY, mx1 = -INFINITY;
+          float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 64; i += 2) {
+          for (int i = 0; i < 32; i += 2) {
             mx0 = fmax3(mx0, s[i], s[i + 1]);
-            mx1 = fmax3(mx1, s[64 + i], s[64 + i + 1]);
+            mx1 = fmax3(mx1, s[32 + i], s[32 + i + 1]);
+            mx2 = fmax3(mx2, s[64 + i], s[64 + i + 1]);
+            mx3 = fmax3(mx3, s[96 + i], s[96 + i + 1]);
           }
-          const float mx = fmaxf(mx0, mx1) * p.scale_log2;
+          const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
           // Keep the stale max unless the new one exceeds it by more than 2^8.
           grow = mx > m_used + ATT_RESCALE_LOG2;
           m_new = grow ? mx : m_used;
@@ -528,27 +531,34 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           // The previous O^T update has read P and written O^T.
           if (ok) ok = mbar_wait(p_free, (gj - 1) & 1, abort_flag);
           tc_fence_after();
-          // Rows whose max grew: scale their O^T columns (all 8 warps, each
-          // its 32 head dims x its tile's 128 queries) before the next update.
-          row_f[q] = alpha;
-          if (__any_sync(0xffffffffu, grow) && lane == 0) *grow_flag = 1;
+          // Rows whose max grew: scale their O^T columns before the next
+          // update. Grow flags as in attn_ot_kernel, the set chosen by the
+          // CTA's key-tile count (the epilogues between segments are named
+          // barriers of all eight warps too, so a set is read by every warp
+          // before it is written again).
+          volatile int* gw = grow_w + (gj & 1) * 8;
+          const bool g_any = __any_sync(0xffffffffu, grow);
+          if (lane == 0) gw[warp] = g_any ? 1 : 0;
           asm volatile("bar.sync 1, 256;" ::: "memory");
-          const bool rescale = *grow_flag != 0;
-          if (rescale && ok) {
+          const bool rescale = (gw[0] | gw[1] | gw[2] | gw[3] | gw[4] | gw[5] | gw[6] | gw[7]) != 0;
+          if (rescale) {
+            row_f[q] = alpha;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            if (ok) {
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              float o[32];
-              const uint32_t oc = 256 + t * 128 + c * 32;
-              tmem_ld32(tmem + lane_base + oc, o);
-              tmem_wait_ld();
+              for (int c = 0; c < 4; ++c) {
+                float o[32];
+                const uint32_t oc = 256 + t * 128 + c * 32;
+                tmem_ld32(tmem + lane_base + oc, o);
+                tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= row_f[t * 128 + c * 32 + i];
-              tmem_st32(tmem + lane_base + oc, o);
+                for (int i = 0; i < 32; ++i) o[i] *= row_f[t * 128 + c * 32 + i];
+                tmem_st32(tmem + lane_base + oc, o);
+              }
+              tmem_wait_st();
             }
-            tmem_wait_st();
+            asm volatile("bar.sync 1, 256;" ::: "memory");
           }
-          asm volatile("bar.sync 1, 256;" ::: "memory");   // every warp read the flag and alphas
-          if (rescale && threadIdx.x == 0) *grow_flag = 0;
         }
 #pragma unroll
         for (int c = 0; c < 12; ++c) store_p(c);
@@ -556,7 +566,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
         for (int c = 12; c < 16; ++c) store_p(c);
         {
-          const float2 sv = f2_split(sum2);
+          const float2 sv = f2_split(fadd2(sum2, sum2p));
           lsum = sv.x + sv.y;
         }
         fence_proxy_async();
